@@ -1,0 +1,453 @@
+#!/usr/bin/env python
+"""Benchmark of the GGUF quantized-linear hot path on B200.
+
+Headline workload (config 2 of the benchmark plan): the Q4_K decode GEMV over
+the seven projections of one Llama-7B-shaped decoder layer (q, k, v, o
+4096x4096; gate, up 11008x4096; down 4096x11008), fp32 activations at batch 1.
+One "step" = one grouped dequant-GEMV launch over the whole layer set (plus
+its activation-prep kernel).  The metric is HBM GB/s of algorithmic bytes
+(packed weights + fp32 x + fp32 y) per second.
+
+Timing rules applied:
+* W warm-up steps, then exactly K timed steps between barrier +
+  cuda.synchronize on both sides, CUDA events on the launching stream; the
+  max over ranks is reported (one rank at N=1).
+* Inputs larger than L2: R distinct copies of the layer set (R * 113.8 MB >=
+  4x the 126 MB L2) are used round-robin, one per step, so no step finds its
+  weights in L2.
+* SM clock and clock-event reasons are sampled through NVML during the run.
+
+Usage:
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--mix q4_k|q4_k_m]
+  python bench.py --impl reference ...   # the reference's CPU path (oracle port) on host cores
+Multi-GPU (N > 1, under torchrun): the layer set is sharded tensor-parallel,
+column-parallel q/k/v/gate/up and row-parallel o/down (super-block aligned
+K ranges), with an NCCL all-gather after the column-parallel outputs and an
+all-reduce after the row-parallel ones.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+METRIC = "Q4_K dequant-GEMV HBM GB/s (% of 8 TB/s); prefill dequant-GEMM TFLOP/s"
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--mix", choices=["q4_k", "q4_k_m"], default="q4_k")
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--sweep", action="store_true", help="also time batch 4 and 16 (reported under 'batches')")
+    return ap.parse_args(argv)
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return dict(FALLBACK_PEAKS)
+
+
+def profiled_traffic(key: str):
+    """Per-launch DRAM bytes of `key` from profiles/traffic.txt (ncu capture summaries)."""
+    p = ROOT / "profiles" / "traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == key and not line.startswith("#"):
+            try:
+                return int(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the reference's own algorithm (oracle port of gguf._dequantize +
+# GenericGemmKernel.matmul_f32) on the host cores
+# ---------------------------------------------------------------------------
+def cpu_reference_leg(specs, packed, batch, seed, budget_s=12.0, steps=None):
+    from oracle import gguf_oracle as O
+
+    rng = np.random.default_rng(seed + 7)
+    t0 = time.perf_counter()
+    weights = [O.dequantize_matrix(s.qtype, p, s.n_rows, s.k) for s, p in zip(specs, packed)]
+    t_dequant = time.perf_counter() - t0
+    xs = [rng.standard_normal((batch, s.k)).astype(np.float32) for s in specs]
+    # warm (steady-state) path of the reference: fp32 cache @ x per projection
+    for x, w in zip(xs, weights):
+        O.matmul_f32(x, w)
+    per = []
+    n = 0
+    t_start = time.perf_counter()
+    i = 0
+    while True:
+        j = i % len(specs)
+        t = time.perf_counter()
+        O.matmul_f32(xs[j], weights[j])
+        per.append((j, time.perf_counter() - t))
+        i += 1
+        n += 1
+        if steps is not None and n >= steps:
+            break
+        if steps is None and time.perf_counter() - t_start > budget_s and i % len(specs) == 0:
+            break
+    by = {}
+    for j, dt in per:
+        by.setdefault(j, []).append(dt)
+    layer_s = sum(float(np.median(v)) for v in by.values())
+    from dracort_b200.workloads import algorithmic_bytes
+
+    gbs = algorithmic_bytes(specs, batch) / layer_s / 1e9
+    cold_s = t_dequant + layer_s
+    return {
+        "layer_warm_s": layer_s,
+        "layer_cold_s": cold_s,
+        "dequant_s": t_dequant,
+        "value_warm_gbs": gbs,
+        "value_cold_gbs": algorithmic_bytes(specs, batch) / cold_s / 1e9,
+        "matmuls_timed": n,
+        "per_step": per,
+    }
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from dracort_b200.workloads import algorithmic_bytes, encode_specs, layer_specs
+
+    specs = layer_specs(args.mix)
+    packed = encode_specs(specs, args.seed)
+    for _ in range(max(0, args.warmup)):
+        pass
+    # each step: one projection's matmul on the fp32 cache (rotating through the
+    # seven), i.e. a bounded sample of the layer-set workload
+    res = cpu_reference_leg(specs, packed, args.batch, args.seed, steps=max(1, args.steps))
+    step_bytes = []
+    total_t = 0.0
+    total_b = 0
+    for j, dt in res["per_step"]:
+        s = specs[j]
+        total_b += s.nbytes + 4 * args.batch * (s.k + s.n_rows)
+        total_t += dt
+    value = total_b / total_t / 1e9
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total_t / max(1, len(res["per_step"])), 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.02) weights, GGUF-encoded; N(0,1) activations)",
+        "config": {"workload": f"config2_{args.mix}_layer_decode_gemv", "batch": args.batch,
+                   "step": "one projection matmul of the layer set, rotating q,k,v,o,gate,up,down",
+                   "parallelism": "host"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": f"{len(res['per_step'])} projection matmuls on the fp32 dequant cache "
+                                   f"(reference steady state, numpy/OpenBLAS default threads); "
+                                   f"first-touch dequant of the layer set took {res['dequant_s']:.2f} s"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist.group.WORLD
+
+    from dracort_b200 import gguf_ops as G
+    from dracort_b200.telemetry import ClockSampler
+    from dracort_b200.workloads import algorithmic_bytes, encode_specs, layer_specs
+
+    peaks = measured_peaks()
+    specs_full = layer_specs(args.mix)
+    packed_full = encode_specs(specs_full, args.seed)  # same seed on every rank
+    batch = args.batch
+
+    if world > 1:
+        from dracort_b200.parallel.tp import TPDecodeLayer
+
+        layer = TPDecodeLayer(specs_full, packed_full, rank, world, batch, dev, seed=args.seed, group=pg)
+        step_fn = layer.step
+        n_copies = layer.n_copies
+        gpu_launches_per_step = layer.launches_per_step
+        local_bytes = layer.local_weight_bytes
+    else:
+        layer = None
+
+    sampler = ClockSampler(local).start()
+    result = {}
+
+    if world == 1:
+        raw = [torch.from_numpy(p.reshape(-1)).to(dev) for p in packed_full]
+        tiled0 = [G.repack(s.qtype, r, s.n_rows, s.k) for s, r in zip(specs_full, raw)]
+        del raw
+        set_bytes = sum(t.numel() for t in tiled0)
+        n_copies = max(2, math.ceil(4 * L2_BYTES / set_bytes))
+        copies = [tiled0] + [[t.clone() for t in tiled0] for _ in range(n_copies - 1)]
+        rng = torch.Generator(device="cpu").manual_seed(args.seed + 1)
+        xs = [torch.randn((batch, s.k), generator=rng).to(dev) for s in specs_full]
+        ys = [torch.empty((batch, s.n_rows), device=dev) for s in specs_full]
+        plans = [G.GemvPlan([G.GemvProblem(s.qtype, c[i], xs[i], ys[i], s.n_rows, s.k)
+                             for i, s in enumerate(specs_full)]) for c in copies]
+        local_bytes = set_bytes
+        gpu_launches_per_step = 2
+
+        def step_fn(i):
+            plans[i % n_copies].run()
+
+    # -- warm-up (eager), then CUDA-graph capture of one rotation ---------------
+    for i in range(max(3, args.warmup)):
+        step_fn(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+    graphs = {}
+
+    def graph_for(nsteps):
+        if nsteps not in graphs:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(nsteps):
+                    step_fn(i)
+            graphs[nsteps] = g
+        return graphs[nsteps]
+
+    use_graph = world == 1 or (layer is not None and layer.graph_safe)
+    if use_graph:
+        gfull = graph_for(n_copies)
+        for _ in range(2):
+            gfull.replay()
+        torch.cuda.synchronize()
+
+    K = args.steps
+
+    def timed(fn_steps):
+        if pg is not None:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        t_wall0 = time.perf_counter()
+        s_ev = torch.cuda.Event(enable_timing=True)
+        e_ev = torch.cuda.Event(enable_timing=True)
+        cur = torch.cuda.current_stream()
+        s_ev.record(cur)
+        fn_steps()
+        e_ev.record(cur)
+        torch.cuda.synchronize()
+        if pg is not None:
+            torch.distributed.barrier()
+        t_wall1 = time.perf_counter()
+        ms = s_ev.elapsed_time(e_ev)
+        if pg is not None:
+            t = torch.tensor([ms], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms, t_wall0, t_wall1
+
+    def graph_steps():
+        full, rem = divmod(K, n_copies)
+        for _ in range(full):
+            gfull.replay()
+        if rem:
+            graph_for(rem).replay()
+
+    def eager_steps():
+        for i in range(K):
+            step_fn(i)
+
+    if use_graph:
+        graph_for(K % n_copies) if K % n_copies else None
+        torch.cuda.synchronize()
+    ms, tw0, tw1 = timed(graph_steps if use_graph else eager_steps)
+    ms_step = ms / K
+    alg = algorithmic_bytes(specs_full, batch)
+    value = alg / (ms_step * 1e-3) / 1e9  # whole-job GB/s (all ranks' shards together)
+    clocks = sampler.summary(tw0, tw1)
+
+    # -- batch sweep (config 2 lists batch 1, 4 and 16) -------------------------
+    batches = {}
+    if args.sweep and world == 1:
+        for b2 in (4, 16):
+            xs2 = [torch.randn((b2, s.k), device=dev) for s in specs_full]
+            ys2 = [torch.empty((b2, s.n_rows), device=dev) for s in specs_full]
+            plans2 = [G.GemvPlan([G.GemvProblem(s.qtype, c[i], xs2[i], ys2[i], s.n_rows, s.k)
+                                  for i, s in enumerate(specs_full)]) for c in copies]
+            for i in range(10):
+                plans2[i % n_copies].run()
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=stream):
+                for i in range(n_copies):
+                    plans2[i].run()
+            reps = max(1, K // n_copies)
+            torch.cuda.synchronize()
+            s_ev = torch.cuda.Event(enable_timing=True)
+            e_ev = torch.cuda.Event(enable_timing=True)
+            s_ev.record()
+            for _ in range(reps):
+                g2.replay()
+            e_ev.record()
+            torch.cuda.synchronize()
+            ms2 = s_ev.elapsed_time(e_ev) / (reps * n_copies)
+            batches[str(b2)] = {"gbs": round(algorithmic_bytes(specs_full, b2) / (ms2 * 1e-3) / 1e9, 1),
+                                "us_per_step": round(ms2 * 1e3, 3)}
+            del g2, plans2
+
+    # -- end to end through the public API, host buffers -----------------------
+    e2e = None
+    if not args.no_e2e and world == 1:
+        xh = [torch.randn((batch, s.k)).pin_memory() for s in specs_full]
+        yh = [torch.empty((batch, s.n_rows)).pin_memory() for s in specs_full]
+        h2d = sum(t.numel() * 4 for t in xh)
+        d2h = sum(t.numel() * 4 for t in yh)
+
+        def e2e_steps():
+            for i in range(K):
+                for a, b in zip(xs, xh):
+                    a.copy_(b, non_blocking=True)
+                plans[i % n_copies].run()
+                for a, b in zip(yh, ys):
+                    a.copy_(b, non_blocking=True)
+
+        for _ in range(3):
+            pass
+        ms_e2e, _, _ = timed(e2e_steps)
+        e2e = {"value": round(alg / (ms_e2e / K * 1e-3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "ms_per_step": round(ms_e2e / K, 5),
+               "path": "pinned host x -> cuda (7 copies) -> GemvPlan.run (C ABI) -> pinned host y (7 copies), eager"}
+    elif world > 1 and not args.no_e2e and layer is not None:
+        e2e = layer.e2e(K, timed)
+
+    sampler.stop()
+
+    # -- CPU baseline (rank 0, N=1) --------------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res = cpu_reference_leg(specs_full, packed_full, batch, args.seed, budget_s=10.0)
+        cpu = {"value": round(res["value_warm_gbs"], 3), "unit": "GB/s", "cores": os.cpu_count(),
+               "kind": "port",
+               "sample": (f"reference path (oracle port of gguf._dequantize + GenericGemmKernel.matmul_f32) over "
+                          f"the same layer set at batch {batch}: {res['matmuls_timed']} projection matmuls on the "
+                          f"fp32 cache, median per projection summed = {res['layer_warm_s'] * 1e3:.2f} ms/layer "
+                          f"(warm); cold first touch incl. dequant = {res['layer_cold_s']:.2f} s/layer "
+                          f"({res['value_cold_gbs']:.4f} GB/s); numpy/OpenBLAS default threads")}
+
+    if rank == 0:
+        achieved = value
+        traffic = profiled_traffic(f"gemv_{args.mix}_layer_b{batch}")
+        line = {
+            "metric": METRIC,
+            "value": round(value, 3),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 6),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights, GGUF-encoded; N(0,1) fp32 activations)",
+            "config": {
+                "workload": f"config2_{args.mix}_layer_decode_gemv",
+                "batch": batch,
+                "weights": "q,k,v,o 4096x4096; gate,up 11008x4096; down 4096x11008",
+                "l2": f"inputs larger than L2: {n_copies} layer-set copies rotated "
+                      f"({n_copies * local_bytes / 1e6:.0f} MB per GPU > 4x126 MB L2)",
+                "parallelism": f"tp{world}",
+                "graph": bool(use_graph),
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": round(achieved, 2),
+                "peak": peaks["hbm_gbs"] * world,
+                "unit": "GB/s",
+                "frac": round(achieved / (peaks["hbm_gbs"] * world), 4),
+                "traffic": traffic,
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs x {world} GPUs)",
+                "kernel": "gemv_kernel (+ gemv_prep_kernel) per step; algorithmic bytes "
+                          f"{alg} per step / device time per step",
+            },
+            "gpu_launches": gpu_launches_per_step * K,
+            "clocks": clocks,
+        }
+        if batches:
+            line["batches"] = batches
+        if e2e is not None:
+            line["e2e"] = e2e
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+    if layer is not None:
+        layer.close()
+    graphs.clear()
+    if pg is not None:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,174 @@
+// capi.cu — the extern "C" surface declared in include/draco_gguf.h:
+// argument checks, status codes, thread-local error strings, dispatch.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace draco {
+
+static thread_local char g_err[512] = {0};
+
+static int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+static int ok() {
+  g_err[0] = 0;
+  return DRACO_OK;
+}
+static int cuda_fail(cudaError_t e, const char* what) {
+  return fail(DRACO_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int device_sm_count() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+static bool type_ok(int qt) { return qt == kQ8_0 || qt == kQ4_K || qt == kQ6_K; }
+
+// Shape / type / layout checks shared by the weight entry points.  Mirrors the
+// reference's DracoFormatError cases (gguf.py:284-296).
+static int check_weight(int qt, int layout, const void* p, int64_t n_rows, int64_t k, const char* fn) {
+  if (!type_ok(qt))
+    return fail(DRACO_ERR_TYPE, "%s: GGUF quantization type %d is not supported (supported: Q8_0=8, Q4_K=12, Q6_K=14)",
+                fn, qt);
+  if (layout != DRACO_LAYOUT_GGUF && layout != DRACO_LAYOUT_GGUF_DLAST && layout != DRACO_LAYOUT_TILED)
+    return fail(DRACO_ERR_TYPE, "%s: unknown layout %d", fn, layout);
+  if (n_rows < 0 || k < 0) return fail(DRACO_ERR_SHAPE, "%s: negative shape [%lld, %lld]", fn, (long long)n_rows,
+                                       (long long)k);
+  const int bs = block_size_of(qt);
+  if (k % bs != 0)
+    return fail(DRACO_ERR_SHAPE, "%s: row length %lld is not divisible by block size %d for ggml type %d", fn,
+                (long long)k, bs, qt);
+  if (n_rows > (int64_t)1 << 30 || k > (int64_t)1 << 30)
+    return fail(DRACO_ERR_SHAPE, "%s: shape [%lld, %lld] too large", fn, (long long)n_rows, (long long)k);
+  if (n_rows * k > 0 && p == nullptr) return fail(DRACO_ERR_ARG, "%s: null weight pointer", fn);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+  if (layout == DRACO_LAYOUT_TILED && (a & 15)) return fail(DRACO_ERR_ALIGN, "%s: TILED weight must be 16-byte aligned", fn);
+  if (layout != DRACO_LAYOUT_TILED && (a & 1)) return fail(DRACO_ERR_ALIGN, "%s: GGUF weight must be 2-byte aligned", fn);
+  return DRACO_OK;
+}
+
+}  // namespace draco
+
+using namespace draco;
+
+extern "C" {
+
+const char* draco_version(void) { return "draco_gguf 0.1.0 sm_100a"; }
+
+const char* draco_last_error_string(void) { return g_err; }
+
+int draco_gguf_block_geometry(int qtype, int* block_size, int* block_bytes) {
+  if (!type_ok(qtype)) return fail(DRACO_ERR_TYPE, "block_geometry: unsupported ggml type %d", qtype);
+  if (block_size) *block_size = block_size_of(qtype);
+  if (block_bytes) *block_bytes = block_bytes_of(qtype);
+  return ok();
+}
+
+int64_t draco_gguf_packed_bytes(int qtype, int64_t n_rows, int64_t k) {
+  if (!type_ok(qtype) || n_rows < 0 || k < 0 || k % block_size_of(qtype)) return -1;
+  return n_rows * (k / block_size_of(qtype)) * block_bytes_of(qtype);
+}
+
+int64_t draco_gguf_tiled_bytes(int qtype, int64_t n_rows, int64_t k) {
+  if (!type_ok(qtype) || n_rows < 0 || k < 0 || k % block_size_of(qtype)) return -1;
+  return tiled_total_bytes(tiled_geom(qtype, n_rows, k));
+}
+
+int draco_gguf_dequant(int qtype, int layout, const void* blocks, float* out, int64_t n_rows, int64_t k,
+                       void* stream) {
+  int rc = check_weight(qtype, layout, blocks, n_rows, k, "dequant");
+  if (rc) return rc;
+  if (n_rows * k == 0) return ok();
+  if (!out) return fail(DRACO_ERR_ARG, "dequant: null output");
+  if (reinterpret_cast<uintptr_t>(out) & 15) return fail(DRACO_ERR_ALIGN, "dequant: output must be 16-byte aligned");
+  cudaError_t e = launch_dequant_f32(qtype, layout, blocks, out, n_rows, k, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "dequant");
+}
+
+int draco_gguf_dequant_bf16(int qtype, int layout, const void* blocks, uint16_t* out, int64_t n_rows, int64_t k,
+                            void* stream) {
+  int rc = check_weight(qtype, layout, blocks, n_rows, k, "dequant_bf16");
+  if (rc) return rc;
+  if (n_rows * k == 0) return ok();
+  if (!out) return fail(DRACO_ERR_ARG, "dequant_bf16: null output");
+  if (reinterpret_cast<uintptr_t>(out) & 15)
+    return fail(DRACO_ERR_ALIGN, "dequant_bf16: output must be 16-byte aligned");
+  cudaError_t e = launch_dequant_bf16(qtype, layout, blocks, out, n_rows, k, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "dequant_bf16");
+}
+
+int draco_gguf_repack(int qtype, int src_layout, const void* src, void* dst, int64_t n_rows, int64_t k,
+                      void* stream) {
+  if (src_layout == DRACO_LAYOUT_TILED) return fail(DRACO_ERR_TYPE, "repack: source must be a GGUF layout");
+  int rc = check_weight(qtype, src_layout, src, n_rows, k, "repack");
+  if (rc) return rc;
+  if (n_rows * k == 0) return ok();
+  if (!dst) return fail(DRACO_ERR_ARG, "repack: null destination");
+  if (reinterpret_cast<uintptr_t>(dst) & 15) return fail(DRACO_ERR_ALIGN, "repack: destination must be 16-byte aligned");
+  cudaError_t e = launch_repack(qtype, src_layout, src, dst, n_rows, k, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "repack");
+}
+
+static int check_gemv_problems(const draco_gemv_problem* probs, int n, int batch) {
+  if (!probs || n < 1 || n > DRACO_GEMV_MAX_PROBLEMS)
+    return fail(DRACO_ERR_ARG, "gemv: need 1..%d problems, got %d", DRACO_GEMV_MAX_PROBLEMS, n);
+  if (batch < 1 || batch > DRACO_GEMV_MAX_BATCH)
+    return fail(DRACO_ERR_ARG, "gemv: batch %d outside 1..%d", batch, DRACO_GEMV_MAX_BATCH);
+  for (int i = 0; i < n; ++i) {
+    const draco_gemv_problem& q = probs[i];
+    int rc = check_weight(q.qtype, DRACO_LAYOUT_TILED, q.w, q.n_rows, q.k, "gemv");
+    if (rc) return rc;
+    if (q.n_rows * q.k > 0 && (!q.x || !q.y)) return fail(DRACO_ERR_ARG, "gemv: problem %d has a null x or y", i);
+    if (q.ldx < q.k || q.ldy < q.n_rows)
+      return fail(DRACO_ERR_SHAPE, "gemv: problem %d leading dimensions too small", i);
+  }
+  return DRACO_OK;
+}
+
+size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* probs, int n_problems, int batch) {
+  if (check_gemv_problems(probs, n_problems, batch)) return 0;
+  return gemv_workspace_bytes(probs, n_problems, batch);
+}
+
+int draco_gguf_gemv_grouped(const draco_gemv_problem* probs, int n_problems, int batch, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  int rc = check_gemv_problems(probs, n_problems, batch);
+  if (rc) return rc;
+  char msg[256] = {0};
+  rc = gemv_launch(probs, n_problems, batch, workspace, workspace_bytes, (cudaStream_t)stream, msg, sizeof(msg));
+  if (rc) return fail(rc, "%s", msg);
+  return ok();
+}
+
+int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias, int batch,
+                    int64_t n_rows, int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
+  draco_gemv_problem p;
+  memset(&p, 0, sizeof(p));
+  p.qtype = qtype;
+  p.w = w_tiled;
+  p.x = x;
+  p.y = y;
+  p.bias = bias;
+  p.n_rows = n_rows;
+  p.k = k;
+  p.ldx = k;
+  p.ldy = n_rows;
+  return draco_gguf_gemv_grouped(&p, 1, batch, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

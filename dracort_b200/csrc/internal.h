@@ -1,0 +1,26 @@
+// internal.h — declarations shared between the kernel translation units and
+// the C ABI (capi.cu).  Not part of the public interface.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/draco_gguf.h"
+
+namespace draco {
+
+cudaError_t launch_dequant_f32(int qt, int layout, const void* src, float* out, int64_t n_rows, int64_t k,
+                               cudaStream_t st);
+cudaError_t launch_dequant_bf16(int qt, int layout, const void* src, uint16_t* out, int64_t n_rows, int64_t k,
+                                cudaStream_t st);
+cudaError_t launch_repack(int qt, int src_layout, const void* src, void* dst, int64_t n_rows, int64_t k,
+                          cudaStream_t st);
+
+// Grouped GEMV: plan + launch.  Returns a DRACO_* status; fills `msg` on error.
+size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch);
+int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
+                char* msg, size_t msg_len);
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+}  // namespace draco

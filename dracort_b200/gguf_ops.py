@@ -1,0 +1,253 @@
+"""Torch-facing functions over the C ABI (libdraco_gguf.so).
+
+Every function here takes CUDA tensors, passes raw pointers and the current
+CUDA stream to the library, and raises the reference exception classes on
+failure.  There is no CPU path: a CPU tensor or a missing library raises.
+
+Functions and the reference code they replace:
+
+* ``dequantize``       — draco/format/gguf.py:_dequantize (gguf.py:272-497)
+* ``repack``           — GGUFReader.get_tensor's first-access transform
+                          (gguf.py:820-834), here into the TILED device layout
+* ``gemv``/``gemv_grouped`` — executor._linear (executor.py:47-79) with
+                          GenericGemmKernel.matmul_f32 (generic.py:32-33)
+"""
+
+from __future__ import annotations
+
+import threading
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+
+from dracort_b200 import _native as N
+from dracort_b200.exceptions import DracoFormatError, KernelError
+from dracort_b200.format.gguf_types import BLOCK_LAYOUTS, Q6K_D_FIRST, Q6K_D_LAST
+
+LAYOUTS = {"gguf": N.LAYOUT_GGUF, "gguf_dlast": N.LAYOUT_GGUF_DLAST, "tiled": N.LAYOUT_TILED}
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this library has no CPU path)")
+
+
+def _layout_id(layout: str) -> int:
+    try:
+        return LAYOUTS[layout]
+    except KeyError:
+        raise ValueError(f"unknown layout {layout!r}; expected one of {sorted(LAYOUTS)}") from None
+
+
+def layout_for_q6k_order(order: str) -> str:
+    return "gguf_dlast" if order == Q6K_D_LAST else "gguf"
+
+
+def packed_nbytes(qtype: int, n_rows: int, k: int) -> int:
+    n = N.load().draco_gguf_packed_bytes(qtype, n_rows, k)
+    if n < 0:
+        raise DracoFormatError(f"ggml type {qtype} with row length {k} is not a supported GGUF block tensor")
+    return int(n)
+
+
+def tiled_nbytes(qtype: int, n_rows: int, k: int) -> int:
+    n = N.load().draco_gguf_tiled_bytes(qtype, n_rows, k)
+    if n < 0:
+        raise DracoFormatError(f"ggml type {qtype} with row length {k} is not a supported GGUF block tensor")
+    return int(n)
+
+
+def dequantize(qtype: int, blocks: torch.Tensor, n_rows: int, k: int, layout: str = "gguf",
+               out_dtype: torch.dtype = torch.float32, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Dequantize a GGUF weight on the GPU into an [n_rows, k] fp32 (bit-exact) or bf16 tensor."""
+    _require_cuda(blocks, "blocks")
+    lib = N.load()
+    if out is None:
+        out = torch.empty((n_rows, k), dtype=out_dtype, device=blocks.device)
+    if out_dtype == torch.float32:
+        fn = lib.draco_gguf_dequant
+    elif out_dtype == torch.bfloat16:
+        fn = lib.draco_gguf_dequant_bf16
+    else:
+        raise ValueError("out_dtype must be float32 or bfloat16")
+    need = tiled_nbytes(qtype, n_rows, k) if layout == "tiled" else packed_nbytes(qtype, n_rows, k)
+    if blocks.numel() * blocks.element_size() < need:
+        raise DracoFormatError(f"payload of {blocks.numel() * blocks.element_size()} bytes, {need} needed")
+    rc = fn(qtype, _layout_id(layout), blocks.data_ptr(), out.data_ptr(), n_rows, k, _stream_ptr(blocks.device))
+    N.check(rc, "dequant")
+    return out
+
+
+def repack(qtype: int, blocks: torch.Tensor, n_rows: int, k: int, layout: str = "gguf") -> torch.Tensor:
+    """GGUF-layout payload (CUDA uint8) -> TILED payload (new CUDA uint8 tensor)."""
+    _require_cuda(blocks, "blocks")
+    if blocks.numel() * blocks.element_size() < packed_nbytes(qtype, n_rows, k):
+        raise DracoFormatError("payload shorter than the tensor's block count")
+    dst = torch.empty(tiled_nbytes(qtype, n_rows, k), dtype=torch.uint8, device=blocks.device)
+    rc = N.load().draco_gguf_repack(qtype, _layout_id(layout), blocks.data_ptr(), dst.data_ptr(), n_rows, k,
+                                    _stream_ptr(blocks.device))
+    N.check(rc, "repack")
+    return dst
+
+
+# ---------------------------------------------------------------------------
+# GEMV workspace: one zero-initialised buffer per (device, stream), grown on
+# demand.  The kernels leave their counters at zero after every call.
+# ---------------------------------------------------------------------------
+_ws_lock = threading.Lock()
+_workspaces: Dict[Tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    key = (device.index if device.index is not None else torch.cuda.current_device(), _stream_ptr(device))
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        return ws
+
+
+def reset_workspaces() -> None:
+    """Drop cached workspaces (after an error their counters may be stale)."""
+    with _ws_lock:
+        _workspaces.clear()
+
+
+def workspace_status(device: Optional[torch.device] = None) -> int:
+    """Status word the GEMV kernels record (0 = ok, else a DRACO_ERR_* code).  Synchronises."""
+    dev = device or torch.device("cuda", torch.cuda.current_device())
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(), _stream_ptr(dev))
+    ws = _workspaces.get(key)
+    if ws is None:
+        return 0
+    return int(ws[:4].view(torch.int32).item())
+
+
+@dataclass
+class GemvProblem:
+    """One linear layer of a grouped GEMV call (host-side mirror of draco_gemv_problem)."""
+
+    qtype: int
+    w_tiled: torch.Tensor
+    x: torch.Tensor  # [B, k] fp32 CUDA
+    y: torch.Tensor  # [B, n_rows] fp32 CUDA
+    n_rows: int
+    k: int
+    bias: Optional[torch.Tensor] = None
+
+
+def _to_struct(p: GemvProblem) -> N.GemvProblem:
+    for t, nm in ((p.w_tiled, "w_tiled"), (p.x, "x"), (p.y, "y")):
+        _require_cuda(t, nm)
+    if p.x.dtype != torch.float32 or p.y.dtype != torch.float32:
+        raise ValueError("gemv: x and y must be float32")
+    if p.x.dim() != 2 or p.y.dim() != 2 or p.x.stride(1) != 1 or p.y.stride(1) != 1:
+        raise ValueError("gemv: x and y must be 2-D with unit inner stride")
+    if p.x.shape[1] != p.k or p.y.shape[1] != p.n_rows or p.x.shape[0] != p.y.shape[0]:
+        raise DracoFormatError(
+            f"gemv: x {tuple(p.x.shape)} / y {tuple(p.y.shape)} do not match weight [{p.n_rows}, {p.k}]")
+    if p.bias is not None:
+        _require_cuda(p.bias, "bias")
+        if p.bias.dtype != torch.float32 or p.bias.numel() != p.n_rows or not p.bias.is_contiguous():
+            raise ValueError("gemv: bias must be a contiguous float32 [n_rows] tensor")
+    s = N.GemvProblem()
+    s.qtype = p.qtype
+    s.w = p.w_tiled.data_ptr()
+    s.x = p.x.data_ptr()
+    s.y = p.y.data_ptr()
+    s.bias = p.bias.data_ptr() if p.bias is not None else None
+    s.n_rows = p.n_rows
+    s.k = p.k
+    s.ldx = p.x.stride(0)
+    s.ldy = p.y.stride(0)
+    return s
+
+
+def gemv_grouped(problems: Sequence[GemvProblem]) -> None:
+    """y_i = x_i @ dequant(W_i)^T (+ bias_i) for up to 8 weights in one launch.
+
+    All x_i share one batch size (1..32).  Outputs are written in place.
+    """
+    if not problems:
+        return
+    if len(problems) > N.GEMV_MAX_PROBLEMS:
+        for i in range(0, len(problems), N.GEMV_MAX_PROBLEMS):
+            gemv_grouped(problems[i:i + N.GEMV_MAX_PROBLEMS])
+        return
+    batch = problems[0].x.shape[0]
+    if any(p.x.shape[0] != batch for p in problems):
+        raise ValueError("gemv_grouped: all problems must share one batch size")
+    if batch == 0:
+        return
+    if batch > N.GEMV_MAX_BATCH:
+        for b0 in range(0, batch, N.GEMV_MAX_BATCH):
+            sub = [GemvProblem(p.qtype, p.w_tiled, p.x[b0:b0 + N.GEMV_MAX_BATCH], p.y[b0:b0 + N.GEMV_MAX_BATCH],
+                               p.n_rows, p.k, p.bias) for p in problems]
+            gemv_grouped(sub)
+        return
+    lib = N.load()
+    arr = (N.GemvProblem * len(problems))(*[_to_struct(p) for p in problems])
+    need = lib.draco_gguf_gemv_workspace_bytes(arr, len(problems), batch)
+    if need == 0:
+        N.check(N.DRACO_ERR_ARG, "gemv workspace query failed")
+    dev = problems[0].x.device
+    ws = _workspace(dev, int(need))
+    rc = lib.draco_gguf_gemv_grouped(arr, len(problems), batch, ws.data_ptr(), ws.numel(), _stream_ptr(dev))
+    N.check(rc, "gemv")
+
+
+class GemvPlan:
+    """A fixed grouped-GEMV call (same buffers every time), validated once.
+
+    ``run()`` enqueues the prep + GEMV kernels on the current stream with no
+    per-call Python validation, so decode loops and CUDA-graph capture pay
+    only the C launch cost.  The problems' tensors must stay alive and keep
+    their storage while the plan is used.
+    """
+
+    def __init__(self, problems: Sequence[GemvProblem]) -> None:
+        if not problems or len(problems) > N.GEMV_MAX_PROBLEMS:
+            raise ValueError(f"GemvPlan takes 1..{N.GEMV_MAX_PROBLEMS} problems")
+        self.problems = list(problems)
+        self.batch = problems[0].x.shape[0]
+        if any(p.x.shape[0] != self.batch for p in problems) or not 1 <= self.batch <= N.GEMV_MAX_BATCH:
+            raise ValueError("GemvPlan: all problems need one batch size in 1..32")
+        self._lib = N.load()
+        self._arr = (N.GemvProblem * len(problems))(*[_to_struct(p) for p in problems])
+        need = self._lib.draco_gguf_gemv_workspace_bytes(self._arr, len(problems), self.batch)
+        if need == 0:
+            N.check(N.DRACO_ERR_ARG, "gemv workspace query failed")
+        self.device = problems[0].x.device
+        self.workspace = torch.zeros(int(need), dtype=torch.uint8, device=self.device)
+        self.bytes_weights = sum(tiled_nbytes(p.qtype, p.n_rows, p.k) for p in problems)
+
+    def run(self) -> None:
+        rc = self._lib.draco_gguf_gemv_grouped(self._arr, len(self.problems), self.batch,
+                                               self.workspace.data_ptr(), self.workspace.numel(),
+                                               _stream_ptr(self.device))
+        if rc:
+            N.check(rc, "gemv")
+
+    def status(self) -> int:
+        """Kernel-recorded status word (0 = ok).  Synchronises."""
+        return int(self.workspace[:4].view(torch.int32).item())
+
+
+def gemv(qtype: int, w_tiled: torch.Tensor, x: torch.Tensor, n_rows: int, k: int,
+         bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x @ dequant(W)^T (+ bias); x [B, k] fp32 CUDA -> y [B, n_rows] fp32."""
+    squeeze = x.dim() == 1
+    x2 = x.reshape(1, -1) if squeeze else x
+    if x2.dtype != torch.float32:
+        x2 = x2.float()
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    y = out if out is not None else torch.empty((x2.shape[0], n_rows), dtype=torch.float32, device=x2.device)
+    gemv_grouped([GemvProblem(qtype, w_tiled, x2, y, n_rows, k, bias)])
+    return y.reshape(-1) if squeeze else y

@@ -1,0 +1,85 @@
+"""Synthetic workloads with the benchmark configurations' shapes.
+
+* Config 1 — Q8_0 GEMV, W 4096x4096, x fp32 [1, 4096].
+* Config 2 — Q4_K decode GEMV over one Llama-7B-shaped decoder layer's seven
+  projections (q, k, v, o 4096x4096; gate, up 11008x4096; down 4096x11008),
+  x fp32 at batch 1, 4, 16.
+* Config 4 — the same projections in Q4_K_M (Q6_K for v and down).
+
+Weights are drawn from N(0, 0.02) with a recorded seed and encoded with the
+synthetic GGUF encoders (dracort_b200.format.quantize); activations from
+N(0, 1).  Algorithmic bytes count the packed weights plus fp32 x and y once.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Sequence, Tuple
+
+import numpy as np
+
+from dracort_b200.format.gguf_types import (
+    GGML_TYPE_Q4_K,
+    GGML_TYPE_Q6_K,
+    GGML_TYPE_Q8_0,
+    packed_nbytes,
+)
+from dracort_b200.format.quantize import encode, random_weight
+
+HIDDEN = 4096
+FFN = 11008
+
+#: (name, n_rows = out_features, k = in_features) of one Llama-7B decoder layer
+LLAMA7B_PROJECTIONS: Tuple[Tuple[str, int, int], ...] = (
+    ("q_proj", HIDDEN, HIDDEN),
+    ("k_proj", HIDDEN, HIDDEN),
+    ("v_proj", HIDDEN, HIDDEN),
+    ("o_proj", HIDDEN, HIDDEN),
+    ("gate_proj", FFN, HIDDEN),
+    ("up_proj", FFN, HIDDEN),
+    ("down_proj", HIDDEN, FFN),
+)
+
+
+@dataclass
+class WeightSpec:
+    name: str
+    qtype: int
+    n_rows: int
+    k: int
+
+    @property
+    def nbytes(self) -> int:
+        return packed_nbytes(self.qtype, self.n_rows, self.k)
+
+
+def layer_specs(mix: str = "q4_k") -> List[WeightSpec]:
+    """Projection specs of one decoder layer: 'q4_k' (config 2) or 'q4_k_m' (config 4)."""
+    out = []
+    for name, n, k in LLAMA7B_PROJECTIONS:
+        qt = GGML_TYPE_Q4_K
+        if mix == "q4_k_m" and name in ("v_proj", "down_proj"):
+            qt = GGML_TYPE_Q6_K
+        elif mix not in ("q4_k", "q4_k_m"):
+            raise ValueError(f"unknown mix {mix!r}")
+        out.append(WeightSpec(name, qt, n, k))
+    return out
+
+
+def q8_0_spec() -> List[WeightSpec]:
+    return [WeightSpec("w", GGML_TYPE_Q8_0, 4096, 4096)]
+
+
+def encode_specs(specs: Sequence[WeightSpec], seed: int) -> List[np.ndarray]:
+    """Seeded N(0, 0.02) weights encoded per spec (packed uint8 arrays)."""
+    rng = np.random.default_rng(seed)
+    return [encode(s.qtype, random_weight(rng, s.n_rows, s.k)) for s in specs]
+
+
+def algorithmic_bytes(specs: Sequence[WeightSpec], batch: int) -> int:
+    """Packed weights + fp32 activations in + fp32 outputs, each counted once."""
+    return sum(s.nbytes + 4 * batch * (s.k + s.n_rows) for s in specs)
+
+
+def flops(specs: Sequence[WeightSpec], batch: int) -> int:
+    return sum(2 * batch * s.n_rows * s.k for s in specs)

@@ -1,0 +1,163 @@
+/*
+ * draco_gguf.h — C ABI of the B200 (sm_100a) GGUF quantized-linear library
+ * (libdraco_gguf.so).
+ *
+ * The library replaces DracoRT's numpy GGUF path:
+ *   draco/format/gguf.py:_dequantize            (gguf.py:272-497)
+ *   draco/runtime/cpu/executor.py:_linear       (executor.py:47-79)
+ *   draco/runtime/cpu/kernels/generic.py:matmul_f32 (generic.py:32-33)
+ *   draco/quantization/base.py:QuantizationBackend.dequantize / quantized_linear
+ *                                               (base.py:64-99)
+ * with CUDA kernels that read the packed GGUF blocks directly.
+ *
+ * Conventions
+ *   - A weight is GGUF-shaped [n_rows, k]: n_rows output features (GGML ne1),
+ *     k reduction elements (GGML ne0, contiguous).  Blocks run along k inside
+ *     each row (gguf.py:646-648).
+ *   - All pointers are device pointers unless a comment says otherwise; the
+ *     caller owns every buffer.  `stream` is a cudaStream_t (NULL = legacy
+ *     default stream).  Work is enqueued on that stream; nothing synchronises
+ *     the host except where stated.
+ *   - Every function returns a DRACO_* status code.  The message of the last
+ *     failure on the calling host thread is available from
+ *     draco_last_error_string().
+ *   - The library holds no mutable global state except the thread-local error
+ *     string and per-device attribute caches; calls on different streams are
+ *     independent.
+ */
+#ifndef DRACO_GGUF_H
+#define DRACO_GGUF_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml_type ids, identical to GGML_TYPE_* in draco/format/gguf.py:56-71. */
+#define DRACO_GGML_TYPE_Q8_0 8
+#define DRACO_GGML_TYPE_Q4_K 12
+#define DRACO_GGML_TYPE_Q6_K 14
+
+/* Byte layouts of a weight buffer.
+ *   GGUF        : row-major blocks exactly as draco/format/gguf.py reads them
+ *                 (_BLOCK_LAYOUTS, gguf.py:75-87).  For Q6_K this is the
+ *                 reference's field order: d first (gguf.py:470-474).
+ *   GGUF_DLAST  : row-major blocks as llama.cpp writes .gguf files; differs
+ *                 from GGUF only for Q6_K, whose fp16 d is the LAST 2 bytes.
+ *   TILED       : the device layout produced by draco_gguf_repack().  Same
+ *                 payload bytes regrouped into 16-row x 256-element chunks,
+ *                 128-row slabs, rows padded to a multiple of 16 and k to a
+ *                 multiple of 256 with zero blocks.  Size from
+ *                 draco_gguf_tiled_bytes(). */
+#define DRACO_LAYOUT_GGUF 0
+#define DRACO_LAYOUT_GGUF_DLAST 1
+#define DRACO_LAYOUT_TILED 2
+
+/* Status codes.  The Python wrapper maps them onto the reference exception
+ * classes: TYPE/SHAPE -> DracoFormatError (gguf.py:284-296), ALIGN/ARG ->
+ * ValueError, CUDA/TIMEOUT -> KernelError. */
+#define DRACO_OK 0
+#define DRACO_ERR_TYPE 1      /* unsupported qtype or layout             */
+#define DRACO_ERR_SHAPE 2     /* k not a multiple of the block size, etc */
+#define DRACO_ERR_ALIGN 3     /* pointer not aligned as required         */
+#define DRACO_ERR_CUDA 4      /* a CUDA runtime call failed              */
+#define DRACO_ERR_TIMEOUT 5   /* a bounded device wait ran out           */
+#define DRACO_ERR_ARG 6       /* null pointer, bad batch, too many problems */
+#define DRACO_ERR_WORKSPACE 7 /* workspace missing or too small          */
+
+/* Output element types for the GEMM. */
+#define DRACO_DTYPE_F32 0
+#define DRACO_DTYPE_BF16 1
+
+/* Library version string, e.g. "draco_gguf 0.1.0 sm_100a". */
+const char* draco_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* draco_last_error_string(void);
+
+/* (block_size, block_bytes) of a qtype: Q8_0 (32, 34), Q4_K (256, 144),
+ * Q6_K (256, 210).  Replaces the table lookup _BLOCK_LAYOUTS[qtype]
+ * (gguf.py:75-87).  Returns DRACO_ERR_TYPE for other types.  Host only. */
+int draco_gguf_block_geometry(int qtype, int* block_size, int* block_bytes);
+
+/* Bytes of a weight in the GGUF layouts: n_rows * (k / block_size) * block_bytes
+ * (gguf.py:639-645).  Returns -1 on an unsupported type or k that is not a
+ * multiple of the block size.  Host only. */
+int64_t draco_gguf_packed_bytes(int qtype, int64_t n_rows, int64_t k);
+
+/* Bytes of the same weight in the TILED layout (>= packed bytes; equal when
+ * n_rows % 16 == 0 and k % 256 == 0).  -1 on error.  Host only. */
+int64_t draco_gguf_tiled_bytes(int qtype, int64_t n_rows, int64_t k);
+
+/* Dequantize a whole weight to fp32, out[n_rows, k] row-major.
+ * Bit-exact with draco/format/gguf.py:_dequantize (gguf.py:272-497) for
+ * Q8_0 (:300-303), Q4_K (:425-456) and Q6_K (:470-495).
+ * `layout` is any DRACO_LAYOUT_*; GGUF layouts need `blocks` 2-byte aligned,
+ * TILED needs 16-byte alignment. */
+int draco_gguf_dequant(int qtype, int layout, const void* blocks, float* out,
+                       int64_t n_rows, int64_t k, void* stream);
+
+/* Same as draco_gguf_dequant, writing bf16 (round-to-nearest-even of the
+ * exact fp32 value) as uint16_t bit patterns. */
+int draco_gguf_dequant_bf16(int qtype, int layout, const void* blocks, uint16_t* out,
+                            int64_t n_rows, int64_t k, void* stream);
+
+/* Regroup a GGUF-layout weight (src_layout GGUF or GGUF_DLAST) into the
+ * TILED layout.  `dst` must hold draco_gguf_tiled_bytes() bytes and be
+ * 16-byte aligned.  Bytes are moved, never changed, so dequantizing dst gives
+ * bit-identical values.  Replaces the reference's first-access transform
+ * GGUFReader.get_tensor (gguf.py:820-834), which caches fp32 instead. */
+int draco_gguf_repack(int qtype, int src_layout, const void* src, void* dst,
+                      int64_t n_rows, int64_t k, void* stream);
+
+/* One linear layer of a grouped GEMV launch: y = x @ dequant(W)^T (+ bias).
+ *   w     : TILED weight [n_rows, k] of type qtype
+ *   x     : fp32 [batch, k], row stride ldx elements
+ *   y     : fp32 [batch, n_rows], row stride ldy elements (written, not added)
+ *   bias  : fp32 [n_rows] or NULL
+ * Replaces one executor._linear call (executor.py:47-79) whose matmul is
+ * GenericGemmKernel.matmul_f32 (generic.py:32-33). */
+typedef struct draco_gemv_problem {
+  int qtype;
+  int reserved;
+  const void* w;
+  const float* x;
+  float* y;
+  const float* bias;
+  int64_t n_rows;
+  int64_t k;
+  int64_t ldx;
+  int64_t ldy;
+} draco_gemv_problem;
+
+#define DRACO_GEMV_MAX_PROBLEMS 8
+#define DRACO_GEMV_MAX_BATCH 32
+
+/* Workspace bytes the grouped GEMV needs for these problems at this batch.
+ * The workspace must be 256-byte aligned and ZERO-FILLED before its first
+ * use; every call leaves its counters at zero again, so one allocation can
+ * serve any number of calls on one stream (not concurrent calls).  Host only. */
+size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* problems, int n_problems,
+                                       int batch);
+
+/* Decode GEMV over 1..DRACO_GEMV_MAX_PROBLEMS weights in one persistent
+ * launch (the 7 projections of a decoder layer fit in one call).
+ * 1 <= batch <= DRACO_GEMV_MAX_BATCH.  fp32 in, fp32 out, fp32 accumulate;
+ * activations enter the tensor cores as an exact-to-2^-22 fp16 hi/lo pair
+ * after a per-row power-of-two rescale, so results track the fp32 oracle to
+ * ~1e-6 relative L2.  `problems` is a host array. */
+int draco_gguf_gemv_grouped(const draco_gemv_problem* problems, int n_problems, int batch,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* Single-weight convenience form of draco_gguf_gemv_grouped. */
+int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias,
+                    int batch, int64_t n_rows, int64_t k, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DRACO_GGUF_H */
