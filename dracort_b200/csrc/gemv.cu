@@ -6,30 +6,34 @@
 // (draco/runtime/cpu/kernels/generic.py:32-33) on the fp32 cache produced by
 // gguf._dequantize (draco/format/gguf.py:272-497).
 //
-// Design (B200, HBM-bound):
-//  * Persistent grid, one CTA per SM.  The weights of all problems are cut
-//    into "slabs" (128 rows x 256 k, contiguous in the TILED layout) and every
-//    CTA owns a contiguous, byte-balanced range of slabs (stream-K).  A warp
-//    that is the only owner of a row group writes y directly; row groups split
-//    between CTAs are combined deterministically by the last CTA to finish
-//    (arrival counter in the workspace, partial sums added in CTA order).
-//  * Warp 8 is the producer: it streams each slab, plus the matching slice of
-//    the prepared activations, into a ring of shared-memory stages with 1-D
-//    bulk copies (TMA engine) completing on mbarriers.  Warps 0-7 consume; warp
-//    w owns row tile w (16 rows) of every slab.
-//  * The quants enter the m16n8k16 tensor-core MMA as exact integers in fp16
-//    (bit tricks: 0x6400 | nibble == 1024 + q).  Activations enter as an fp16
-//    hi/lo pair (x = hi + lo to ~2^-22 after a per-row power-of-two rescale),
-//    one MMA column each, so the product is accurate to fp32 level.  The
-//    per-sub-block scales (and the 1024 offset, and Q4_K's mins) are applied in
-//    fp32 to each sub-block's MMA result: y += alpha*c - beta*sum(x).
-//  * A separate small kernel (gemv_prep) converts x into that fragment order
-//    and computes the per-16-element sums once per call.
+// Design (B200, HBM-bound), one persistent launch per call:
+//  * One CTA per SM.  The weights of all problems are cut into "slabs"
+//    (128 rows x 256 k, contiguous in the TILED layout) and every CTA owns a
+//    contiguous, byte-balanced range of slabs (stream-K).  Row groups
+//    (128 rows x all k) owned by one CTA are written directly; row groups
+//    split between CTAs are combined deterministically by the last CTA to
+//    finish (arrival counter in the workspace, partials added in CTA order).
+//  * Warp 16 (producer) streams each slab into a ring of shared-memory stages
+//    with 1-D bulk copies (TMA engine) completing on mbarriers; it starts at
+//    launch, before the preceding kernel has finished (programmatic dependent
+//    launch), since weights do not depend on it.
+//  * Warps 17-19 (converters) fill each stage's activation slice: they read
+//    the slab's 256 x B activations from global memory (L2), rescale each
+//    32-element pair by a power of two u, split into fp16 hi + lo, and store
+//    them in MMA-fragment order together with the per-16-element sums.
+//  * Warps 0-15 consume: warp w owns row tile (w % 8) of the slabs whose
+//    parity is w / 8.  Quants enter the m16n8k16 tensor-core MMA as exact
+//    integers in fp16 (0x6400 | nibble == 1024 + q), activations as the hi/lo
+//    pair (one MMA column each), accumulating in fp32.  The sub-block scale,
+//    the 1024 offset and Q4_K's min are applied in fp32 per sub-block:
+//        y += alpha * u * c - beta * sum(x)
+//  * Batch 1-2 ("diagonal" activation layout): each sub-block's activations
+//    sit in their own pair of MMA columns, so one accumulator collects
+//    4 (B=1) or 2 (B=2) sub-blocks and every lane owns one sub-block's sum.
+//    Batch >= 3 ("dense"): columns are (batch, hi/lo).
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
-#include <mutex>
-#include <vector>
 
 #include "common.cuh"
 #include "internal.h"
@@ -38,8 +42,11 @@ namespace draco {
 
 constexpr int kMaxCta = 192;
 constexpr int kMaxStages = 8;
-constexpr int kConsumerWarps = 8;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kRowWarps = 8;                   // one per row tile of a slab
+constexpr int kConsumerWarps = 2 * kRowWarps;  // even / odd slabs
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kConvWarps = 3;
+constexpr int kThreads = (kConsumerWarps + 1 + kConvWarps) * 32;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
 
 struct GemvProbDev {
@@ -48,20 +55,17 @@ struct GemvProbDev {
   float* y;
   const float* bias;
   int64_t ldx, ldy;
-  int64_t slab0;   // global index of the problem's first slab
-  int64_t xs_off;  // workspace byte offsets
-  int64_t s_off;
-  int64_t sc_off;
-  int qt, n_rows, k, nb, n_rg, n_tiles, cb, pad_;
+  int slab0;  // global index of the problem's first slab
+  int qt, n_rows, k, nb, n_rg, n_tiles, cb;
 };
 
 struct GemvParams {
   GemvProbDev prob[DRACO_GEMV_MAX_PROBLEMS];
   uint8_t* ws;
   int64_t status_off, cnt_off, part_off;
-  int64_t total_slabs;
+  int total_slabs;
   int n_prob, batch, nt, n_cta;
-  int w_stage, xs_bytes, s_bytes, stage_bytes, n_stages, pad_;
+  int w_stage, xs_bytes, su_bytes, stage_bytes, n_stages;
   int cta_start[kMaxCta + 1];
 };
 
@@ -77,13 +81,12 @@ static inline int64_t align256(int64_t v) { return (v + 255) & ~(int64_t)255; }
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 __device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-__device__ __forceinline__ float2 lds64f(const uint8_t* p) { return *reinterpret_cast<const float2*>(p); }
+__device__ __forceinline__ float4 lds128f(const uint8_t* p) { return *reinterpret_cast<const float4*>(p); }
 
-// exact float of byte i of w (unsigned), via the 2^23 magic number
-__device__ __forceinline__ float ubyte_f(uint32_t w, int i) {
-  uint32_t m = __byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)i);
-  return __uint_as_float(m) - 8388608.f;
-}
+// byte i of w (runtime i) as an unsigned int
+__device__ __forceinline__ uint32_t ubyte(uint32_t w, int i) { return __byte_perm(w, 0u, 0x4440u | (uint32_t)i); }
+// exact float of a small non-negative integer v < 2^23, via the 2^23 magic number
+__device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.f; }
 // exact float of byte i of w read as int8
 __device__ __forceinline__ float sbyte_f(uint32_t w, int i) {
   uint32_t m = __byte_perm(w ^ 0x80808080u, 0x4B000000u, 0x7440u | (uint32_t)i);
@@ -94,300 +97,367 @@ __device__ __forceinline__ uint32_t nib_hi(uint32_t w) { return (w & 0x00F000F0u
 // bytes 0,2 / 1,3 of w into the low bytes of two fp16 lanes with 0x64 exponent
 __device__ __forceinline__ uint32_t byte02(uint32_t w) { return __byte_perm(w, 0x64646464u, 0x4240u); }
 __device__ __forceinline__ uint32_t byte13(uint32_t w) { return __byte_perm(w, 0x64646464u, 0x4341u); }
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+  __half2 h = __halves2half2(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void mma_acc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  mma_f16_16816_acc(d, a0, a1, a2, a3, b0, b1);
+}
 
-__device__ __forceinline__ void named_bar_consumers() {
+__device__ __forceinline__ void consumers_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 }
 
-__device__ __forceinline__ void locate_slab(const GemvParams& P, int64_t s, int& p, int64_t& rg, int64_t& j) {
-  p = 0;
-#pragma unroll 1
-  for (int q = 1; q < P.n_prob; ++q)
-    if (s >= P.prob[q].slab0) p = q;
-  const int64_t local = s - P.prob[p].slab0;
-  const int64_t nb = P.prob[p].nb;
-  rg = local / nb;
-  j = local - rg * nb;
-}
-
-__device__ __forceinline__ int slab_tiles(const GemvProbDev& pr, int64_t rg) {
-  int64_t r = pr.n_tiles - rg * kGroupTiles;
-  return (int)(r < kGroupTiles ? r : kGroupTiles);
+__device__ __forceinline__ int rg_tile_count(const GemvProbDev& pr, int rg) {
+  const int r = pr.n_tiles - rg * kGroupTiles;
+  return r < kGroupTiles ? r : kGroupTiles;
 }
 
 __device__ __forceinline__ void record_error(const GemvParams& P, int code) {
   atomicCAS(reinterpret_cast<int*>(P.ws + P.status_off), 0, code);
 }
 
-// ---------------------------------------------------------------------------
-// activation preparation: x fp32 -> fp16 (hi, lo) fragment order + sums
-// grid (4*NT batch slots, n_prob), 256 threads
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) gemv_prep_kernel(const __grid_constant__ GemvParams P) {
-  // let the GEMV launch now: its CTAs start streaming weights (which do not
-  // depend on this kernel) and wait on griddepcontrol.wait for our outputs
-  grid_launch_dependents();
-  grid_dependency_wait();
-  const int b = blockIdx.x, p = blockIdx.y;
-  const GemvProbDev& pr = P.prob[p];
-  const int ncols = 8 * P.nt;
-  const int bslots = 4 * P.nt;
-  const int64_t nk = pr.nb * 16;  // 16-element steps (k padded to 256)
-  uint8_t* xs = P.ws + pr.xs_off;
-  float* S = reinterpret_cast<float*>(P.ws + pr.s_off);
-  float* unscale = reinterpret_cast<float*>(P.ws + pr.sc_off);
-  __shared__ float red[8];
-  __shared__ float s_scale;
-
-  if (b >= P.batch) {
-    for (int64_t kk = threadIdx.x; kk < nk; kk += blockDim.x) {
-      uint4 z = make_uint4(0, 0, 0, 0);
-      uint4* d0 = reinterpret_cast<uint4*>(xs + ((kk * ncols + 2 * b) * 4) * 8);
-      d0[0] = z; d0[1] = z; d0[2] = z; d0[3] = z;  // cols 2b, 2b+1: 64 contiguous bytes
-      S[((kk >> 1) * bslots + b) * 2 + (kk & 1)] = 0.f;
-    }
-    if (threadIdx.x == 0) unscale[b] = 0.f;
-    return;
+// Slab cursor: (problem, row group, super-block) of a global slab index,
+// advanced incrementally.
+struct SlabCursor {
+  int p, rg, j;
+  __device__ void seek(const GemvParams& P, int s) {
+    p = 0;
+    for (int q = 1; q < P.n_prob; ++q)
+      if (s >= P.prob[q].slab0) p = q;
+    const int local = s - P.prob[p].slab0;
+    rg = local / P.prob[p].nb;
+    j = local - rg * P.prob[p].nb;
   }
+  __device__ void next(const GemvParams& P) {
+    if (++j == P.prob[p].nb) {
+      j = 0;
+      if (++rg == P.prob[p].n_rg) {
+        rg = 0;
+        ++p;
+      }
+    }
+  }
+};
 
-  const float* x = pr.x + (int64_t)b * pr.ldx;
-  float amax = 0.f;
-  for (int64_t i = threadIdx.x; i < pr.k; i += blockDim.x) amax = fmaxf(amax, fabsf(x[i]));
+// ---------------------------------------------------------------------------
+// activation conversion of one slab (problem pr, super-block j) by one warp.
+// Lane quad (lane / 4) takes the 32-element pair m of a batch row, lane % 4
+// eight of its elements.  Per pair: u = 2^e with max|x| * 2^-e in
+// [2^13, 2^14), hi = fp16(x / u), lo = fp16(x / u - hi), S = u * sum(hi + lo).
+//   xs[m][col][t][16 B]: (x[4t], x[4t+2]), (x[4t+1], x[4t+3]) for the pair's
+//       16-element steps 0 (bytes 0-7) and 1 (bytes 8-15); the column is
+//         dense   : 2b + hl
+//         diagonal: ((sub-block mod G) * Bp + b) * 2 + hl,  G = 4 / Bp,
+//       a Q4_K / Q8_0 sub-block being the pair and a Q6_K sub-block one step;
+//       the other sub-block slots of a diagonal entry are written as zeros;
+//   su[m][b] = (S_step0, S_step1, u, 0).
+// ---------------------------------------------------------------------------
+template <int G, int NT>
+__device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProbDev& pr, int j, uint8_t* xs,
+                                             uint8_t* su, int lane) {
+  constexpr bool kDiag = G > 1;
+  constexpr int Bp = kDiag ? 4 / G : 4 * NT;
+  constexpr int kCols = 8 * NT;
+  constexpr int kSlots = 4 * NT;
+  const int m = lane >> 2, r = lane & 3, kap = r >> 1, t0 = 2 * (r & 1);
+  const int kk0 = 256 * j + 32 * m + 8 * r;
+  const bool q6 = pr.qt == kQ6_K;
+  for (int b = 0; b < P.batch; ++b) {
+    const float* xp = pr.x + (int64_t)b * pr.ldx + kk0;
+    float v[8];
+    float amax = 0.f;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float m = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+    for (int i = 0; i < 8; ++i) {
+      v[i] = (kk0 + i < pr.k) ? __ldg(xp + i) : 0.f;
+      amax = fmaxf(amax, fabsf(v[i]));
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
     int e = 0;
-    if (m > 0.f && m <= 3.0e38f) e = ilogbf(m) - 13;
+    if (amax > 0.f && amax <= 3.0e38f) e = ilogbf(amax) - 13;
     e = max(-110, min(110, e));
-    s_scale = ldexpf(1.f, -e);
-    unscale[b] = ldexpf(1.f, e);
-  }
-  __syncthreads();
-  const float sc = s_scale;
-  for (int64_t kk = threadIdx.x; kk < nk; kk += blockDim.x) {
-    __half hi[16], lo[16];
-    float sum = 0.f;
+    const float sc = ldexpf(1.f, -e), u = ldexpf(1.f, e);
+    __half hi[8], lo[8];
+    float s = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int64_t kx = kk * 16 + i;
-      const float v = (kx < pr.k) ? x[kx] * sc : 0.f;
-      hi[i] = __float2half_rn(v);
+    for (int i = 0; i < 8; ++i) {
+      const float a = v[i] * sc;
+      hi[i] = __float2half_rn(a);
       const float hf = __half2float(hi[i]);
-      lo[i] = __float2half_rn(v - hf);
-      sum += hf + __half2float(lo[i]);
+      lo[i] = __float2half_rn(a - hf);
+      s += hf + __half2float(lo[i]);
     }
-    uint32_t* dh = reinterpret_cast<uint32_t*>(xs + ((kk * ncols + 2 * b) * 4) * 8);
-    uint32_t* dl = reinterpret_cast<uint32_t*>(xs + ((kk * ncols + 2 * b + 1) * 4) * 8);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);               // sum of this 16-element step
+    const float s_other = __shfl_xor_sync(0xffffffffu, s, 2);  // the pair's other step
+    if (r == 0) *reinterpret_cast<float4*>(su + (m * kSlots + b) * 16) = make_float4(s * u, s_other * u, u, 0.f);
+    uint2 eh[2], el[2];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      __half2 h02 = __halves2half2(hi[4 * t], hi[4 * t + 2]);
-      __half2 h13 = __halves2half2(hi[4 * t + 1], hi[4 * t + 3]);
-      __half2 l02 = __halves2half2(lo[4 * t], lo[4 * t + 2]);
-      __half2 l13 = __halves2half2(lo[4 * t + 1], lo[4 * t + 3]);
-      dh[2 * t] = *reinterpret_cast<uint32_t*>(&h02);
-      dh[2 * t + 1] = *reinterpret_cast<uint32_t*>(&h13);
-      dl[2 * t] = *reinterpret_cast<uint32_t*>(&l02);
-      dl[2 * t + 1] = *reinterpret_cast<uint32_t*>(&l13);
+    for (int tt = 0; tt < 2; ++tt) {
+      eh[tt] = make_uint2(pack_h2(hi[4 * tt], hi[4 * tt + 2]), pack_h2(hi[4 * tt + 1], hi[4 * tt + 3]));
+      el[tt] = make_uint2(pack_h2(lo[4 * tt], lo[4 * tt + 2]), pack_h2(lo[4 * tt + 1], lo[4 * tt + 3]));
     }
-    S[((kk >> 1) * bslots + b) * 2 + (kk & 1)] = sum;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// per-chunk consumers.  ch: 16-row chunk in smem; xs: activation slice of the
-// slab's super-block [16 steps][8*NT cols][4 t][8 B]; S: sums [8 pairs][4*NT][2];
-// scr: per-warp 16 x 16 float scratch for decoded scales.
-// acc[nt][0] -> (row g, batch 4nt+t), acc[nt][1] -> (row g+8, batch 4nt+t)
-// ---------------------------------------------------------------------------
-template <int NT>
-__device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, const uint8_t* S, float* scr,
-                                          int lane, float (&acc)[NT][2]) {
-  const int g = lane >> 2, t = lane & 3;
-  {  // cooperative decode: lane -> row r, sub-blocks 4h..4h+3 -> (alpha, beta)
-    const int r = lane >> 1, h = lane & 1;
-    const uint8_t* sp = ch + 2048 + 24 * (r & 7) + 12 * (r >> 3);
-    const uint32_t A = lds32(sp), Bw = lds32(sp + 4), C = lds32(sp + 8);
-    const uint32_t dd = lds32(ch + 2240 + 8 * (r & 7) + 4 * (r >> 3));
-    const float d = f16_bits_to_f32(dd), dmin = f16_bits_to_f32(dd >> 16);
-    uint32_t scw, mw;
-    if (h == 0) {
-      scw = A & 0x3F3F3F3Fu;
-      mw = Bw & 0x3F3F3F3Fu;
+    uint8_t* base = xs + (size_t)m * kCols * 64 + (size_t)t0 * 16 + 8 * kap;
+    if constexpr (kDiag) {
+      const int slot = (q6 ? (2 * m + kap) : m) % G;
+#pragma unroll
+      for (int jj = 0; jj < G; ++jj)
+#pragma unroll
+        for (int hl = 0; hl < 2; ++hl) {
+          const int col = (jj * Bp + b) * 2 + hl;
+#pragma unroll
+          for (int tt = 0; tt < 2; ++tt) {
+            const uint2 val = (jj == slot) ? (hl ? el[tt] : eh[tt]) : make_uint2(0u, 0u);
+            *reinterpret_cast<uint2*>(base + col * 64 + tt * 16) = val;
+          }
+        }
     } else {
-      scw = (C & 0x0F0F0F0Fu) | ((A >> 2) & 0x30303030u);
-      mw = ((C >> 4) & 0x0F0F0F0Fu) | ((Bw >> 2) & 0x30303030u);
-    }
-    float* dst = scr + r * 16;
+      (void)q6;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int jj = 4 * h + i;
-      const float a = d * ubyte_f(scw, i);
-      const float mu = dmin * ubyte_f(mw, i);
-      // even sub-blocks: low nibbles (1024 + q); odd: high nibbles (1024 + 16 q)
-      const float al = (jj & 1) ? a * 0.0625f : a;
-      const float be = fmaf((jj & 1) ? 64.f : 1024.f, a, mu);
-      dst[jj] = al;
-      dst[8 + jj] = be;
-    }
-  }
-  __syncwarp();
-  float al0[8], be0[8], al1[8], be1[8];
-  {
-    const float4* r0 = reinterpret_cast<const float4*>(scr + g * 16);
-    const float4* r1 = reinterpret_cast<const float4*>(scr + (g + 8) * 16);
-    float4 v;
-    v = r0[0]; al0[0] = v.x; al0[1] = v.y; al0[2] = v.z; al0[3] = v.w;
-    v = r0[1]; al0[4] = v.x; al0[5] = v.y; al0[6] = v.z; al0[7] = v.w;
-    v = r0[2]; be0[0] = v.x; be0[1] = v.y; be0[2] = v.z; be0[3] = v.w;
-    v = r0[3]; be0[4] = v.x; be0[5] = v.y; be0[6] = v.z; be0[7] = v.w;
-    v = r1[0]; al1[0] = v.x; al1[1] = v.y; al1[2] = v.z; al1[3] = v.w;
-    v = r1[1]; al1[4] = v.x; al1[5] = v.y; al1[6] = v.z; al1[7] = v.w;
-    v = r1[2]; be1[0] = v.x; be1[1] = v.y; be1[2] = v.z; be1[3] = v.w;
-    v = r1[3]; be1[4] = v.x; be1[5] = v.y; be1[6] = v.z; be1[7] = v.w;
-  }
-  __syncwarp();
-  const int xs_step = NT * 256;
+      for (int hl = 0; hl < 2; ++hl)
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint4 v = lds128(ch + 512 * q + 16 * lane);
-    const uint32_t x8 = v.x >> 8, y8 = v.y >> 8, z8 = v.z >> 8, w8 = v.w >> 8;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint8_t* xb = xs + nt * 256 + lane * 8;
-      const uint2 b0 = lds64(xb + (4 * q + 0) * xs_step);
-      const uint2 b1 = lds64(xb + (4 * q + 1) * xs_step);
-      const uint2 b2 = lds64(xb + (4 * q + 2) * xs_step);
-      const uint2 b3 = lds64(xb + (4 * q + 3) * xs_step);
-      float c[4], e[4];
-      mma_f16_16816(c, nib_lo(v.x), nib_lo(v.z), nib_lo(x8), nib_lo(z8), b0.x, b0.y);
-      mma_f16_16816_acc(c, nib_lo(v.y), nib_lo(v.w), nib_lo(y8), nib_lo(w8), b1.x, b1.y);
-      mma_f16_16816(e, nib_hi(v.x), nib_hi(v.z), nib_hi(x8), nib_hi(z8), b2.x, b2.y);
-      mma_f16_16816_acc(e, nib_hi(v.y), nib_hi(v.w), nib_hi(y8), nib_hi(w8), b3.x, b3.y);
-      const float2 s_lo = lds64f(S + ((2 * q) * 4 * NT + 4 * nt + t) * 8);
-      const float2 s_hi = lds64f(S + ((2 * q + 1) * 4 * NT + 4 * nt + t) * 8);
-      const float sl = s_lo.x + s_lo.y, sh = s_hi.x + s_hi.y;
-      float a0 = acc[nt][0], a1 = acc[nt][1];
-      a0 = fmaf(al0[2 * q], c[0] + c[1], a0);
-      a0 = fmaf(-be0[2 * q], sl, a0);
-      a1 = fmaf(al1[2 * q], c[2] + c[3], a1);
-      a1 = fmaf(-be1[2 * q], sl, a1);
-      a0 = fmaf(al0[2 * q + 1], e[0] + e[1], a0);
-      a0 = fmaf(-be0[2 * q + 1], sh, a0);
-      a1 = fmaf(al1[2 * q + 1], e[2] + e[3], a1);
-      a1 = fmaf(-be1[2 * q + 1], sh, a1);
-      acc[nt][0] = a0;
-      acc[nt][1] = a1;
+        for (int tt = 0; tt < 2; ++tt)
+          *reinterpret_cast<uint2*>(base + (2 * b + hl) * 64 + tt * 16) = hl ? el[tt] : eh[tt];
     }
   }
 }
 
-template <int NT>
-__device__ __forceinline__ void chunk_q6k(const uint8_t* ch, const uint8_t* xs, const uint8_t* S, float* scr,
-                                          int lane, float (&acc)[NT][2]) {
+// ---------------------------------------------------------------------------
+// per-chunk consumers: one warp, one 16-row x 256-element chunk.
+//   ch : chunk bytes in smem;  xs : slab activation slice [8 pairs][ncols][4][16 B]
+//   su : [8 pairs][4 or bp slots][float4]
+//   G  : sub-blocks per MMA accumulator (4: batch 1, 2: batch 2, 1: dense)
+//   acc[nt][0] -> (row g, batch b), acc[nt][1] -> (row g+8, batch b), with
+//   b = t % Bp (diagonal, nt = 0) or 4 nt + t (dense)
+// ---------------------------------------------------------------------------
+// Q4_K (alpha, beta) of 32-element sub-block j for the row whose 12 scale bytes
+// are (A, Bw, C): low nibbles (even j) carry 1024 + q, high ones 1024 + 16 q.
+__device__ __forceinline__ void q4k_ab(uint32_t A, uint32_t Bw, uint32_t C, float d, float dmin, int j, bool high_j4,
+                                       float& al, float& be) {
+  uint32_t sc, m;
+  if (!high_j4) {
+    sc = ubyte(A, j) & 63u;
+    m = ubyte(Bw, j) & 63u;
+  } else {
+    const int i = j - 4;
+    const uint32_t c = ubyte(C, i);
+    sc = (c & 15u) | ((ubyte(A, i) >> 6) << 4);
+    m = (c >> 4) | ((ubyte(Bw, i) >> 6) << 4);
+  }
+  const float a = d * u2f(sc), mu = dmin * u2f(m);
+  const bool odd = j & 1;
+  al = odd ? a * 0.0625f : a;
+  be = fmaf(odd ? 64.f : 1024.f, a, mu);
+}
+
+template <int G, int NT>
+__device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, const uint8_t* su, int lane,
+                                          float (&acc)[NT][2]) {
   const int g = lane >> 2, t = lane & 3;
-  {  // cooperative decode: lane -> row r, sub-blocks 8h..8h+7 -> alpha = d * sc
-    const int r = lane >> 1, h = lane & 1;
-    const uint2 sc8 = lds64(ch + 3072 + 32 * (r & 7) + 16 * (r >> 3) + 8 * h);
-    const uint32_t dw = *reinterpret_cast<const uint16_t*>(ch + 3328 + 4 * (r & 7) + 2 * (r >> 3));
-    const float d = f16_bits_to_f32(dw);
-    float* dst = scr + r * 16 + 8 * h;
+  const uint8_t* sp0 = ch + 2048 + 24 * g;  // row g: 12 bytes, row g+8: next 12
+  const uint32_t A0 = lds32(sp0), B0 = lds32(sp0 + 4), C0 = lds32(sp0 + 8);
+  const uint32_t A1 = lds32(sp0 + 12), B1 = lds32(sp0 + 16), C1 = lds32(sp0 + 20);
+  const uint2 dd = lds64(ch + 2240 + 8 * g);
+  const float d0 = f16_bits_to_f32(dd.x), m0 = f16_bits_to_f32(dd.x >> 16);
+  const float d1 = f16_bits_to_f32(dd.y), m1 = f16_bits_to_f32(dd.y >> 16);
+  const int pair_stride = (G > 1 ? 8 : 8 * NT) * 64;
+  if constexpr (G > 1) {
+    constexpr int Bp = 4 / G, NF = 8 / G;
+    float fr[NF][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      dst[i] = d * sbyte_f(sc8.x, i);
-      dst[4 + i] = d * sbyte_f(sc8.y, i);
+    for (int f = 0; f < NF; ++f) fr[f][0] = fr[f][1] = fr[f][2] = fr[f][3] = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 v = lds128(ch + 512 * q + 16 * lane);
+      const uint32_t x8 = v.x >> 8, y8 = v.y >> 8, z8 = v.z >> 8, w8 = v.w >> 8;
+      const uint4 bl = lds128(xs + (2 * q) * pair_stride + lane * 16);
+      const uint4 bh = lds128(xs + (2 * q + 1) * pair_stride + lane * 16);
+      float(&fl)[4] = fr[(2 * q) / G];
+      mma_acc(fl, nib_lo(v.x), nib_lo(v.z), nib_lo(x8), nib_lo(z8), bl.x, bl.y);
+      mma_acc(fl, nib_lo(v.y), nib_lo(v.w), nib_lo(y8), nib_lo(w8), bl.z, bl.w);
+      float(&fh)[4] = fr[(2 * q + 1) / G];
+      mma_acc(fh, nib_hi(v.x), nib_hi(v.z), nib_hi(x8), nib_hi(z8), bh.x, bh.y);
+      mma_acc(fh, nib_hi(v.y), nib_hi(v.w), nib_hi(y8), nib_hi(w8), bh.z, bh.w);
+    }
+    const int b = t % Bp;
+#pragma unroll
+    for (int f = 0; f < NF; ++f) {
+      const int j = f * G + t / Bp;  // this lane's sub-block in fragment f
+      float al0, be0, al1, be1;
+      q4k_ab(A0, B0, C0, d0, m0, j, f * G >= 4, al0, be0);
+      q4k_ab(A1, B1, C1, d1, m1, j, f * G >= 4, al1, be1);
+      const float4 s = lds128f(su + (j * 4 + b) * 16);
+      const float S = s.x + s.y;
+      acc[0][0] = fmaf(al0, (fr[f][0] + fr[f][1]) * s.z, fmaf(-be0, S, acc[0][0]));
+      acc[0][1] = fmaf(al1, (fr[f][2] + fr[f][3]) * s.z, fmaf(-be1, S, acc[0][1]));
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float al0l, be0l, al1l, be1l, al0h, be0h, al1h, be1h;
+      q4k_ab(A0, B0, C0, d0, m0, 2 * q, q >= 2, al0l, be0l);
+      q4k_ab(A1, B1, C1, d1, m1, 2 * q, q >= 2, al1l, be1l);
+      q4k_ab(A0, B0, C0, d0, m0, 2 * q + 1, q >= 2, al0h, be0h);
+      q4k_ab(A1, B1, C1, d1, m1, 2 * q + 1, q >= 2, al1h, be1h);
+      const uint4 v = lds128(ch + 512 * q + 16 * lane);
+      const uint32_t x8 = v.x >> 8, y8 = v.y >> 8, z8 = v.z >> 8, w8 = v.w >> 8;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint4 bl = lds128(xs + (2 * q) * pair_stride + nt * 512 + lane * 16);
+        const uint4 bh = lds128(xs + (2 * q + 1) * pair_stride + nt * 512 + lane * 16);
+        float c[4], e[4];
+        mma_f16_16816(c, nib_lo(v.x), nib_lo(v.z), nib_lo(x8), nib_lo(z8), bl.x, bl.y);
+        mma_acc(c, nib_lo(v.y), nib_lo(v.w), nib_lo(y8), nib_lo(w8), bl.z, bl.w);
+        mma_f16_16816(e, nib_hi(v.x), nib_hi(v.z), nib_hi(x8), nib_hi(z8), bh.x, bh.y);
+        mma_acc(e, nib_hi(v.y), nib_hi(v.w), nib_hi(y8), nib_hi(w8), bh.z, bh.w);
+        const float4 sl = lds128f(su + ((2 * q) * 4 * NT + 4 * nt + t) * 16);
+        const float4 sh = lds128f(su + ((2 * q + 1) * 4 * NT + 4 * nt + t) * 16);
+        const float Sl = sl.x + sl.y, Sh = sh.x + sh.y;
+        float r0 = acc[nt][0], r1 = acc[nt][1];
+        r0 = fmaf(al0l, (c[0] + c[1]) * sl.z, fmaf(-be0l, Sl, r0));
+        r1 = fmaf(al1l, (c[2] + c[3]) * sl.z, fmaf(-be1l, Sl, r1));
+        r0 = fmaf(al0h, (e[0] + e[1]) * sh.z, fmaf(-be0h, Sh, r0));
+        r1 = fmaf(al1h, (e[2] + e[3]) * sh.z, fmaf(-be1h, Sh, r1));
+        acc[nt][0] = r0;
+        acc[nt][1] = r1;
+      }
     }
   }
-  __syncwarp();
-  float al0[16], al1[16];
-  {
-    const float4* r0 = reinterpret_cast<const float4*>(scr + g * 16);
-    const float4* r1 = reinterpret_cast<const float4*>(scr + (g + 8) * 16);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float4 v = r0[i];
-      al0[4 * i] = v.x; al0[4 * i + 1] = v.y; al0[4 * i + 2] = v.z; al0[4 * i + 3] = v.w;
-      v = r1[i];
-      al1[4 * i] = v.x; al1[4 * i + 1] = v.y; al1[4 * i + 2] = v.z; al1[4 * i + 3] = v.w;
-    }
-  }
-  __syncwarp();
+}
+
+template <int G, int NT>
+__device__ __forceinline__ void chunk_q6k(const uint8_t* ch, const uint8_t* xs, const uint8_t* su, int lane,
+                                          float (&acc)[NT][2]) {
+  const int g = lane >> 2, t = lane & 3;
+  const uint8_t* scp = ch + 3072 + 32 * g;  // row g: 16 int8 scales, row g+8: next 16
+  const uint32_t dw = lds32(ch + 3328 + 4 * g);
+  const float d0 = f16_bits_to_f32(dw), d1 = f16_bits_to_f32(dw >> 16);
   uint32_t W[24];
 #pragma unroll
   for (int i = 0; i < 6; ++i) {
     const uint4 v = lds128(ch + 512 * i + 16 * lane);
     W[4 * i] = v.x; W[4 * i + 1] = v.y; W[4 * i + 2] = v.z; W[4 * i + 3] = v.w;
   }
-  const int xs_step = NT * 256;
+  const int pair_stride = (G > 1 ? 8 : 8 * NT) * 64;
+  if constexpr (G > 1) {
+    constexpr int Bp = 4 / G, NF = 16 / G;
+    float fr[NF][4];
 #pragma unroll
-  for (int nu = 0; nu < 4; ++nu) {
-    const int n = nu >> 1, is = nu & 1;
+    for (int f = 0; f < NF; ++f) fr[f][0] = fr[f][1] = fr[f][2] = fr[f][3] = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int s = 8 * n + 2 * i + is;  // sub-block == 16-element step index
-      uint32_t qg, qg8;
-      {
-        const uint32_t l0 = W[6 * nu + (i & 1)], h0 = W[6 * nu + 2];
-        const uint32_t l1 = W[6 * nu + 3 + (i & 1)], h1 = W[6 * nu + 5];
-        const uint32_t n0 = (i < 2 ? l0 : (l0 >> 4)) & 0x0F0F0F0Fu;
-        const uint32_t n1 = (i < 2 ? l1 : (l1 >> 4)) & 0x0F0F0F0Fu;
-        qg = n0 | (((h0 >> (2 * i)) << 4) & 0x30303030u);
-        qg8 = n1 | (((h1 >> (2 * i)) << 4) & 0x30303030u);
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 bx = lds128(xs + (4 * n + i) * pair_stride + lane * 16);
+#pragma unroll
+        for (int is = 0; is < 2; ++is) {
+          const int nu = 2 * n + is, s = 8 * n + 2 * i + is;
+          const uint32_t l0 = W[6 * nu + (i & 1)], h0 = W[6 * nu + 2];
+          const uint32_t l1 = W[6 * nu + 3 + (i & 1)], h1 = W[6 * nu + 5];
+          const uint32_t n0 = (i < 2 ? l0 : (l0 >> 4)) & 0x0F0F0F0Fu;
+          const uint32_t n1 = (i < 2 ? l1 : (l1 >> 4)) & 0x0F0F0F0Fu;
+          const uint32_t qg = n0 | (((h0 >> (2 * i)) << 4) & 0x30303030u);
+          const uint32_t qg8 = n1 | (((h1 >> (2 * i)) << 4) & 0x30303030u);
+          mma_acc(fr[s / G], byte02(qg), byte02(qg8), byte13(qg), byte13(qg8), is ? bx.z : bx.x, is ? bx.w : bx.y);
+        }
       }
-      const uint32_t a0 = byte02(qg), a2 = byte13(qg), a1 = byte02(qg8), a3 = byte13(qg8);
+    const int b = t % Bp;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const uint2 b = lds64(xs + nt * 256 + lane * 8 + s * xs_step);
-        float c[4];
-        mma_f16_16816(c, a0, a1, a2, a3, b.x, b.y);
-        const float2 sp = lds64f(S + ((s >> 1) * 4 * NT + 4 * nt + t) * 8);
-        const float ss = (s & 1) ? sp.y : sp.x;
-        acc[nt][0] = fmaf(al0[s], fmaf(-1056.f, ss, c[0] + c[1]), acc[nt][0]);
-        acc[nt][1] = fmaf(al1[s], fmaf(-1056.f, ss, c[2] + c[3]), acc[nt][1]);
-      }
+    for (int f = 0; f < NF; ++f) {
+      const int s = f * G + t / Bp;
+      const float a0 = d0 * (float)(int8_t)scp[s];
+      const float a1 = d1 * (float)(int8_t)scp[16 + s];
+      const float4 sv = lds128f(su + ((s >> 1) * 4 + b) * 16);
+      const float S = (s & 1) ? sv.y : sv.x;
+      acc[0][0] = fmaf(a0, fmaf(-1056.f, S, (fr[f][0] + fr[f][1]) * sv.z), acc[0][0]);
+      acc[0][1] = fmaf(a1, fmaf(-1056.f, S, (fr[f][2] + fr[f][3]) * sv.z), acc[0][1]);
     }
+  } else {
+    const uint4 s0a = lds128(scp), s0b = lds128(scp + 16);  // row g: sc[0..15]
+    const uint32_t sw0[4] = {s0a.x, s0a.y, s0a.z, s0a.w};
+    const uint32_t sw1[4] = {s0b.x, s0b.y, s0b.z, s0b.w};
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int pm = 4 * n + i;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint4 bx = lds128(xs + pm * pair_stride + nt * 512 + lane * 16);
+          const float4 sv = lds128f(su + (pm * 4 * NT + 4 * nt + t) * 16);
+#pragma unroll
+          for (int is = 0; is < 2; ++is) {
+            const int nu = 2 * n + is, s = 8 * n + 2 * i + is;
+            const uint32_t l0 = W[6 * nu + (i & 1)], h0 = W[6 * nu + 2];
+            const uint32_t l1 = W[6 * nu + 3 + (i & 1)], h1 = W[6 * nu + 5];
+            const uint32_t n0 = (i < 2 ? l0 : (l0 >> 4)) & 0x0F0F0F0Fu;
+            const uint32_t n1 = (i < 2 ? l1 : (l1 >> 4)) & 0x0F0F0F0Fu;
+            const uint32_t qg = n0 | (((h0 >> (2 * i)) << 4) & 0x30303030u);
+            const uint32_t qg8 = n1 | (((h1 >> (2 * i)) << 4) & 0x30303030u);
+            float c[4];
+            mma_f16_16816(c, byte02(qg), byte02(qg8), byte13(qg), byte13(qg8), is ? bx.z : bx.x, is ? bx.w : bx.y);
+            const float S = is ? sv.y : sv.x;
+            const float a0 = d0 * sbyte_f(sw0[s >> 2], s & 3);
+            const float a1 = d1 * sbyte_f(sw1[s >> 2], s & 3);
+            acc[nt][0] = fmaf(a0, fmaf(-1056.f, S, (c[0] + c[1]) * sv.z), acc[nt][0]);
+            acc[nt][1] = fmaf(a1, fmaf(-1056.f, S, (c[2] + c[3]) * sv.z), acc[nt][1]);
+          }
+        }
+      }
   }
 }
 
-template <int NT>
-__device__ __forceinline__ void chunk_q80(const uint8_t* ch, const uint8_t* xs, const uint8_t* S, int lane,
+template <int G, int NT>
+__device__ __forceinline__ void chunk_q80(const uint8_t* ch, const uint8_t* xs, const uint8_t* su, int lane,
                                           float (&acc)[NT][2]) {
   const int g = lane >> 2, t = lane & 3;
-  float d0[8], d1[8];
-  {
-    const uint4 u0 = lds128(ch + 4096 + 32 * g);
-    const uint4 u1 = lds128(ch + 4096 + 32 * g + 16);
-    const uint32_t w0[4] = {u0.x, u0.y, u0.z, u0.w};
-    const uint32_t w1[4] = {u1.x, u1.y, u1.z, u1.w};
+  const uint8_t* dp = ch + 4096 + 32 * g;  // row g: 8 fp16 d, row g+8: next 8
+  const int pair_stride = (G > 1 ? 8 : 8 * NT) * 64;
+  if constexpr (G > 1) {
+    constexpr int Bp = 4 / G, NF = 8 / G;
+    float fr[NF][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      d0[2 * i] = f16_bits_to_f32(w0[i]);
-      d0[2 * i + 1] = f16_bits_to_f32(w0[i] >> 16);
-      d1[2 * i] = f16_bits_to_f32(w1[i]);
-      d1[2 * i + 1] = f16_bits_to_f32(w1[i] >> 16);
+    for (int f = 0; f < NF; ++f) fr[f][0] = fr[f][1] = fr[f][2] = fr[f][3] = 0.f;
+#pragma unroll
+    for (int bk = 0; bk < 8; ++bk) {
+      const uint4 v = lds128(ch + 512 * bk + 16 * lane);
+      const uint32_t ux = v.x ^ 0x80808080u, uy = v.y ^ 0x80808080u;
+      const uint32_t uz = v.z ^ 0x80808080u, uw = v.w ^ 0x80808080u;
+      const uint4 bx = lds128(xs + bk * pair_stride + lane * 16);
+      float(&f4)[4] = fr[bk / G];
+      mma_acc(f4, byte02(ux), byte02(uz), byte13(ux), byte13(uz), bx.x, bx.y);
+      mma_acc(f4, byte02(uy), byte02(uw), byte13(uy), byte13(uw), bx.z, bx.w);
     }
-  }
-  const int xs_step = NT * 256;
+    const int b = t % Bp;
 #pragma unroll
-  for (int b = 0; b < 8; ++b) {
-    const uint4 v = lds128(ch + 512 * b + 16 * lane);
-    const uint32_t ux = v.x ^ 0x80808080u, uy = v.y ^ 0x80808080u;
-    const uint32_t uz = v.z ^ 0x80808080u, uw = v.w ^ 0x80808080u;
+    for (int f = 0; f < NF; ++f) {
+      const int bk = f * G + t / Bp;
+      const float dg = ld_f16(dp + 2 * bk), dg8 = ld_f16(dp + 16 + 2 * bk);
+      const float4 sv = lds128f(su + (bk * 4 + b) * 16);
+      const float S = sv.x + sv.y;
+      acc[0][0] = fmaf(dg, fmaf(-1152.f, S, (fr[f][0] + fr[f][1]) * sv.z), acc[0][0]);
+      acc[0][1] = fmaf(dg8, fmaf(-1152.f, S, (fr[f][2] + fr[f][3]) * sv.z), acc[0][1]);
+    }
+  } else {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint8_t* xb = xs + nt * 256 + lane * 8;
-      const uint2 b0 = lds64(xb + (2 * b) * xs_step);
-      const uint2 b1 = lds64(xb + (2 * b + 1) * xs_step);
-      float c[4];
-      mma_f16_16816(c, byte02(ux), byte02(uz), byte13(ux), byte13(uz), b0.x, b0.y);
-      mma_f16_16816_acc(c, byte02(uy), byte02(uw), byte13(uy), byte13(uw), b1.x, b1.y);
-      const float2 sp = lds64f(S + (b * 4 * NT + 4 * nt + t) * 8);
-      const float s32 = sp.x + sp.y;
-      acc[nt][0] = fmaf(d0[b], fmaf(-1152.f, s32, c[0] + c[1]), acc[nt][0]);
-      acc[nt][1] = fmaf(d1[b], fmaf(-1152.f, s32, c[2] + c[3]), acc[nt][1]);
+    for (int bk = 0; bk < 8; ++bk) {
+      const uint4 v = lds128(ch + 512 * bk + 16 * lane);
+      const uint32_t ux = v.x ^ 0x80808080u, uy = v.y ^ 0x80808080u;
+      const uint32_t uz = v.z ^ 0x80808080u, uw = v.w ^ 0x80808080u;
+      const float dg = ld_f16(dp + 2 * bk), dg8 = ld_f16(dp + 16 + 2 * bk);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint4 bx = lds128(xs + bk * pair_stride + nt * 512 + lane * 16);
+        const float4 sv = lds128f(su + (bk * 4 * NT + 4 * nt + t) * 16);
+        float c[4];
+        mma_f16_16816(c, byte02(ux), byte02(uz), byte13(ux), byte13(uz), bx.x, bx.y);
+        mma_acc(c, byte02(uy), byte02(uw), byte13(uy), byte13(uw), bx.z, bx.w);
+        const float S = sv.x + sv.y;
+        acc[nt][0] = fmaf(dg, fmaf(-1152.f, S, (c[0] + c[1]) * sv.z), acc[nt][0]);
+        acc[nt][1] = fmaf(dg8, fmaf(-1152.f, S, (c[2] + c[3]) * sv.z), acc[nt][1]);
+      }
     }
   }
 }
@@ -396,21 +466,19 @@ __device__ __forceinline__ void chunk_q80(const uint8_t* ch, const uint8_t* xs, 
 // output of one row group
 // ---------------------------------------------------------------------------
 template <int NT>
-__device__ __forceinline__ void write_rows(const GemvParams& P, const GemvProbDev& pr, int64_t rg, int warp,
-                                           int lane, const float (&v)[NT][2]) {
+__device__ __forceinline__ void write_rows(const GemvParams& P, const GemvProbDev& pr, int rg, int rw, int lane,
+                                           const float (&v)[NT][2]) {
   const int g = lane >> 2, t = lane & 3;
-  const float* unscale = reinterpret_cast<const float*>(P.ws + pr.sc_off);
-  const int64_t row0 = (rg * kGroupTiles + warp) * kChunkRows + g;
+  const int64_t row0 = ((int64_t)rg * kGroupTiles + rw) * kChunkRows + g;
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     const int b = 4 * nt + t;
     if (b >= P.batch) continue;
-    const float us = unscale[b];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int64_t row = row0 + 8 * h;
+    for (int hh = 0; hh < 2; ++hh) {
+      const int64_t row = row0 + 8 * hh;
       if (row < pr.n_rows) {
-        float out = v[nt][h] * us;
+        float out = v[nt][hh];
         if (pr.bias) out += pr.bias[row];
         pr.y[(int64_t)b * pr.ldy + row] = out;
       }
@@ -418,7 +486,7 @@ __device__ __forceinline__ void write_rows(const GemvParams& P, const GemvProbDe
   }
 }
 
-__device__ __forceinline__ int cta_of_slab(const GemvParams& P, int64_t s) {
+__device__ __forceinline__ int cta_of_slab(const GemvParams& P, int s) {
   int lo = 0, hi = P.n_cta - 1;  // largest c with cta_start[c] <= s
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -428,28 +496,59 @@ __device__ __forceinline__ int cta_of_slab(const GemvParams& P, int64_t s) {
   return lo;
 }
 
-template <int NT>
-__device__ void finish_rowgroup(const GemvParams& P, int p, int64_t rg, int64_t s_begin, int64_t s_end, int warp,
-                                int lane, float (&acc)[NT][2], int* s_flag) {
+// Called by all 16 consumer warps at the end of a row group (or of the CTA's
+// range).  Every consumer thread passes the same named barriers.
+template <int G, int NT>
+__device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int s_begin, int s_end, int warp, int lane,
+                                float (&acc)[NT][2], float* red, int* s_flag) {
   const GemvProbDev& pr = P.prob[p];
-  const int nrt = slab_tiles(pr, rg);
-  const int64_t rg_start = pr.slab0 + rg * pr.nb, rg_end = rg_start + pr.nb;
+  const int nrt = rg_tile_count(pr, rg);
+  const int rw = warp & (kRowWarps - 1);
+  if constexpr (G > 1) {
+    // diagonal layout: lanes t with the same batch slot hold different sub-blocks
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      if (G == 4) acc[0][hh] += __shfl_xor_sync(0xffffffffu, acc[0][hh], 1);
+      acc[0][hh] += __shfl_xor_sync(0xffffffffu, acc[0][hh], 2);
+    }
+  }
+  // 1. fold the two slab parities: warps 8..15 hand their sums to warps 0..7
+  float* rp = red + ((rw * 32 + lane) * NT * 2);
+  if (warp >= kRowWarps) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      rp[2 * nt] = acc[nt][0];
+      rp[2 * nt + 1] = acc[nt][1];
+    }
+  }
+  consumers_sync();
+  if (warp < kRowWarps) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      acc[nt][0] += rp[2 * nt];
+      acc[nt][1] += rp[2 * nt + 1];
+    }
+  }
+  const int rg_start = pr.slab0 + rg * pr.nb, rg_end = rg_start + pr.nb;
   if (s_begin <= rg_start && rg_end <= s_end) {
-    if (warp < nrt) write_rows<NT>(P, pr, rg, warp, lane, acc);
+    if (warp < nrt) write_rows<NT>(P, pr, rg, rw, lane, acc);
+    consumers_sync();  // `red` is reused by the next row group
     return;
   }
-  // split row group: publish the partial, the last contributor reduces
+  // 2. split row group: publish the partial, the last contributor reduces
   const int cta = blockIdx.x;
   const int slot = (s_begin >= rg_start) ? 0 : 1;
-  float* part = reinterpret_cast<float*>(P.ws + P.part_off) +
-                ((((int64_t)cta * 2 + slot) * kConsumerWarps + warp) * 32 + lane) * (NT * 2);
+  if (warp < kRowWarps) {
+    float* part = reinterpret_cast<float*>(P.ws + P.part_off) +
+                  ((((int64_t)cta * 2 + slot) * kRowWarps + warp) * 32 + lane) * (NT * 2);
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    __stcg(part + 2 * nt, acc[nt][0]);
-    __stcg(part + 2 * nt + 1, acc[nt][1]);
+    for (int nt = 0; nt < NT; ++nt) {
+      __stcg(part + 2 * nt, acc[nt][0]);
+      __stcg(part + 2 * nt + 1, acc[nt][1]);
+    }
+    __threadfence();
   }
-  __threadfence();
-  named_bar_consumers();
+  consumers_sync();
   if (threadIdx.x == 0) {
     const int c_first = cta_of_slab(P, rg_start);
     const int c_last = cta_of_slab(P, rg_end - 1);
@@ -463,7 +562,7 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int64_t rg, int64_t 
     }
     *s_flag = last ? (1 + c_first + (c_last << 12)) : 0;
   }
-  named_bar_consumers();
+  consumers_sync();
   const int f = *s_flag;
   if (f && warp < nrt) {
     const int c_first = (f - 1) & 0xFFF, c_last = (f - 1) >> 12;
@@ -473,7 +572,7 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int64_t rg, int64_t 
     for (int c = c_first; c <= c_last; ++c) {
       const int sl = (P.cta_start[c] >= rg_start) ? 0 : 1;
       const float* q = reinterpret_cast<const float*>(P.ws + P.part_off) +
-                       ((((int64_t)c * 2 + sl) * kConsumerWarps + warp) * 32 + lane) * (NT * 2);
+                       ((((int64_t)c * 2 + sl) * kRowWarps + warp) * 32 + lane) * (NT * 2);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         sum[nt][0] += __ldcg(q + 2 * nt);
@@ -482,105 +581,169 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int64_t rg, int64_t 
     }
     write_rows<NT>(P, pr, rg, warp, lane, sum);
   }
+  consumers_sync();  // s_flag and `red` are reused by the next row group
+}
+
+// ---------------------------------------------------------------------------
+// consumer side: the slabs of one row-group segment that have this warp's parity
+// ---------------------------------------------------------------------------
+template <int QT, int G, int NT>
+__device__ __forceinline__ void consume_segment(const GemvParams& P, const uint8_t* smem, uint64_t* full_bar,
+                                                uint64_t* empty_bar, int i, int i_end, int NS, int rw, int nrt,
+                                                int cb, int lane, bool& failed, float (&acc)[NT][2]) {
+  if (i >= i_end) return;
+  int st = i % NS;
+  uint32_t ph = (uint32_t)((i / NS) & 1);
+  for (; i < i_end; i += 2) {
+    if (!failed && !mbar_wait_bounded(&full_bar[st], ph, kWaitLimitNs)) {
+      record_error(P, DRACO_ERR_TIMEOUT);
+      failed = true;
+    }
+    if (!failed && rw < nrt) {
+      const uint8_t* stage = smem + (size_t)st * P.stage_bytes;
+      const uint8_t* ch = stage + rw * cb;
+      const uint8_t* xs = stage + P.w_stage;
+      const uint8_t* su = xs + P.xs_bytes;
+      if (QT == kQ4_K) chunk_q4k<G, NT>(ch, xs, su, lane, acc);
+      else if (QT == kQ6_K) chunk_q6k<G, NT>(ch, xs, su, lane, acc);
+      else chunk_q80<G, NT>(ch, xs, su, lane, acc);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[st]);
+    st += 2;
+    if (st >= NS) {
+      st -= NS;
+      ph ^= 1u;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
 // the persistent GEMV kernel
 // ---------------------------------------------------------------------------
-template <int NT>
+template <int G, int NT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-  __shared__ __align__(16) float scratch[kConsumerWarps][16 * 16];
+  __shared__ __align__(16) float red[kRowWarps * 32 * 2 * NT];
   __shared__ int s_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
-  const int64_t s_begin = P.cta_start[cta], s_end = P.cta_start[cta + 1];
+  const int s_begin = P.cta_start[cta], s_end = P.cta_start[cta + 1];
   const int NS = P.n_stages;
+  const int n = s_end - s_begin;
 
+  // zero the stages once: columns of padded batch slots are never rewritten
+  {
+    uint4* z = reinterpret_cast<uint4*>(smem);
+    const int n16 = (NS * P.stage_bytes) >> 4;
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before the TMA engine writes the stages
+  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], kConsumerWarps);
+      mbar_init(&full_bar[i], 2);  // producer (with the weight bytes) + converter
+      mbar_init(&empty_bar[i], kRowWarps);
     }
     fence_mbar_init();
   }
   __syncthreads();
+  // allow the next kernel in the stream to launch; it waits for our completion
+  // (griddepcontrol.wait) before touching anything we read or write
+  grid_launch_dependents();
 
-  if (warp == kConsumerWarps) {
-    // ---------------- producer ----------------
+  if (warp == kProducerWarp) {
+    // ---------------- producer: weights ----------------
     if (lane == 0) {
-      // Weights do not depend on the preceding kernel; the activation slices do.
-      bool dep_done = false;
-      int64_t i = 0;
-      for (int64_t s = s_begin; s < s_end; ++s, ++i) {
-        const int st = (int)(i % NS);
-        const uint32_t ph = (uint32_t)((i / NS) & 1);
+      SlabCursor cur;
+      cur.seek(P, s_begin);
+      int st = 0;
+      uint32_t ph = 0;
+      for (int i = 0; i < n; ++i) {
         if (i >= NS && !mbar_wait_bounded(&empty_bar[st], ph ^ 1u, kWaitLimitNs)) {
           record_error(P, DRACO_ERR_TIMEOUT);
           break;
         }
-        int p;
-        int64_t rg, j;
-        locate_slab(P, s, p, rg, j);
-        const GemvProbDev& pr = P.prob[p];
-        const TiledGeom geo = tiled_geom(pr.qt, pr.n_rows, pr.k);
-        const uint32_t wbytes = (uint32_t)(slab_tiles(pr, rg) * pr.cb);
-        uint8_t* stage = smem + (size_t)st * P.stage_bytes;
-        mbar_arrive_expect_tx(&full_bar[st], wbytes + P.xs_bytes + P.s_bytes);
-        bulk_g2s(stage, pr.w + slab_offset(geo, rg, j), wbytes, &full_bar[st]);
-        if (!dep_done) {
-          grid_dependency_wait();
-          dep_done = true;
+        const GemvProbDev& pr = P.prob[cur.p];
+        const int nrt = rg_tile_count(pr, cur.rg);
+        const uint32_t wbytes = (uint32_t)(nrt * pr.cb);
+        const int64_t woff = (int64_t)cur.rg * kGroupTiles * pr.nb * pr.cb + (int64_t)cur.j * nrt * pr.cb;
+        mbar_arrive_expect_tx(&full_bar[st], wbytes);
+        bulk_g2s(smem + (size_t)st * P.stage_bytes, pr.w + woff, wbytes, &full_bar[st]);
+        cur.next(P);
+        if (++st == NS) {
+          st = 0;
+          ph ^= 1u;
         }
-        bulk_g2s(stage + P.w_stage, P.ws + pr.xs_off + j * (int64_t)P.xs_bytes, P.xs_bytes, &full_bar[st]);
-        bulk_g2s(stage + P.w_stage + P.xs_bytes, P.ws + pr.s_off + j * (int64_t)P.s_bytes, P.s_bytes,
-                 &full_bar[st]);
       }
     }
     return;
   }
 
+  if (warp > kProducerWarp) {
+    // ---------------- converters: activations ----------------
+    const int c = warp - kProducerWarp - 1;
+    grid_dependency_wait();  // x is written by the preceding kernel
+    SlabCursor cur;
+    cur.seek(P, s_begin);
+    for (int q = 0; q < c && q < n; ++q) cur.next(P);
+    for (int i = c; i < n; i += kConvWarps) {
+      const int st = i % NS;
+      const uint32_t ph = (uint32_t)((i / NS) & 1);
+      if (i >= NS && !mbar_wait_bounded(&empty_bar[st], ph ^ 1u, kWaitLimitNs)) {
+        record_error(P, DRACO_ERR_TIMEOUT);
+        break;
+      }
+      uint8_t* xs = smem + (size_t)st * P.stage_bytes + P.w_stage;
+      convert_slab<G, NT>(P, P.prob[cur.p], cur.j, xs, xs + P.xs_bytes, lane);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full_bar[st]);
+      for (int q = 0; q < kConvWarps; ++q) cur.next(P);
+    }
+    return;
+  }
+
   // ---------------- consumers ----------------
-  grid_dependency_wait();  // outputs (y) may be read by the preceding kernel
+  grid_dependency_wait();  // y may still be read by the preceding kernel
+  const int par = warp / kRowWarps, rw = warp % kRowWarps;
   float acc[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
-  float* scr = scratch[warp];
   // After a timed-out wait the warp stops waiting and computing but keeps
   // walking its range, so every consumer warp still reaches each named
   // barrier and the kernel ends.  The status word tells the host.
   bool failed = false;
-  int64_t i = 0;
-  for (int64_t s = s_begin; s < s_end; ++s, ++i) {
-    const int st = (int)(i % NS);
-    const uint32_t ph = (uint32_t)((i / NS) & 1);
-    if (!failed && !mbar_wait_bounded(&full_bar[st], ph, kWaitLimitNs)) {
-      record_error(P, DRACO_ERR_TIMEOUT);
-      failed = true;
-    }
-    int p;
-    int64_t rg, j;
-    locate_slab(P, s, p, rg, j);
-    const GemvProbDev& pr = P.prob[p];
-    const int nrt = slab_tiles(pr, rg);
-    const uint8_t* stage = smem + (size_t)st * P.stage_bytes;
-    if (!failed && warp < nrt) {
-      const uint8_t* ch = stage + warp * pr.cb;
-      const uint8_t* xs = stage + P.w_stage;
-      const uint8_t* S = xs + P.xs_bytes;
-      if (pr.qt == kQ4_K) chunk_q4k<NT>(ch, xs, S, scr, lane, acc);
-      else if (pr.qt == kQ6_K) chunk_q6k<NT>(ch, xs, S, scr, lane, acc);
-      else chunk_q80<NT>(ch, xs, S, lane, acc);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[st]);
-    if (j == pr.nb - 1 || s == s_end - 1) {
-      finish_rowgroup<NT>(P, p, rg, s_begin, s_end, warp, lane, acc, &s_flag);
+  SlabCursor cur;
+  cur.seek(P, s_begin);
+  int s = s_begin;
+  while (s < s_end) {
+    const GemvProbDev& pr = P.prob[cur.p];
+    const int seg = min(pr.nb - cur.j, s_end - s);  // slabs of this row group in our range
+    const int i0 = s - s_begin;
+    const int i_first = i0 + (((i0 & 1) != par) ? 1 : 0);
+    const int nrt = rg_tile_count(pr, cur.rg);
+    if (pr.qt == kQ4_K)
+      consume_segment<kQ4_K, G, NT>(P, smem, full_bar, empty_bar, i_first, i0 + seg, NS, rw, nrt, pr.cb, lane,
+                                    failed, acc);
+    else if (pr.qt == kQ6_K)
+      consume_segment<kQ6_K, G, NT>(P, smem, full_bar, empty_bar, i_first, i0 + seg, NS, rw, nrt, pr.cb, lane,
+                                    failed, acc);
+    else
+      consume_segment<kQ8_0, G, NT>(P, smem, full_bar, empty_bar, i_first, i0 + seg, NS, rw, nrt, pr.cb, lane,
+                                    failed, acc);
+    finish_rowgroup<G, NT>(P, cur.p, cur.rg, s_begin, s_end, warp, lane, acc, red, &s_flag);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
+    s += seg;
+    cur.j += seg;
+    if (cur.j == pr.nb) {
+      cur.j = 0;
+      if (++cur.rg == pr.n_rg) {
+        cur.rg = 0;
+        ++cur.p;
+      }
     }
   }
 }
@@ -596,18 +759,20 @@ struct HostPlan {
 
 static int nt_of_batch(int batch) { return batch <= 4 ? 1 : batch <= 8 ? 2 : batch <= 16 ? 4 : 8; }
 
+// Dynamic shared memory budget of the GEMV kernel (stages); static shared
+// memory (barriers, reduction buffer) comes on top.
+constexpr int kSmemBudget = 200 * 1024;
+
 static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, HostPlan& hp, char* msg,
                        size_t ml) {
   GemvParams& P = hp.P;
   memset(&P, 0, sizeof(P));
   P.n_prob = n;
   P.batch = batch;
-  P.nt = nt_of_batch(batch);
+  P.nt = batch <= 2 ? 1 : nt_of_batch(batch);
   const int NT = P.nt;
-  P.xs_bytes = 16 * 8 * NT * 32;  // 16 steps x 8*NT cols x 4 t x 8 B
-  P.s_bytes = 8 * 4 * NT * 8;     // 8 pairs x 4*NT slots x 2 floats
-  int64_t off = kWsCounters + kWsCountersBytes;
-  off = align256(off);
+  P.xs_bytes = 8 * (8 * NT) * 64;  // 8 pairs x 8*NT columns x 4 t x 16 B
+  P.su_bytes = 8 * (4 * NT) * 16;  // 8 pairs x 4*NT slots x float4
   int64_t slab0 = 0;
   int w_stage = 0;
   for (int p = 0; p < n; ++p) {
@@ -627,26 +792,23 @@ static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_
     d.n_rg = (int)g.n_rg;
     d.n_tiles = (int)g.n_tiles;
     d.cb = g.cb;
-    d.slab0 = slab0;
+    d.slab0 = (int)slab0;
     slab0 += g.n_rg * g.nb;
     w_stage = std::max(w_stage, kGroupTiles * g.cb);
-    const int64_t nk = g.nb * 16;
-    d.xs_off = off;
-    off = align256(off + nk * 8 * NT * 32);
-    d.s_off = off;
-    off = align256(off + (nk / 2) * 4 * NT * 8);
-    d.sc_off = off;
-    off = align256(off + 4 * NT * 4);
   }
+  if (slab0 > (int64_t)1 << 30) {
+    snprintf(msg, ml, "gemv: problem set too large");
+    return false;
+  }
+  int64_t off = align256(kWsCounters + kWsCountersBytes);
   P.part_off = off;
-  off = align256(off + (int64_t)kMaxCta * 2 * kConsumerWarps * 32 * NT * 2 * 4);
+  off = align256(off + (int64_t)kMaxCta * 2 * kRowWarps * 32 * NT * 2 * 4);
   P.status_off = kWsStatus;
   P.cnt_off = kWsCounters;
-  P.total_slabs = slab0;
+  P.total_slabs = (int)slab0;
   P.w_stage = w_stage;
-  P.stage_bytes = w_stage + P.xs_bytes + P.s_bytes;
-  const int smem_budget = 200 * 1024;
-  P.n_stages = std::min(kMaxStages, smem_budget / P.stage_bytes);
+  P.stage_bytes = w_stage + P.xs_bytes + P.su_bytes;
+  P.n_stages = std::min(kMaxStages, kSmemBudget / P.stage_bytes);
   if (P.n_stages < 2) {
     snprintf(msg, ml, "gemv: stage of %d bytes does not fit shared memory twice", P.stage_bytes);
     return false;
@@ -701,38 +863,32 @@ size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch) {
   return local.ws_needed;
 }
 
-template <int NT>
-static cudaError_t launch_nt(const HostPlan& hp, cudaStream_t st) {
+template <int G, int NT>
+static cudaError_t launch_gemv(const HostPlan& hp, cudaStream_t st) {
   static int attr_set[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && attr_set[dev] < (int)hp.smem_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         200 * 1024);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(gemv_kernel<G, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
     if (e != cudaSuccess) return e;
-    attr_set[dev] = 200 * 1024;
+    attr_set[dev] = 1;
   }
   const GemvParams& P = hp.P;
-  // prep kernel (plain launch; waits for nothing but stream order)
-  {
-    dim3 grid(4 * P.nt, P.n_prob);
-    gemv_prep_kernel<<<grid, 256, 0, st>>>(P);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
-  // main kernel with programmatic dependent launch so that its weight
-  // prefetch overlaps the prep kernel
+  // programmatic dependent launch: the kernel may start before its
+  // predecessor in the stream finishes; it streams weights at once and waits
+  // (griddepcontrol.wait) before reading x or writing y
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(P.n_cta);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = hp.smem_bytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<NT>, P);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<G, NT>, P);
 }
 
 int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
@@ -752,12 +908,14 @@ int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, siz
   }
   hp.P.ws = static_cast<uint8_t*>(ws);
   cudaError_t e;
-  switch (hp.P.nt) {
-    case 1: e = launch_nt<1>(hp, st); break;
-    case 2: e = launch_nt<2>(hp, st); break;
-    case 4: e = launch_nt<4>(hp, st); break;
-    default: e = launch_nt<8>(hp, st); break;
-  }
+  if (batch == 1) e = launch_gemv<4, 1>(hp, st);
+  else if (batch == 2) e = launch_gemv<2, 1>(hp, st);
+  else switch (hp.P.nt) {
+      case 1: e = launch_gemv<1, 1>(hp, st); break;
+      case 2: e = launch_gemv<1, 2>(hp, st); break;
+      case 4: e = launch_gemv<1, 4>(hp, st); break;
+      default: e = launch_gemv<1, 8>(hp, st); break;
+    }
   if (e != cudaSuccess) {
     snprintf(msg, ml, "gemv: launch failed: %s", cudaGetErrorString(e));
     return DRACO_ERR_CUDA;
