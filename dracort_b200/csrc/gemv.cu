@@ -18,19 +18,23 @@
 //    launch, before the preceding kernel has finished (programmatic dependent
 //    launch), since weights do not depend on it.
 //  * Warps 17-19 (converters) fill each stage's activation slice: they read
-//    the slab's 256 x B activations from global memory (L2), rescale each
-//    32-element pair by a power of two u, split into fp16 hi + lo, and store
-//    them in MMA-fragment order together with the per-16-element sums.
+//    the slab's 256 x B activations from global memory (L2), scale each
+//    32-element group by a power of two u (max |x| / u in [2^13, 2^14)),
+//    round to an integer q and split it into two int8 digits,
+//    q = 256 * hi + lo, stored in MMA-fragment order with the group sums.
 //  * Warps 0-15 consume: warp w owns row tile (w % 8) of the slabs whose
-//    parity is w / 8.  Quants enter the m16n8k16 tensor-core MMA as exact
-//    integers in fp16 (0x6400 | nibble == 1024 + q), activations as the hi/lo
-//    pair (one MMA column each), accumulating in fp32.  The sub-block scale,
-//    the 1024 offset and Q4_K's min are applied in fp32 per sub-block:
-//        y += alpha * u * c - beta * sum(x)
+//    parity is w / 8.  The quants enter the int8 tensor-core MMA
+//    (m16n8k32, u8 x s8 -> s32) as they are: Q4_K nibbles with one mask,
+//    Q6_K as ql | qh << 4, Q8_0 bytes unchanged; each activation digit is one
+//    MMA column.  Integer accumulation is exact; the sub-block scale and
+//    Q4_K's min / Q6_K's -32 offset are applied in fp32 per sub-block:
+//        y += d_sc * u * (256 * C_hi + C_lo) - d_min_m * S
+//    The activation rounding (one step of u) bounds the result error at
+//    about 5e-5 relative L2 for Gaussian activations.
 //  * Batch 1-2 ("diagonal" activation layout): each sub-block's activations
 //    sit in their own pair of MMA columns, so one accumulator collects
 //    4 (B=1) or 2 (B=2) sub-blocks and every lane owns one sub-block's sum.
-//    Batch >= 3 ("dense"): columns are (batch, hi/lo).
+//    Batch >= 3 ("dense"): columns are (batch, digit).
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -143,18 +147,55 @@ struct SlabCursor {
 };
 
 // ---------------------------------------------------------------------------
-// activation conversion of one slab (problem pr, super-block j) by one warp.
-// Lane quad (lane / 4) takes the 32-element pair m of a batch row, lane % 4
-// eight of its elements.  Per pair: u = 2^e with max|x| * 2^-e in
-// [2^13, 2^14), hi = fp16(x / u), lo = fp16(x / u - hi), S = u * sum(hi + lo).
-//   xs[m][col][t][16 B]: (x[4t], x[4t+2]), (x[4t+1], x[4t+3]) for the pair's
-//       16-element steps 0 (bytes 0-7) and 1 (bytes 8-15); the column is
-//         dense   : 2b + hl
-//         diagonal: ((sub-block mod G) * Bp + b) * 2 + hl,  G = 4 / Bp,
-//       a Q4_K / Q8_0 sub-block being the pair and a Q6_K sub-block one step;
-//       the other sub-block slots of a diagonal entry are written as zeros;
-//   su[m][b] = (S_step0, S_step1, u, 0).
+// int8 tensor-core MMA (legacy warp-level path, exact int32 accumulation)
+//   m16n8k32: A 16x32 (a0: row g, k 4t..4t+3; a1: row g+8; a2: row g, k 16+4t..;
+//             a3: row g+8, k 16+4t..), B 32x8 (b0: k 4t..4t+3, col g; b1: k 16+4t..)
+//   m16n8k16: A 16x16 (a0: row g, k 4t..; a1: row g+8), B 16x8 (b0: k 4t.., col g)
+//   D 16x8 s32: d0, d1 -> (row g, cols 2t, 2t+1); d2, d3 -> row g+8
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ void imma_u8_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_s8_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_u8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+               : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+               : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ void zero4(int (&d)[4]) { d[0] = d[1] = d[2] = d[3] = 0; }
+// the two activation digits of one row: x / u = 256 * hi + lo
+__device__ __forceinline__ float digits(int hi, int lo) { return __int2float_rn(hi * 256 + lo); }
+
+constexpr uint32_t kNib = 0x0F0F0F0Fu;
+
+// ---------------------------------------------------------------------------
+// activation conversion of one slab (problem pr, super-block j) by one warp.
+// Lane quad (lane / 4) takes the 32-element group m of a batch row, lane % 4
+// eight of its elements.  Per group: u = 2^e with max|x| / u in [2^13, 2^14),
+// q = rint(x / u) split into two int8 digits q = 256 * hi + lo, and the sums
+// S = u * sum(q) of its two 16-element halves.
+//   xs[m][col][t][8 B]: bytes 0-3 = digits of elements 4t..4t+3, bytes 4-7 =
+//       elements 16+4t..16+4t+3; the column is
+//         dense   : 2b + digit
+//         diagonal: ((sub-block mod G) * Bp + b) * 2 + digit,  G = 4 / Bp,
+//       a Q4_K / Q8_0 sub-block being the group and a Q6_K sub-block one half
+//       (the halves then go to different columns); unused slots hold zeros;
+//   su[m][b] = (S_half0, S_half1, u, 0).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 template <int G, int NT>
 __device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProbDev& pr, int j, uint8_t* xs,
                                              uint8_t* su, int lane) {
@@ -179,65 +220,64 @@ __device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProb
     int e = 0;
     if (amax > 0.f && amax <= 3.0e38f) e = ilogbf(amax) - 13;
     e = max(-110, min(110, e));
-    const float sc = ldexpf(1.f, -e), u = ldexpf(1.f, e);
-    __half hi[8], lo[8];
-    float s = 0.f;
+    const float inv = ldexpf(1.f, -e), u = ldexpf(1.f, e);
+    int hi[8], lo[8], qs = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float a = v[i] * sc;
-      hi[i] = __float2half_rn(a);
-      const float hf = __half2float(hi[i]);
-      lo[i] = __float2half_rn(a - hf);
-      s += hf + __half2float(lo[i]);
+      // round to nearest even via the 1.5 * 2^23 magic number (|x / u| < 2^14)
+      const int q = __float_as_int(fmaf(v[i], inv, 12582912.f)) - 0x4B400000;
+      hi[i] = (q + 128) >> 8;
+      lo[i] = q - (hi[i] << 8);
+      qs += q;
     }
-    s += __shfl_xor_sync(0xffffffffu, s, 1);               // sum of this 16-element step
-    const float s_other = __shfl_xor_sync(0xffffffffu, s, 2);  // the pair's other step
-    if (r == 0) *reinterpret_cast<float4*>(su + (m * kSlots + b) * 16) = make_float4(s * u, s_other * u, u, 0.f);
-    uint2 eh[2], el[2];
+    qs += __shfl_xor_sync(0xffffffffu, qs, 1);               // sum of this 16-element half
+    const int qs_other = __shfl_xor_sync(0xffffffffu, qs, 2);  // the group's other half
+    if (r == 0)
+      *reinterpret_cast<float4*>(su + (m * kSlots + b) * 16) =
+          make_float4(__int2float_rn(qs) * u, __int2float_rn(qs_other) * u, u, 0.f);
+    uint32_t dh[2], dl[2];
 #pragma unroll
     for (int tt = 0; tt < 2; ++tt) {
-      eh[tt] = make_uint2(pack_h2(hi[4 * tt], hi[4 * tt + 2]), pack_h2(hi[4 * tt + 1], hi[4 * tt + 3]));
-      el[tt] = make_uint2(pack_h2(lo[4 * tt], lo[4 * tt + 2]), pack_h2(lo[4 * tt + 1], lo[4 * tt + 3]));
+      dh[tt] = pack4(hi[4 * tt], hi[4 * tt + 1], hi[4 * tt + 2], hi[4 * tt + 3]);
+      dl[tt] = pack4(lo[4 * tt], lo[4 * tt + 1], lo[4 * tt + 2], lo[4 * tt + 3]);
     }
-    uint8_t* base = xs + (size_t)m * kCols * 64 + (size_t)t0 * 16 + 8 * kap;
+    uint8_t* base = xs + (size_t)m * kCols * 32 + (size_t)t0 * 8 + 4 * kap;
     if constexpr (kDiag) {
       const int slot = (q6 ? (2 * m + kap) : m) % G;
 #pragma unroll
       for (int jj = 0; jj < G; ++jj)
 #pragma unroll
-        for (int hl = 0; hl < 2; ++hl) {
-          const int col = (jj * Bp + b) * 2 + hl;
+        for (int dg = 0; dg < 2; ++dg) {
+          const int col = (jj * Bp + b) * 2 + dg;
 #pragma unroll
-          for (int tt = 0; tt < 2; ++tt) {
-            const uint2 val = (jj == slot) ? (hl ? el[tt] : eh[tt]) : make_uint2(0u, 0u);
-            *reinterpret_cast<uint2*>(base + col * 64 + tt * 16) = val;
-          }
+          for (int tt = 0; tt < 2; ++tt)
+            *reinterpret_cast<uint32_t*>(base + col * 32 + tt * 8) = (jj == slot) ? (dg ? dl[tt] : dh[tt]) : 0u;
         }
     } else {
       (void)q6;
 #pragma unroll
-      for (int hl = 0; hl < 2; ++hl)
+      for (int dg = 0; dg < 2; ++dg)
 #pragma unroll
         for (int tt = 0; tt < 2; ++tt)
-          *reinterpret_cast<uint2*>(base + (2 * b + hl) * 64 + tt * 16) = hl ? el[tt] : eh[tt];
+          *reinterpret_cast<uint32_t*>(base + (2 * b + dg) * 32 + tt * 8) = dg ? dl[tt] : dh[tt];
     }
   }
 }
 
 // ---------------------------------------------------------------------------
 // per-chunk consumers: one warp, one 16-row x 256-element chunk.
-//   ch : chunk bytes in smem;  xs : slab activation slice [8 pairs][ncols][4][16 B]
-//   su : [8 pairs][4 or bp slots][float4]
-//   G  : sub-blocks per MMA accumulator (4: batch 1, 2: batch 2, 1: dense)
+//   ch : chunk bytes in smem;  xs : slab activation slice [8 groups][8NT cols][4][8 B]
+//   su : [8 groups][4NT slots][float4]
+//   G  : sub-blocks per accumulator (4: batch 1, 2: batch 2, 1: dense)
 //   acc[nt][0] -> (row g, batch b), acc[nt][1] -> (row g+8, batch b), with
 //   b = t % Bp (diagonal, nt = 0) or 4 nt + t (dense)
 // ---------------------------------------------------------------------------
-// Q4_K (alpha, beta) of 32-element sub-block j for the row whose 12 scale bytes
-// are (A, Bw, C): low nibbles (even j) carry 1024 + q, high ones 1024 + 16 q.
-__device__ __forceinline__ void q4k_ab(uint32_t A, uint32_t Bw, uint32_t C, float d, float dmin, int j, bool high_j4,
-                                       float& al, float& be) {
+// Q4_K (d * sc, dmin * m) of sub-block j for the row whose 12 scale bytes are
+// (A, Bw, C) (gguf.py:436-442).
+__device__ __forceinline__ void q4k_sm(uint32_t A, uint32_t Bw, uint32_t C, float d, float dmin, int j,
+                                       bool upper, float& ds, float& mm) {
   uint32_t sc, m;
-  if (!high_j4) {
+  if (!upper) {
     sc = ubyte(A, j) & 63u;
     m = ubyte(Bw, j) & 63u;
   } else {
@@ -246,10 +286,8 @@ __device__ __forceinline__ void q4k_ab(uint32_t A, uint32_t Bw, uint32_t C, floa
     sc = (c & 15u) | ((ubyte(A, i) >> 6) << 4);
     m = (c >> 4) | ((ubyte(Bw, i) >> 6) << 4);
   }
-  const float a = d * u2f(sc), mu = dmin * u2f(m);
-  const bool odd = j & 1;
-  al = odd ? a * 0.0625f : a;
-  be = fmaf(odd ? 64.f : 1024.f, a, mu);
+  ds = d * u2f(sc);
+  mm = dmin * u2f(m);
 }
 
 template <int G, int NT>
@@ -262,69 +300,73 @@ __device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, 
   const uint2 dd = lds64(ch + 2240 + 8 * g);
   const float d0 = f16_bits_to_f32(dd.x), m0 = f16_bits_to_f32(dd.x >> 16);
   const float d1 = f16_bits_to_f32(dd.y), m1 = f16_bits_to_f32(dd.y >> 16);
-  const int pair_stride = (G > 1 ? 8 : 8 * NT) * 64;
+  constexpr int kColBytes = 8 * NT * 32;  // one group's activation entries
   if constexpr (G > 1) {
     constexpr int Bp = 4 / G, NF = 8 / G;
-    float fr[NF][4];
+    int fr[NF][4];
 #pragma unroll
-    for (int f = 0; f < NF; ++f) fr[f][0] = fr[f][1] = fr[f][2] = fr[f][3] = 0.f;
+    for (int f = 0; f < NF; ++f) zero4(fr[f]);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint4 v = lds128(ch + 512 * q + 16 * lane);
-      const uint32_t x8 = v.x >> 8, y8 = v.y >> 8, z8 = v.z >> 8, w8 = v.w >> 8;
-      const uint4 bl = lds128(xs + (2 * q) * pair_stride + lane * 16);
-      const uint4 bh = lds128(xs + (2 * q + 1) * pair_stride + lane * 16);
-      float(&fl)[4] = fr[(2 * q) / G];
-      mma_acc(fl, nib_lo(v.x), nib_lo(v.z), nib_lo(x8), nib_lo(z8), bl.x, bl.y);
-      mma_acc(fl, nib_lo(v.y), nib_lo(v.w), nib_lo(y8), nib_lo(w8), bl.z, bl.w);
-      float(&fh)[4] = fr[(2 * q + 1) / G];
-      mma_acc(fh, nib_hi(v.x), nib_hi(v.z), nib_hi(x8), nib_hi(z8), bh.x, bh.y);
-      mma_acc(fh, nib_hi(v.y), nib_hi(v.w), nib_hi(y8), nib_hi(w8), bh.z, bh.w);
+      const uint2 bl = lds64(xs + (2 * q) * kColBytes + lane * 8);
+      const uint2 bh = lds64(xs + (2 * q + 1) * kColBytes + lane * 8);
+      imma_u8_k32(fr[(2 * q) / G], v.x & kNib, v.z & kNib, v.y & kNib, v.w & kNib, bl.x, bl.y);
+      imma_u8_k32(fr[(2 * q + 1) / G], (v.x >> 4) & kNib, (v.z >> 4) & kNib, (v.y >> 4) & kNib, (v.w >> 4) & kNib,
+                  bh.x, bh.y);
     }
     const int b = t % Bp;
 #pragma unroll
     for (int f = 0; f < NF; ++f) {
-      const int j = f * G + t / Bp;  // this lane's sub-block in fragment f
-      float al0, be0, al1, be1;
-      q4k_ab(A0, B0, C0, d0, m0, j, f * G >= 4, al0, be0);
-      q4k_ab(A1, B1, C1, d1, m1, j, f * G >= 4, al1, be1);
+      const int j = f * G + t / Bp;  // this lane's sub-block in accumulator f
+      float ds0, mm0, ds1, mm1;
+      q4k_sm(A0, B0, C0, d0, m0, j, f * G >= 4, ds0, mm0);
+      q4k_sm(A1, B1, C1, d1, m1, j, f * G >= 4, ds1, mm1);
       const float4 s = lds128f(su + (j * 4 + b) * 16);
       const float S = s.x + s.y;
-      acc[0][0] = fmaf(al0, (fr[f][0] + fr[f][1]) * s.z, fmaf(-be0, S, acc[0][0]));
-      acc[0][1] = fmaf(al1, (fr[f][2] + fr[f][3]) * s.z, fmaf(-be1, S, acc[0][1]));
+      acc[0][0] = fmaf(ds0 * s.z, digits(fr[f][0], fr[f][1]), fmaf(-mm0, S, acc[0][0]));
+      acc[0][1] = fmaf(ds1 * s.z, digits(fr[f][2], fr[f][3]), fmaf(-mm1, S, acc[0][1]));
     }
   } else {
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      float al0l, be0l, al1l, be1l, al0h, be0h, al1h, be1h;
-      q4k_ab(A0, B0, C0, d0, m0, 2 * q, q >= 2, al0l, be0l);
-      q4k_ab(A1, B1, C1, d1, m1, 2 * q, q >= 2, al1l, be1l);
-      q4k_ab(A0, B0, C0, d0, m0, 2 * q + 1, q >= 2, al0h, be0h);
-      q4k_ab(A1, B1, C1, d1, m1, 2 * q + 1, q >= 2, al1h, be1h);
+      float dsl0, mml0, dsl1, mml1, dsh0, mmh0, dsh1, mmh1;
+      q4k_sm(A0, B0, C0, d0, m0, 2 * q, q >= 2, dsl0, mml0);
+      q4k_sm(A1, B1, C1, d1, m1, 2 * q, q >= 2, dsl1, mml1);
+      q4k_sm(A0, B0, C0, d0, m0, 2 * q + 1, q >= 2, dsh0, mmh0);
+      q4k_sm(A1, B1, C1, d1, m1, 2 * q + 1, q >= 2, dsh1, mmh1);
       const uint4 v = lds128(ch + 512 * q + 16 * lane);
-      const uint32_t x8 = v.x >> 8, y8 = v.y >> 8, z8 = v.z >> 8, w8 = v.w >> 8;
+      const uint32_t l0 = v.x & kNib, l1 = v.z & kNib, l2 = v.y & kNib, l3 = v.w & kNib;
+      const uint32_t h0 = (v.x >> 4) & kNib, h1 = (v.z >> 4) & kNib, h2 = (v.y >> 4) & kNib, h3 = (v.w >> 4) & kNib;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint4 bl = lds128(xs + (2 * q) * pair_stride + nt * 512 + lane * 16);
-        const uint4 bh = lds128(xs + (2 * q + 1) * pair_stride + nt * 512 + lane * 16);
-        float c[4], e[4];
-        mma_f16_16816(c, nib_lo(v.x), nib_lo(v.z), nib_lo(x8), nib_lo(z8), bl.x, bl.y);
-        mma_acc(c, nib_lo(v.y), nib_lo(v.w), nib_lo(y8), nib_lo(w8), bl.z, bl.w);
-        mma_f16_16816(e, nib_hi(v.x), nib_hi(v.z), nib_hi(x8), nib_hi(z8), bh.x, bh.y);
-        mma_acc(e, nib_hi(v.y), nib_hi(v.w), nib_hi(y8), nib_hi(w8), bh.z, bh.w);
+        const uint2 bl = lds64(xs + (2 * q) * kColBytes + nt * 256 + lane * 8);
+        const uint2 bh = lds64(xs + (2 * q + 1) * kColBytes + nt * 256 + lane * 8);
+        int c[4], e[4];
+        zero4(c);
+        zero4(e);
+        imma_u8_k32(c, l0, l1, l2, l3, bl.x, bl.y);
+        imma_u8_k32(e, h0, h1, h2, h3, bh.x, bh.y);
         const float4 sl = lds128f(su + ((2 * q) * 4 * NT + 4 * nt + t) * 16);
         const float4 sh = lds128f(su + ((2 * q + 1) * 4 * NT + 4 * nt + t) * 16);
-        const float Sl = sl.x + sl.y, Sh = sh.x + sh.y;
         float r0 = acc[nt][0], r1 = acc[nt][1];
-        r0 = fmaf(al0l, (c[0] + c[1]) * sl.z, fmaf(-be0l, Sl, r0));
-        r1 = fmaf(al1l, (c[2] + c[3]) * sl.z, fmaf(-be1l, Sl, r1));
-        r0 = fmaf(al0h, (e[0] + e[1]) * sh.z, fmaf(-be0h, Sh, r0));
-        r1 = fmaf(al1h, (e[2] + e[3]) * sh.z, fmaf(-be1h, Sh, r1));
+        r0 = fmaf(dsl0 * sl.z, digits(c[0], c[1]), fmaf(-mml0, sl.x + sl.y, r0));
+        r1 = fmaf(dsl1 * sl.z, digits(c[2], c[3]), fmaf(-mml1, sl.x + sl.y, r1));
+        r0 = fmaf(dsh0 * sh.z, digits(e[0], e[1]), fmaf(-mmh0, sh.x + sh.y, r0));
+        r1 = fmaf(dsh1 * sh.z, digits(e[2], e[3]), fmaf(-mmh1, sh.x + sh.y, r1));
         acc[nt][0] = r0;
         acc[nt][1] = r1;
       }
     }
   }
+}
+
+// q6 bytes (0..63) of four elements: low nibble from word l (>> 4 for i >= 2),
+// high 2 bits from qh word h (bits 2i, 2i+1) (gguf.py:476-494)
+__device__ __forceinline__ uint32_t q6_bytes(uint32_t l, uint32_t h, int i) {
+  const uint32_t nib = (i < 2 ? l : (l >> 4)) & kNib;
+  const uint32_t hb = (i < 2 ? (h << (4 - 2 * i)) : (h >> (2 * i - 4))) & 0x30303030u;
+  return nib | hb;
 }
 
 template <int G, int NT>
@@ -340,28 +382,24 @@ __device__ __forceinline__ void chunk_q6k(const uint8_t* ch, const uint8_t* xs, 
     const uint4 v = lds128(ch + 512 * i + 16 * lane);
     W[4 * i] = v.x; W[4 * i + 1] = v.y; W[4 * i + 2] = v.z; W[4 * i + 3] = v.w;
   }
-  const int pair_stride = (G > 1 ? 8 : 8 * NT) * 64;
+  constexpr int kColBytes = 8 * NT * 32;
   if constexpr (G > 1) {
     constexpr int Bp = 4 / G, NF = 16 / G;
-    float fr[NF][4];
+    int fr[NF][4];
 #pragma unroll
-    for (int f = 0; f < NF; ++f) fr[f][0] = fr[f][1] = fr[f][2] = fr[f][3] = 0.f;
+    for (int f = 0; f < NF; ++f) zero4(fr[f]);
 #pragma unroll
     for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const uint4 bx = lds128(xs + (4 * n + i) * pair_stride + lane * 16);
-#pragma unroll
-        for (int is = 0; is < 2; ++is) {
-          const int nu = 2 * n + is, s = 8 * n + 2 * i + is;
-          const uint32_t l0 = W[6 * nu + (i & 1)], h0 = W[6 * nu + 2];
-          const uint32_t l1 = W[6 * nu + 3 + (i & 1)], h1 = W[6 * nu + 5];
-          const uint32_t n0 = (i < 2 ? l0 : (l0 >> 4)) & 0x0F0F0F0Fu;
-          const uint32_t n1 = (i < 2 ? l1 : (l1 >> 4)) & 0x0F0F0F0Fu;
-          const uint32_t qg = n0 | (((h0 >> (2 * i)) << 4) & 0x30303030u);
-          const uint32_t qg8 = n1 | (((h1 >> (2 * i)) << 4) & 0x30303030u);
-          mma_acc(fr[s / G], byte02(qg), byte02(qg8), byte13(qg), byte13(qg8), is ? bx.z : bx.x, is ? bx.w : bx.y);
-        }
+        const int m = 4 * n + i;  // 32-element group: sub-blocks 2m (elements 0-15) and 2m+1
+        const uint2 bx = lds64(xs + m * kColBytes + lane * 8);
+        const int w0 = 6 * (2 * n), w1 = 6 * (2 * n + 1);  // words of the two 16-element halves
+        const uint32_t a0 = q6_bytes(W[w0 + (i & 1)], W[w0 + 2], i);
+        const uint32_t a1 = q6_bytes(W[w0 + 3 + (i & 1)], W[w0 + 5], i);
+        const uint32_t a2 = q6_bytes(W[w1 + (i & 1)], W[w1 + 2], i);
+        const uint32_t a3 = q6_bytes(W[w1 + 3 + (i & 1)], W[w1 + 5], i);
+        imma_u8_k32(fr[(2 * m) / G], a0, a1, a2, a3, bx.x, bx.y);
       }
     const int b = t % Bp;
 #pragma unroll
@@ -371,38 +409,35 @@ __device__ __forceinline__ void chunk_q6k(const uint8_t* ch, const uint8_t* xs, 
       const float a1 = d1 * (float)(int8_t)scp[16 + s];
       const float4 sv = lds128f(su + ((s >> 1) * 4 + b) * 16);
       const float S = (s & 1) ? sv.y : sv.x;
-      acc[0][0] = fmaf(a0, fmaf(-1056.f, S, (fr[f][0] + fr[f][1]) * sv.z), acc[0][0]);
-      acc[0][1] = fmaf(a1, fmaf(-1056.f, S, (fr[f][2] + fr[f][3]) * sv.z), acc[0][1]);
+      acc[0][0] = fmaf(a0, fmaf(-32.f, S, sv.z * digits(fr[f][0], fr[f][1])), acc[0][0]);
+      acc[0][1] = fmaf(a1, fmaf(-32.f, S, sv.z * digits(fr[f][2], fr[f][3])), acc[0][1]);
     }
   } else {
-    const uint4 s0a = lds128(scp), s0b = lds128(scp + 16);  // row g: sc[0..15]
+    const uint4 s0a = lds128(scp), s0b = lds128(scp + 16);  // rows g, g+8: sc[0..15]
     const uint32_t sw0[4] = {s0a.x, s0a.y, s0a.z, s0a.w};
     const uint32_t sw1[4] = {s0b.x, s0b.y, s0b.z, s0b.w};
 #pragma unroll
     for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int pm = 4 * n + i;
+        const int m = 4 * n + i;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const uint4 bx = lds128(xs + pm * pair_stride + nt * 512 + lane * 16);
-          const float4 sv = lds128f(su + (pm * 4 * NT + 4 * nt + t) * 16);
+        for (int is = 0; is < 2; ++is) {
+          const int w = 6 * (2 * n + is), s = 2 * m + is;
+          const uint32_t a0 = q6_bytes(W[w + (i & 1)], W[w + 2], i);
+          const uint32_t a1 = q6_bytes(W[w + 3 + (i & 1)], W[w + 5], i);
+          const float al0 = d0 * sbyte_f(sw0[s >> 2], s & 3);
+          const float al1 = d1 * sbyte_f(sw1[s >> 2], s & 3);
 #pragma unroll
-          for (int is = 0; is < 2; ++is) {
-            const int nu = 2 * n + is, s = 8 * n + 2 * i + is;
-            const uint32_t l0 = W[6 * nu + (i & 1)], h0 = W[6 * nu + 2];
-            const uint32_t l1 = W[6 * nu + 3 + (i & 1)], h1 = W[6 * nu + 5];
-            const uint32_t n0 = (i < 2 ? l0 : (l0 >> 4)) & 0x0F0F0F0Fu;
-            const uint32_t n1 = (i < 2 ? l1 : (l1 >> 4)) & 0x0F0F0F0Fu;
-            const uint32_t qg = n0 | (((h0 >> (2 * i)) << 4) & 0x30303030u);
-            const uint32_t qg8 = n1 | (((h1 >> (2 * i)) << 4) & 0x30303030u);
-            float c[4];
-            mma_f16_16816(c, byte02(qg), byte02(qg8), byte13(qg), byte13(qg8), is ? bx.z : bx.x, is ? bx.w : bx.y);
+          for (int nt = 0; nt < NT; ++nt) {
+            const uint2 bx = lds64(xs + m * kColBytes + nt * 256 + lane * 8);
+            const float4 sv = lds128f(su + (m * 4 * NT + 4 * nt + t) * 16);
+            int c[4];
+            zero4(c);
+            imma_u8_k16(c, a0, a1, is ? bx.y : bx.x);
             const float S = is ? sv.y : sv.x;
-            const float a0 = d0 * sbyte_f(sw0[s >> 2], s & 3);
-            const float a1 = d1 * sbyte_f(sw1[s >> 2], s & 3);
-            acc[nt][0] = fmaf(a0, fmaf(-1056.f, S, (c[0] + c[1]) * sv.z), acc[nt][0]);
-            acc[nt][1] = fmaf(a1, fmaf(-1056.f, S, (c[2] + c[3]) * sv.z), acc[nt][1]);
+            acc[nt][0] = fmaf(al0, fmaf(-32.f, S, sv.z * digits(c[0], c[1])), acc[nt][0]);
+            acc[nt][1] = fmaf(al1, fmaf(-32.f, S, sv.z * digits(c[2], c[3])), acc[nt][1]);
           }
         }
       }
@@ -414,49 +449,41 @@ __device__ __forceinline__ void chunk_q80(const uint8_t* ch, const uint8_t* xs, 
                                           float (&acc)[NT][2]) {
   const int g = lane >> 2, t = lane & 3;
   const uint8_t* dp = ch + 4096 + 32 * g;  // row g: 8 fp16 d, row g+8: next 8
-  const int pair_stride = (G > 1 ? 8 : 8 * NT) * 64;
+  constexpr int kColBytes = 8 * NT * 32;
   if constexpr (G > 1) {
     constexpr int Bp = 4 / G, NF = 8 / G;
-    float fr[NF][4];
+    int fr[NF][4];
 #pragma unroll
-    for (int f = 0; f < NF; ++f) fr[f][0] = fr[f][1] = fr[f][2] = fr[f][3] = 0.f;
+    for (int f = 0; f < NF; ++f) zero4(fr[f]);
 #pragma unroll
     for (int bk = 0; bk < 8; ++bk) {
       const uint4 v = lds128(ch + 512 * bk + 16 * lane);
-      const uint32_t ux = v.x ^ 0x80808080u, uy = v.y ^ 0x80808080u;
-      const uint32_t uz = v.z ^ 0x80808080u, uw = v.w ^ 0x80808080u;
-      const uint4 bx = lds128(xs + bk * pair_stride + lane * 16);
-      float(&f4)[4] = fr[bk / G];
-      mma_acc(f4, byte02(ux), byte02(uz), byte13(ux), byte13(uz), bx.x, bx.y);
-      mma_acc(f4, byte02(uy), byte02(uw), byte13(uy), byte13(uw), bx.z, bx.w);
+      const uint2 bx = lds64(xs + bk * kColBytes + lane * 8);
+      imma_s8_k32(fr[bk / G], v.x, v.z, v.y, v.w, bx.x, bx.y);
     }
     const int b = t % Bp;
 #pragma unroll
     for (int f = 0; f < NF; ++f) {
       const int bk = f * G + t / Bp;
       const float dg = ld_f16(dp + 2 * bk), dg8 = ld_f16(dp + 16 + 2 * bk);
-      const float4 sv = lds128f(su + (bk * 4 + b) * 16);
-      const float S = sv.x + sv.y;
-      acc[0][0] = fmaf(dg, fmaf(-1152.f, S, (fr[f][0] + fr[f][1]) * sv.z), acc[0][0]);
-      acc[0][1] = fmaf(dg8, fmaf(-1152.f, S, (fr[f][2] + fr[f][3]) * sv.z), acc[0][1]);
+      const float u = lds128f(su + (bk * 4 + b) * 16).z;
+      acc[0][0] = fmaf(dg * u, digits(fr[f][0], fr[f][1]), acc[0][0]);
+      acc[0][1] = fmaf(dg8 * u, digits(fr[f][2], fr[f][3]), acc[0][1]);
     }
   } else {
 #pragma unroll
     for (int bk = 0; bk < 8; ++bk) {
       const uint4 v = lds128(ch + 512 * bk + 16 * lane);
-      const uint32_t ux = v.x ^ 0x80808080u, uy = v.y ^ 0x80808080u;
-      const uint32_t uz = v.z ^ 0x80808080u, uw = v.w ^ 0x80808080u;
       const float dg = ld_f16(dp + 2 * bk), dg8 = ld_f16(dp + 16 + 2 * bk);
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const uint4 bx = lds128(xs + bk * pair_stride + nt * 512 + lane * 16);
-        const float4 sv = lds128f(su + (bk * 4 * NT + 4 * nt + t) * 16);
-        float c[4];
-        mma_f16_16816(c, byte02(ux), byte02(uz), byte13(ux), byte13(uz), bx.x, bx.y);
-        mma_acc(c, byte02(uy), byte02(uw), byte13(uy), byte13(uw), bx.z, bx.w);
-        const float S = sv.x + sv.y;
-        acc[nt][0] = fmaf(dg, fmaf(-1152.f, S, (c[0] + c[1]) * sv.z), acc[nt][0]);
-        acc[nt][1] = fmaf(dg8, fmaf(-1152.f, S, (c[2] + c[3]) * sv.z), acc[nt][1]);
+        const uint2 bx = lds64(xs + bk * kColBytes + nt * 256 + lane * 8);
+        const float u = lds128f(su + (bk * 4 * NT + 4 * nt + t) * 16).z;
+        int c[4];
+        zero4(c);
+        imma_s8_k32(c, v.x, v.z, v.y, v.w, bx.x, bx.y);
+        acc[nt][0] = fmaf(dg * u, digits(c[0], c[1]), acc[nt][0]);
+        acc[nt][1] = fmaf(dg8 * u, digits(c[2], c[3]), acc[nt][1]);
       }
     }
   }
@@ -771,8 +798,8 @@ static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_
   P.batch = batch;
   P.nt = batch <= 2 ? 1 : nt_of_batch(batch);
   const int NT = P.nt;
-  P.xs_bytes = 8 * (8 * NT) * 64;  // 8 pairs x 8*NT columns x 4 t x 16 B
-  P.su_bytes = 8 * (4 * NT) * 16;  // 8 pairs x 4*NT slots x float4
+  P.xs_bytes = 8 * (8 * NT) * 32;  // 8 groups x 8*NT columns x 4 t x 8 B
+  P.su_bytes = 8 * (4 * NT) * 16;  // 8 groups x 4*NT slots x float4
   int64_t slab0 = 0;
   int w_stage = 0;
   for (int p = 0; p < n; ++p) {

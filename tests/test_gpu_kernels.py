@@ -99,7 +99,7 @@ def _gemv_case(qtype, n, k, batch, seed, bias=False, xscale=1.0):
 def test_gemv_small_batches(qtype, batch):
     y, ref, ref64 = _gemv_case(qtype, 272, 1024, batch, seed=batch * 31 + qtype)
     assert O.rel_l2(y, ref) < GEMV_TOL
-    assert O.rel_l2(y, ref64) < 1e-4  # hi/lo activations: ~1e-5 (the 1024 offset of the fp16 conversion costs a few bits)
+    assert O.rel_l2(y, ref64) < 3e-4  # int8-digit activations: ~6.5e-5 expected for Gaussian x
 
 
 @pytest.mark.parametrize("qtype", [8, 12, 14])
