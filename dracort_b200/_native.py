@@ -48,6 +48,7 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv_workspace_bytes",
     "draco_gguf_gemv_grouped",
     "draco_gguf_gemv",
+    "draco_gguf_gemv_grouped_noalloc",
 )
 
 
@@ -114,6 +115,8 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_gemv_workspace_bytes.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int]
         lib.draco_gguf_gemv_grouped.restype = c_int
         lib.draco_gguf_gemv_grouped.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp, ctypes.c_size_t, vp]
+        lib.draco_gguf_gemv_grouped_noalloc.restype = c_int
+        lib.draco_gguf_gemv_grouped_noalloc.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp]
         lib.draco_gguf_gemv.restype = c_int
         lib.draco_gguf_gemv.argtypes = [c_int, vp, vp, vp, vp, c_int, i64, i64, vp, ctypes.c_size_t, vp]
         _lib = lib

@@ -155,6 +155,15 @@ int draco_gguf_gemv_grouped(const draco_gemv_problem* probs, int n_problems, int
   return ok();
 }
 
+int draco_gguf_gemv_grouped_noalloc(const draco_gemv_problem* probs, int n_problems, int batch, void* stream) {
+  int rc = check_gemv_problems(probs, n_problems, batch);
+  if (rc) return rc;
+  char msg[256] = {0};
+  rc = gemv_launch_noalloc(probs, n_problems, batch, (cudaStream_t)stream, msg, sizeof(msg));
+  if (rc) return fail(rc, "%s", msg);
+  return ok();
+}
+
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias, int batch,
                     int64_t n_rows, int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
   draco_gemv_problem p;

@@ -950,4 +950,76 @@ int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, siz
   return DRACO_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free entry: the scratch (status word, arrival counters, partial
+// sums) lives in a fixed file-scope device array instead of a caller-supplied
+// workspace.  Every GPU that loads the library holds this array until the
+// process exits.  All calls share it, so calls that overlap on the GPU race.
+// ---------------------------------------------------------------------------
+constexpr size_t kStaticScratchBytes = (size_t)1 << 20;  // 1 MiB: enough for batch <= 4
+static __device__ __align__(256) uint8_t g_gemv_static_scratch[kStaticScratchBytes];
+
+size_t gemv_static_scratch_bytes() { return kStaticScratchBytes; }
+
+// Device address of the array on the current device, looked up once per
+// device (host code may not use the symbol itself as a pointer).
+static int static_scratch_address(uint8_t** out, char* msg, size_t ml) {
+  static uint8_t* cache[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    snprintf(msg, ml, "gemv_noalloc: cudaGetDevice failed: %s", cudaGetErrorString(e));
+    return DRACO_ERR_CUDA;
+  }
+  if (dev < 0 || dev >= 64) {
+    snprintf(msg, ml, "gemv_noalloc: device index %d out of range", dev);
+    return DRACO_ERR_ARG;
+  }
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_gemv_static_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      snprintf(msg, ml, "gemv_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+      return DRACO_ERR_CUDA;
+    }
+    cache[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = cache[dev];
+  return DRACO_OK;
+}
+
+int gemv_launch_noalloc(const draco_gemv_problem* probs, int n, int batch, cudaStream_t st, char* msg,
+                        size_t ml) {
+  HostPlan hp;
+  const int n_sm = device_sm_count();
+  if (!build_plan(probs, n, batch, n_sm, hp, msg, ml)) return DRACO_ERR_ARG;
+  if (hp.P.total_slabs == 0) return DRACO_OK;
+  if (hp.ws_needed > kStaticScratchBytes) {
+    snprintf(msg, ml,
+             "gemv_noalloc: this call needs %zu bytes of scratch but the fixed array holds %zu "
+             "(batch <= 4 fits); use draco_gguf_gemv_grouped with a workspace",
+             hp.ws_needed, kStaticScratchBytes);
+    return DRACO_ERR_WORKSPACE;
+  }
+  uint8_t* scratch = nullptr;
+  int rc = static_scratch_address(&scratch, msg, ml);
+  if (rc != DRACO_OK) return rc;
+  // the status word and arrival counters must start at zero; a call that
+  // failed on the device may have left them set
+  cudaError_t e = cudaMemsetAsync(scratch, 0, (size_t)(kWsCounters + kWsCountersBytes), st);
+  if (e != cudaSuccess) {
+    snprintf(msg, ml, "gemv_noalloc: clearing the scratch counters failed: %s", cudaGetErrorString(e));
+    return DRACO_ERR_CUDA;
+  }
+  hp.P.ws = scratch;
+  if (batch == 1) e = launch_gemv<4, 1>(hp, st);
+  else if (batch == 2) e = launch_gemv<2, 1>(hp, st);
+  else e = launch_gemv<1, 1>(hp, st);  // 3 <= batch <= 4 (larger batches exceed the array)
+  if (e != cudaSuccess) {
+    snprintf(msg, ml, "gemv_noalloc: launch failed: %s", cudaGetErrorString(e));
+    return DRACO_ERR_CUDA;
+  }
+  return DRACO_OK;
+}
+
 }  // namespace draco

@@ -20,6 +20,11 @@ size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch);
 int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
                 char* msg, size_t msg_len);
 
+// Allocation-free grouped GEMV (scratch in a fixed device array).
+int gemv_launch_noalloc(const draco_gemv_problem* probs, int n, int batch, cudaStream_t st, char* msg,
+                        size_t msg_len);
+size_t gemv_static_scratch_bytes();
+
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 

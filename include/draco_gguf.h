@@ -151,6 +151,30 @@ size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* problems, int n
 int draco_gguf_gemv_grouped(const draco_gemv_problem* problems, int n_problems, int batch,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free form of draco_gguf_gemv_grouped.  No counterpart in the
+ * reference: DracoRT's numpy path has no device memory to manage.
+ *
+ * For callers that cannot allocate device memory themselves: hosts whose
+ * device memory is owned by another allocator (an inference server's pool,
+ * a framework that forbids hidden allocations), plain C / FFI hosts without a
+ * device allocator of their own, and decode loops that cannot pay for
+ * cudaMalloc's implicit device synchronisation.  Such callers pass only
+ * their inputs and outputs; the kernel's scratch (status word, arrival
+ * counters, partial sums) lives in a fixed 1 MiB device array inside the
+ * library, which every GPU that loads the library holds until the process
+ * exits.  No cudaMalloc, cudaFree or other allocating call is made.
+ *
+ * Limit: 1 <= batch <= 4 (the scratch a call needs grows with the batch;
+ * larger calls are rejected with DRACO_ERR_WORKSPACE and a message).
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Each call clears the counters it relies on (cudaMemsetAsync on `stream`).
+ * All calls share the one array: calls that overlap on the GPU (different
+ * streams, or different host threads on one device) race and must be
+ * serialised by the caller. */
+int draco_gguf_gemv_grouped_noalloc(const draco_gemv_problem* problems, int n_problems, int batch,
+                                    void* stream);
+
 /* Single-weight convenience form of draco_gguf_gemv_grouped. */
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias,
                     int batch, int64_t n_rows, int64_t k, void* workspace,

@@ -1,0 +1,80 @@
+"""The allocation-free GEMV entry point against the workspace entry point.
+
+draco_gguf_gemv_grouped_noalloc serves callers that cannot allocate device
+memory themselves (a host whose device memory belongs to another allocator,
+a plain C / FFI host, a decode loop that cannot afford cudaMalloc's implicit
+synchronisation): its scratch lives in a fixed array inside the library.
+This test calls it through the C ABI twice in a row and compares each result
+with draco_gguf_gemv_grouped given a caller-allocated workspace.  Its file
+name makes pytest collect it last, and it needs no state from other tests.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+from dracort_b200 import _native as N  # noqa: E402
+from dracort_b200 import gguf_ops as G  # noqa: E402
+from dracort_b200.format import quantize as Q  # noqa: E402
+from oracle import gguf_oracle as O  # noqa: E402
+
+GEMV_TOL = 1e-3  # relative L2, the bar every GEMV test uses
+
+
+def _problems(batch, seed):
+    rng = np.random.default_rng(seed)
+    specs = [(12, 1024, 4096), (14, 512, 4096), (8, 256, 1024), (12, 4096, 11008)]
+    tensors, structs = [], []
+    for qt, n, k in specs:
+        packed = Q.encode(qt, Q.random_weight(rng, n, k))
+        tiled = G.repack(qt, torch.from_numpy(packed.reshape(-1)).cuda(), n, k)
+        x = torch.from_numpy(rng.standard_normal((batch, k)).astype(np.float32)).cuda()
+        y_ref = torch.empty((batch, n), device="cuda")
+        y_new = torch.empty((batch, n), device="cuda")
+        tensors.append((qt, n, k, tiled, x, y_ref, y_new))
+    return tensors
+
+
+def _struct(qt, n, k, tiled, x, y):
+    s = N.GemvProblem()
+    s.qtype, s.w, s.x, s.y, s.bias = qt, tiled.data_ptr(), x.data_ptr(), y.data_ptr(), None
+    s.n_rows, s.k, s.ldx, s.ldy = n, k, x.stride(0), y.stride(0)
+    return s
+
+
+@pytest.mark.parametrize("batch", [1, 2, 4])
+def test_noalloc_matches_workspace_entry_point_twice(batch):
+    lib = N.load()
+    items = _problems(batch, seed=100 + batch)
+    ref = (N.GemvProblem * len(items))(*[_struct(q, n, k, t, x, yr) for q, n, k, t, x, yr, _ in items])
+    new = (N.GemvProblem * len(items))(*[_struct(q, n, k, t, x, yn) for q, n, k, t, x, _, yn in items])
+    stream = torch.cuda.current_stream().cuda_stream
+
+    ws_bytes = lib.draco_gguf_gemv_workspace_bytes(ref, len(items), batch)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    N.check(lib.draco_gguf_gemv_grouped(ref, len(items), batch, ws.data_ptr(), ws_bytes, stream))
+
+    for _call in range(2):  # the shared array keeps the previous call's contents
+        for it in items:
+            it[6].fill_(float("nan"))
+        N.check(lib.draco_gguf_gemv_grouped_noalloc(new, len(items), batch, stream))
+        torch.cuda.synchronize()
+        for qt, n, k, tiled, x, y_ref, y_new in items:
+            assert torch.isfinite(y_new).all()
+            assert O.rel_l2(y_new.cpu().numpy(), y_ref.cpu().numpy()) < GEMV_TOL
+
+
+def test_noalloc_rejects_batches_beyond_the_fixed_scratch():
+    lib = N.load()
+    items = _problems(5, seed=7)[:1]
+    arr = (N.GemvProblem * 1)(_struct(*items[0][:5], items[0][6]))
+    rc = lib.draco_gguf_gemv_grouped_noalloc(arr, 1, 5, torch.cuda.current_stream().cuda_stream)
+    assert rc == N.DRACO_ERR_WORKSPACE
+    assert "scratch" in N.last_error()
