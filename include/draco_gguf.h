@@ -144,10 +144,12 @@ size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* problems, int n
 
 /* Decode GEMV over 1..DRACO_GEMV_MAX_PROBLEMS weights in one persistent
  * launch (the 7 projections of a decoder layer fit in one call).
- * 1 <= batch <= DRACO_GEMV_MAX_BATCH.  fp32 in, fp32 out, fp32 accumulate;
- * activations enter the tensor cores as an exact-to-2^-22 fp16 hi/lo pair
- * after a per-row power-of-two rescale, so results track the fp32 oracle to
- * ~1e-6 relative L2.  `problems` is a host array. */
+ * 1 <= batch <= DRACO_GEMV_MAX_BATCH.  fp32 in, fp32 out.  The quants and the
+ * activations meet in int8 tensor-core MMAs with exact integer accumulation;
+ * each 32-element group of activations is represented to one step of a
+ * power-of-two scale u (max|x| / u in [2^13, 2^14)), which keeps results
+ * within ~1e-4 relative L2 of the fp32 oracle (~6.5e-5 for Gaussian inputs).
+ * `problems` is a host array. */
 int draco_gguf_gemv_grouped(const draco_gemv_problem* problems, int n_problems, int batch,
                             void* workspace, size_t workspace_bytes, void* stream);
 
