@@ -49,7 +49,12 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv_grouped",
     "draco_gguf_gemv",
     "draco_gguf_gemv_grouped_noalloc",
+    "draco_gguf_gemm",
 )
+
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+GEMM_MAX_PROBLEMS = 4
 
 
 class GemvProblem(ctypes.Structure):
@@ -62,6 +67,23 @@ class GemvProblem(ctypes.Structure):
         ("x", ctypes.c_void_p),
         ("y", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
+        ("n_rows", ctypes.c_int64),
+        ("k", ctypes.c_int64),
+        ("ldx", ctypes.c_int64),
+        ("ldy", ctypes.c_int64),
+    ]
+
+
+class GemmProblem(ctypes.Structure):
+    """Mirror of ``draco_gemm_problem``."""
+
+    _fields_ = [
+        ("qtype", ctypes.c_int),
+        ("ydtype", ctypes.c_int),
+        ("w", ctypes.c_void_p),
+        ("x", ctypes.c_void_p),
+        ("y", ctypes.c_void_p),
+        ("m", ctypes.c_int64),
         ("n_rows", ctypes.c_int64),
         ("k", ctypes.c_int64),
         ("ldx", ctypes.c_int64),
@@ -117,6 +139,8 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_gemv_grouped.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp, ctypes.c_size_t, vp]
         lib.draco_gguf_gemv_grouped_noalloc.restype = c_int
         lib.draco_gguf_gemv_grouped_noalloc.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp]
+        lib.draco_gguf_gemm.restype = c_int
+        lib.draco_gguf_gemm.argtypes = [ctypes.POINTER(GemmProblem), c_int, vp, vp]
         lib.draco_gguf_gemv.restype = c_int
         lib.draco_gguf_gemv.argtypes = [c_int, vp, vp, vp, vp, c_int, i64, i64, vp, ctypes.c_size_t, vp]
         _lib = lib

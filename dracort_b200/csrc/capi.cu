@@ -164,6 +164,29 @@ int draco_gguf_gemv_grouped_noalloc(const draco_gemv_problem* probs, int n_probl
   return ok();
 }
 
+int draco_gguf_gemm(const draco_gemm_problem* probs, int n_problems, int* status, void* stream) {
+  if (!probs || n_problems < 1 || n_problems > DRACO_GEMM_MAX_PROBLEMS)
+    return fail(DRACO_ERR_ARG, "gemm: need 1..%d problems, got %d", DRACO_GEMM_MAX_PROBLEMS, n_problems);
+  for (int i = 0; i < n_problems; ++i) {
+    const draco_gemm_problem& q = probs[i];
+    int rc = check_weight(q.qtype, DRACO_LAYOUT_TILED, q.w, q.n_rows, q.k, "gemm");
+    if (rc) return rc;
+    if (q.m < 0) return fail(DRACO_ERR_SHAPE, "gemm: problem %d has negative m", i);
+    if (q.m * q.n_rows * q.k == 0) continue;
+    if (!q.x || !q.y) return fail(DRACO_ERR_ARG, "gemm: problem %d has a null x or y", i);
+    if (q.ydtype != DRACO_DTYPE_BF16 && q.ydtype != DRACO_DTYPE_F32)
+      return fail(DRACO_ERR_TYPE, "gemm: problem %d output dtype %d unsupported", i, q.ydtype);
+    if (q.ldx < q.k || q.ldy < q.n_rows) return fail(DRACO_ERR_SHAPE, "gemm: problem %d leading dimensions too small", i);
+    if ((reinterpret_cast<uintptr_t>(q.x) & 15) || (q.ldx % 8))
+      return fail(DRACO_ERR_ALIGN, "gemm: problem %d: x must be 16-byte aligned with ldx a multiple of 8", i);
+    if (q.m > (int64_t)1 << 30) return fail(DRACO_ERR_SHAPE, "gemm: problem %d m too large", i);
+  }
+  char msg[256] = {0};
+  int rc = gemm_launch(probs, n_problems, status, (cudaStream_t)stream, msg, sizeof(msg));
+  if (rc) return fail(rc, "%s", msg);
+  return ok();
+}
+
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias, int batch,
                     int64_t n_rows, int64_t k, void* workspace, size_t workspace_bytes, void* stream) {
   draco_gemv_problem p;

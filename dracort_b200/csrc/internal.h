@@ -25,6 +25,10 @@ int gemv_launch_noalloc(const draco_gemv_problem* probs, int n, int batch, cudaS
                         size_t msg_len);
 size_t gemv_static_scratch_bytes();
 
+// Prefill dequant-GEMM (tcgen05).  `status` is an optional device int the
+// kernel sets to a DRACO_* code on a device-side failure.
+int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_t st, char* msg, size_t msg_len);
+
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 

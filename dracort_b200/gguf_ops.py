@@ -251,3 +251,67 @@ def gemv(qtype: int, w_tiled: torch.Tensor, x: torch.Tensor, n_rows: int, k: int
     y = out if out is not None else torch.empty((x2.shape[0], n_rows), dtype=torch.float32, device=x2.device)
     gemv_grouped([GemvProblem(qtype, w_tiled, x2, y, n_rows, k, bias)])
     return y.reshape(-1) if squeeze else y
+
+
+# ---------------------------------------------------------------------------
+# prefill dequant-GEMM (tcgen05)
+# ---------------------------------------------------------------------------
+@dataclass
+class GemmProblem:
+    """One weight of a grouped prefill GEMM: y = x @ dequant(W)^T (x bf16 [m, k])."""
+
+    qtype: int
+    w_tiled: torch.Tensor
+    x: torch.Tensor  # [m, k] bf16 CUDA
+    y: torch.Tensor  # [m, n_rows] bf16 or fp32 CUDA
+    n_rows: int
+    k: int
+
+
+def _gemm_struct(p: GemmProblem) -> N.GemmProblem:
+    for t, nm in ((p.w_tiled, "w_tiled"), (p.x, "x"), (p.y, "y")):
+        _require_cuda(t, nm)
+    if p.x.dtype != torch.bfloat16:
+        raise ValueError("gemm: x must be bfloat16")
+    if p.y.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("gemm: y must be bfloat16 or float32")
+    if p.x.dim() != 2 or p.y.dim() != 2 or p.x.stride(1) != 1 or p.y.stride(1) != 1:
+        raise ValueError("gemm: x and y must be 2-D with unit inner stride")
+    if p.x.shape[1] != p.k or p.y.shape[1] != p.n_rows or p.x.shape[0] != p.y.shape[0]:
+        raise DracoFormatError(
+            f"gemm: x {tuple(p.x.shape)} / y {tuple(p.y.shape)} do not match weight [{p.n_rows}, {p.k}]")
+    s = N.GemmProblem()
+    s.qtype = p.qtype
+    s.ydtype = N.DTYPE_BF16 if p.y.dtype == torch.bfloat16 else N.DTYPE_F32
+    s.w, s.x, s.y = p.w_tiled.data_ptr(), p.x.data_ptr(), p.y.data_ptr()
+    s.m, s.n_rows, s.k = p.x.shape[0], p.n_rows, p.k
+    s.ldx, s.ldy = p.x.stride(0), p.y.stride(0)
+    return s
+
+
+def gemm_grouped(problems: Sequence[GemmProblem], status: Optional[torch.Tensor] = None) -> None:
+    """Y_i = X_i @ dequant(W_i)^T for up to 4 weights in one tcgen05 launch."""
+    if not problems:
+        return
+    if len(problems) > N.GEMM_MAX_PROBLEMS:
+        for i in range(0, len(problems), N.GEMM_MAX_PROBLEMS):
+            gemm_grouped(problems[i:i + N.GEMM_MAX_PROBLEMS], status)
+        return
+    lib = N.load()
+    arr = (N.GemmProblem * len(problems))(*[_gemm_struct(p) for p in problems])
+    dev = problems[0].x.device
+    st = status.data_ptr() if status is not None else None
+    N.check(lib.draco_gguf_gemm(arr, len(problems), st, _stream_ptr(dev)), "gemm")
+
+
+def gemm(qtype: int, w_tiled: torch.Tensor, x: torch.Tensor, n_rows: int, k: int,
+         out_dtype: torch.dtype = torch.bfloat16, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Y = X @ dequant(W)^T with X cast to bf16; returns [m, n_rows] of out_dtype."""
+    x2 = x.reshape(-1, k)
+    if x2.dtype != torch.bfloat16:
+        x2 = x2.to(torch.bfloat16)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    y = out if out is not None else torch.empty((x2.shape[0], n_rows), dtype=out_dtype, device=x2.device)
+    gemm_grouped([GemmProblem(qtype, w_tiled, x2, y, n_rows, k)])
+    return y

@@ -177,6 +177,36 @@ int draco_gguf_gemv_grouped(const draco_gemv_problem* problems, int n_problems, 
 int draco_gguf_gemv_grouped_noalloc(const draco_gemv_problem* problems, int n_problems, int batch,
                                     void* stream);
 
+/* One weight of a prefill GEMM launch: Y = X @ dequant(W)^T.
+ *   w      : TILED weight [n_rows, k] of type qtype (16-byte aligned)
+ *   x      : bf16 [m, k] row-major, row stride ldx elements (16-byte aligned,
+ *            ldx a multiple of 8)
+ *   y      : [m, n_rows] of ydtype (DRACO_DTYPE_BF16 or DRACO_DTYPE_F32), row
+ *            stride ldy elements
+ * Replaces executor._linear (executor.py:47-79) at prompt length, whose
+ * matmul is GenericGemmKernel.matmul_f32 (generic.py:32-33). */
+typedef struct draco_gemm_problem {
+  int qtype;
+  int ydtype;
+  const void* w;
+  const void* x;
+  void* y;
+  int64_t m;
+  int64_t n_rows;
+  int64_t k;
+  int64_t ldx;
+  int64_t ldy;
+} draco_gemm_problem;
+
+#define DRACO_GEMM_MAX_PROBLEMS 4
+
+/* Prefill dequant-GEMM over 1..DRACO_GEMM_MAX_PROBLEMS weights in one
+ * persistent launch: tcgen05 tensor-core MMAs (bf16 x bf16, fp32 accumulate
+ * in tensor memory) fed by weights dequantized to bf16 in shared memory.
+ * `status` is NULL or a device int that the kernel sets to a DRACO_* code if
+ * a device-side wait runs out (it never traps).  `problems` is a host array. */
+int draco_gguf_gemm(const draco_gemm_problem* problems, int n_problems, int* status, void* stream);
+
 /* Single-weight convenience form of draco_gguf_gemv_grouped. */
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias,
                     int batch, int64_t n_rows, int64_t k, void* workspace,
