@@ -7,25 +7,33 @@
 // (draco/runtime/cpu/kernels/generic.py:32-33) on gguf._dequantize's fp32
 // cache (draco/format/gguf.py:272-497), at M = prompt length.
 //
-// Design (B200, tensor-bound), persistent, one CTA (16 warps) per SM:
-//  * tile = 128 weight rows (one TILED row group) x 512 tokens; the K loop
-//    runs in 64-element blocks (one 128-byte swizzle atom of bf16).
-//  * warp 0 (one lane): TMA loads of the X tiles (cp.async.bulk.tensor.2d,
-//    128-byte swizzle, 256 tokens x 64 k per box) and 1-D bulk copies of the
-//    packed weight slabs (128 rows x 256 k, contiguous in the TILED layout).
-//  * warps 8-15 (dequant): expand each 64-k block of the packed slab into a
-//    bf16 A tile (128 x 64, K-major, 128-byte swizzle) in shared memory; each
-//    value is the fp32 dequantized weight (same operations as gguf._dequantize)
-//    rounded to bf16.  fence.proxy.async makes the stores visible to the
-//    tensor cores.
-//  * warp 1: allocates 512 TMEM columns; one lane issues
-//    tcgen05.mma.cta_group::1.kind::f16 (M128 N256 K16, bf16 x bf16 -> fp32)
-//    into two 256-column accumulators (tokens 0-255 and 256-511 of the tile)
-//    and signals stage reuse with tcgen05.commit.
-//  * warps 4-7 (epilogue): tcgen05.ld the accumulators (warp w reads TMEM lanes
-//    32(w%4)..+31 = weight rows), convert and store Y[token][row].
+// Design (B200, tensor-bound): persistent clusters of two CTAs (one SM pair),
+// one CTA per SM, 16 warps each.  The pair runs tcgen05.mma.cta_group::2
+// (M256 N256 K16, bf16 x bf16 -> fp32): the 256 tokens of the M dimension are
+// split 128 per CTA (A = X, loaded by TMA), the 256 weight rows of the N
+// dimension 128 per CTA (B = dequantized W, one TILED row group per CTA), so
+// every SM feeds the tensor core 8 KB of shared memory per MMA instead of the
+// 12 KB a single-SM M128 N256 MMA needs.
+//  * pair tile = 256 weight rows x 512 tokens: two 256-column fp32
+//    accumulators per CTA (its 128 tokens of each 256-token half x all 256
+//    rows) fill the 512 TMEM columns; the K loop runs in 64-element blocks
+//    (one 128-byte swizzle atom of bf16).
+//  * warp 0 (one lane, both CTAs): TMA loads of this CTA's X boxes (64 k x 128
+//    tokens, 128-byte swizzle, completion counted on the leader CTA's barrier)
+//    and 1-D bulk copies of this CTA's packed weight slab (128 rows x 256 k,
+//    contiguous in the TILED layout).
+//  * warps 8-15 (dequant, both CTAs): expand each 64-k block of the slab into
+//    a bf16 B tile (128 rows x 64 k, K-major, 128-byte swizzle); each value is
+//    the fp32 dequantized weight (same operations as gguf._dequantize) rounded
+//    to bf16.  fence.proxy.async, then an arrive on the leader's barrier.
+//  * warp 1: allocates the 512 TMEM columns (cta_group::2, both CTAs); in the
+//    leader CTA one lane issues the MMAs and tcgen05.commit with a cluster
+//    multicast so both CTAs see stage and accumulator completion.
+//  * warps 4-7 (epilogue, both CTAs): tcgen05.ld of the CTA's accumulators
+//    (warp w reads TMEM lanes 32(w%4)..+31 = tokens), each lane holding 32
+//    consecutive weight rows of one token, stored as 16-byte vectors.
 //  * every wait is bounded; on a timeout the kernel records DRACO_ERR_TIMEOUT,
-//    unwinds, and still frees its TMEM.
+//    unwinds, waits for its own MMAs, and still frees its TMEM.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -39,23 +47,26 @@
 namespace draco {
 
 constexpr int kGemmMaxProblems = 4;
-constexpr int kBM = 128;                      // weight rows per tile
-constexpr int kHalf = 256;                    // tokens per accumulator (UMMA N)
-constexpr int kNH = 2;                        // accumulators per tile
-constexpr int kBK = 64;                       // k per block
-constexpr int kXBox = kHalf * kBK * 2;        // 32 KB: one TMA box of X
-constexpr int kATile = kBM * kBK * 2;         // 16 KB: one dequantized A tile
+constexpr int kBM = 128;                          // weight rows per CTA (one TILED row group)
+constexpr int kTokCta = 128;                      // tokens per CTA per accumulator
+constexpr int kNH = 2;                            // accumulators per CTA
+constexpr int kUmmaN = 256;                       // weight rows per pair (UMMA N)
+constexpr int kUmmaM = 256;                       // tokens per pair and accumulator (UMMA M)
+constexpr int kTileTok = kNH * kUmmaM;            // 512 tokens per pair tile
+constexpr int kBK = 64;                           // k per block
+constexpr int kXBox = kTokCta * kBK * 2;          // 16 KB: one TMA box of X
+constexpr int kATile = kBM * kBK * 2;             // 16 KB: one dequantized weight tile
 constexpr int kGemmThreads = 16 * 32;
 constexpr int kDeqWarp0 = 8, kDeqWarps = 8;
-constexpr int kEpiWarp0 = 4;
-constexpr int kMaxXStages = 4, kMaxWpStages = 2, kAStages = 2;
+constexpr int kEpiWarp0 = 4, kEpiWarps = 4;
+constexpr int kMaxXStages = 10, kMaxWpStages = 2, kMaxAStages = 4;
 constexpr uint64_t kGemmWaitNs = 4000000000ull;  // 4 s
 
 struct GemmProbDev {
   const uint8_t* w;
   void* y;
   int64_t ldy;
-  int qt, ydtype, m, n, k, nb, n_rg, n_tiles, cb, tblocks, tile0, pad_;
+  int qt, ydtype, m, n, k, nb, n_rg, n_tiles, cb, tblocks, tile0, vec;
 };
 
 struct __align__(64) GemmParams {
@@ -63,7 +74,7 @@ struct __align__(64) GemmParams {
   GemmProbDev prob[kGemmMaxProblems];
   int* status;
   int n_prob, total_tiles;
-  int nx, nwp, wp_stage;
+  int nx, na, wp_stage;
   int x_off, a_off, wp_off, smem_bytes;
 };
 
@@ -74,11 +85,55 @@ __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence:
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+// ----- cluster (CTA pair) helpers
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared-memory object in CTA `rank`
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
+  return d;
+}
+// arrive on an mbarrier of another CTA of the cluster (release at cluster scope)
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait with cluster-scope acquire (for barriers that other CTAs, or
+// tensor-core work issued by the other CTA, complete)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  uint64_t t0 = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+}
+
+// TMA 2-D tile load into this CTA's shared memory; the transaction bytes are
+// counted on `bar_cluster` (a barrier of the leader CTA of the pair).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
       : "memory");
 }
 
@@ -97,16 +152,27 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
+// D[tmem] (+)= A[smem] . B[smem]^T across the CTA pair (issued by the leader)
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+// arrive (once) on the barrier at the same offset in both CTAs of the pair
+// when all previously issued MMAs of this thread have completed
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"((uint16_t)3)
+      : "memory");
+}
+// arrive on this CTA's barrier only
+__device__ __forceinline__ void umma_commit_local(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
@@ -259,58 +325,107 @@ __device__ __forceinline__ void gemm_error(const GemmParams& P, int code) {
   if (P.status) atomicCAS(P.status, 0, code);
 }
 
+// position in a ring of n stages and the parity of its current phase
+// (incremented instead of divided: the MMA issue loop must stay lean)
+struct Ring {
+  int s = 0;
+  uint32_t ph = 0;
+  __device__ __forceinline__ void next(int n) {
+    if (++s == n) {
+      s = 0;
+      ph ^= 1u;
+    }
+  }
+};
+
+// pair tile t -> (problem, row pair, 512-token block)
 struct TileCursor {
-  int p, rg, tb, nkb;
+  int p, rp, tb, nkb;
   __device__ void at(const GemmParams& P, int t) {
     p = 0;
     for (int q = 1; q < P.n_prob; ++q)
       if (t >= P.prob[q].tile0) p = q;
     const int local = t - P.prob[p].tile0;
-    rg = local / P.prob[p].tblocks;
-    tb = local - rg * P.prob[p].tblocks;
+    rp = local / P.prob[p].tblocks;
+    tb = local - rp * P.prob[p].tblocks;
     nkb = P.prob[p].nb * 4;
   }
 };
+
+__device__ __forceinline__ void store_rows(const GemmProbDev& pr, int tok, int row0, const uint32_t (&v)[32]) {
+  if (tok >= pr.m || row0 >= pr.n) return;
+  if (pr.ydtype == DRACO_DTYPE_BF16) {
+    __nv_bfloat16* y = static_cast<__nv_bfloat16*>(pr.y) + (int64_t)tok * pr.ldy + row0;
+    if (pr.vec && row0 + 32 <= pr.n) {
+      uint4* d = reinterpret_cast<uint4*>(y);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        d[i] = make_uint4(bf16x2(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
+                          bf16x2(__uint_as_float(v[8 * i + 2]), __uint_as_float(v[8 * i + 3])),
+                          bf16x2(__uint_as_float(v[8 * i + 4]), __uint_as_float(v[8 * i + 5])),
+                          bf16x2(__uint_as_float(v[8 * i + 6]), __uint_as_float(v[8 * i + 7])));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (row0 + j < pr.n) y[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
+    }
+  } else {
+    float* y = static_cast<float*>(pr.y) + (int64_t)tok * pr.ldy + row0;
+    if (pr.vec && row0 + 32 <= pr.n) {
+      uint4* d = reinterpret_cast<uint4*>(y);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) d[i] = make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (row0 + j < pr.n) y[j] = __uint_as_float(v[j]);
+    }
+  }
+}
 
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_x[kMaxXStages], empty_x[kMaxXStages];
   __shared__ __align__(8) uint64_t full_wp[kMaxWpStages], empty_wp[kMaxWpStages];
-  __shared__ __align__(8) uint64_t full_a[kAStages], empty_a[kAStages];
-  __shared__ __align__(8) uint64_t acc_full[kNH], acc_empty[kNH];
+  __shared__ __align__(8) uint64_t full_a[kMaxAStages], empty_a[kMaxAStages], deq_done[kMaxAStages];
+  __shared__ __align__(8) uint64_t acc_full[kNH], acc_empty[kNH], mma_done;
   __shared__ uint32_t s_tmem;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NX = P.nx, NWP = P.nwp;
+  const int NX = P.nx, NA = P.na;
+  const uint32_t rank = cluster_rank();        // 0 = leader (issues the MMAs)
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NX; ++i) {
-      mbar_init(&full_x[i], 1);
-      mbar_init(&empty_x[i], 1);
+      mbar_init(&full_x[i], 1);                 // leader: its producer's expect_tx; bytes from both CTAs
+      mbar_init(&empty_x[i], 1);                // MMA commit (multicast)
     }
-    for (int i = 0; i < NWP; ++i) {
+    for (int i = 0; i < kMaxWpStages; ++i) {
       mbar_init(&full_wp[i], 1);
       mbar_init(&empty_wp[i], kDeqWarps);
     }
-    for (int i = 0; i < kAStages; ++i) {
-      mbar_init(&full_a[i], kDeqWarps);
-      mbar_init(&empty_a[i], 1);
+    for (int i = 0; i < NA; ++i) {
+      mbar_init(&full_a[i], kDeqWarps + 1);     // leader: its dequant warps + the peer's relay
+      mbar_init(&empty_a[i], 1);                // MMA commit (multicast)
+      mbar_init(&deq_done[i], kDeqWarps);       // peer: its dequant warps (relayed to the leader)
     }
     for (int i = 0; i < kNH; ++i) {
-      mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_full[i], 1);               // MMA commit (multicast)
+      mbar_init(&acc_empty[i], 2 * kEpiWarps);  // leader: epilogue warps of both CTAs
     }
+    mbar_init(&mma_done, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                  "r"(512)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote arrive or TMA
   tc_fence_after();
   const uint32_t tmem = s_tmem;
   grid_dependency_wait();  // X may be written by the preceding kernel
@@ -322,164 +437,159 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      int ix = 0, iw = 0;
+      Ring rx, rw;
       bool ok = true;
-      for (int t = blockIdx.x; t < P.total_tiles && ok; t += gridDim.x) {
+      for (int t = pair; t < P.total_tiles && ok; t += npairs) {
         TileCursor c;
         c.at(P, t);
         const GemmProbDev& pr = P.prob[c.p];
         const TiledGeom geo = tiled_geom(pr.qt, pr.n, pr.k);
-        const uint32_t slab_bytes = (uint32_t)(rg_tiles(geo, c.rg) * pr.cb);
+        const int rg = 2 * c.rp + (int)rank;
+        const uint32_t slab_bytes = rg < pr.n_rg ? (uint32_t)(rg_tiles(geo, rg) * pr.cb) : 0u;
         for (int kb = 0; kb < c.nkb && ok; ++kb) {
           if ((kb & 3) == 0) {
-            const int s = iw % NWP;
-            const uint32_t ph = (uint32_t)((iw / NWP) & 1);
-            if (!mbar_wait_bounded(&empty_wp[s], ph ^ 1u, kGemmWaitNs)) {
+            if (!mbar_wait_bounded(&empty_wp[rw.s], rw.ph ^ 1u, kGemmWaitNs)) {
               gemm_error(P, DRACO_ERR_TIMEOUT);
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full_wp[s], slab_bytes);
-            bulk_g2s(wps + (size_t)s * P.wp_stage, pr.w + slab_offset(geo, c.rg, kb >> 2), slab_bytes, &full_wp[s]);
-            ++iw;
+            if (slab_bytes) {
+              mbar_arrive_expect_tx(&full_wp[rw.s], slab_bytes);
+              bulk_g2s(wps + (size_t)rw.s * P.wp_stage, pr.w + slab_offset(geo, rg, kb >> 2), slab_bytes,
+                       &full_wp[rw.s]);
+            } else {
+              mbar_arrive(&full_wp[rw.s]);  // row group past n_rows: dequant writes zeros
+            }
+            rw.next(kMaxWpStages);
           }
 #pragma unroll 1
           for (int hh = 0; hh < kNH; ++hh) {
-            const int s = ix % NX;
-            const uint32_t ph = (uint32_t)((ix / NX) & 1);
-            if (!mbar_wait_bounded(&empty_x[s], ph ^ 1u, kGemmWaitNs)) {
+            if (!mbar_wait_cluster(&empty_x[rx.s], rx.ph ^ 1u, kGemmWaitNs)) {
               gemm_error(P, DRACO_ERR_TIMEOUT);
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&full_x[s], kXBox);
-            tma_load_2d(xs + (size_t)s * kXBox, &P.tmap[c.p], kb * kBK, (c.tb * kNH + hh) * kHalf, &full_x[s]);
-            ++ix;
+            if (rank == 0) mbar_arrive_expect_tx(&full_x[rx.s], 2 * kXBox);
+            const int tok = c.tb * kTileTok + hh * kUmmaM + (int)rank * kTokCta;
+            tma_load_2d_pair(xs + (size_t)rx.s * kXBox, &P.tmap[c.p], kb * kBK, tok, map_to_rank(&full_x[rx.s], 0));
+            rx.next(NX);
           }
         }
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(kBM, kHalf);
-      int ix = 0, ia = 0, it = 0;
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = idesc_bf16(kUmmaM, kUmmaN);
+      const uint32_t x_base = smem_u32(xs), a_base = smem_u32(as);
+      Ring rx, ra;
+      uint32_t acc_ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < P.total_tiles && ok; t += gridDim.x, ++it) {
+      for (int t = pair; t < P.total_tiles && ok; t += npairs, acc_ph ^= 1u) {
         TileCursor c;
         c.at(P, t);
-        const uint32_t acc_ph = (uint32_t)(it & 1);
-        for (int hh = 0; hh < kNH && ok; ++hh)
-          if (!mbar_wait_bounded(&acc_empty[hh], acc_ph ^ 1u, kGemmWaitNs)) {
-            gemm_error(P, DRACO_ERR_TIMEOUT);
-            ok = false;
-          }
-        tc_fence_after();
         for (int kb = 0; kb < c.nkb && ok; ++kb) {
-          const int sa = ia % kAStages;
-          if (!mbar_wait_bounded(&full_a[sa], (uint32_t)((ia / kAStages) & 1), kGemmWaitNs)) {
+          if (!mbar_wait_cluster(&full_a[ra.s], ra.ph, kGemmWaitNs)) {
             gemm_error(P, DRACO_ERR_TIMEOUT);
             ok = false;
             break;
           }
-          const uint32_t a_addr = smem_u32(as + (size_t)sa * kATile);
-#pragma unroll 1
+          const uint32_t a_addr = a_base + (uint32_t)ra.s * kATile;
+#pragma unroll
           for (int hh = 0; hh < kNH; ++hh) {
-            const int sx = ix % NX;
-            if (!mbar_wait_bounded(&full_x[sx], (uint32_t)((ix / NX) & 1), kGemmWaitNs)) {
+            if (kb == 0) {
+              if (!mbar_wait_cluster(&acc_empty[hh], acc_ph ^ 1u, kGemmWaitNs)) {
+                gemm_error(P, DRACO_ERR_TIMEOUT);
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            if (!mbar_wait_cluster(&full_x[rx.s], rx.ph, kGemmWaitNs)) {
               gemm_error(P, DRACO_ERR_TIMEOUT);
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint32_t b_addr = smem_u32(xs + (size_t)sx * kXBox);
+            const uint32_t x_addr = x_base + (uint32_t)rx.s * kXBox;
+            const uint32_t d = tmem + hh * kUmmaN;
+            umma_bf16_pair(d, sdesc_sw128(x_addr), sdesc_sw128(a_addr), idesc, kb != 0);
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_bf16(tmem + hh * kHalf, sdesc_sw128(a_addr + 32 * kk), sdesc_sw128(b_addr + 32 * kk), idesc,
-                        (kb | kk) != 0);
-            umma_commit(&empty_x[sx]);
-            ++ix;
+            for (int kk = 1; kk < kBK / 16; ++kk)
+              umma_bf16_pair(d, sdesc_sw128(x_addr + 32 * kk), sdesc_sw128(a_addr + 32 * kk), idesc, 1u);
+            umma_commit_pair(&empty_x[rx.s]);
+            rx.next(NX);
           }
-          umma_commit(&empty_a[sa]);
-          ++ia;
+          if (!ok) break;
+          umma_commit_pair(&empty_a[ra.s]);
+          ra.next(NA);
         }
-        for (int hh = 0; hh < kNH; ++hh) umma_commit(&acc_full[hh]);
+        if (ok)
+          for (int hh = 0; hh < kNH; ++hh) umma_commit_pair(&acc_full[hh]);
       }
+      // every MMA issued has completed before the pair may free TMEM or exit
+      umma_commit_local(&mma_done);
+      if (!mbar_wait_cluster(&mma_done, 0u, kGemmWaitNs)) gemm_error(P, DRACO_ERR_TIMEOUT);
     }
-  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + 4) {
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
     // ------------------------------------------------------------ epilogue
-    const int e = warp & 3;  // TMEM lane quarter
-    int it = 0;
-    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++it) {
+    const int e = warp & 3;  // TMEM lane quarter = tokens 32e..32e+31 of this CTA's 128
+    const uint32_t acc_empty_leader[kNH] = {map_to_rank(&acc_empty[0], 0), map_to_rank(&acc_empty[1], 0)};
+    uint32_t acc_ph = 0;
+    for (int t = pair; t < P.total_tiles; t += npairs, acc_ph ^= 1u) {
       TileCursor c;
       c.at(P, t);
       const GemmProbDev& pr = P.prob[c.p];
-      const int row = c.rg * kBM + 32 * e + lane;
       bool ok = true;
 #pragma unroll 1
       for (int hh = 0; hh < kNH; ++hh) {
-        if (!mbar_wait_bounded(&acc_full[hh], (uint32_t)(it & 1), kGemmWaitNs)) {
+        if (!mbar_wait_cluster(&acc_full[hh], acc_ph, kGemmWaitNs)) {
           gemm_error(P, DRACO_ERR_TIMEOUT);
           ok = false;
           break;
         }
         tc_fence_after();
-        const int tok0 = (c.tb * kNH + hh) * kHalf;
+        const int tok = c.tb * kTileTok + hh * kUmmaM + (int)rank * kTokCta + 32 * e + lane;
 #pragma unroll 1
-        for (int cc = 0; cc < kHalf / 32; ++cc) {
+        for (int cc = 0; cc < kUmmaN / 32; ++cc) {
           uint32_t v[32];
-          tmem_ld32(tmem + ((uint32_t)(32 * e) << 16) + hh * kHalf + 32 * cc, v);
-          if (row < pr.n) {
-            const int tb = tok0 + 32 * cc;
-            if (pr.ydtype == DRACO_DTYPE_BF16) {
-              __nv_bfloat16* y = static_cast<__nv_bfloat16*>(pr.y) + row;
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (tb + j < pr.m) y[(int64_t)(tb + j) * pr.ldy] = __float2bfloat16_rn(__uint_as_float(v[j]));
-            } else {
-              float* y = static_cast<float*>(pr.y) + row;
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (tb + j < pr.m) y[(int64_t)(tb + j) * pr.ldy] = __uint_as_float(v[j]);
-            }
-          }
+          tmem_ld32(tmem + ((uint32_t)(32 * e) << 16) + hh * kUmmaN + 32 * cc, v);
+          store_rows(pr, tok, c.rp * kUmmaN + 32 * cc, v);
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(acc_empty_leader[hh]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0)
-        for (int hh = 0; hh < kNH; ++hh) mbar_arrive(&acc_empty[hh]);
       if (!ok) break;
     }
   } else if (warp >= kDeqWarp0) {
     // ------------------------------------------------------------ dequant
     const int dt = threadIdx.x - kDeqWarp0 * 32;
     const int r = dt >> 1, h = dt & 1;
-    int iw = 0, ia = 0;
+    Ring rw, ra;
+    uint64_t* const done_bar = rank == 0 ? full_a : deq_done;  // leader: straight to the MMA barrier
     bool ok = true;
-    for (int t = blockIdx.x; t < P.total_tiles && ok; t += gridDim.x) {
+    for (int t = pair; t < P.total_tiles && ok; t += npairs) {
       TileCursor c;
       c.at(P, t);
       const GemmProbDev& pr = P.prob[c.p];
       const TiledGeom geo = tiled_geom(pr.qt, pr.n, pr.k);
-      const int nrows = rg_tiles(geo, c.rg) * kChunkRows;
+      const int rg = 2 * c.rp + (int)rank;
+      const int nrows = rg < pr.n_rg ? rg_tiles(geo, rg) * kChunkRows : 0;
       for (int sb = 0; sb < pr.nb && ok; ++sb) {
-        const int sw = iw % NWP;
-        if (!mbar_wait_bounded(&full_wp[sw], (uint32_t)((iw / NWP) & 1), kGemmWaitNs)) {
+        if (!mbar_wait_bounded(&full_wp[rw.s], rw.ph, kGemmWaitNs)) {
           gemm_error(P, DRACO_ERR_TIMEOUT);
           ok = false;
           break;
         }
-        const uint8_t* slab = wps + (size_t)sw * P.wp_stage;
+        const uint8_t* slab = wps + (size_t)rw.s * P.wp_stage;
 #pragma unroll 1
         for (int q = 0; q < 4; ++q) {
-          const int sa = ia % kAStages;
-          if (!mbar_wait_bounded(&empty_a[sa], (uint32_t)(((ia / kAStages) & 1) ^ 1), kGemmWaitNs)) {
+          if (!mbar_wait_cluster(&empty_a[ra.s], ra.ph ^ 1u, kGemmWaitNs)) {
             gemm_error(P, DRACO_ERR_TIMEOUT);
             ok = false;
             break;
           }
-          uint8_t* a = as + (size_t)sa * kATile;
+          uint8_t* a = as + (size_t)ra.s * kATile;
           if (r < nrows) {
             if (pr.qt == kQ4_K) dequant_q4k(slab, pr.cb, q, r, h, a);
             else if (pr.qt == kQ6_K) dequant_q6k(slab, pr.cb, q, r, h, a);
@@ -495,21 +605,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
           }
           fence_async_smem();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&full_a[sa]);
-          ++ia;
+          if (lane == 0) mbar_arrive(&done_bar[ra.s]);
+          ra.next(NA);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_wp[sw]);
-        ++iw;
+        if (lane == 0) mbar_arrive(&empty_wp[rw.s]);
+        rw.next(kMaxWpStages);
+      }
+    }
+  } else if (warp == 2 && rank == 1 && lane == 0) {
+    // ------------------------------------------------------------ relay (peer CTA)
+    // one cluster-scope arrive on the leader's MMA barrier per dequantized
+    // tile, after all of this CTA's dequant warps have finished it
+    Ring ra;
+    bool ok = true;
+    for (int t = pair; t < P.total_tiles && ok; t += npairs) {
+      TileCursor c;
+      c.at(P, t);
+      for (int kb = 0; kb < c.nkb; ++kb) {
+        if (!mbar_wait_bounded(&deq_done[ra.s], ra.ph, kGemmWaitNs)) {
+          gemm_error(P, DRACO_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        mbar_arrive_remote(map_to_rank(&full_a[ra.s], 0));
+        ra.next(NA);
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // the peer no longer touches this CTA's barriers or shared memory
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
   }
 }
 
@@ -528,6 +658,57 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+// Per device: opt the kernel into the whole dynamic shared-memory budget
+// (the per-block opt-in limit less the kernel's static barriers) and count how
+// many CTA pairs can be resident at once.
+static int g_gemm_pairs[64] = {0};
+static int g_gemm_dyn_smem[64] = {0};
+
+static int gemm_max_pairs(int* dyn_smem, char* msg, size_t ml) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && g_gemm_pairs[dev] > 0) {
+    *dyn_smem = g_gemm_dyn_smem[dev];
+    return g_gemm_pairs[dev];
+  }
+  int optin = 0;
+  cudaFuncAttributes fa;
+  if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+      cudaFuncGetAttributes(&fa, gemm_kernel) != cudaSuccess) {
+    snprintf(msg, ml, "gemm: cannot query shared-memory limits");
+    return -1;
+  }
+  const int dyn = optin - (int)fa.sharedSizeBytes;
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+  if (e != cudaSuccess) {
+    snprintf(msg, ml, "gemm: cudaFuncSetAttribute(%d bytes) failed: %s", dyn, cudaGetErrorString(e));
+    return -1;
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 256);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = dyn;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel, &cfg);
+  if (e != cudaSuccess || n < 1) {
+    snprintf(msg, ml, "gemm: no CTA pair fits on this device (%s)", cudaGetErrorString(e));
+    return -1;
+  }
+  if (dev < 64) {
+    g_gemm_pairs[dev] = n;
+    g_gemm_dyn_smem[dev] = dyn;
+  }
+  *dyn_smem = dyn;
+  return n;
+}
+
 int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_t st, char* msg, size_t ml) {
   if (n < 1 || n > kGemmMaxProblems) {
     snprintf(msg, ml, "gemm: need 1..%d problems, got %d", kGemmMaxProblems, n);
@@ -540,11 +721,18 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
     snprintf(msg, ml, "gemm: cuTensorMapEncodeTiled unavailable");
     return DRACO_ERR_CUDA;
   }
+  // problems with the longest K first: their tiles are the longest, and the
+  // pairs that take them first finish with the short ones (fewer idle SMs at
+  // the end of a grouped launch)
+  int order[kGemmMaxProblems];
+  for (int p = 0; p < n; ++p) order[p] = p;
+  std::stable_sort(order, order + n, [&](int a, int b) { return probs[a].k > probs[b].k; });
   int tiles = 0, max_slab = 0;
   for (int p = 0; p < n; ++p) {
-    const draco_gemm_problem& q = probs[p];
+    const draco_gemm_problem& q = probs[order[p]];
     GemmProbDev& d = P.prob[p];
     const TiledGeom g = tiled_geom(q.qtype, q.n_rows, q.k);
+    const int esize = q.ydtype == DRACO_DTYPE_BF16 ? 2 : 4;
     d.w = static_cast<const uint8_t*>(q.w);
     d.y = q.y;
     d.ldy = q.ldy;
@@ -557,20 +745,21 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
     d.n_rg = (int)g.n_rg;
     d.n_tiles = (int)g.n_tiles;
     d.cb = g.cb;
-    d.tblocks = (int)((q.m + kNH * kHalf - 1) / (kNH * kHalf));
+    d.tblocks = (int)((q.m + kTileTok - 1) / kTileTok);
+    d.vec = (reinterpret_cast<uintptr_t>(q.y) % 16 == 0) && ((q.ldy * esize) % 16 == 0);
     d.tile0 = tiles;
-    tiles += d.n_rg * d.tblocks;
+    tiles += (d.n_rg + 1) / 2 * d.tblocks;
     max_slab = std::max(max_slab, kGroupTiles * g.cb);
-    // X [m, k] bf16 row-major (row stride ldx elements): box 64 k x 256 tokens, 128-byte swizzle
+    // X [m, k] bf16 row-major (row stride ldx elements): box 64 k x 128 tokens, 128-byte swizzle
     cuuint64_t gdim[2] = {(cuuint64_t)q.k, (cuuint64_t)q.m};
     cuuint64_t gstride[1] = {(cuuint64_t)q.ldx * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kHalf};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kTokCta};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(&P.tmap[p], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(q.x), gdim, gstride, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
-      snprintf(msg, ml, "gemm: cuTensorMapEncodeTiled failed (%d) for problem %d", (int)r, p);
+      snprintf(msg, ml, "gemm: cuTensorMapEncodeTiled failed (%d) for problem %d", (int)r, order[p]);
       return DRACO_ERR_ARG;
     }
   }
@@ -578,42 +767,39 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
   P.total_tiles = tiles;
   P.status = status;
   if (tiles == 0) return DRACO_OK;
+  int dyn_smem = 0;
+  const int max_pairs = gemm_max_pairs(&dyn_smem, msg, ml);
+  if (max_pairs < 1) return DRACO_ERR_CUDA;
+  // shared memory: packed slabs (2 stages), dequantized tiles, X boxes (two per k-block)
   P.wp_stage = (max_slab + 127) & ~127;
-  P.nwp = 2;
-  const int budget = 220 * 1024;
-  const int fixed = kAStages * kATile + P.nwp * P.wp_stage + 1024;  // + alignment slack
-  P.nx = std::min(kMaxXStages, (budget - fixed) / kXBox);
-  if (P.nx < 2) {
+  const int budget = dyn_smem - 1024;  // less the slack for 1024-byte alignment
+  const int rest = budget - kMaxWpStages * P.wp_stage;
+  P.na = 3;
+  P.nx = std::min(kMaxXStages, (rest - P.na * kATile) / kXBox);
+  if (P.nx < 4) {
     snprintf(msg, ml, "gemm: shared memory budget exceeded");
     return DRACO_ERR_ARG;
   }
   P.x_off = 0;
   P.a_off = P.nx * kXBox;
-  P.wp_off = P.a_off + kAStages * kATile;
-  P.smem_bytes = P.wp_off + P.nwp * P.wp_stage + 1024;
+  P.wp_off = P.a_off + P.na * kATile;
+  P.smem_bytes = P.wp_off + kMaxWpStages * P.wp_stage + 1024;
 
-  static int attr_set[64] = {0};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && attr_set[dev] < P.smem_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P.smem_bytes);
-    if (e != cudaSuccess) {
-      snprintf(msg, ml, "gemm: cudaFuncSetAttribute(%d bytes) failed: %s", P.smem_bytes, cudaGetErrorString(e));
-      return DRACO_ERR_CUDA;
-    }
-    attr_set[dev] = P.smem_bytes;
-  }
-  const int grid = std::min(device_sm_count(), tiles);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const int pairs = std::min(max_pairs, tiles);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
+  cfg.gridDim = dim3(2 * pairs);
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = P.smem_bytes;
   cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel, P);
   if (e != cudaSuccess) {
     snprintf(msg, ml, "gemm: launch failed: %s", cudaGetErrorString(e));
