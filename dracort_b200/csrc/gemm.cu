@@ -187,138 +187,179 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// byte offset of 16-byte chunk c (k = 8c..8c+7) of row r in a 128-byte-swizzled
-// K-major tile with 128-byte rows
-__device__ __forceinline__ uint32_t sw128(int r, int c) {
-  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
-}
-
 __device__ __forceinline__ uint32_t bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
-// exact float of byte i (unsigned) of w
-__device__ __forceinline__ float gbyte_f(uint32_t w, int i) {
-  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)i)) - 8388608.f;
-}
-// exact float of byte i of w read as int8
-__device__ __forceinline__ float gsbyte_f(uint32_t w, int i) {
-  return __uint_as_float(__byte_perm(w ^ 0x80808080u, 0x4B000000u, 0x7440u | (uint32_t)i)) - 8388736.f;
-}
-__device__ __forceinline__ uint32_t gbyte(uint32_t w, int i) { return __byte_perm(w, 0u, 0x4440u | (uint32_t)i); }
-__device__ __forceinline__ uint32_t lds32_g(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-// exact float of a small non-negative integer (< 2^23)
-__device__ __forceinline__ float u2f_g(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.f; }
 
 // ---------------------------------------------------------------------------
-// dequantization of one 64-k block of a packed slab into a bf16 A tile.
-// 256 threads: thread dt -> row r = dt / 2, half h = dt % 2.  Every value is
-// fp32 exactly as gguf._dequantize computes it, then rounded to bf16.
+// dequantization of one 64-k block of a packed slab into the bf16 B tile
+// (128 rows x 64 k, K-major, 128-byte swizzle).  Warp w takes chunk w (rows
+// 16w..16w+15); lane L = 4g + t reads the 16-byte unit L of the chunk's
+// fragment-ordered fields (rows g and g+8, one 128-bit shared load) and
+// produces 32 values: 8 groups of 4 consecutive k, each stored as 8 bytes.
+// The two 32-k halves of the block are visited in the order g&1, g&1^1, so
+// that every half-warp's 8-byte stores cover all 32 banks once.
+// Every value is the fp32 number gguf._dequantize computes (the products with
+// the scales are exact; the one rounding is the same), then rounded to bf16;
+// the arithmetic runs two values at a time in the packed f32x2 pipes.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void store_chunk(uint8_t* a, int r, int c, const float (&v)[8]) {
-  *reinterpret_cast<uint4*>(a + sw128(r, c)) =
-      make_uint4(bf16x2(v[0], v[1]), bf16x2(v[2], v[3]), bf16x2(v[4], v[5]), bf16x2(v[6], v[7]));
-}
-__device__ __forceinline__ void zero_chunk(uint8_t* a, int r, int c) {
-  *reinterpret_cast<uint4*>(a + sw128(r, c)) = make_uint4(0, 0, 0, 0);
-}
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
-// Q4_K: k-block q of the super-block = qs bytes 32q..32q+31 of each row; low
-// nibbles are k 0-31 (sub-block 2q), high nibbles k 32-63 (sub-block 2q+1).
-// Half h takes bytes 16h..16h+15: output chunks 2h, 2h+1 (low) and 4+2h, 5+2h (high).
-__device__ __forceinline__ void dequant_q4k(const uint8_t* slab, int cb, int q, int r, int h, uint8_t* a) {
-  const uint8_t* ch = slab + (r >> 4) * cb;
-  const int rr = r & 15, g = rr & 7, hi = rr >> 3;
-  const uint8_t* sp = ch + 2048 + 24 * g + 12 * hi;
-  const uint32_t A = lds32_g(sp), Bw = lds32_g(sp + 4), C = lds32_g(sp + 8);
-  const uint32_t dd = lds32_g(ch + 2240 + 8 * g + 4 * hi);
-  const float d = f16_bits_to_f32(dd), dmin = f16_bits_to_f32(dd >> 16);
-  float ds[2], dm[2];
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
+__device__ __forceinline__ uint64_t splat2(float v) { return pack2(__float_as_uint(v), __float_as_uint(v)); }
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// (lo, hi) fp32 pair -> bf16x2 with lo in the low half
+__device__ __forceinline__ uint32_t bf16x2_of(uint64_t v) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "r"((uint32_t)(v >> 32)), "r"((uint32_t)v));
+  return r;
+}
+// bytes 2j, 2j+1 of w as the fp32 pair (2^23 + byte) (exact)
+constexpr uint32_t kMagic23 = 0x4B000000u;
+__device__ __forceinline__ uint64_t magic_pair(uint32_t w, int j) {
+  return pack2(__byte_perm(w, kMagic23, 0x7440u | (2 * j)), __byte_perm(w, kMagic23, 0x7440u | (2 * j + 1)));
+}
+// the 4 bytes of w (each < 2^8, minus `bias`) scaled: returns the 4 bf16 values as uint2
+__device__ __forceinline__ uint2 scale4_mul(uint32_t w, uint64_t bias2, uint64_t s2) {
+  const uint64_t v01 = mul2(add2(magic_pair(w, 0), bias2), s2);
+  const uint64_t v23 = mul2(add2(magic_pair(w, 1), bias2), s2);
+  return make_uint2(bf16x2_of(v01), bf16x2_of(v23));
+}
+__device__ __forceinline__ uint2 scale4_fma(uint32_t w, uint64_t bias2, uint64_t s2, uint64_t c2) {
+  const uint64_t v01 = fma2(add2(magic_pair(w, 0), bias2), s2, c2);
+  const uint64_t v23 = fma2(add2(magic_pair(w, 1), bias2), s2, c2);
+  return make_uint2(bf16x2_of(v01), bf16x2_of(v23));
+}
+// 8 bytes (k = 8c + 4(t&1) .. +3 of tile row g + 8hi of this warp's chunk)
+__device__ __forceinline__ void st_piece(uint8_t* tw, int hi, int g, int t, int c, uint2 v) {
+  *reinterpret_cast<uint2*>(tw + hi * 1024 + g * 128 + ((c ^ g) << 4) + 8 * (t & 1)) = v;
+}
+__device__ __forceinline__ float f16lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
+__device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+
+// Q4_K: k-block q = sub-blocks 2q (low nibbles of qs bytes 32q..32q+31) and
+// 2q+1 (high nibbles).  Unit word (hi, h): row g+8hi, qs bytes 16h+4t..+3.
+__device__ __forceinline__ void deq_q4k(const uint8_t* ch, int q, int lane, uint8_t* tw) {
+  const int g = lane >> 2, t = lane & 3, g0 = g & 1;
+  const uint4 U = lds128(ch + 512 * q + 16 * lane);
+  const uint2 S0 = lds64(ch + 2048 + 24 * g), S1 = lds64(ch + 2056 + 24 * g), S2 = lds64(ch + 2064 + 24 * g);
+  const uint2 DD = lds64(ch + 2240 + 8 * g);
+  const uint64_t bias = splat2(-8388608.f);
 #pragma unroll
-  for (int s = 0; s < 2; ++s) {
-    const int j = 2 * q + s;
-    uint32_t sc, m;
-    if (j < 4) {
-      sc = gbyte(A, j) & 63u;
-      m = gbyte(Bw, j) & 63u;
+  for (int hi = 0; hi < 2; ++hi) {
+    const uint32_t A = hi ? S1.y : S0.x, B = hi ? S2.x : S0.y, C = hi ? S2.y : S1.x;
+    const uint32_t dd = hi ? DD.y : DD.x;
+    // (scale, min) 6-bit pairs of sub-blocks 2q (byte 0) and 2q+1 (byte 1)
+    uint32_t scp, mp;
+    if (q < 2) {
+      scp = (A >> (16 * q)) & 0x3F3Fu;
+      mp = (B >> (16 * q)) & 0x3F3Fu;
     } else {
-      const uint32_t c = gbyte(C, j - 4);
-      sc = (c & 15u) | ((gbyte(A, j - 4) >> 6) << 4);
-      m = (c >> 4) | ((gbyte(Bw, j - 4) >> 6) << 4);
+      const int s = 16 * (q - 2);
+      const uint32_t a = A >> s, b = B >> s, c = C >> s;
+      scp = (c & 0x0F0Fu) | ((a >> 2) & 0x3030u);
+      mp = ((c >> 4) & 0x0F0Fu) | ((b >> 2) & 0x3030u);
     }
-    ds[s] = __fmul_rn(d, (float)sc);
-    dm[s] = __fmul_rn(dmin, (float)m);
-  }
-  uint32_t w[4];
+    const uint64_t ds = mul2(add2(magic_pair(scp, 0), bias), splat2(f16lo(dd)));   // d * sc   (exact)
+    const uint64_t dm = mul2(add2(magic_pair(mp, 0), bias), splat2(-f16hi(dd)));   // -dmin * m (exact)
+    const uint32_t ds_lo = (uint32_t)ds, ds_hi = (uint32_t)(ds >> 32), dm_lo = (uint32_t)dm, dm_hi = (uint32_t)(dm >> 32);
+    const uint64_t dsA = splat2(__uint_as_float(g0 ? ds_hi : ds_lo)), dsB = splat2(__uint_as_float(g0 ? ds_lo : ds_hi));
+    const uint64_t dmA = splat2(__uint_as_float(g0 ? dm_hi : dm_lo)), dmB = splat2(__uint_as_float(g0 ? dm_lo : dm_hi));
 #pragma unroll
-  for (int tp = 0; tp < 4; ++tp) w[tp] = lds32_g(ch + 512 * q + 16 * (4 * g + tp) + 4 * (2 * hi + h));
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t w = hi ? (h ? U.w : U.z) : (h ? U.y : U.x);
 #pragma unroll
-  for (int s = 0; s < 2; ++s)      // low / high nibbles
-#pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {  // two chunks of 8 values
-      float v[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t word = w[2 * cc + (i >> 2)];
-        const uint32_t nib = s ? ((word >> (8 * (i & 3) + 4)) & 15u) : ((word >> (8 * (i & 3))) & 15u);
-        v[i] = __fsub_rn(__fmul_rn(ds[s], u2f_g(nib)), dm[s]);
+      for (int n0 = 0; n0 < 2; ++n0) {
+        const int nib = g0 ^ n0;
+        const uint32_t wq = (w >> (4 * nib)) & 0x0F0F0F0Fu;
+        st_piece(tw, hi, g, t, 4 * nib + 2 * h + (t >> 1), scale4_fma(wq, bias, n0 ? dsB : dsA, n0 ? dmB : dmA));
       }
-      store_chunk(a, r, 4 * s + 2 * h + cc, v);
-    }
-}
-
-// Q6_K: k-block q = elements 64q..64q+63: half n = q / 2, 32-element groups
-// i = 2(q%2) + h (one per thread), l = 0..31 -> chunks 4h + l/8.
-__device__ __forceinline__ void dequant_q6k(const uint8_t* slab, int cb, int q, int r, int h, uint8_t* a) {
-  const uint8_t* ch = slab + (r >> 4) * cb;
-  const int rr = r & 15, g = rr & 7, hi = rr >> 3;
-  const int n = q >> 1, i = 2 * (q & 1) + h;
-  const float d = ld_f16(ch + 3328 + 4 * g + 2 * hi);
-  const uint8_t* scp = ch + 3072 + 32 * g + 16 * hi;
-#pragma unroll
-  for (int is = 0; is < 2; ++is) {  // 16-element halves: sub-block 8n + 2i + is
-    const float dl = __fmul_rn(d, (float)(int8_t)scp[8 * n + 2 * i + is]);
-    const int nu = 2 * n + is;
-#pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      float v[8];
-#pragma unroll
-      for (int tt = 0; tt < 2; ++tt) {
-        const int t = 2 * cc + tt;  // l = 16 is + 4 t .. +3
-        const uint8_t* lb = ch + 16 * (4 * g + t);
-        const int wbase = 6 * nu + 3 * hi;
-        const uint32_t ql = lds32_g(lb + 512 * ((wbase + (i & 1)) >> 2) + 4 * ((wbase + (i & 1)) & 3));
-        const uint32_t qh = lds32_g(lb + 512 * ((wbase + 2) >> 2) + 4 * ((wbase + 2) & 3));
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const uint32_t lo = (i < 2) ? ((ql >> (8 * b)) & 15u) : ((ql >> (8 * b + 4)) & 15u);
-          const uint32_t hb = (qh >> (8 * b + 2 * i)) & 3u;
-          v[4 * tt + b] = __fmul_rn(dl, (float)((int)(lo | (hb << 4)) - 32));
-        }
-      }
-      store_chunk(a, r, 4 * h + 2 * is + cc, v);
     }
   }
 }
 
-// Q8_0: k-block q = blocks 2q, 2q+1 of the super-block; thread half h takes block 2q+h.
-__device__ __forceinline__ void dequant_q80(const uint8_t* slab, int cb, int q, int r, int h, uint8_t* a) {
-  const uint8_t* ch = slab + (r >> 4) * cb;
-  const int rr = r & 15, g = rr & 7, hi = rr >> 3;
-  const int b = 2 * q + h;
-  const float d = ld_f16(ch + 4096 + 32 * g + 16 * hi + 2 * b);
+// Q6_K: k-block q = groups i = 2(q&1) + ii (ii = 0, 1) of half n = q/2.
+// Lane words 12n..12n+11 (three units): word 6is + 3hi + {0: ql l, 1: ql l+32, 2: qh}.
+__device__ __forceinline__ void deq_q6k(const uint8_t* ch, int q, int lane, uint8_t* tw) {
+  const int g = lane >> 2, t = lane & 3, g0 = g & 1;
+  const int n = q >> 1, odd = q & 1;
+  const uint4 P0 = lds128(ch + 512 * (3 * n) + 16 * lane);
+  const uint4 P1 = lds128(ch + 512 * (3 * n + 1) + 16 * lane);
+  const uint4 P2 = lds128(ch + 512 * (3 * n + 2) + 16 * lane);
+  const uint32_t W[12] = {P0.x, P0.y, P0.z, P0.w, P1.x, P1.y, P1.z, P1.w, P2.x, P2.y, P2.z, P2.w};
+  const uint32_t dd = lds32(ch + 3328 + 4 * g);
+  const uint64_t bias8 = splat2(-8388736.f);   // -(2^23 + 128): int8 scales stored ^ 0x80
+  const uint64_t bias6 = splat2(-8388640.f);   // -(2^23 + 32)
 #pragma unroll
-  for (int cc = 0; cc < 4; ++cc) {  // k = 8cc..8cc+7 of the block
-    const int half = cc >> 1, t0 = 2 * (cc & 1);
-    float v[8];
+  for (int hi = 0; hi < 2; ++hi) {
+    // int8 scales of groups (is, ii) at byte is + 2ii
+    const uint32_t scw = lds32(ch + 3072 + 32 * g + 16 * hi + 8 * n + 4 * odd) ^ 0x80808080u;
+    const uint64_t d2 = splat2(hi ? f16hi(dd) : f16lo(dd));
+    const uint64_t dl01 = mul2(add2(magic_pair(scw, 0), bias8), d2);  // (is0 ii0, is1 ii0)
+    const uint64_t dl23 = mul2(add2(magic_pair(scw, 1), bias8), d2);  // (is0 ii1, is1 ii1)
 #pragma unroll
-    for (int tt = 0; tt < 2; ++tt) {
-      const uint32_t w = lds32_g(ch + 512 * b + 16 * (4 * g + t0 + tt) + 4 * (2 * hi + half));
+    for (int is = 0; is < 2; ++is) {
+      const uint32_t s_ii0 = is ? (uint32_t)(dl01 >> 32) : (uint32_t)dl01;
+      const uint32_t s_ii1 = is ? (uint32_t)(dl23 >> 32) : (uint32_t)dl23;
+      const uint32_t qh = W[6 * is + 3 * hi + 2];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) v[4 * tt + i] = __fmul_rn(gsbyte_f(w, i), d);
+      for (int n0 = 0; n0 < 2; ++n0) {
+        const int ii = g0 ^ n0;
+        const uint32_t ql = ii ? W[6 * is + 3 * hi + 1] : W[6 * is + 3 * hi];
+        const uint32_t lo = (ql >> (4 * odd)) & 0x0F0F0F0Fu;
+        const uint32_t hb = (qh >> (2 * (2 * odd + ii))) & 0x03030303u;
+        const uint32_t q6 = lo | (hb << 4);
+        st_piece(tw, hi, g, t, 4 * ii + 2 * is + (t >> 1),
+                 scale4_mul(q6, bias6, splat2(__uint_as_float(ii ? s_ii1 : s_ii0))));
+      }
     }
-    store_chunk(a, r, 4 * h + cc, v);
   }
+}
+
+// Q8_0: k-block q = blocks 2q, 2q+1.  Unit word (hi, h): row g+8hi, qs bytes 16h+4t..+3.
+__device__ __forceinline__ void deq_q80(const uint8_t* ch, int q, int lane, uint8_t* tw) {
+  const int g = lane >> 2, t = lane & 3, g0 = g & 1;
+  const uint4 U0 = lds128(ch + 512 * (2 * q) + 16 * lane);
+  const uint4 U1 = lds128(ch + 512 * (2 * q + 1) + 16 * lane);
+  const uint64_t bias8 = splat2(-8388736.f);
+#pragma unroll
+  for (int hi = 0; hi < 2; ++hi) {
+    const uint32_t dw = lds32(ch + 4096 + 32 * g + 16 * hi + 4 * q);  // d of blocks 2q (lo), 2q+1 (hi)
+    const uint64_t dA = splat2(g0 ? f16hi(dw) : f16lo(dw)), dB = splat2(g0 ? f16lo(dw) : f16hi(dw));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t w0 = hi ? (h ? U0.w : U0.z) : (h ? U0.y : U0.x);
+      const uint32_t w1 = hi ? (h ? U1.w : U1.z) : (h ? U1.y : U1.x);
+#pragma unroll
+      for (int n0 = 0; n0 < 2; ++n0) {
+        const int bb = g0 ^ n0;
+        st_piece(tw, hi, g, t, 4 * bb + 2 * h + (t >> 1),
+                 scale4_mul((bb ? w1 : w0) ^ 0x80808080u, bias8, n0 ? dB : dA));
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void zero_rows16(uint8_t* tw, int lane) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(tw + 512 * i + 16 * lane) = make_uint4(0, 0, 0, 0);
 }
 
 __device__ __forceinline__ void gemm_error(const GemmParams& P, int code) {
@@ -563,8 +604,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     }
   } else if (warp >= kDeqWarp0) {
     // ------------------------------------------------------------ dequant
-    const int dt = threadIdx.x - kDeqWarp0 * 32;
-    const int r = dt >> 1, h = dt & 1;
+    const int dw = warp - kDeqWarp0;  // row tile (16 rows) of the 128-row B tile
     Ring rw, ra;
     uint64_t* const done_bar = rank == 0 ? full_a : deq_done;  // leader: straight to the MMA barrier
     bool ok = true;
@@ -574,7 +614,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       const GemmProbDev& pr = P.prob[c.p];
       const TiledGeom geo = tiled_geom(pr.qt, pr.n, pr.k);
       const int rg = 2 * c.rp + (int)rank;
-      const int nrows = rg < pr.n_rg ? rg_tiles(geo, rg) * kChunkRows : 0;
+      const int nchunks = rg < pr.n_rg ? rg_tiles(geo, rg) : 0;
       for (int sb = 0; sb < pr.nb && ok; ++sb) {
         if (!mbar_wait_bounded(&full_wp[rw.s], rw.ph, kGemmWaitNs)) {
           gemm_error(P, DRACO_ERR_TIMEOUT);
@@ -589,19 +629,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             ok = false;
             break;
           }
-          uint8_t* a = as + (size_t)ra.s * kATile;
-          if (r < nrows) {
-            if (pr.qt == kQ4_K) dequant_q4k(slab, pr.cb, q, r, h, a);
-            else if (pr.qt == kQ6_K) dequant_q6k(slab, pr.cb, q, r, h, a);
-            else dequant_q80(slab, pr.cb, q, r, h, a);
-          } else if (pr.qt == kQ4_K) {  // rows past n_rows: zeros in this thread's chunks
-            zero_chunk(a, r, 2 * h);
-            zero_chunk(a, r, 2 * h + 1);
-            zero_chunk(a, r, 4 + 2 * h);
-            zero_chunk(a, r, 5 + 2 * h);
+          uint8_t* tw = as + (size_t)ra.s * kATile + dw * 2048;
+          if (dw < nchunks) {
+            const uint8_t* ch = slab + dw * pr.cb;
+            if (pr.qt == kQ4_K) deq_q4k(ch, q, lane, tw);
+            else if (pr.qt == kQ6_K) deq_q6k(ch, q, lane, tw);
+            else deq_q80(ch, q, lane, tw);
           } else {
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc) zero_chunk(a, r, 4 * h + cc);
+            zero_rows16(tw, lane);  // row tile past n_rows
           }
           fence_async_smem();
           __syncwarp();
