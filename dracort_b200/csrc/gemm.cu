@@ -59,23 +59,26 @@ constexpr int kATile = kBM * kBK * 2;             // 16 KB: one dequantized weig
 constexpr int kGemmThreads = 16 * 32;
 constexpr int kDeqWarp0 = 8, kDeqWarps = 8;
 constexpr int kEpiWarp0 = 4, kEpiWarps = 4;
-constexpr int kMaxXStages = 10, kMaxWpStages = 2, kMaxAStages = 4;
+constexpr int kMaxStages = 6;
+constexpr int kStageBytes = 32 * 32 * 4;          // epilogue staging tile (32 tokens x 32 rows, fp32 max)
 constexpr uint64_t kGemmWaitNs = 4000000000ull;  // 4 s
 
 struct GemmProbDev {
   const uint8_t* w;
   void* y;
   int64_t ldy;
-  int qt, ydtype, m, n, k, nb, n_rg, n_tiles, cb, tblocks, tile0, vec;
+  int qt, ydtype, m, n, k, nb, n_rg, n_tiles, cb, tblocks, tile0, vec, ymode;
 };
+constexpr int kYDirect = 0, kYTma = 1;  // epilogue: direct stores or staged TMA stores
 
 struct __align__(64) GemmParams {
-  CUtensorMap tmap[kGemmMaxProblems];
+  CUtensorMap xmap[kGemmMaxProblems];
+  CUtensorMap ymap[kGemmMaxProblems];
   GemmProbDev prob[kGemmMaxProblems];
   int* status;
   int n_prob, total_tiles;
-  int nx, na, wp_stage;
-  int x_off, a_off, wp_off, smem_bytes;
+  int ns;  // k-block stages
+  int x_off, a_off, st_off, smem_bytes;
 };
 
 // ---------------------------------------------------------------------------
@@ -104,27 +107,11 @@ __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// bounded wait with cluster-scope acquire (for barriers that other CTAs, or
-// tensor-core work issued by the other CTA, complete)
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  uint64_t t0 = global_timer_ns();
-  while (true) {
-    for (int i = 0; i < 64; ++i)
-      if (mbar_try_wait_cluster(bar, parity)) return true;
-    if (global_timer_ns() - t0 > limit_ns) return false;
-  }
-}
+// Waits on barriers that the other CTA or the pair's tensor-core work completes
+// use the default (CTA-scope) try_wait: the arriving side releases at cluster
+// scope (remote arrives) or completes through the async proxy (TMA bytes,
+// tcgen05.commit).  A cluster-scope acquire on every poll costs a few hundred
+// cycles, which the MMA issue loop cannot afford three times per k-block.
 
 // TMA 2-D tile load into this CTA's shared memory; the transaction bytes are
 // counted on `bar_cluster` (a barrier of the leader CTA of the pair).
@@ -175,6 +162,22 @@ __device__ __forceinline__ void umma_commit_local(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+// wait for this thread's tcgen05.ld results; v is tied to the wait so no use
+// of the loaded registers can be scheduled before it
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&v)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])::"memory");
+}
+__device__ __forceinline__ void reg_tie(uint32_t (&v)[32]) { asm volatile("" : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]), "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]), "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15]), "+r"(v[16]), "+r"(v[17]), "+r"(v[18]), "+r"(v[19]), "+r"(v[20]), "+r"(v[21]), "+r"(v[22]), "+r"(v[23]), "+r"(v[24]), "+r"(v[25]), "+r"(v[26]), "+r"(v[27]), "+r"(v[28]), "+r"(v[29]), "+r"(v[30]), "+r"(v[31])); }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -204,9 +207,56 @@ __device__ __forceinline__ uint32_t bf16x2(float a, float b) {
 // the scales are exact; the one rounding is the same), then rounded to bf16;
 // the arithmetic runs two values at a time in the packed f32x2 pipes.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
-__device__ __forceinline__ uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
-__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+// read-only global loads that bypass L1 (each packed byte is used once per tile)
+__device__ __forceinline__ uint4 ldg128(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ldg64(const uint8_t* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg32(const uint8_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// One lane's packed inputs for one 64-k block of its row tile (loaded a block
+// ahead of use so the global-load latency hides behind the previous block):
+//  Q4_K: u0 = qs unit; s0..s5 = scale bytes of rows g, g+8; s6, s7 = (d, dmin) of rows g, g+8
+//  Q6_K: u0..u2 = ql/qh units of half q/2; s0, s1 = int8 scales of rows g, g+8; s2 = d of both rows
+//  Q8_0: u0, u1 = qs units of blocks 2q, 2q+1; s0, s1 = d of both blocks for rows g, g+8
+struct Packed {
+  uint4 u0, u1, u2;
+  uint32_t s0, s1, s2, s3, s4, s5, s6, s7;
+};
+__device__ __forceinline__ void fetch_packed(int qt, const uint8_t* ch, int q, int lane, Packed& pk) {
+  const int g = lane >> 2;
+  if (qt == kQ4_K) {
+    pk.u0 = ldg128(ch + 512 * q + 16 * lane);
+    const uint2 a = ldg64(ch + 2048 + 24 * g), b = ldg64(ch + 2056 + 24 * g), c = ldg64(ch + 2064 + 24 * g);
+    const uint2 d = ldg64(ch + 2240 + 8 * g);
+    pk.s0 = a.x, pk.s1 = a.y, pk.s2 = b.x, pk.s3 = b.y, pk.s4 = c.x, pk.s5 = c.y, pk.s6 = d.x, pk.s7 = d.y;
+  } else if (qt == kQ6_K) {
+    const int n = q >> 1, odd = q & 1;
+    pk.u0 = ldg128(ch + 512 * (3 * n) + 16 * lane);
+    pk.u1 = ldg128(ch + 512 * (3 * n + 1) + 16 * lane);
+    pk.u2 = ldg128(ch + 512 * (3 * n + 2) + 16 * lane);
+    pk.s0 = ldg32(ch + 3072 + 32 * g + 8 * n + 4 * odd);
+    pk.s1 = ldg32(ch + 3072 + 32 * g + 16 + 8 * n + 4 * odd);
+    pk.s2 = ldg32(ch + 3328 + 4 * g);
+  } else {
+    pk.u0 = ldg128(ch + 512 * (2 * q) + 16 * lane);
+    pk.u1 = ldg128(ch + 512 * (2 * q + 1) + 16 * lane);
+    pk.s0 = ldg32(ch + 4096 + 32 * g + 4 * q);
+    pk.s1 = ldg32(ch + 4096 + 32 * g + 16 + 4 * q);
+  }
+}
 
 __device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) { return ((uint64_t)hi << 32) | lo; }
 __device__ __forceinline__ uint64_t splat2(float v) { return pack2(__float_as_uint(v), __float_as_uint(v)); }
@@ -256,11 +306,11 @@ __device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushor
 
 // Q4_K: k-block q = sub-blocks 2q (low nibbles of qs bytes 32q..32q+31) and
 // 2q+1 (high nibbles).  Unit word (hi, h): row g+8hi, qs bytes 16h+4t..+3.
-__device__ __forceinline__ void deq_q4k(const uint8_t* ch, int q, int lane, uint8_t* tw) {
+__device__ __forceinline__ void deq_q4k(const Packed& pk, int q, int lane, uint8_t* tw) {
   const int g = lane >> 2, t = lane & 3, g0 = g & 1;
-  const uint4 U = lds128(ch + 512 * q + 16 * lane);
-  const uint2 S0 = lds64(ch + 2048 + 24 * g), S1 = lds64(ch + 2056 + 24 * g), S2 = lds64(ch + 2064 + 24 * g);
-  const uint2 DD = lds64(ch + 2240 + 8 * g);
+  const uint4 U = pk.u0;
+  const uint2 S0 = make_uint2(pk.s0, pk.s1), S1 = make_uint2(pk.s2, pk.s3), S2 = make_uint2(pk.s4, pk.s5);
+  const uint2 DD = make_uint2(pk.s6, pk.s7);
   const uint64_t bias = splat2(-8388608.f);
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
@@ -297,20 +347,18 @@ __device__ __forceinline__ void deq_q4k(const uint8_t* ch, int q, int lane, uint
 
 // Q6_K: k-block q = groups i = 2(q&1) + ii (ii = 0, 1) of half n = q/2.
 // Lane words 12n..12n+11 (three units): word 6is + 3hi + {0: ql l, 1: ql l+32, 2: qh}.
-__device__ __forceinline__ void deq_q6k(const uint8_t* ch, int q, int lane, uint8_t* tw) {
+__device__ __forceinline__ void deq_q6k(const Packed& pk, int q, int lane, uint8_t* tw) {
   const int g = lane >> 2, t = lane & 3, g0 = g & 1;
-  const int n = q >> 1, odd = q & 1;
-  const uint4 P0 = lds128(ch + 512 * (3 * n) + 16 * lane);
-  const uint4 P1 = lds128(ch + 512 * (3 * n + 1) + 16 * lane);
-  const uint4 P2 = lds128(ch + 512 * (3 * n + 2) + 16 * lane);
+  const int odd = q & 1;
+  const uint4 P0 = pk.u0, P1 = pk.u1, P2 = pk.u2;
   const uint32_t W[12] = {P0.x, P0.y, P0.z, P0.w, P1.x, P1.y, P1.z, P1.w, P2.x, P2.y, P2.z, P2.w};
-  const uint32_t dd = lds32(ch + 3328 + 4 * g);
+  const uint32_t dd = pk.s2;
   const uint64_t bias8 = splat2(-8388736.f);   // -(2^23 + 128): int8 scales stored ^ 0x80
   const uint64_t bias6 = splat2(-8388640.f);   // -(2^23 + 32)
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
     // int8 scales of groups (is, ii) at byte is + 2ii
-    const uint32_t scw = lds32(ch + 3072 + 32 * g + 16 * hi + 8 * n + 4 * odd) ^ 0x80808080u;
+    const uint32_t scw = (hi ? pk.s1 : pk.s0) ^ 0x80808080u;
     const uint64_t d2 = splat2(hi ? f16hi(dd) : f16lo(dd));
     const uint64_t dl01 = mul2(add2(magic_pair(scw, 0), bias8), d2);  // (is0 ii0, is1 ii0)
     const uint64_t dl23 = mul2(add2(magic_pair(scw, 1), bias8), d2);  // (is0 ii1, is1 ii1)
@@ -334,14 +382,13 @@ __device__ __forceinline__ void deq_q6k(const uint8_t* ch, int q, int lane, uint
 }
 
 // Q8_0: k-block q = blocks 2q, 2q+1.  Unit word (hi, h): row g+8hi, qs bytes 16h+4t..+3.
-__device__ __forceinline__ void deq_q80(const uint8_t* ch, int q, int lane, uint8_t* tw) {
+__device__ __forceinline__ void deq_q80(const Packed& pk, int lane, uint8_t* tw) {
   const int g = lane >> 2, t = lane & 3, g0 = g & 1;
-  const uint4 U0 = lds128(ch + 512 * (2 * q) + 16 * lane);
-  const uint4 U1 = lds128(ch + 512 * (2 * q + 1) + 16 * lane);
+  const uint4 U0 = pk.u0, U1 = pk.u1;
   const uint64_t bias8 = splat2(-8388736.f);
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
-    const uint32_t dw = lds32(ch + 4096 + 32 * g + 16 * hi + 4 * q);  // d of blocks 2q (lo), 2q+1 (hi)
+    const uint32_t dw = hi ? pk.s1 : pk.s0;  // d of blocks 2q (lo), 2q+1 (hi)
     const uint64_t dA = splat2(g0 ? f16hi(dw) : f16lo(dw)), dB = splat2(g0 ? f16lo(dw) : f16hi(dw));
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -424,32 +471,86 @@ __device__ __forceinline__ void store_rows(const GemmProbDev& pr, int tok, int r
   }
 }
 
+// TMA 2-D tile store from this CTA's shared memory (bulk-group completion)
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// 32 tokens x 32 rows of the accumulator -> staging tile [token][row] in the
+// swizzle the Y tensor map uses (64-byte rows for bf16, 128-byte for fp32)
+__device__ __forceinline__ void stage_rows(uint8_t* buf, int ydtype, int lane, const uint32_t (&v)[32]) {
+  if (ydtype == DRACO_DTYPE_BF16) {
+    uint8_t* row = buf + 64 * lane;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(row + ((j ^ sw) << 4)) =
+          make_uint4(bf16x2(__uint_as_float(v[8 * j]), __uint_as_float(v[8 * j + 1])),
+                     bf16x2(__uint_as_float(v[8 * j + 2]), __uint_as_float(v[8 * j + 3])),
+                     bf16x2(__uint_as_float(v[8 * j + 4]), __uint_as_float(v[8 * j + 5])),
+                     bf16x2(__uint_as_float(v[8 * j + 6]), __uint_as_float(v[8 * j + 7])));
+  } else {
+    uint8_t* row = buf + 128 * lane;
+    const int sw = lane & 7;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      *reinterpret_cast<uint4*>(row + ((j ^ sw) << 4)) = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+}
+
+// dequant-side view of one pair tile: this CTA's row tile dw of its row group
+struct DeqTile {
+  int t, nkb, qt;
+  const uint8_t* base;  // chunk dw of super-block 0 (null: row tile past n_rows)
+  int64_t sb_stride;    // bytes between super-blocks of one row tile
+  __device__ bool at(const GemmParams& P, int tile, int rank, int dw) {
+    if (tile >= P.total_tiles) return false;
+    TileCursor c;
+    c.at(P, tile);
+    const GemmProbDev& pr = P.prob[c.p];
+    const TiledGeom geo = tiled_geom(pr.qt, pr.n, pr.k);
+    const int rg = 2 * c.rp + rank;
+    const int nch = rg < pr.n_rg ? rg_tiles(geo, rg) : 0;
+    t = tile;
+    nkb = c.nkb;
+    qt = pr.qt;
+    base = dw < nch ? pr.w + slab_offset(geo, rg, 0) + (int64_t)dw * pr.cb : nullptr;
+    sb_stride = (int64_t)nch * pr.cb;
+    return true;
+  }
+  __device__ __forceinline__ void fetch(int kb, int lane, Packed& pk) const {
+    if (base) fetch_packed(qt, base + (kb >> 2) * sb_stride, kb & 3, lane, pk);
+  }
+};
+
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t full_x[kMaxXStages], empty_x[kMaxXStages];
-  __shared__ __align__(8) uint64_t full_wp[kMaxWpStages], empty_wp[kMaxWpStages];
-  __shared__ __align__(8) uint64_t full_a[kMaxAStages], empty_a[kMaxAStages], deq_done[kMaxAStages];
+  // one ring of k-block stages: X boxes of both accumulators + the dequantized weight tile
+  __shared__ __align__(8) uint64_t full_kb[kMaxStages], empty_kb[kMaxStages], deq_done[kMaxStages];
   __shared__ __align__(8) uint64_t acc_full[kNH], acc_empty[kNH], mma_done;
   __shared__ uint32_t s_tmem;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NX = P.nx, NA = P.na;
+  const int NS = P.ns;
   const uint32_t rank = cluster_rank();        // 0 = leader (issues the MMAs)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NX; ++i) {
-      mbar_init(&full_x[i], 1);                 // leader: its producer's expect_tx; bytes from both CTAs
-      mbar_init(&empty_x[i], 1);                // MMA commit (multicast)
-    }
-    for (int i = 0; i < kMaxWpStages; ++i) {
-      mbar_init(&full_wp[i], 1);
-      mbar_init(&empty_wp[i], kDeqWarps);
-    }
-    for (int i = 0; i < NA; ++i) {
-      mbar_init(&full_a[i], kDeqWarps + 1);     // leader: its dequant warps + the peer's relay
-      mbar_init(&empty_a[i], 1);                // MMA commit (multicast)
+    for (int i = 0; i < NS; ++i) {
+      // leader: its producer's expect_tx (X bytes of both CTAs), its dequant
+      // warps, and the peer's relay
+      mbar_init(&full_kb[i], 1 + kDeqWarps + 1);
+      mbar_init(&empty_kb[i], 1);               // MMA commit (multicast)
       mbar_init(&deq_done[i], kDeqWarps);       // peer: its dequant warps (relayed to the leader)
     }
     for (int i = 0; i < kNH; ++i) {
@@ -473,48 +574,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
   uint8_t* xs = smem + P.x_off;
   uint8_t* as = smem + P.a_off;
-  uint8_t* wps = smem + P.wp_off;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producer (X boxes)
     if (lane == 0) {
-      Ring rx, rw;
+      Ring rs;
       bool ok = true;
       for (int t = pair; t < P.total_tiles && ok; t += npairs) {
         TileCursor c;
         c.at(P, t);
-        const GemmProbDev& pr = P.prob[c.p];
-        const TiledGeom geo = tiled_geom(pr.qt, pr.n, pr.k);
-        const int rg = 2 * c.rp + (int)rank;
-        const uint32_t slab_bytes = rg < pr.n_rg ? (uint32_t)(rg_tiles(geo, rg) * pr.cb) : 0u;
-        for (int kb = 0; kb < c.nkb && ok; ++kb) {
-          if ((kb & 3) == 0) {
-            if (!mbar_wait_bounded(&empty_wp[rw.s], rw.ph ^ 1u, kGemmWaitNs)) {
-              gemm_error(P, DRACO_ERR_TIMEOUT);
-              ok = false;
-              break;
-            }
-            if (slab_bytes) {
-              mbar_arrive_expect_tx(&full_wp[rw.s], slab_bytes);
-              bulk_g2s(wps + (size_t)rw.s * P.wp_stage, pr.w + slab_offset(geo, rg, kb >> 2), slab_bytes,
-                       &full_wp[rw.s]);
-            } else {
-              mbar_arrive(&full_wp[rw.s]);  // row group past n_rows: dequant writes zeros
-            }
-            rw.next(kMaxWpStages);
+        for (int kb = 0; kb < c.nkb; ++kb) {
+          if (!mbar_wait_bounded(&empty_kb[rs.s], rs.ph ^ 1u, kGemmWaitNs)) {
+            gemm_error(P, DRACO_ERR_TIMEOUT);
+            ok = false;
+            break;
           }
-#pragma unroll 1
+          if (rank == 0) mbar_arrive_expect_tx(&full_kb[rs.s], 2 * kNH * kXBox);
+          const uint32_t bar = map_to_rank(&full_kb[rs.s], 0);
+#pragma unroll
           for (int hh = 0; hh < kNH; ++hh) {
-            if (!mbar_wait_cluster(&empty_x[rx.s], rx.ph ^ 1u, kGemmWaitNs)) {
-              gemm_error(P, DRACO_ERR_TIMEOUT);
-              ok = false;
-              break;
-            }
-            if (rank == 0) mbar_arrive_expect_tx(&full_x[rx.s], 2 * kXBox);
             const int tok = c.tb * kTileTok + hh * kUmmaM + (int)rank * kTokCta;
-            tma_load_2d_pair(xs + (size_t)rx.s * kXBox, &P.tmap[c.p], kb * kBK, tok, map_to_rank(&full_x[rx.s], 0));
-            rx.next(NX);
+            tma_load_2d_pair(xs + (size_t)(rs.s * kNH + hh) * kXBox, &P.xmap[c.p], kb * kBK, tok, bar);
           }
+          rs.next(NS);
         }
       }
     }
@@ -523,59 +605,56 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     if (rank == 0 && lane == 0) {
       const uint32_t idesc = idesc_bf16(kUmmaM, kUmmaN);
       const uint32_t x_base = smem_u32(xs), a_base = smem_u32(as);
-      Ring rx, ra;
+      Ring rs;
       uint32_t acc_ph = 0;
       bool ok = true;
       for (int t = pair; t < P.total_tiles && ok; t += npairs, acc_ph ^= 1u) {
         TileCursor c;
         c.at(P, t);
+        // both accumulators free (drained by the epilogues of both CTAs)
+        for (int hh = 0; hh < kNH && ok; ++hh)
+          if (!mbar_wait_bounded(&acc_empty[hh], acc_ph ^ 1u, kGemmWaitNs)) {
+            gemm_error(P, DRACO_ERR_TIMEOUT);
+            ok = false;
+          }
+        tc_fence_after();
         for (int kb = 0; kb < c.nkb && ok; ++kb) {
-          if (!mbar_wait_cluster(&full_a[ra.s], ra.ph, kGemmWaitNs)) {
+          // one wait per k-block: X boxes of both CTAs landed, both weight tiles dequantized
+          if (!mbar_wait_bounded(&full_kb[rs.s], rs.ph, kGemmWaitNs)) {
             gemm_error(P, DRACO_ERR_TIMEOUT);
             ok = false;
             break;
           }
-          const uint32_t a_addr = a_base + (uint32_t)ra.s * kATile;
+          const uint32_t a_addr = a_base + (uint32_t)rs.s * kATile;
+          const uint32_t x_addr0 = x_base + (uint32_t)(rs.s * kNH) * kXBox;
 #pragma unroll
           for (int hh = 0; hh < kNH; ++hh) {
-            if (kb == 0) {
-              if (!mbar_wait_cluster(&acc_empty[hh], acc_ph ^ 1u, kGemmWaitNs)) {
-                gemm_error(P, DRACO_ERR_TIMEOUT);
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-            }
-            if (!mbar_wait_cluster(&full_x[rx.s], rx.ph, kGemmWaitNs)) {
-              gemm_error(P, DRACO_ERR_TIMEOUT);
-              ok = false;
-              break;
-            }
-            const uint32_t x_addr = x_base + (uint32_t)rx.s * kXBox;
+            const uint32_t x_addr = x_addr0 + hh * kXBox;
             const uint32_t d = tmem + hh * kUmmaN;
             umma_bf16_pair(d, sdesc_sw128(x_addr), sdesc_sw128(a_addr), idesc, kb != 0);
 #pragma unroll
             for (int kk = 1; kk < kBK / 16; ++kk)
               umma_bf16_pair(d, sdesc_sw128(x_addr + 32 * kk), sdesc_sw128(a_addr + 32 * kk), idesc, 1u);
-            umma_commit_pair(&empty_x[rx.s]);
-            rx.next(NX);
           }
-          if (!ok) break;
-          umma_commit_pair(&empty_a[ra.s]);
-          ra.next(NA);
+          umma_commit_pair(&empty_kb[rs.s]);
+          rs.next(NS);
         }
         if (ok)
           for (int hh = 0; hh < kNH; ++hh) umma_commit_pair(&acc_full[hh]);
       }
       // every MMA issued has completed before the pair may free TMEM or exit
       umma_commit_local(&mma_done);
-      if (!mbar_wait_cluster(&mma_done, 0u, kGemmWaitNs)) gemm_error(P, DRACO_ERR_TIMEOUT);
+      if (!mbar_wait_bounded(&mma_done, 0u, kGemmWaitNs)) gemm_error(P, DRACO_ERR_TIMEOUT);
     }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kEpiWarps) {
     // ------------------------------------------------------------ epilogue
-    const int e = warp & 3;  // TMEM lane quarter = tokens 32e..32e+31 of this CTA's 128
+    // warp e owns TMEM lanes 32e..32e+31 = tokens 32e.. of this CTA's 128;
+    // 32 x 32 blocks go through a staging tile in shared memory to TMA stores
+    const int e = warp & 3;
+    uint8_t* stage = smem + P.st_off + e * 2 * kStageBytes;
     const uint32_t acc_empty_leader[kNH] = {map_to_rank(&acc_empty[0], 0), map_to_rank(&acc_empty[1], 0)};
     uint32_t acc_ph = 0;
+    int nst = 0;  // stores issued by this warp (alternating staging buffers)
     for (int t = pair; t < P.total_tiles; t += npairs, acc_ph ^= 1u) {
       TileCursor c;
       c.at(P, t);
@@ -583,18 +662,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       bool ok = true;
 #pragma unroll 1
       for (int hh = 0; hh < kNH; ++hh) {
-        if (!mbar_wait_cluster(&acc_full[hh], acc_ph, kGemmWaitNs)) {
+        if (!mbar_wait_bounded(&acc_full[hh], acc_ph, kGemmWaitNs)) {
           gemm_error(P, DRACO_ERR_TIMEOUT);
           ok = false;
           break;
         }
         tc_fence_after();
-        const int tok = c.tb * kTileTok + hh * kUmmaM + (int)rank * kTokCta + 32 * e + lane;
+        const int tok0 = c.tb * kTileTok + hh * kUmmaM + (int)rank * kTokCta + 32 * e;
+        const uint32_t tbase = tmem + ((uint32_t)(32 * e) << 16) + hh * kUmmaN;
+        if (tok0 < pr.m) {
 #pragma unroll 1
-        for (int cc = 0; cc < kUmmaN / 32; ++cc) {
-          uint32_t v[32];
-          tmem_ld32(tmem + ((uint32_t)(32 * e) << 16) + hh * kUmmaN + 32 * cc, v);
-          store_rows(pr, tok, c.rp * kUmmaN + 32 * cc, v);
+          for (int cc = 0; cc < kUmmaN / 32; cc += 2) {
+            uint32_t v0[32], v1[32];
+            tmem_ld32_nowait(tbase + 32 * cc, v0);
+            tmem_ld32_nowait(tbase + 32 * (cc + 1), v1);
+            tmem_ld_wait(v0);
+            reg_tie(v1);
+            const int row0 = c.rp * kUmmaN + 32 * cc;
+            if (pr.ymode == kYTma) {
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                uint8_t* buf = stage + (nst & 1) * kStageBytes;
+                if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+                __syncwarp();
+                stage_rows(buf, pr.ydtype, lane, u ? v1 : v0);
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0 && row0 + 32 * u < pr.n) {
+                  tma_store_2d(&P.ymap[c.p], row0 + 32 * u, tok0, buf);
+                }
+                if (lane == 0) bulk_commit();
+                ++nst;
+              }
+            } else {
+              store_rows(pr, tok0 + lane, row0, v0);
+              store_rows(pr, tok0 + lane, row0 + 32, v1);
+            }
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -602,51 +706,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       }
       if (!ok) break;
     }
+    if (lane == 0) bulk_wait_all();  // Y written before the kernel ends
   } else if (warp >= kDeqWarp0) {
     // ------------------------------------------------------------ dequant
-    const int dw = warp - kDeqWarp0;  // row tile (16 rows) of the 128-row B tile
-    Ring rw, ra;
-    uint64_t* const done_bar = rank == 0 ? full_a : deq_done;  // leader: straight to the MMA barrier
-    bool ok = true;
-    for (int t = pair; t < P.total_tiles && ok; t += npairs) {
-      TileCursor c;
-      c.at(P, t);
-      const GemmProbDev& pr = P.prob[c.p];
-      const TiledGeom geo = tiled_geom(pr.qt, pr.n, pr.k);
-      const int rg = 2 * c.rp + (int)rank;
-      const int nchunks = rg < pr.n_rg ? rg_tiles(geo, rg) : 0;
-      for (int sb = 0; sb < pr.nb && ok; ++sb) {
-        if (!mbar_wait_bounded(&full_wp[rw.s], rw.ph, kGemmWaitNs)) {
-          gemm_error(P, DRACO_ERR_TIMEOUT);
-          ok = false;
-          break;
-        }
-        const uint8_t* slab = wps + (size_t)rw.s * P.wp_stage;
-#pragma unroll 1
-        for (int q = 0; q < 4; ++q) {
-          if (!mbar_wait_cluster(&empty_a[ra.s], ra.ph ^ 1u, kGemmWaitNs)) {
-            gemm_error(P, DRACO_ERR_TIMEOUT);
-            ok = false;
-            break;
-          }
-          uint8_t* tw = as + (size_t)ra.s * kATile + dw * 2048;
-          if (dw < nchunks) {
-            const uint8_t* ch = slab + dw * pr.cb;
-            if (pr.qt == kQ4_K) deq_q4k(ch, q, lane, tw);
-            else if (pr.qt == kQ6_K) deq_q6k(ch, q, lane, tw);
-            else deq_q80(ch, q, lane, tw);
-          } else {
-            zero_rows16(tw, lane);  // row tile past n_rows
-          }
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&done_bar[ra.s]);
-          ra.next(NA);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_wp[rw.s]);
-        rw.next(kMaxWpStages);
+    // warp dw: row tile dw (16 rows) of this CTA's 128-row B tile.  The packed
+    // inputs of the next 64-k block are loaded before waiting for a free stage.
+    const int dw = warp - kDeqWarp0;
+    uint64_t* const done_bar = rank == 0 ? full_kb : deq_done;  // leader: straight to the MMA barrier
+    Ring ra;
+    DeqTile cur;
+    bool have = cur.at(P, pair, (int)rank, dw);
+    int kb = 0;
+    Packed pk;
+    if (have) cur.fetch(0, lane, pk);
+    while (have) {
+      // position and inputs of the next block
+      DeqTile nxt = cur;
+      int kb_n = kb + 1;
+      bool have_n = true;
+      if (kb_n == cur.nkb) {
+        have_n = nxt.at(P, cur.t + npairs, (int)rank, dw);
+        kb_n = 0;
       }
+      Packed pk_n;
+      if (have_n) nxt.fetch(kb_n, lane, pk_n);
+      if (!mbar_wait_bounded(&empty_kb[ra.s], ra.ph ^ 1u, kGemmWaitNs)) {
+        gemm_error(P, DRACO_ERR_TIMEOUT);
+        break;
+      }
+      uint8_t* tw = as + (size_t)ra.s * kATile + dw * 2048;
+      if (cur.base) {
+        if (cur.qt == kQ4_K) deq_q4k(pk, kb & 3, lane, tw);
+        else if (cur.qt == kQ6_K) deq_q6k(pk, kb & 3, lane, tw);
+        else deq_q80(pk, lane, tw);
+      } else {
+        zero_rows16(tw, lane);  // row tile past n_rows
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&done_bar[ra.s]);
+      ra.next(NS);
+      cur = nxt;
+      kb = kb_n;
+      pk = pk_n;
+      have = have_n;
     }
   } else if (warp == 2 && rank == 1 && lane == 0) {
     // ------------------------------------------------------------ relay (peer CTA)
@@ -663,8 +766,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
           ok = false;
           break;
         }
-        mbar_arrive_remote(map_to_rank(&full_a[ra.s], 0));
-        ra.next(NA);
+        mbar_arrive_remote(map_to_rank(&full_kb[ra.s], 0));
+        ra.next(NS);
       }
     }
   }
@@ -762,7 +865,7 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
   int order[kGemmMaxProblems];
   for (int p = 0; p < n; ++p) order[p] = p;
   std::stable_sort(order, order + n, [&](int a, int b) { return probs[a].k > probs[b].k; });
-  int tiles = 0, max_slab = 0;
+  int tiles = 0;
   for (int p = 0; p < n; ++p) {
     const draco_gemm_problem& q = probs[order[p]];
     GemmProbDev& d = P.prob[p];
@@ -784,18 +887,31 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
     d.vec = (reinterpret_cast<uintptr_t>(q.y) % 16 == 0) && ((q.ldy * esize) % 16 == 0);
     d.tile0 = tiles;
     tiles += (d.n_rg + 1) / 2 * d.tblocks;
-    max_slab = std::max(max_slab, kGroupTiles * g.cb);
     // X [m, k] bf16 row-major (row stride ldx elements): box 64 k x 128 tokens, 128-byte swizzle
     cuuint64_t gdim[2] = {(cuuint64_t)q.k, (cuuint64_t)q.m};
     cuuint64_t gstride[1] = {(cuuint64_t)q.ldx * 2};
     cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kTokCta};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(&P.tmap[p], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(q.x), gdim, gstride, box,
+    CUresult r = enc(&P.xmap[p], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(q.x), gdim, gstride, box,
                      estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       snprintf(msg, ml, "gemm: cuTensorMapEncodeTiled failed (%d) for problem %d", (int)r, order[p]);
       return DRACO_ERR_ARG;
+    }
+    // Y [m, n] (row stride ldy elements): 32 rows x 32 tokens per store,
+    // swizzled like the staging tile; needs a 16-byte aligned base and stride
+    d.ymode = kYDirect;
+    if (d.vec) {
+      cuuint64_t ydim[2] = {(cuuint64_t)q.n_rows, (cuuint64_t)q.m};
+      cuuint64_t ystride[1] = {(cuuint64_t)q.ldy * esize};
+      cuuint32_t ybox[2] = {32, 32};
+      const bool bf = q.ydtype == DRACO_DTYPE_BF16;
+      r = enc(&P.ymap[p], bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, q.y, ydim,
+              ystride, ybox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              bf ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r == CUDA_SUCCESS) d.ymode = kYTma;
     }
   }
   P.n_prob = n;
@@ -805,20 +921,19 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
   int dyn_smem = 0;
   const int max_pairs = gemm_max_pairs(&dyn_smem, msg, ml);
   if (max_pairs < 1) return DRACO_ERR_CUDA;
-  // shared memory: packed slabs (2 stages), dequantized tiles, X boxes (two per k-block)
-  P.wp_stage = (max_slab + 127) & ~127;
+  // shared memory: epilogue staging (2 tiles per epilogue warp), dequantized
+  // weight tiles, X boxes (two per k-block)
   const int budget = dyn_smem - 1024;  // less the slack for 1024-byte alignment
-  const int rest = budget - kMaxWpStages * P.wp_stage;
-  P.na = 3;
-  P.nx = std::min(kMaxXStages, (rest - P.na * kATile) / kXBox);
-  if (P.nx < 4) {
+  const int staging = kEpiWarps * 2 * kStageBytes;
+  P.ns = std::min(kMaxStages, (budget - staging) / (kNH * kXBox + kATile));
+  if (P.ns < 2) {
     snprintf(msg, ml, "gemm: shared memory budget exceeded");
     return DRACO_ERR_ARG;
   }
   P.x_off = 0;
-  P.a_off = P.nx * kXBox;
-  P.wp_off = P.a_off + P.na * kATile;
-  P.smem_bytes = P.wp_off + kMaxWpStages * P.wp_stage + 1024;
+  P.a_off = P.ns * kNH * kXBox;
+  P.st_off = P.a_off + P.ns * kATile;
+  P.smem_bytes = P.st_off + staging + 1024;
 
   const int pairs = std::min(max_pairs, tiles);
   cudaLaunchAttribute attr[2];
