@@ -103,9 +103,13 @@ __device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(smem_u32(p)), "r"(rank));
   return d;
 }
-// arrive on an mbarrier of another CTA of the cluster (release at cluster scope)
+// arrive on an mbarrier of another CTA of the cluster.  Default (CTA-scope)
+// release: the shared-memory writes the arrive publishes were made visible to
+// the async proxy by fence.proxy.async before it, and the tensor core of the
+// pair reads them only after the barrier completes.  A cluster-scope release
+// costs about a thousand cycles per arrive.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // Waits on barriers that the other CTA or the pair's tensor-core work completes
 // use the default (CTA-scope) try_wait: the arriving side releases at cluster
@@ -536,7 +540,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   // one ring of k-block stages: X boxes of both accumulators + the dequantized weight tile
-  __shared__ __align__(8) uint64_t full_kb[kMaxStages], empty_kb[kMaxStages], deq_done[kMaxStages];
+  __shared__ __align__(8) uint64_t full_kb[kMaxStages], empty_kb[kMaxStages];
   __shared__ __align__(8) uint64_t acc_full[kNH], acc_empty[kNH], mma_done;
   __shared__ uint32_t s_tmem;
 
@@ -547,11 +551,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
-      // leader: its producer's expect_tx (X bytes of both CTAs), its dequant
-      // warps, and the peer's relay
-      mbar_init(&full_kb[i], 1 + kDeqWarps + 1);
+      // leader: its producer's expect_tx (X bytes of both CTAs) and the
+      // dequant warps of both CTAs
+      mbar_init(&full_kb[i], 1 + 2 * kDeqWarps);
       mbar_init(&empty_kb[i], 1);               // MMA commit (multicast)
-      mbar_init(&deq_done[i], kDeqWarps);       // peer: its dequant warps (relayed to the leader)
     }
     for (int i = 0; i < kNH; ++i) {
       mbar_init(&acc_full[i], 1);               // MMA commit (multicast)
@@ -611,13 +614,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       for (int t = pair; t < P.total_tiles && ok; t += npairs, acc_ph ^= 1u) {
         TileCursor c;
         c.at(P, t);
-        // both accumulators free (drained by the epilogues of both CTAs)
-        for (int hh = 0; hh < kNH && ok; ++hh)
-          if (!mbar_wait_bounded(&acc_empty[hh], acc_ph ^ 1u, kGemmWaitNs)) {
-            gemm_error(P, DRACO_ERR_TIMEOUT);
-            ok = false;
-          }
-        tc_fence_after();
         for (int kb = 0; kb < c.nkb && ok; ++kb) {
           // one wait per k-block: X boxes of both CTAs landed, both weight tiles dequantized
           if (!mbar_wait_bounded(&full_kb[rs.s], rs.ph, kGemmWaitNs)) {
@@ -629,6 +625,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
           const uint32_t x_addr0 = x_base + (uint32_t)(rs.s * kNH) * kXBox;
 #pragma unroll
           for (int hh = 0; hh < kNH; ++hh) {
+            if (kb == 0) {
+              // accumulator hh drained by the epilogues of both CTAs (the
+              // first one is free while the second still drains)
+              if (!mbar_wait_bounded(&acc_empty[hh], acc_ph ^ 1u, kGemmWaitNs)) {
+                gemm_error(P, DRACO_ERR_TIMEOUT);
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
             const uint32_t x_addr = x_addr0 + hh * kXBox;
             const uint32_t d = tmem + hh * kUmmaN;
             umma_bf16_pair(d, sdesc_sw128(x_addr), sdesc_sw128(a_addr), idesc, kb != 0);
@@ -636,6 +642,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             for (int kk = 1; kk < kBK / 16; ++kk)
               umma_bf16_pair(d, sdesc_sw128(x_addr + 32 * kk), sdesc_sw128(a_addr + 32 * kk), idesc, 1u);
           }
+          if (!ok) break;
           umma_commit_pair(&empty_kb[rs.s]);
           rs.next(NS);
         }
@@ -682,8 +689,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             if (pr.ymode == kYTma) {
 #pragma unroll
               for (int u = 0; u < 2; ++u) {
-                uint8_t* buf = stage + (nst & 1) * kStageBytes;
-                if (lane == 0) bulk_wait_read<1>();  // the store that last used this buffer has read it
+                // bf16: 4 staging tiles of 2 KB, fp32: 2 of 4 KB; wait until
+                // the store that last used this tile has read it
+                uint8_t* buf;
+                if (pr.ydtype == DRACO_DTYPE_BF16) {
+                  buf = stage + (nst & 3) * (kStageBytes / 2);
+                  if (lane == 0) bulk_wait_read<3>();
+                } else {
+                  buf = stage + (nst & 1) * kStageBytes;
+                  if (lane == 0) bulk_wait_read<1>();
+                }
                 __syncwarp();
                 stage_rows(buf, pr.ydtype, lane, u ? v1 : v0);
                 fence_async_smem();
@@ -712,7 +727,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     // warp dw: row tile dw (16 rows) of this CTA's 128-row B tile.  The packed
     // inputs of the next 64-k block are loaded before waiting for a free stage.
     const int dw = warp - kDeqWarp0;
-    uint64_t* const done_bar = rank == 0 ? full_kb : deq_done;  // leader: straight to the MMA barrier
     Ring ra;
     DeqTile cur;
     bool have = cur.at(P, pair, (int)rank, dw);
@@ -744,31 +758,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       }
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&done_bar[ra.s]);
+      if (lane == 0) mbar_arrive_remote(map_to_rank(&full_kb[ra.s], 0));
       ra.next(NS);
       cur = nxt;
       kb = kb_n;
       pk = pk_n;
       have = have_n;
-    }
-  } else if (warp == 2 && rank == 1 && lane == 0) {
-    // ------------------------------------------------------------ relay (peer CTA)
-    // one cluster-scope arrive on the leader's MMA barrier per dequantized
-    // tile, after all of this CTA's dequant warps have finished it
-    Ring ra;
-    bool ok = true;
-    for (int t = pair; t < P.total_tiles && ok; t += npairs) {
-      TileCursor c;
-      c.at(P, t);
-      for (int kb = 0; kb < c.nkb; ++kb) {
-        if (!mbar_wait_bounded(&deq_done[ra.s], ra.ph, kGemmWaitNs)) {
-          gemm_error(P, DRACO_ERR_TIMEOUT);
-          ok = false;
-          break;
-        }
-        mbar_arrive_remote(map_to_rank(&full_kb[ra.s], 0));
-        ra.next(NS);
-      }
     }
   }
 
