@@ -23,6 +23,13 @@ Multi-GPU (N > 1, under torchrun): the layer set is sharded tensor-parallel,
 column-parallel q/k/v/gate/up and row-parallel o/down (super-block aligned
 K ranges), with an NCCL all-gather after the column-parallel outputs and an
 all-reduce after the row-parallel ones.
+
+The same JSON line carries the second half of the metric under "prefill":
+config 3, the mixed Q4_K/Q6_K prefill dequant-GEMM (gate and up 11008x4096
+Q4_K, down 4096x11008 Q6_K, M = 2048 bf16 tokens, fp32 accumulation), one step
+= one grouped tcgen05 GEMM launch over the three projections (tensor-parallel
+at N > 1: gate/up column shards, down row shard + NCCL all-reduce), reported
+in TFLOP/s with its roofline against the measured dense-bf16 peak.
 """
 
 from __future__ import annotations
@@ -58,6 +65,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--sweep", action="store_true", help="also time batch 4 and 16 (reported under 'batches')")
+    ap.add_argument("--prefill-steps", type=int, default=200, help="timed steps of the prefill GEMM leg")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM leg")
     return ap.parse_args(argv)
 
 
@@ -187,8 +196,149 @@ def run_reference(args):
                                    f"first-touch dequant of the layer set took {res['dequant_s']:.2f} s"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_prefill:
+        from dracort_b200.workloads import encode_specs as enc, prefill_specs
+
+        pspecs = prefill_specs("mixed")
+        pres = cpu_prefill_leg(pspecs, enc(pspecs, args.seed + 100), args.seed)
+        line["prefill"] = {
+            "metric": "prefill dequant-GEMM TFLOP/s", "value": round(pres["tflops"], 5), "unit": "TFLOP/s",
+            "config": {"workload": "config3_mixed_q4k_q6k_prefill_gemm", "tokens_sampled": pres["tokens"]},
+            "cpu_baseline": {"value": round(pres["tflops"], 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+                             "sample": f"{pres['tokens']} tokens through gate, up, down on the fp32 dequant cache"},
+        }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def cpu_prefill_leg(specs, packed, seed, tokens=64):
+    """Reference prefill path on the host: fp32 dequant cache @ a token sample."""
+    from oracle import gguf_oracle as O
+
+    rng = np.random.default_rng(seed + 11)
+    t0 = time.perf_counter()
+    weights = [O.dequantize_matrix(s.qtype, p, s.n_rows, s.k) for s, p in zip(specs, packed)]
+    t_dequant = time.perf_counter() - t0
+    xs = [rng.standard_normal((tokens, s.k)).astype(np.float32) for s in specs]
+    for x, w in zip(xs, weights):
+        O.matmul_f32(x, w)
+    best = []
+    for x, w in zip(xs, weights):
+        ts = []
+        for _ in range(3):
+            t = time.perf_counter()
+            O.matmul_f32(x, w)
+            ts.append(time.perf_counter() - t)
+        best.append(float(np.median(ts)))
+    flops = sum(2 * tokens * s.n_rows * s.k for s in specs)
+    return {"tflops": flops / sum(best) / 1e12, "tokens": tokens, "dequant_s": t_dequant,
+            "step_s": sum(best)}
+
+
+def prefill_leg(args, dev, peaks, rank, world, pg, timed, want_e2e, want_cpu):
+    """Config 3 prefill dequant-GEMM (TP-sharded at N > 1); returns the 'prefill' object."""
+    import torch
+
+    from dracort_b200 import gguf_ops as G
+    from dracort_b200.parallel.prefill import TPPrefillLayer
+    from dracort_b200.telemetry import ClockSampler
+    from dracort_b200.workloads import PREFILL_TOKENS, encode_specs, prefill_specs
+
+    specs = prefill_specs("mixed")
+    packed = encode_specs(specs, args.seed + 100)
+    m = PREFILL_TOKENS
+    layer = TPPrefillLayer(specs, packed, rank, world, m, dev, seed=args.seed, group=pg, copies=2)
+    K = max(1, args.prefill_steps)
+    for i in range(max(3, args.warmup)):
+        layer.step(i)
+    torch.cuda.synchronize()
+    if layer.check_status() != 0:
+        raise RuntimeError(f"prefill GEMM reported status {layer.check_status()}")
+    sampler = ClockSampler(dev.index or 0).start()
+
+    def steps():
+        for i in range(K):
+            layer.step(i)
+
+    ms, tw0, tw1 = timed(steps)
+    clocks = sampler.summary(tw0, tw1)
+    sampler.stop()
+    ms_step = ms / K
+    value = layer.flops_total / (ms_step * 1e-3) / 1e12
+
+    # the GEMM launch alone (no collective), on the launching stream, for the roofline
+    gemm_ms = ms_step
+    if world > 1:
+        def gemm_only():
+            for i in range(K):
+                G.gemm_grouped(layer.problems[i % layer.n_copies], layer.status)
+
+        gemm_ms, _, _ = timed(gemm_only)
+        gemm_ms /= K
+    achieved = layer.flops_local / (gemm_ms * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    out = {
+        "metric": "prefill dequant-GEMM TFLOP/s",
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "ms_per_step": round(ms_step, 5),
+        "steps": K,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "dtype": "bf16",
+        "config": {"workload": "config3_mixed_q4k_q6k_prefill_gemm", "tokens": m,
+                   "weights": "gate,up 11008x4096 Q4_K; down 4096x11008 Q6_K",
+                   "accumulate": "fp32 (TMEM)", "output": "bf16",
+                   "parallelism": f"tp{world}" + (" (gate/up column, down row + NCCL all-reduce)" if world > 1 else ""),
+                   "l2": f"step working set {layer.local_weight_bytes / 1e6:.0f} MB packed weights x 2 copies "
+                         f"rotated + {sum(x.numel() * 2 for x in layer.x_local) / 1e6:.0f} MB bf16 inputs + "
+                         f"{sum(y.numel() * 2 for y in layer.y_local) / 1e6:.0f} MB bf16 outputs > 126 MB L2"},
+        "roofline": {
+            "bound": "tensor",
+            "achieved": round(achieved, 2),
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4),
+            "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4),
+            "traffic": profiled_traffic("gemm_config3_prefill") if world == 1 else None,
+            "peak_source": f"{peaks['source']} MEASURED_PEAKS.json bf16_tflops_sustained (kernel timed in a "
+                           f"{K}-launch loop under the power cap); frac_of_burst uses bf16_tflops",
+            "kernel": f"gemm_kernel, one launch per step, {layer.flops_local} algorithmic FLOP per launch per GPU",
+        },
+        "gpu_launches": layer.launches_per_step * K,
+        "clocks": clocks,
+    }
+    if want_e2e and world == 1:
+        pairs = []  # (device input, pinned host copy); gate and up share one input
+        for x in layer.x_local:
+            if all(x is not a for a, _ in pairs):
+                pairs.append((x, x.cpu().pin_memory()))
+        yh = [torch.empty(y.shape, dtype=y.dtype).pin_memory() for y in layer.y_local]
+        h2d = sum(a.numel() * 2 for a, _ in pairs)
+        d2h = sum(y.numel() * 2 for y in layer.y_local)
+
+        def e2e_steps():
+            for i in range(K):
+                for a, b in pairs:
+                    a.copy_(b, non_blocking=True)
+                layer.step(i)
+                for a, b in zip(yh, layer.y_local):
+                    a.copy_(b, non_blocking=True)
+
+        ms_e, _, _ = timed(e2e_steps)
+        out["e2e"] = {"value": round(layer.flops_total / (ms_e / K * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e / K, 5),
+                      "path": "pinned host bf16 x -> cuda -> gemm_grouped (C ABI) -> pinned host bf16 y, eager"}
+    if want_cpu and rank == 0 and world == 1:
+        res = cpu_prefill_leg(specs, packed, args.seed)
+        out["cpu_baseline"] = {
+            "value": round(res["tflops"], 5), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": (f"reference prefill path (oracle port of gguf._dequantize + GenericGemmKernel.matmul_f32, "
+                       f"fp32) on {res['tokens']} of the {m} tokens through gate, up and down on the warm fp32 "
+                       f"cache: {res['step_s'] * 1e3:.1f} ms; first-touch dequant of the three weights "
+                       f"{res['dequant_s']:.1f} s; numpy/OpenBLAS default threads")}
+    layer.close()
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -375,6 +525,11 @@ def run_ours(args):
 
     sampler.stop()
 
+    # -- prefill dequant-GEMM (config 3), the second half of the metric --------
+    prefill = None
+    if not args.no_prefill:
+        prefill = prefill_leg(args, dev, peaks, rank, world, pg, timed, not args.no_e2e, not args.no_cpu)
+
     # -- CPU baseline (rank 0, N=1) --------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -432,6 +587,8 @@ def run_ours(args):
             line["e2e"] = e2e
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if prefill is not None:
+            line["prefill"] = prefill
         print(json.dumps(line), flush=True)
 
     if layer is not None:

@@ -71,12 +71,18 @@ struct GemmProbDev {
 };
 constexpr int kYDirect = 0, kYTma = 1;  // epilogue: direct stores or staged TMA stores
 
+constexpr int kMaxPairs = 96;     // CTA pairs a launch may use (148 SMs -> 74)
+constexpr int kMaxSched = 4096;   // tiles a precomputed schedule may hold
+
 struct __align__(64) GemmParams {
   CUtensorMap xmap[kGemmMaxProblems];
   CUtensorMap ymap[kGemmMaxProblems];
   GemmProbDev prob[kGemmMaxProblems];
   int* status;
   int n_prob, total_tiles;
+  int sched_ok;                       // 1: pair p runs tiles sched[off[p] .. off[p+1]); 0: strided
+  uint16_t off[kMaxPairs + 1];
+  uint16_t sched[kMaxSched];
   int ns;  // k-block stages
   int x_off, a_off, st_off, smem_bytes;
 };
@@ -116,6 +122,12 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 // scope (remote arrives) or completes through the async proxy (TMA bytes,
 // tcgen05.commit).  A cluster-scope acquire on every poll costs a few hundred
 // cycles, which the MMA issue loop cannot afford three times per k-block.
+
+// L2 prefetch of a contiguous global range by the TMA engine (no completion
+// tracking; 16-byte aligned address, size a multiple of 16)
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 // TMA 2-D tile load into this CTA's shared memory; the transaction bytes are
 // counted on `bar_cluster` (a barrier of the leader CTA of the pair).
@@ -230,14 +242,15 @@ __device__ __forceinline__ uint32_t ldg32(const uint8_t* p) {
   return v;
 }
 
-// One lane's packed inputs for one 64-k block of its row tile (loaded a block
-// ahead of use so the global-load latency hides behind the previous block):
-//  Q4_K: u0 = qs unit; s0..s5 = scale bytes of rows g, g+8; s6, s7 = (d, dmin) of rows g, g+8
-//  Q6_K: u0..u2 = ql/qh units of half q/2; s0, s1 = int8 scales of rows g, g+8; s2 = d of both rows
-//  Q8_0: u0, u1 = qs units of blocks 2q, 2q+1; s0, s1 = d of both blocks for rows g, g+8
+// One lane's packed inputs for one 64-k block of its row tile, 16 registers
+// whatever the type (loaded two blocks ahead of use, so the global-load
+// latency hides behind the dequantization of the blocks before):
+//  Q4_K: u0 = qs unit; u1 = scale bytes 0-7 (row g), 8-11 (row g), 0-3 (row g+8);
+//        u2 = scale bytes 4-11 (row g+8), (d, dmin) of row g, of row g+8
+//  Q6_K: u0..u2 = ql/qh units of half q/2; u3 = int8 scales of rows g, g+8, d of both rows
+//  Q8_0: u0, u1 = qs units of blocks 2q, 2q+1; u2.x, u2.y = d of both blocks for rows g, g+8
 struct Packed {
-  uint4 u0, u1, u2;
-  uint32_t s0, s1, s2, s3, s4, s5, s6, s7;
+  uint4 u0, u1, u2, u3;
 };
 __device__ __forceinline__ void fetch_packed(int qt, const uint8_t* ch, int q, int lane, Packed& pk) {
   const int g = lane >> 2;
@@ -245,20 +258,21 @@ __device__ __forceinline__ void fetch_packed(int qt, const uint8_t* ch, int q, i
     pk.u0 = ldg128(ch + 512 * q + 16 * lane);
     const uint2 a = ldg64(ch + 2048 + 24 * g), b = ldg64(ch + 2056 + 24 * g), c = ldg64(ch + 2064 + 24 * g);
     const uint2 d = ldg64(ch + 2240 + 8 * g);
-    pk.s0 = a.x, pk.s1 = a.y, pk.s2 = b.x, pk.s3 = b.y, pk.s4 = c.x, pk.s5 = c.y, pk.s6 = d.x, pk.s7 = d.y;
+    pk.u1 = make_uint4(a.x, a.y, b.x, b.y);
+    pk.u2 = make_uint4(c.x, c.y, d.x, d.y);
   } else if (qt == kQ6_K) {
     const int n = q >> 1, odd = q & 1;
     pk.u0 = ldg128(ch + 512 * (3 * n) + 16 * lane);
     pk.u1 = ldg128(ch + 512 * (3 * n + 1) + 16 * lane);
     pk.u2 = ldg128(ch + 512 * (3 * n + 2) + 16 * lane);
-    pk.s0 = ldg32(ch + 3072 + 32 * g + 8 * n + 4 * odd);
-    pk.s1 = ldg32(ch + 3072 + 32 * g + 16 + 8 * n + 4 * odd);
-    pk.s2 = ldg32(ch + 3328 + 4 * g);
+    pk.u3.x = ldg32(ch + 3072 + 32 * g + 8 * n + 4 * odd);
+    pk.u3.y = ldg32(ch + 3072 + 32 * g + 16 + 8 * n + 4 * odd);
+    pk.u3.z = ldg32(ch + 3328 + 4 * g);
   } else {
     pk.u0 = ldg128(ch + 512 * (2 * q) + 16 * lane);
     pk.u1 = ldg128(ch + 512 * (2 * q + 1) + 16 * lane);
-    pk.s0 = ldg32(ch + 4096 + 32 * g + 4 * q);
-    pk.s1 = ldg32(ch + 4096 + 32 * g + 16 + 4 * q);
+    pk.u2.x = ldg32(ch + 4096 + 32 * g + 4 * q);
+    pk.u2.y = ldg32(ch + 4096 + 32 * g + 16 + 4 * q);
   }
 }
 
@@ -313,8 +327,8 @@ __device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushor
 __device__ __forceinline__ void deq_q4k(const Packed& pk, int q, int lane, uint8_t* tw) {
   const int g = lane >> 2, t = lane & 3, g0 = g & 1;
   const uint4 U = pk.u0;
-  const uint2 S0 = make_uint2(pk.s0, pk.s1), S1 = make_uint2(pk.s2, pk.s3), S2 = make_uint2(pk.s4, pk.s5);
-  const uint2 DD = make_uint2(pk.s6, pk.s7);
+  const uint2 S0 = make_uint2(pk.u1.x, pk.u1.y), S1 = make_uint2(pk.u1.z, pk.u1.w), S2 = make_uint2(pk.u2.x, pk.u2.y);
+  const uint2 DD = make_uint2(pk.u2.z, pk.u2.w);
   const uint64_t bias = splat2(-8388608.f);
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
@@ -356,13 +370,13 @@ __device__ __forceinline__ void deq_q6k(const Packed& pk, int q, int lane, uint8
   const int odd = q & 1;
   const uint4 P0 = pk.u0, P1 = pk.u1, P2 = pk.u2;
   const uint32_t W[12] = {P0.x, P0.y, P0.z, P0.w, P1.x, P1.y, P1.z, P1.w, P2.x, P2.y, P2.z, P2.w};
-  const uint32_t dd = pk.s2;
+  const uint32_t dd = pk.u3.z;
   const uint64_t bias8 = splat2(-8388736.f);   // -(2^23 + 128): int8 scales stored ^ 0x80
   const uint64_t bias6 = splat2(-8388640.f);   // -(2^23 + 32)
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
     // int8 scales of groups (is, ii) at byte is + 2ii
-    const uint32_t scw = (hi ? pk.s1 : pk.s0) ^ 0x80808080u;
+    const uint32_t scw = (hi ? pk.u3.y : pk.u3.x) ^ 0x80808080u;
     const uint64_t d2 = splat2(hi ? f16hi(dd) : f16lo(dd));
     const uint64_t dl01 = mul2(add2(magic_pair(scw, 0), bias8), d2);  // (is0 ii0, is1 ii0)
     const uint64_t dl23 = mul2(add2(magic_pair(scw, 1), bias8), d2);  // (is0 ii1, is1 ii1)
@@ -392,7 +406,7 @@ __device__ __forceinline__ void deq_q80(const Packed& pk, int lane, uint8_t* tw)
   const uint64_t bias8 = splat2(-8388736.f);
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
-    const uint32_t dw = hi ? pk.s1 : pk.s0;  // d of blocks 2q (lo), 2q+1 (hi)
+    const uint32_t dw = hi ? pk.u2.y : pk.u2.x;  // d of blocks 2q (lo), 2q+1 (hi)
     const uint64_t dA = splat2(g0 ? f16hi(dw) : f16lo(dw)), dB = splat2(g0 ? f16lo(dw) : f16hi(dw));
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -429,6 +443,17 @@ struct Ring {
     }
   }
 };
+
+// i-th pair tile of `pair` (-1 past its last): the host's balanced schedule,
+// or tiles pair, pair + npairs, ... when the launch has too many tiles for it
+__device__ __forceinline__ int tile_at(const GemmParams& P, int pair, int i, int npairs) {
+  if (P.sched_ok) {
+    const int j = (int)P.off[pair] + i;
+    return j < (int)P.off[pair + 1] ? (int)P.sched[j] : -1;
+  }
+  const int t = pair + i * npairs;
+  return t < P.total_tiles ? t : -1;
+}
 
 // pair tile t -> (problem, row pair, 512-token block)
 struct TileCursor {
@@ -513,18 +538,19 @@ __device__ __forceinline__ void stage_rows(uint8_t* buf, int ydtype, int lane, c
 
 // dequant-side view of one pair tile: this CTA's row tile dw of its row group
 struct DeqTile {
-  int t, nkb, qt;
+  int i, nkb, qt;       // i: index of the tile in this pair's sequence
   const uint8_t* base;  // chunk dw of super-block 0 (null: row tile past n_rows)
   int64_t sb_stride;    // bytes between super-blocks of one row tile
-  __device__ bool at(const GemmParams& P, int tile, int rank, int dw) {
-    if (tile >= P.total_tiles) return false;
+  __device__ bool at(const GemmParams& P, int pair, int idx, int npairs, int rank, int dw) {
+    const int tile = tile_at(P, pair, idx, npairs);
+    if (tile < 0) return false;
     TileCursor c;
     c.at(P, tile);
     const GemmProbDev& pr = P.prob[c.p];
     const TiledGeom geo = tiled_geom(pr.qt, pr.n, pr.k);
     const int rg = 2 * c.rp + rank;
     const int nch = rg < pr.n_rg ? rg_tiles(geo, rg) : 0;
-    t = tile;
+    i = idx;
     nkb = c.nkb;
     qt = pr.qt;
     base = dw < nch ? pr.w + slab_offset(geo, rg, 0) + (int64_t)dw * pr.cb : nullptr;
@@ -533,6 +559,12 @@ struct DeqTile {
   }
   __device__ __forceinline__ void fetch(int kb, int lane, Packed& pk) const {
     if (base) fetch_packed(qt, base + (kb >> 2) * sb_stride, kb & 3, lane, pk);
+  }
+  // next k-block of this CTA's sequence (crossing into its next pair tile)
+  __device__ __forceinline__ bool advance(const GemmParams& P, int& kb, int pair, int npairs, int rank, int dw) {
+    if (++kb < nkb) return true;
+    kb = 0;
+    return at(P, pair, i + 1, npairs, rank, dw);
   }
 };
 
@@ -583,10 +615,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     if (lane == 0) {
       Ring rs;
       bool ok = true;
-      for (int t = pair; t < P.total_tiles && ok; t += npairs) {
+      for (int i = 0, t; ok && (t = tile_at(P, pair, i, npairs)) >= 0; ++i) {
         TileCursor c;
         c.at(P, t);
+        // this CTA's packed slabs, pulled into L2 two super-blocks ahead of the
+        // dequant warps' loads
+        const GemmProbDev& pr = P.prob[c.p];
+        const TiledGeom geo = tiled_geom(pr.qt, pr.n, pr.k);
+        const int rg = 2 * c.rp + (int)rank;
+        const bool has_rg = rg < pr.n_rg;
+        const uint8_t* rg_base = has_rg ? pr.w + slab_offset(geo, rg, 0) : nullptr;
+        const uint32_t slab_bytes = has_rg ? (uint32_t)(rg_tiles(geo, rg) * pr.cb) : 0u;
+        if (has_rg)
+          for (int sb = 0; sb < 2 && sb < pr.nb; ++sb) bulk_prefetch_l2(rg_base + (int64_t)sb * slab_bytes, slab_bytes);
         for (int kb = 0; kb < c.nkb; ++kb) {
+          if (has_rg && (kb & 3) == 0 && (kb >> 2) + 2 < pr.nb)
+            bulk_prefetch_l2(rg_base + (int64_t)((kb >> 2) + 2) * slab_bytes, slab_bytes);
           if (!mbar_wait_bounded(&empty_kb[rs.s], rs.ph ^ 1u, kGemmWaitNs)) {
             gemm_error(P, DRACO_ERR_TIMEOUT);
             ok = false;
@@ -611,7 +655,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       Ring rs;
       uint32_t acc_ph = 0;
       bool ok = true;
-      for (int t = pair; t < P.total_tiles && ok; t += npairs, acc_ph ^= 1u) {
+      for (int i = 0, t; ok && (t = tile_at(P, pair, i, npairs)) >= 0; ++i, acc_ph ^= 1u) {
         TileCursor c;
         c.at(P, t);
         for (int kb = 0; kb < c.nkb && ok; ++kb) {
@@ -662,7 +706,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     const uint32_t acc_empty_leader[kNH] = {map_to_rank(&acc_empty[0], 0), map_to_rank(&acc_empty[1], 0)};
     uint32_t acc_ph = 0;
     int nst = 0;  // stores issued by this warp (alternating staging buffers)
-    for (int t = pair; t < P.total_tiles; t += npairs, acc_ph ^= 1u) {
+    for (int i = 0, t; (t = tile_at(P, pair, i, npairs)) >= 0; ++i, acc_ph ^= 1u) {
       TileCursor c;
       c.at(P, t);
       const GemmProbDev& pr = P.prob[c.p];
@@ -728,22 +772,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     // inputs of the next 64-k block are loaded before waiting for a free stage.
     const int dw = warp - kDeqWarp0;
     Ring ra;
-    DeqTile cur;
-    bool have = cur.at(P, pair, (int)rank, dw);
-    int kb = 0;
-    Packed pk;
-    if (have) cur.fetch(0, lane, pk);
-    while (have) {
-      // position and inputs of the next block
-      DeqTile nxt = cur;
-      int kb_n = kb + 1;
-      bool have_n = true;
-      if (kb_n == cur.nkb) {
-        have_n = nxt.at(P, cur.t + npairs, (int)rank, dw);
-        kb_n = 0;
-      }
-      Packed pk_n;
-      if (have_n) nxt.fetch(kb_n, lane, pk_n);
+    // blocks n (c0, being dequantized), n+1 (c1) and n+2 (c2, fetched now)
+    DeqTile c0, c1;
+    int kb0 = 0, kb1 = 0;
+    bool h0 = c0.at(P, pair, 0, npairs, (int)rank, dw);
+    c1 = c0;
+    bool h1 = h0 && c1.advance(P, kb1, pair, npairs, (int)rank, dw);
+    Packed p0, p1;
+    if (h0) c0.fetch(kb0, lane, p0);
+    if (h1) c1.fetch(kb1, lane, p1);
+    while (h0) {
+      DeqTile c2 = c1;
+      int kb2 = kb1;
+      const bool h2 = h1 && c2.advance(P, kb2, pair, npairs, (int)rank, dw);
+      Packed p2;
+      if (h2) c2.fetch(kb2, lane, p2);
+      const DeqTile& cur = c0;
+      const int kb = kb0;
+      const Packed& pk = p0;
       if (!mbar_wait_bounded(&empty_kb[ra.s], ra.ph ^ 1u, kGemmWaitNs)) {
         gemm_error(P, DRACO_ERR_TIMEOUT);
         break;
@@ -760,10 +806,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_to_rank(&full_kb[ra.s], 0));
       ra.next(NS);
-      cur = nxt;
-      kb = kb_n;
-      pk = pk_n;
-      have = have_n;
+      c0 = c1, kb0 = kb1, h0 = h1, p0 = p1;
+      c1 = c2, kb1 = kb2, h1 = h2, p1 = p2;
     }
   }
 
@@ -840,6 +884,76 @@ static int gemm_max_pairs(int* dyn_smem, char* msg, size_t ml) {
   }
   *dyn_smem = dyn;
   return n;
+}
+
+// Balanced assignment of pair tiles to CTA pairs.  A tile of problem p costs
+// nb_p * 4 k-blocks; the static order (tiles pair, pair + npairs, ...) leaves
+// some pairs with an extra long tile at the end of a grouped launch.  The
+// smallest per-pair capacity C for which first-fit-decreasing packs every tile
+// (problems are already ordered longest first) gives the schedule; tiles of
+// one problem go round-robin over the pairs that take them, so the pairs
+// running at the same time share row pairs (weights) in L2.  Kept only when it
+// shortens the longest pair.
+static void build_schedule(GemmParams& P, int pairs) {
+  P.sched_ok = 0;
+  if (P.total_tiles > kMaxSched || pairs > kMaxPairs || P.total_tiles < 1) return;
+  const int np = P.n_prob;
+  int64_t cnt[kGemmMaxProblems], len[kGemmMaxProblems], total = 0;
+  for (int p = 0; p < np; ++p) {
+    cnt[p] = (int64_t)(P.prob[p].n_rg + 1) / 2 * P.prob[p].tblocks;
+    len[p] = (int64_t)P.prob[p].nb * 4;
+    total += cnt[p] * len[p];
+  }
+  // makespan of the static order
+  int64_t strided = 0;
+  for (int b = 0; b < pairs; ++b) {
+    int64_t load = 0;
+    for (int t = b; t < P.total_tiles; t += pairs) {
+      int p = 0;
+      for (int q = 1; q < np; ++q)
+        if (t >= P.prob[q].tile0) p = q;
+      load += len[p];
+    }
+    strided = std::max(strided, load);
+  }
+  static thread_local int quota[kMaxPairs][kGemmMaxProblems];
+  auto pack = [&](int64_t cap) {
+    int64_t load[kMaxPairs] = {0};
+    for (int p = 0; p < np; ++p) {
+      int64_t rem = cnt[p];
+      for (int b = 0; b < pairs; ++b) {
+        const int64_t fit = std::min(rem, (cap - load[b]) / len[p]);
+        quota[b][p] = (int)std::max<int64_t>(fit, 0);
+        load[b] += quota[b][p] * len[p];
+        rem -= quota[b][p];
+      }
+      if (rem > 0) return false;
+    }
+    return true;
+  };
+  int64_t cap = (total + pairs - 1) / pairs;
+  while (cap < strided && !pack(cap)) ++cap;
+  if (cap >= strided) return;
+  // lay out: pair b holds its tiles of problem 0, then 1, ...
+  int pos[kMaxPairs][kGemmMaxProblems];
+  int o = 0;
+  for (int b = 0; b < pairs; ++b) {
+    P.off[b] = (uint16_t)o;
+    for (int p = 0; p < np; ++p) {
+      pos[b][p] = o;
+      o += quota[b][p];
+    }
+  }
+  P.off[pairs] = (uint16_t)o;
+  for (int p = 0; p < np; ++p) {
+    int next = P.prob[p].tile0;
+    int maxq = 0;
+    for (int b = 0; b < pairs; ++b) maxq = std::max(maxq, quota[b][p]);
+    for (int r = 0; r < maxq; ++r)
+      for (int b = 0; b < pairs; ++b)
+        if (quota[b][p] > r) P.sched[pos[b][p]++] = (uint16_t)next++;
+  }
+  P.sched_ok = 1;
 }
 
 int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_t st, char* msg, size_t ml) {
@@ -931,6 +1045,7 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
   P.smem_bytes = P.st_off + staging + 1024;
 
   const int pairs = std::min(max_pairs, tiles);
+  build_schedule(P, pairs);
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;

@@ -11,11 +11,12 @@ _BLOCK_LAYOUTS :75-87, _dequantize :272-497):
 * ``group_size`` is the block size (32 for Q8_0, 256 for the K-quants).
 
 ``dequantize`` returns the fp32 weight bit-identical to gguf._dequantize.
-``quantized_linear`` runs the fused dequant-GEMV kernel: the weight is
-regrouped once into the TILED device layout (cached per weight tensor, the
-way GGUFReader.get_tensor caches its first-access transform, gguf.py:827-834,
-but at 4.5-8.5 bits per weight instead of 32) and every call streams the
-packed blocks through the tensor cores.
+``quantized_linear`` runs the fused dequant kernels: the weight is regrouped
+once into the TILED device layout (cached per weight tensor, the way
+GGUFReader.get_tensor caches its first-access transform, gguf.py:827-834, but
+at 4.5-8.5 bits per weight instead of 32) and every call streams the packed
+blocks through the tensor cores: the dequant-GEMV for decode batches, the
+tcgen05 dequant-GEMM for bf16 prefill batches (see ``gguf_linear``).
 
 ``GGUFLinear`` is an nn.Module drop-in for the nn.Linear projections of the
 model adapters (e.g. draco/models/llama/adapter.py:91-94, 153-155) and of the
@@ -50,6 +51,8 @@ _BITS = {GGML_TYPE_Q8_0: 8, GGML_TYPE_Q4_K: 4, GGML_TYPE_Q6_K: 6}
 
 #: largest activation row count handled by one GEMV launch
 GEMV_MAX_ROWS = N.GEMV_MAX_BATCH
+#: rows (tokens) from which bf16/fp16 activations take the prefill GEMM
+PREFILL_MIN_ROWS = 64
 
 
 def infer_k(qtype: int, row_bytes: int) -> int:
@@ -205,20 +208,36 @@ class GGUFBackend(QuantizationBackend):
 
 
 def gguf_linear(x: torch.Tensor, qtype: int, w_tiled: torch.Tensor, n_rows: int, k: int,
-                bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+                bias: Optional[torch.Tensor] = None, prefill: Optional[bool] = None) -> torch.Tensor:
     """y = x @ dequant(W)^T (+ bias) over the TILED weight; x [..., k] -> [..., n_rows].
 
-    Computes in fp32 and returns the input's floating dtype.
+    Two kernels serve the call, as the reference's executor._linear serves both
+    decode and prefill from one fp32 path (draco/runtime/cpu/executor.py:47-79):
+    * decode (fp32 activations, or fewer than PREFILL_MIN_ROWS rows): the
+      dequant-GEMV, fp32 throughout (1e-3 relative L2 bar);
+    * prefill (bf16/fp16 activations with at least PREFILL_MIN_ROWS rows, or
+      prefill=True): the tcgen05 dequant-GEMM on bf16 activations with fp32
+      accumulation (the bf16 prefill bar, 5e-3 relative L2).
+    Returns the input's floating dtype.
     """
     if x.shape[-1] != k:
         raise DracoFormatError(f"input feature size {x.shape[-1]} != weight row length {k}")
     lead = x.shape[:-1]
     x2 = x.reshape(-1, k)
+    m = x2.shape[0]
+    if prefill is None:
+        prefill = x2.dtype in (torch.bfloat16, torch.float16) and m >= PREFILL_MIN_ROWS
+    if prefill and m > 0:
+        ydt = x.dtype if x.dtype in (torch.bfloat16, torch.float32) else torch.float32
+        y = G.gemm(qtype, w_tiled, x2, n_rows, k, out_dtype=ydt)
+        if bias is not None:
+            y = y + bias.to(device=y.device, dtype=y.dtype)
+        out = y.reshape(*lead, n_rows)
+        return out if out.dtype == x.dtype else out.to(x.dtype)
     if x2.dtype != torch.float32:
         x2 = x2.float()
     if not x2.is_contiguous():
         x2 = x2.contiguous()
-    m = x2.shape[0]
     y = torch.empty((m, n_rows), dtype=torch.float32, device=x2.device)
     b = None
     if bias is not None:

@@ -32,7 +32,7 @@ def decode_reasons(mask: int) -> List[str]:
 class ClockSampler:
     """Background thread sampling SM clock and clock-event reasons every `period_s`."""
 
-    def __init__(self, device_index: int = 0, period_s: float = 0.05) -> None:
+    def __init__(self, device_index: int = 0, period_s: float = 0.005) -> None:
         self.period_s = period_s
         self.samples: List[Dict] = []
         self._stop = threading.Event()

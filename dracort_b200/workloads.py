@@ -4,6 +4,8 @@
 * Config 2 — Q4_K decode GEMV over one Llama-7B-shaped decoder layer's seven
   projections (q, k, v, o 4096x4096; gate, up 11008x4096; down 4096x11008),
   x fp32 at batch 1, 4, 16.
+* Config 3 — mixed Q4_K/Q6_K prefill dequant-GEMM, M = 2048 tokens: gate and
+  up 11008x4096 in Q4_K, down 4096x11008 in Q6_K, bf16 activations.
 * Config 4 — the same projections in Q4_K_M (Q6_K for v and down).
 
 Weights are drawn from N(0, 0.02) with a recorded seed and encoded with the
@@ -64,6 +66,21 @@ def layer_specs(mix: str = "q4_k") -> List[WeightSpec]:
             raise ValueError(f"unknown mix {mix!r}")
         out.append(WeightSpec(name, qt, n, k))
     return out
+
+
+PREFILL_TOKENS = 2048
+
+
+def prefill_specs(mix: str = "mixed") -> List[WeightSpec]:
+    """Config 3: gate/up (Q4_K) and down (Q6_K) of one layer; 'q4'/'q6' make all three one type."""
+    qt_gu = GGML_TYPE_Q6_K if mix == "q6" else GGML_TYPE_Q4_K
+    qt_d = GGML_TYPE_Q4_K if mix == "q4" else GGML_TYPE_Q6_K
+    return [WeightSpec("gate_proj", qt_gu, FFN, HIDDEN), WeightSpec("up_proj", qt_gu, FFN, HIDDEN),
+            WeightSpec("down_proj", qt_d, HIDDEN, FFN)]
+
+
+def prefill_flops(specs: Sequence[WeightSpec], m: int = PREFILL_TOKENS) -> int:
+    return sum(2 * m * s.n_rows * s.k for s in specs)
 
 
 def q8_0_spec() -> List[WeightSpec]:

@@ -91,3 +91,54 @@ def test_gemm_prefill_config_shapes(qtype, n, k):
     m = 2048
     packed, xb, tiled, y = _case(qtype, m, n, k, seed=n + k)
     _check(qtype, packed, xb, tiled, y, n, k, tight=5e-5)
+
+
+def test_gguf_linear_prefill_dispatch():
+    # bf16 activations with >= PREFILL_MIN_ROWS rows take the tcgen05 GEMM; fp32
+    # activations stay on the fp32 GEMV path (reference executor._linear semantics)
+    from dracort_b200.quantization.gguf import PREFILL_MIN_ROWS, GGUFLinear
+
+    rng = np.random.default_rng(21)
+    n, k, m = 384, 1024, 200
+    assert m >= PREFILL_MIN_ROWS
+    packed = Q.encode(12, Q.random_weight(rng, n, k))
+    lin = GGUFLinear.from_packed(12, torch.from_numpy(packed), k, n)
+    x32 = rng.standard_normal((m, k)).astype(np.float32)
+    xb = torch.from_numpy(x32).to(torch.bfloat16).cuda()
+    yb = lin(xb)
+    assert yb.dtype == torch.bfloat16 and yb.shape == (m, n)
+    ref_b = O.linear(xb.float().cpu().numpy(), 12, packed, n, k)
+    assert O.rel_l2(yb.float().cpu().numpy(), ref_b) < PREFILL_TOL
+    y32 = lin(torch.from_numpy(x32).cuda())
+    assert y32.dtype == torch.float32
+    assert O.rel_l2(y32.cpu().numpy(), O.linear(x32, 12, packed, n, k)) < 1e-3
+
+
+def test_gemm_grouped_balanced_schedule():
+    # config-3 shapes at M=512: 102 pair tiles of two lengths (64 and 172 k-blocks)
+    # on 74 SM pairs, where the launch uses its packed tile schedule instead of
+    # the strided order; every output must still be complete and exact
+    rng = np.random.default_rng(33)
+    m = 512
+    specs = [(12, 11008, 4096), (12, 11008, 4096), (14, 4096, 11008)]
+    probs, packs, xs = [], [], []
+    for qt, n, k in specs:
+        packed = Q.encode(qt, Q.random_weight(rng, n, k))
+        xb = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).to(torch.bfloat16).cuda()
+        tiled = G.repack(qt, torch.from_numpy(packed.reshape(-1)).cuda(), n, k)
+        y = torch.full((m, n), float("nan"), device="cuda")
+        probs.append(G.GemmProblem(qt, tiled, xb, y, n, k))
+        packs.append(packed)
+        xs.append(xb)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    G.gemm_grouped(probs, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    for (qt, n, k), p, packed, xb in zip(specs, probs, packs, xs):
+        assert torch.isfinite(p.y).all()
+        wb = G.dequantize(qt, p.w_tiled, n, k, layout="tiled", out_dtype=torch.bfloat16).float()
+        exact = xb.float() @ wb.T
+        err = (torch.linalg.norm(p.y - exact) / torch.linalg.norm(exact)).item()
+        assert err < 5e-5
+        ref = O.linear(xb[:64].float().cpu().numpy(), qt, packed, n, k)  # oracle on a token sample
+        assert O.rel_l2(p.y[:64].cpu().numpy(), ref) < PREFILL_TOL
