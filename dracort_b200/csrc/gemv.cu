@@ -52,6 +52,7 @@ constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kConvWarps = 3;
 constexpr int kThreads = (kConsumerWarps + 1 + kConvWarps) * 32;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
+constexpr int kMaxMboxSlots = 4;
 
 struct GemvProbDev {
   const uint8_t* w;
@@ -70,13 +71,14 @@ struct GemvParams {
   int total_slabs;
   int n_prob, batch, nt, n_cta;
   int w_stage, xs_bytes, su_bytes, stage_bytes, n_stages;
+  int mbox_slots, mbox_off;  // row-group mailbox after the stages in dynamic shared memory
   int cta_start[kMaxCta + 1];
 };
 
 // workspace layout (bytes)
 constexpr int64_t kWsStatus = 0;
 constexpr int64_t kWsCounters = 256;
-constexpr int64_t kWsCountersBytes = (int64_t)kMaxCta * 2 * 4;
+constexpr int64_t kWsCountersBytes = (int64_t)kMaxCta * 2 * kRowWarps * 4;  // per (CTA, end, row tile)
 static inline int64_t align256(int64_t v) { return (v + 255) & ~(int64_t)255; }
 
 // ---------------------------------------------------------------------------
@@ -177,6 +179,7 @@ __device__ __forceinline__ void zero4(int (&d)[4]) { d[0] = d[1] = d[2] = d[3] =
 __device__ __forceinline__ float digits(int hi, int lo) { return __int2float_rn(hi * 256 + lo); }
 
 constexpr uint32_t kNib = 0x0F0F0F0Fu;
+constexpr uint32_t kNibHi = 0xF0F0F0F0u;
 
 // ---------------------------------------------------------------------------
 // activation conversion of one slab (problem pr, super-block j) by one warp.
@@ -209,18 +212,25 @@ __device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProb
   for (int b = 0; b < P.batch; ++b) {
     const float* xp = pr.x + (int64_t)b * pr.ldx + kk0;
     float v[8];
+    if (kk0 + 8 <= pr.k && (reinterpret_cast<uintptr_t>(xp) & 15) == 0) {
+      const float4 lo4 = __ldg(reinterpret_cast<const float4*>(xp));
+      const float4 hi4 = __ldg(reinterpret_cast<const float4*>(xp) + 1);
+      v[0] = lo4.x, v[1] = lo4.y, v[2] = lo4.z, v[3] = lo4.w;
+      v[4] = hi4.x, v[5] = hi4.y, v[6] = hi4.z, v[7] = hi4.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = (kk0 + i < pr.k) ? __ldg(xp + i) : 0.f;
+    }
     float amax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[i] = (kk0 + i < pr.k) ? __ldg(xp + i) : 0.f;
-      amax = fmaxf(amax, fabsf(v[i]));
-    }
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    int e = 0;
-    if (amax > 0.f && amax <= 3.0e38f) e = ilogbf(amax) - 13;
+    // e = floor(log2 max|x|) - 13 from the exponent field (clamped, so subnormal
+    // and zero groups take the smallest step and inf/nan the largest)
+    int e = ((__float_as_int(amax) >> 23) & 0xFF) - 127 - 13;
     e = max(-110, min(110, e));
-    const float inv = ldexpf(1.f, -e), u = ldexpf(1.f, e);
+    const float inv = __int_as_float((127 - e) << 23), u = __int_as_float((127 + e) << 23);
     int hi[8], lo[8], qs = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -243,16 +253,26 @@ __device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProb
     }
     uint8_t* base = xs + (size_t)m * kCols * 32 + (size_t)t0 * 8 + 4 * kap;
     if constexpr (kDiag) {
+      // The stages start zeroed and a cell of this lane only ever holds digits
+      // at the slot of a Q6_K slab or at the slot of a Q4_K / Q8_0 slab: write
+      // this slab's slot and clear the other type's, if it differs.
       const int slot = (q6 ? (2 * m + kap) : m) % G;
+      const int other = (q6 ? m : (2 * m + kap)) % G;
 #pragma unroll
-      for (int jj = 0; jj < G; ++jj)
+      for (int dg = 0; dg < 2; ++dg) {
+        const int col = (slot * Bp + b) * 2 + dg;
+#pragma unroll
+        for (int tt = 0; tt < 2; ++tt)
+          *reinterpret_cast<uint32_t*>(base + col * 32 + tt * 8) = dg ? dl[tt] : dh[tt];
+      }
+      if (other != slot) {
 #pragma unroll
         for (int dg = 0; dg < 2; ++dg) {
-          const int col = (jj * Bp + b) * 2 + dg;
+          const int col = (other * Bp + b) * 2 + dg;
 #pragma unroll
-          for (int tt = 0; tt < 2; ++tt)
-            *reinterpret_cast<uint32_t*>(base + col * 32 + tt * 8) = (jj == slot) ? (dg ? dl[tt] : dh[tt]) : 0u;
+          for (int tt = 0; tt < 2; ++tt) *reinterpret_cast<uint32_t*>(base + col * 32 + tt * 8) = 0u;
         }
+      }
     } else {
       (void)q6;
 #pragma unroll
@@ -312,8 +332,8 @@ __device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, 
       const uint2 bl = lds64(xs + (2 * q) * kColBytes + lane * 8);
       const uint2 bh = lds64(xs + (2 * q + 1) * kColBytes + lane * 8);
       imma_u8_k32(fr[(2 * q) / G], v.x & kNib, v.z & kNib, v.y & kNib, v.w & kNib, bl.x, bl.y);
-      imma_u8_k32(fr[(2 * q + 1) / G], (v.x >> 4) & kNib, (v.z >> 4) & kNib, (v.y >> 4) & kNib, (v.w >> 4) & kNib,
-                  bh.x, bh.y);
+      // high nibbles in place: 16 x the quant (exact in the int32 sum)
+      imma_u8_k32(fr[(2 * q + 1) / G], v.x & kNibHi, v.z & kNibHi, v.y & kNibHi, v.w & kNibHi, bh.x, bh.y);
     }
     const int b = t % Bp;
 #pragma unroll
@@ -324,8 +344,9 @@ __device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, 
       q4k_sm(A1, B1, C1, d1, m1, j, f * G >= 4, ds1, mm1);
       const float4 s = lds128f(su + (j * 4 + b) * 16);
       const float S = s.x + s.y;
-      acc[0][0] = fmaf(ds0 * s.z, digits(fr[f][0], fr[f][1]), fmaf(-mm0, S, acc[0][0]));
-      acc[0][1] = fmaf(ds1 * s.z, digits(fr[f][2], fr[f][3]), fmaf(-mm1, S, acc[0][1]));
+      const float us = (j & 1) ? s.z * 0.0625f : s.z;  // odd sub-blocks: high nibbles entered as 16 x q
+      acc[0][0] = fmaf(ds0 * us, digits(fr[f][0], fr[f][1]), fmaf(-mm0, S, acc[0][0]));
+      acc[0][1] = fmaf(ds1 * us, digits(fr[f][2], fr[f][3]), fmaf(-mm1, S, acc[0][1]));
     }
   } else {
 #pragma unroll
@@ -523,14 +544,25 @@ __device__ __forceinline__ int cta_of_slab(const GemvParams& P, int s) {
   return lo;
 }
 
-// Called by all 16 consumer warps at the end of a row group (or of the CTA's
-// range).  Every consumer thread passes the same named barriers.
+// Row-group mailbox in shared memory: for the L-th row group of the CTA's
+// range (slot L % mbox_slots), the two consumer warps sharing row tile rw
+// (one per slab parity) each deposit their partial sums in their half; the
+// second to arrive adds both and finishes the rows.  No CTA-wide barrier: each
+// warp moves on to its next slabs as soon as it has deposited.
+struct Mailbox {
+  float* data;  // [slots][2 parities][kRowWarps][32 lanes][2 NT]
+  int* tag;     // [slots][kRowWarps]: 1 + L of the row group held, 0 = free
+  int* cnt;     // [slots][kRowWarps]: arrivals so far
+  int slots;
+};
+
+// Called by each consumer warp at the end of its part of a row group.
 template <int G, int NT>
-__device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int s_begin, int s_end, int warp, int lane,
-                                float (&acc)[NT][2], float* red, int* s_flag) {
+__device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s_begin, int s_end, int warp, int lane,
+                                float (&acc)[NT][2], const Mailbox& mb, bool& failed) {
   const GemvProbDev& pr = P.prob[p];
   const int nrt = rg_tile_count(pr, rg);
-  const int rw = warp & (kRowWarps - 1);
+  const int rw = warp & (kRowWarps - 1), par = warp / kRowWarps;
   if constexpr (G > 1) {
     // diagonal layout: lanes t with the same batch slot hold different sub-blocks
 #pragma unroll
@@ -539,76 +571,97 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int s_begin,
       acc[0][hh] += __shfl_xor_sync(0xffffffffu, acc[0][hh], 2);
     }
   }
-  // 1. fold the two slab parities: warps 8..15 hand their sums to warps 0..7
-  float* rp = red + ((rw * 32 + lane) * NT * 2);
-  if (warp >= kRowWarps) {
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      rp[2 * nt] = acc[nt][0];
-      rp[2 * nt + 1] = acc[nt][1];
+  const int slot = L % mb.slots;
+  volatile int* tagp = mb.tag + slot * kRowWarps + rw;
+  // the slot may still hold an older row group whose second warp has not
+  // arrived yet (the stage ring bounds how far ahead a warp runs)
+  if (lane == 0 && !failed) {
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+      const int tg = *tagp;
+      if (tg == 0 || tg == L + 1) break;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        record_error(P, DRACO_ERR_TIMEOUT);
+        failed = true;
+        break;
+      }
     }
+    atomicCAS(const_cast<int*>(tagp), 0, L + 1);
   }
-  consumers_sync();
-  if (warp < kRowWarps) {
+  failed = __shfl_sync(0xffffffffu, (int)failed, 0) != 0;
+  float* mine = mb.data + ((((int64_t)slot * 2 + par) * kRowWarps + rw) * 32 + lane) * (NT * 2);
+  float* other = mb.data + ((((int64_t)slot * 2 + (par ^ 1)) * kRowWarps + rw) * 32 + lane) * (NT * 2);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      acc[nt][0] += rp[2 * nt];
-      acc[nt][1] += rp[2 * nt + 1];
-    }
+  for (int nt = 0; nt < NT; ++nt) {
+    mine[2 * nt] = acc[nt][0];
+    mine[2 * nt + 1] = acc[nt][1];
   }
+  __threadfence_block();
+  __syncwarp();
+  int old = 0;
+  if (lane == 0) old = atomicAdd(mb.cnt + slot * kRowWarps + rw, 1);
+  old = __shfl_sync(0xffffffffu, old, 0);
+  if (old == 0) return;  // the partner finishes the rows
+  __threadfence_block();
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    acc[nt][0] += other[2 * nt];
+    acc[nt][1] += other[2 * nt + 1];
+  }
+  __syncwarp();
+  if (lane == 0) {  // free the slot for row group L + slots
+    mb.cnt[slot * kRowWarps + rw] = 0;
+    __threadfence_block();
+    *tagp = 0;
+  }
+  if (rw >= nrt) return;
   const int rg_start = pr.slab0 + rg * pr.nb, rg_end = rg_start + pr.nb;
   if (s_begin <= rg_start && rg_end <= s_end) {
-    if (warp < nrt) write_rows<NT>(P, pr, rg, rw, lane, acc);
-    consumers_sync();  // `red` is reused by the next row group
+    write_rows<NT>(P, pr, rg, rw, lane, acc);
     return;
   }
-  // 2. split row group: publish the partial, the last contributor reduces
+  // split row group: publish this CTA's partial of row tile rw; the last
+  // contributing CTA adds them in CTA order and writes the rows
   const int cta = blockIdx.x;
-  const int slot = (s_begin >= rg_start) ? 0 : 1;
-  if (warp < kRowWarps) {
-    float* part = reinterpret_cast<float*>(P.ws + P.part_off) +
-                  ((((int64_t)cta * 2 + slot) * kRowWarps + warp) * 32 + lane) * (NT * 2);
+  const int cslot = (s_begin >= rg_start) ? 0 : 1;
+  float* part = reinterpret_cast<float*>(P.ws + P.part_off) +
+                ((((int64_t)cta * 2 + cslot) * kRowWarps + rw) * 32 + lane) * (NT * 2);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      __stcg(part + 2 * nt, acc[nt][0]);
-      __stcg(part + 2 * nt + 1, acc[nt][1]);
-    }
-    __threadfence();
+  for (int nt = 0; nt < NT; ++nt) {
+    __stcg(part + 2 * nt, acc[nt][0]);
+    __stcg(part + 2 * nt + 1, acc[nt][1]);
   }
-  consumers_sync();
-  if (threadIdx.x == 0) {
-    const int c_first = cta_of_slab(P, rg_start);
-    const int c_last = cta_of_slab(P, rg_end - 1);
+  __threadfence();
+  __syncwarp();
+  const int c_first = cta_of_slab(P, rg_start);
+  const int c_last = cta_of_slab(P, rg_end - 1);
+  int last = 0;
+  if (lane == 0) {
     const int slot_first = (P.cta_start[c_first] >= rg_start) ? 0 : 1;
-    unsigned int* cnt = reinterpret_cast<unsigned int*>(P.ws + P.cnt_off) + (c_first * 2 + slot_first);
-    const unsigned int old = atomicAdd(cnt, 1u);
-    const bool last = (old == (unsigned int)(c_last - c_first));
+    unsigned int* cnt = reinterpret_cast<unsigned int*>(P.ws + P.cnt_off) + (c_first * 2 + slot_first) * kRowWarps + rw;
+    const unsigned int o = atomicAdd(cnt, 1u);
+    last = (o == (unsigned int)(c_last - c_first));
     if (last) {
       atomicExch(cnt, 0u);
       __threadfence();
     }
-    *s_flag = last ? (1 + c_first + (c_last << 12)) : 0;
   }
-  consumers_sync();
-  const int f = *s_flag;
-  if (f && warp < nrt) {
-    const int c_first = (f - 1) & 0xFFF, c_last = (f - 1) >> 12;
-    float sum[NT][2];
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+  float sum[NT][2];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) sum[nt][0] = sum[nt][1] = 0.f;
-    for (int c = c_first; c <= c_last; ++c) {
-      const int sl = (P.cta_start[c] >= rg_start) ? 0 : 1;
-      const float* q = reinterpret_cast<const float*>(P.ws + P.part_off) +
-                       ((((int64_t)c * 2 + sl) * kRowWarps + warp) * 32 + lane) * (NT * 2);
+  for (int nt = 0; nt < NT; ++nt) sum[nt][0] = sum[nt][1] = 0.f;
+  for (int c = c_first; c <= c_last; ++c) {
+    const int sl = (P.cta_start[c] >= rg_start) ? 0 : 1;
+    const float* q = reinterpret_cast<const float*>(P.ws + P.part_off) +
+                     ((((int64_t)c * 2 + sl) * kRowWarps + rw) * 32 + lane) * (NT * 2);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        sum[nt][0] += __ldcg(q + 2 * nt);
-        sum[nt][1] += __ldcg(q + 2 * nt + 1);
-      }
+    for (int nt = 0; nt < NT; ++nt) {
+      sum[nt][0] += __ldcg(q + 2 * nt);
+      sum[nt][1] += __ldcg(q + 2 * nt + 1);
     }
-    write_rows<NT>(P, pr, rg, warp, lane, sum);
   }
-  consumers_sync();  // s_flag and `red` are reused by the next row group
+  write_rows<NT>(P, pr, rg, rw, lane, sum);
 }
 
 // ---------------------------------------------------------------------------
@@ -653,8 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full_bar[kMaxStages];
   __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
-  __shared__ __align__(16) float red[kRowWarps * 32 * 2 * NT];
-  __shared__ int s_flag;
+  __shared__ int mbox_tag[kMaxMboxSlots * kRowWarps], mbox_cnt[kMaxMboxSlots * kRowWarps];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
@@ -662,13 +714,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   const int NS = P.n_stages;
   const int n = s_end - s_begin;
 
-  // zero the stages once: columns of padded batch slots are never rewritten
-  {
-    uint4* z = reinterpret_cast<uint4*>(smem);
-    const int n16 = (NS * P.stage_bytes) >> 4;
+  // zero the activation slices of the stages once: in the dense layout the
+  // columns of padded batch slots are never written, in the diagonal layout
+  // only the digit slots are
+  for (int st = 0; st < NS; ++st) {
+    uint4* z = reinterpret_cast<uint4*>(smem + (size_t)st * P.stage_bytes + P.w_stage);
+    const int n16 = (P.xs_bytes + P.su_bytes) >> 4;
     for (int i = threadIdx.x; i < n16; i += blockDim.x) z[i] = make_uint4(0, 0, 0, 0);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before the TMA engine writes the stages
   }
+  for (int i = threadIdx.x; i < kMaxMboxSlots * kRowWarps; i += blockDim.x) mbox_tag[i] = mbox_cnt[i] = 0;
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&full_bar[i], 2);  // producer (with the weight bytes) + converter
@@ -742,9 +796,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   // walking its range, so every consumer warp still reaches each named
   // barrier and the kernel ends.  The status word tells the host.
   bool failed = false;
+  const Mailbox mb = {reinterpret_cast<float*>(smem + P.mbox_off), mbox_tag, mbox_cnt, P.mbox_slots};
   SlabCursor cur;
   cur.seek(P, s_begin);
   int s = s_begin;
+  int L = 0;  // row groups finished in this CTA's range
   while (s < s_end) {
     const GemvProbDev& pr = P.prob[cur.p];
     const int seg = min(pr.nb - cur.j, s_end - s);  // slabs of this row group in our range
@@ -760,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     else
       consume_segment<kQ8_0, G, NT>(P, smem, full_bar, empty_bar, i_first, i0 + seg, NS, rw, nrt, pr.cb, lane,
                                     failed, acc);
-    finish_rowgroup<G, NT>(P, cur.p, cur.rg, s_begin, s_end, warp, lane, acc, red, &s_flag);
+    finish_rowgroup<G, NT>(P, cur.p, cur.rg, L++, s_begin, s_end, warp, lane, acc, mb, failed);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
     s += seg;
@@ -786,9 +842,9 @@ struct HostPlan {
 
 static int nt_of_batch(int batch) { return batch <= 4 ? 1 : batch <= 8 ? 2 : batch <= 16 ? 4 : 8; }
 
-// Dynamic shared memory budget of the GEMV kernel (stages); static shared
-// memory (barriers, reduction buffer) comes on top.
-constexpr int kSmemBudget = 200 * 1024;
+// Dynamic shared memory budget of the GEMV kernel (stages + row-group
+// mailbox); static shared memory (barriers, mailbox tags) comes on top.
+constexpr int kSmemBudget = 216 * 1024;
 
 static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, HostPlan& hp, char* msg,
                        size_t ml) {
@@ -835,12 +891,16 @@ static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_
   P.total_slabs = (int)slab0;
   P.w_stage = w_stage;
   P.stage_bytes = w_stage + P.xs_bytes + P.su_bytes;
-  P.n_stages = std::min(kMaxStages, kSmemBudget / P.stage_bytes);
+  // mailbox: slots x 2 parities x row tiles x 32 lanes x 2 NT floats
+  P.mbox_slots = std::max(1, std::min(kMaxMboxSlots, 4 / NT));
+  const int mbox_bytes = P.mbox_slots * 2 * kRowWarps * 32 * 2 * NT * 4;
+  P.n_stages = std::min(kMaxStages, (kSmemBudget - mbox_bytes) / P.stage_bytes);
   if (P.n_stages < 2) {
     snprintf(msg, ml, "gemv: stage of %d bytes does not fit shared memory twice", P.stage_bytes);
     return false;
   }
-  hp.smem_bytes = (size_t)P.n_stages * P.stage_bytes;
+  P.mbox_off = P.n_stages * P.stage_bytes;
+  hp.smem_bytes = (size_t)P.mbox_off + mbox_bytes;
   hp.ws_needed = (size_t)off;
 
   // byte-balanced slab ranges per CTA
