@@ -67,6 +67,8 @@ def parse_args(argv=None):
     ap.add_argument("--sweep", action="store_true", help="also time batch 4 and 16 (reported under 'batches')")
     ap.add_argument("--prefill-steps", type=int, default=200, help="timed steps of the prefill GEMM leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM leg")
+    ap.add_argument("--moe-steps", type=int, default=50, help="timed steps of the MoE (config 5) leg")
+    ap.add_argument("--no-moe", action="store_true", help="skip the MoE expert-parallel leg")
     return ap.parse_args(argv)
 
 
@@ -341,6 +343,66 @@ def prefill_leg(args, dev, peaks, rank, world, pg, timed, want_e2e, want_cpu):
     return out
 
 
+def moe_leg(args, dev, peaks, rank, world, pg, timed):
+    """Config 5: Mixtral-shaped MoE FFN, expert-parallel over the ranks."""
+    import torch
+
+    from dracort_b200.parallel.moe import EPMoELayer
+    from dracort_b200.telemetry import ClockSampler
+    from dracort_b200.workloads import MOE_FFN, MOE_HIDDEN, MOE_TOKENS, MOE_TOP_K, moe_experts
+
+    experts = moe_experts(args.seed + 500)
+    n_exp = len(experts)
+    if n_exp % world or MOE_TOKENS % world:
+        return {"unavailable": f"{n_exp} experts / {MOE_TOKENS} tokens do not split over {world} ranks"}
+    g = torch.Generator().manual_seed(args.seed + 501)
+    x_all = torch.randn((MOE_TOKENS, MOE_HIDDEN), generator=g).to(torch.bfloat16)
+    logits_all = torch.randn((MOE_TOKENS, n_exp), generator=g)
+    tl = MOE_TOKENS // world
+    x = x_all[rank * tl:(rank + 1) * tl].to(dev)
+    logits = logits_all[rank * tl:(rank + 1) * tl].to(dev)
+    layer = EPMoELayer(experts, MOE_HIDDEN, MOE_FFN, MOE_TOP_K, rank, world, dev, group=pg)
+    for _ in range(max(3, args.warmup)):
+        layer.forward(x, logits)
+    torch.cuda.synchronize()
+    if layer.check_status() != 0:
+        raise RuntimeError(f"MoE GEMM reported status {layer.check_status()}")
+    K = max(1, args.moe_steps)
+    sampler = ClockSampler(dev.index or 0).start()
+
+    def steps():
+        for _ in range(K):
+            layer.forward(x, logits)
+
+    ms, tw0, tw1 = timed(steps)
+    clocks = sampler.summary(tw0, tw1)
+    sampler.stop()
+    ms_step = ms / K
+    flops = 2 * 3 * MOE_HIDDEN * MOE_FFN * MOE_TOKENS * MOE_TOP_K  # routed expert FLOP, whole job
+    wbytes = sum(p.size for e in experts for p in e[1:])          # every expert's packed weights, read once
+    gbs = wbytes / (ms_step * 1e-3) / 1e9
+    return {
+        "metric": "MoE FFN layer (config 5) TFLOP/s of routed expert work",
+        "value": round(flops / (ms_step * 1e-3) / 1e12, 3),
+        "unit": "TFLOP/s",
+        "ms_per_step": round(ms_step, 5),
+        "tokens_per_s": round(MOE_TOKENS / (ms_step * 1e-3), 1),
+        "steps": K,
+        "scaling": "strong",
+        "dtype": "bf16",
+        "config": {"workload": "config5_mixtral_moe_ffn", "experts": n_exp, "top_k": MOE_TOP_K,
+                   "hidden": MOE_HIDDEN, "ffn": MOE_FFN, "tokens": MOE_TOKENS, "qtype": "Q4_K",
+                   "parallelism": f"ep{world}" + (" (NCCL all-to-all dispatch + combine)" if world > 1 else ""),
+                   "step": "route -> dispatch -> grouped gate/up GEMM -> SwiGLU -> grouped down GEMM -> combine"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"] * world, "unit": "GB/s",
+                     "frac": round(gbs / (peaks["hbm_gbs"] * world), 4),
+                     "note": f"{wbytes} B of packed expert weights per step (each expert read once) over the "
+                             f"whole step time incl. routing and collectives"},
+        "gpu_launches": 2 * K,
+        "clocks": clocks,
+    }
+
+
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
@@ -530,6 +592,10 @@ def run_ours(args):
     if not args.no_prefill:
         prefill = prefill_leg(args, dev, peaks, rank, world, pg, timed, not args.no_e2e, not args.no_cpu)
 
+    moe = None
+    if not args.no_moe:
+        moe = moe_leg(args, dev, peaks, rank, world, pg, timed)
+
     # -- CPU baseline (rank 0, N=1) --------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -589,6 +655,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if prefill is not None:
             line["prefill"] = prefill
+        if moe is not None:
+            line["moe"] = moe
         print(json.dumps(line), flush=True)
 
     if layer is not None:

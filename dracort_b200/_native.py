@@ -54,7 +54,7 @@ EXPORTED_SYMBOLS = (
 
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
-GEMM_MAX_PROBLEMS = 4
+GEMM_MAX_PROBLEMS = 16
 
 
 class GemvProblem(ctypes.Structure):

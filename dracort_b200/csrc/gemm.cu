@@ -46,7 +46,7 @@
 
 namespace draco {
 
-constexpr int kGemmMaxProblems = 4;
+constexpr int kGemmMaxProblems = DRACO_GEMM_MAX_PROBLEMS;
 constexpr int kBM = 128;                          // weight rows per CTA (one TILED row group)
 constexpr int kTokCta = 128;                      // tokens per CTA per accumulator
 constexpr int kNH = 2;                            // accumulators per CTA

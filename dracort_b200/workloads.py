@@ -7,6 +7,8 @@
 * Config 3 — mixed Q4_K/Q6_K prefill dequant-GEMM, M = 2048 tokens: gate and
   up 11008x4096 in Q4_K, down 4096x11008 in Q6_K, bf16 activations.
 * Config 4 — the same projections in Q4_K_M (Q6_K for v and down).
+* Config 5 — Mixtral-8x7B-shaped MoE FFN: 8 Q4_K experts (gate/up
+  14336x4096, down 4096x14336), top-2 routing, 256 bf16 tokens.
 
 Weights are drawn from N(0, 0.02) with a recorded seed and encoded with the
 synthetic GGUF encoders (dracort_b200.format.quantize); activations from
@@ -81,6 +83,25 @@ def prefill_specs(mix: str = "mixed") -> List[WeightSpec]:
 
 def prefill_flops(specs: Sequence[WeightSpec], m: int = PREFILL_TOKENS) -> int:
     return sum(2 * m * s.n_rows * s.k for s in specs)
+
+
+MOE_EXPERTS, MOE_HIDDEN, MOE_FFN, MOE_TOP_K, MOE_TOKENS = 8, 4096, 14336, 2, 256
+
+
+def moe_experts(seed: int, n_exp: int = MOE_EXPERTS, hidden: int = MOE_HIDDEN, ffn: int = MOE_FFN,
+                qtype: int = GGML_TYPE_Q4_K):
+    """Config-5 experts: (qtype, gate, up, down) packed payloads.  One expert is
+    encoded from seeded N(0, 0.02) weights; the others are seeded row
+    permutations of its packed rows (each row a valid quantized N(0, 0.02)
+    row), which keeps the set distinct without encoding 1.4 G weights."""
+    rng = np.random.default_rng(seed)
+    base = (encode(qtype, random_weight(rng, ffn, hidden)), encode(qtype, random_weight(rng, ffn, hidden)),
+            encode(qtype, random_weight(rng, hidden, ffn)))
+    out = [(qtype,) + base]
+    for _ in range(1, n_exp):
+        out.append((qtype, base[0][rng.permutation(ffn)], base[1][rng.permutation(ffn)],
+                    base[2][rng.permutation(hidden)]))
+    return out
 
 
 def q8_0_spec() -> List[WeightSpec]:

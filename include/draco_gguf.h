@@ -198,7 +198,7 @@ typedef struct draco_gemm_problem {
   int64_t ldy;
 } draco_gemm_problem;
 
-#define DRACO_GEMM_MAX_PROBLEMS 4
+#define DRACO_GEMM_MAX_PROBLEMS 16
 
 /* Prefill dequant-GEMM over 1..DRACO_GEMM_MAX_PROBLEMS weights in one
  * persistent launch: tcgen05 tensor-core MMAs (bf16 x bf16, fp32 accumulate

@@ -1,0 +1,67 @@
+"""GPU parity of the MoE FFN with GGUF experts on the tcgen05 dequant-GEMM.
+
+Reference: ExpertGroup.forward (expert.py:77-129) with TopKRouter
+(router.py:106-111) on the oracle's fp32 dequantized weights.  The GPU path
+runs bf16 activations (x, the SwiGLU product and the expert outputs are bf16
+tensors), so the bar is the bf16 prefill one, 5e-3 relative L2.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import gguf_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():  # pragma: no cover
+    pytest.skip("needs a CUDA GPU", allow_module_level=True)
+
+import torch.nn.functional as F  # noqa: E402
+
+from dracort_b200.format import quantize as Q  # noqa: E402
+from dracort_b200.parallel.moe import EPMoELayer, TopKRouter  # noqa: E402
+
+PREFILL_TOL = 5e-3
+
+
+def _experts(rng, n_exp, hidden, ffn, qtypes):
+    out = []
+    for e in range(n_exp):
+        qt = qtypes[e % len(qtypes)]
+        out.append((qt, Q.encode(qt, Q.random_weight(rng, ffn, hidden)), Q.encode(qt, Q.random_weight(rng, ffn, hidden)),
+                    Q.encode(qt, Q.random_weight(rng, hidden, ffn))))
+    return out
+
+
+def _reference(x, logits, experts, hidden, ffn, top_k):
+    idx, w = TopKRouter(len(experts), top_k).route(logits)
+    out = torch.zeros((x.shape[0], hidden))
+    for e, (qt, g, u, d) in enumerate(experts):
+        mask = (idx == e).any(dim=-1)
+        if not mask.any():
+            continue
+        t = mask.nonzero(as_tuple=True)[0]
+        wg = torch.from_numpy(O.dequantize_matrix(qt, g, ffn, hidden))
+        wu = torch.from_numpy(O.dequantize_matrix(qt, u, ffn, hidden))
+        wd = torch.from_numpy(O.dequantize_matrix(qt, d, hidden, ffn))
+        xe = x[t]
+        ye = (F.silu(xe @ wg.T) * (xe @ wu.T)) @ wd.T
+        we = (w[t] * (idx[t] == e).float()).sum(dim=-1, keepdim=True)
+        out.index_add_(0, t, ye * we)
+    return out
+
+
+@pytest.mark.parametrize("qtypes", [(12,), (12, 14)])
+def test_moe_layer_matches_expert_group(qtypes):
+    rng = np.random.default_rng(7)
+    n_exp, hidden, ffn, top_k, tokens = 8, 512, 1024, 2, 40
+    experts = _experts(rng, n_exp, hidden, ffn, qtypes)
+    x = torch.from_numpy(rng.standard_normal((tokens, hidden)).astype(np.float32)).to(torch.bfloat16)
+    logits = torch.from_numpy(rng.standard_normal((tokens, n_exp)).astype(np.float32))
+    layer = EPMoELayer(experts, hidden, ffn, top_k, 0, 1, torch.device("cuda"))
+    y = layer.forward(x.cuda(), logits.cuda())
+    torch.cuda.synchronize()
+    assert layer.check_status() == 0
+    ref = _reference(x.float(), logits, experts, hidden, ffn, top_k)
+    assert O.rel_l2(y.cpu().numpy(), ref.numpy()) < PREFILL_TOL
