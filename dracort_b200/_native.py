@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv",
     "draco_gguf_gemv_grouped_noalloc",
     "draco_gguf_gemm",
+    "draco_swiglu_bf16",
 )
 
 DTYPE_F32 = 0
@@ -141,6 +142,8 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_gemv_grouped_noalloc.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp]
         lib.draco_gguf_gemm.restype = c_int
         lib.draco_gguf_gemm.argtypes = [ctypes.POINTER(GemmProblem), c_int, vp, vp]
+        lib.draco_swiglu_bf16.restype = c_int
+        lib.draco_swiglu_bf16.argtypes = [vp, vp, vp, i64, vp]
         lib.draco_gguf_gemv.restype = c_int
         lib.draco_gguf_gemv.argtypes = [c_int, vp, vp, vp, vp, c_int, i64, i64, vp, ctypes.c_size_t, vp]
         _lib = lib

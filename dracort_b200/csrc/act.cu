@@ -1,0 +1,53 @@
+// act.cu — SwiGLU product of a gated MLP, out = bf16(silu(gate) * up), computed
+// in fp32 from bf16 inputs with one rounding.  Sits between the gate/up and
+// the down dequant-GEMMs of an expert or decoder MLP: the reference's
+// Expert.forward (draco/models/moe/expert.py:47-49) and the Llama MLP apply
+// act_fn(gate_proj(x)) * up_proj(x) there.  HBM-bound: 6 bytes per element.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "internal.h"
+
+namespace draco {
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
+__device__ __forceinline__ uint32_t swiglu2(uint32_t g2, uint32_t u2) {
+  const float g0 = __uint_as_float(g2 << 16), g1 = __uint_as_float(g2 & 0xFFFF0000u);
+  const float u0 = __uint_as_float(u2 << 16), u1 = __uint_as_float(u2 & 0xFFFF0000u);
+  __nv_bfloat162 r = __floats2bfloat162_rn(silu_mul(g0, u0), silu_mul(g1, u1));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// 8 elements per thread and iteration on 16-byte vectors; the last n % 8
+// elements by single threads
+__global__ void swiglu_bf16_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u,
+                                   uint16_t* __restrict__ o, int64_t n) {
+  const int64_t n8 = n >> 3;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const uint4* g4 = reinterpret_cast<const uint4*>(g);
+  const uint4* u4 = reinterpret_cast<const uint4*>(u);
+  uint4* o4 = reinterpret_cast<uint4*>(o);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += stride) {
+    const uint4 a = __ldg(g4 + i), b = __ldg(u4 + i);
+    o4[i] = make_uint4(swiglu2(a.x, b.x), swiglu2(a.y, b.y), swiglu2(a.z, b.z), swiglu2(a.w, b.w));
+  }
+  const int64_t t = (n8 << 3) + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < n) {
+    const float gv = __uint_as_float((uint32_t)g[t] << 16), uv = __uint_as_float((uint32_t)u[t] << 16);
+    __nv_bfloat16 r = __float2bfloat16_rn(silu_mul(gv, uv));
+    o[t] = *reinterpret_cast<uint16_t*>(&r);
+  }
+}
+
+cudaError_t launch_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, cudaStream_t st) {
+  const int threads = 256;
+  const int64_t want = ((n >> 3) + threads - 1) / threads;
+  const int grid = (int)(want < 1 ? 1 : (want > 8 * device_sm_count() ? 8 * device_sm_count() : want));
+  swiglu_bf16_kernel<<<grid, threads, 0, st>>>(static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(up),
+                                                static_cast<uint16_t*>(out), n);
+  return cudaGetLastError();
+}
+
+}  // namespace draco

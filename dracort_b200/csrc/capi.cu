@@ -204,3 +204,13 @@ int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, co
 }
 
 }  // extern "C"
+
+int draco_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, void* stream) {
+  if (n < 0) return fail(DRACO_ERR_SHAPE, "swiglu: negative length");
+  if (n == 0) return ok();
+  if (!gate || !up || !out) return fail(DRACO_ERR_ARG, "swiglu: null pointer");
+  if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(DRACO_ERR_ALIGN, "swiglu: gate, up and out must be 16-byte aligned");
+  cudaError_t e = draco::launch_swiglu_bf16(gate, up, out, n, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "swiglu");
+}

@@ -636,12 +636,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(&full_kb[rs.s], 2 * kNH * kXBox);
+          // X boxes that hold at least one token below M (a short prompt or
+          // an expert's few tokens leave the upper ones empty): both CTAs
+          // count the same boxes, the leader expects their bytes
+          const int tok_tile = c.tb * kTileTok;
+          const int m = P.prob[c.p].m;
+          if (rank == 0) {
+            int nbox = 0;
+#pragma unroll
+            for (int hh = 0; hh < kNH; ++hh)
+#pragma unroll
+              for (int r = 0; r < 2; ++r) nbox += tok_tile + hh * kUmmaM + r * kTokCta < m;
+            mbar_arrive_expect_tx(&full_kb[rs.s], (uint32_t)nbox * kXBox);
+          }
           const uint32_t bar = map_to_rank(&full_kb[rs.s], 0);
 #pragma unroll
           for (int hh = 0; hh < kNH; ++hh) {
-            const int tok = c.tb * kTileTok + hh * kUmmaM + (int)rank * kTokCta;
-            tma_load_2d_pair(xs + (size_t)(rs.s * kNH + hh) * kXBox, &P.xmap[c.p], kb * kBK, tok, bar);
+            const int tok = tok_tile + hh * kUmmaM + (int)rank * kTokCta;
+            if (tok < m) tma_load_2d_pair(xs + (size_t)(rs.s * kNH + hh) * kXBox, &P.xmap[c.p], kb * kBK, tok, bar);
           }
           rs.next(NS);
         }
@@ -658,6 +670,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       for (int i = 0, t; ok && (t = tile_at(P, pair, i, npairs)) >= 0; ++i, acc_ph ^= 1u) {
         TileCursor c;
         c.at(P, t);
+        // accumulators whose 256 tokens all lie at or past M get no MMAs
+        const int nh_live = c.tb * kTileTok + kUmmaM < P.prob[c.p].m ? 2 : 1;
         for (int kb = 0; kb < c.nkb && ok; ++kb) {
           // one wait per k-block: X boxes of both CTAs landed, both weight tiles dequantized
           if (!mbar_wait_bounded(&full_kb[rs.s], rs.ph, kGemmWaitNs)) {
@@ -679,6 +693,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
               }
               tc_fence_after();
             }
+            if (hh >= nh_live) continue;
             const uint32_t x_addr = x_addr0 + hh * kXBox;
             const uint32_t d = tmem + hh * kUmmaN;
             umma_bf16_pair(d, sdesc_sw128(x_addr), sdesc_sw128(a_addr), idesc, kb != 0);

@@ -29,6 +29,9 @@ size_t gemv_static_scratch_bytes();
 // kernel sets to a DRACO_* code on a device-side failure.
 int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_t st, char* msg, size_t msg_len);
 
+// out = bf16(silu(gate) * up) over n bf16 elements (16-byte aligned).
+cudaError_t launch_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, cudaStream_t st);
+
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 

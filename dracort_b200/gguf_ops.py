@@ -290,7 +290,7 @@ def _gemm_struct(p: GemmProblem) -> N.GemmProblem:
 
 
 def gemm_grouped(problems: Sequence[GemmProblem], status: Optional[torch.Tensor] = None) -> None:
-    """Y_i = X_i @ dequant(W_i)^T for up to 4 weights in one tcgen05 launch."""
+    """Y_i = X_i @ dequant(W_i)^T for up to 16 weights in one tcgen05 launch."""
     if not problems:
         return
     if len(problems) > N.GEMM_MAX_PROBLEMS:
@@ -302,6 +302,39 @@ def gemm_grouped(problems: Sequence[GemmProblem], status: Optional[torch.Tensor]
     dev = problems[0].x.device
     st = status.data_ptr() if status is not None else None
     N.check(lib.draco_gguf_gemm(arr, len(problems), st, _stream_ptr(dev)), "gemm")
+
+
+def gemm_grouped_unchecked(entries: Sequence[tuple], device: torch.device,
+                           status: Optional[torch.Tensor] = None) -> None:
+    """gemm_grouped for internal callers whose tensors are already known valid
+    (CUDA, bf16 x, contiguous rows): entries are (qtype, w_tiled, x, y, n_rows, k),
+    at most GEMM_MAX_PROBLEMS; only the C ABI's own checks run."""
+    if not entries:
+        return
+    lib = N.load()
+    arr = (N.GemmProblem * len(entries))()
+    for s, (qt, w, x, y, n, k) in zip(arr, entries):
+        s.qtype = qt
+        s.ydtype = N.DTYPE_BF16 if y.dtype == torch.bfloat16 else N.DTYPE_F32
+        s.w, s.x, s.y = w.data_ptr(), x.data_ptr(), y.data_ptr()
+        s.m, s.n_rows, s.k = x.shape[0], n, k
+        s.ldx, s.ldy = x.stride(0), y.stride(0)
+    st = status.data_ptr() if status is not None else None
+    N.check(lib.draco_gguf_gemm(arr, len(entries), st, _stream_ptr(device)), "gemm")
+
+
+def swiglu_bf16(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16(silu(gate) * up) in fp32 with one rounding (C ABI draco_swiglu_bf16)."""
+    for t, nm in ((gate, "gate"), (up, "up")):
+        _require_cuda(t, nm)
+        if t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"swiglu: {nm} must be a contiguous bfloat16 CUDA tensor")
+    if gate.shape != up.shape:
+        raise DracoFormatError(f"swiglu: gate {tuple(gate.shape)} and up {tuple(up.shape)} differ")
+    out = out if out is not None else torch.empty_like(gate)
+    N.check(N.load().draco_swiglu_bf16(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(),
+                                       _stream_ptr(gate.device)), "swiglu")
+    return out
 
 
 def gemm(qtype: int, w_tiled: torch.Tensor, x: torch.Tensor, n_rows: int, k: int,

@@ -17,8 +17,9 @@ Mirrors draco/models/moe:
   all-to-all; the source rank adds them with the routing weights.  At world
   size 1 there is no collective.
 
-The hot path is the quantized linear (the GEMM kernel); routing, the token
-permutation and the SwiGLU product are small tensor ops around it.
+The hot path is the quantized linear (the GEMM kernel) and the SwiGLU product
+between gate/up and down (draco_swiglu_bf16); routing and the token
+permutation are small tensor ops around them.
 """
 
 from __future__ import annotations
@@ -85,20 +86,24 @@ class GGUFExpertGroup:
         out = torch.empty((rows, self.hidden), dtype=torch.bfloat16, device=self.device)
         if rows == 0:
             return out
+        if x.dtype != torch.bfloat16 or not x.is_contiguous():
+            x = x.to(torch.bfloat16).contiguous()
         gate = torch.empty((rows, self.ffn), dtype=torch.bfloat16, device=self.device)
         up = torch.empty_like(gate)
-        probs, spans, r0 = [], [], 0
+        gu, down, r0 = [], [], 0
         for i, c in enumerate(counts):
             if c:
-                qt, wg, wu, _ = self.w[i]
-                probs.append(G.GemmProblem(qt, wg, x[r0:r0 + c], gate[r0:r0 + c], self.ffn, self.hidden))
-                probs.append(G.GemmProblem(qt, wu, x[r0:r0 + c], up[r0:r0 + c], self.ffn, self.hidden))
-                spans.append((i, r0, c))
+                qt, wg, wu, wd = self.w[i]
+                gu.append((qt, wg, x[r0:r0 + c], gate[r0:r0 + c], self.ffn, self.hidden))
+                gu.append((qt, wu, x[r0:r0 + c], up[r0:r0 + c], self.ffn, self.hidden))
+                down.append((qt, wd, gate[r0:r0 + c], out[r0:r0 + c], self.hidden, self.ffn))
             r0 += c
-        G.gemm_grouped(probs, self.status)
-        h = (F.silu(gate.float()) * up.float()).to(torch.bfloat16)
-        G.gemm_grouped([G.GemmProblem(self.w[i][0], self.w[i][3], h[r:r + c], out[r:r + c], self.hidden, self.ffn)
-                        for i, r, c in spans], self.status)
+        mx = G.N.GEMM_MAX_PROBLEMS
+        for i in range(0, len(gu), mx):
+            G.gemm_grouped_unchecked(gu[i:i + mx], self.device, self.status)
+        G.swiglu_bf16(gate, up, out=gate)  # the SwiGLU product overwrites gate, the down input
+        for i in range(0, len(down), mx):
+            G.gemm_grouped_unchecked(down[i:i + mx], self.device, self.status)
         return out
 
 

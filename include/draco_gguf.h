@@ -207,6 +207,13 @@ typedef struct draco_gemm_problem {
  * a device-side wait runs out (it never traps).  `problems` is a host array. */
 int draco_gguf_gemm(const draco_gemm_problem* problems, int n_problems, int* status, void* stream);
 
+/* SwiGLU product of a gated MLP between its gate/up and down projections:
+ * out[i] = bf16(silu(gate[i]) * up[i]) in fp32 with one rounding, n bf16
+ * elements, all three pointers 16-byte aligned (out may alias gate or up).
+ * Replaces act_fn(gate_proj(x)) * up_proj(x) of the reference's
+ * Expert.forward (draco/models/moe/expert.py:47-49). */
+int draco_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, void* stream);
+
 /* Single-weight convenience form of draco_gguf_gemv_grouped. */
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias,
                     int batch, int64_t n_rows, int64_t k, void* workspace,

@@ -65,3 +65,20 @@ def test_moe_layer_matches_expert_group(qtypes):
     assert layer.check_status() == 0
     ref = _reference(x.float(), logits, experts, hidden, ffn, top_k)
     assert O.rel_l2(y.cpu().numpy(), ref.numpy()) < PREFILL_TOL
+
+
+@pytest.mark.parametrize("n", [8 * 1000, 8 * 1000 + 5, 3])
+def test_swiglu_bf16_matches_fp32_formula(n):
+    from dracort_b200 import gguf_ops as G
+
+    g = torch.Generator().manual_seed(n)
+    gate = (3 * torch.randn(n, generator=g)).to(torch.bfloat16).cuda()
+    up = torch.randn(n, generator=g).to(torch.bfloat16).cuda()
+    out = G.swiglu_bf16(gate, up)
+    ref = (F.silu(gate.float()) * up.float()).to(torch.bfloat16)
+    diff = (out.float() - ref.float()).abs()
+    # one bf16 rounding of an fp32 value; expf may differ from torch's by an ulp
+    assert torch.all(diff <= 2 ** -7 * ref.float().abs() + 1e-30)
+    inplace = gate.clone()
+    G.swiglu_bf16(inplace, up, out=inplace)
+    assert torch.equal(inplace, out)
