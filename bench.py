@@ -69,6 +69,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM leg")
     ap.add_argument("--moe-steps", type=int, default=50, help="timed steps of the MoE (config 5) leg")
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE expert-parallel leg")
+    ap.add_argument("--model-steps", type=int, default=20, help="timed steps of the 32-layer decode leg")
+    ap.add_argument("--no-model", action="store_true", help="skip the 32-layer decode (config 4) leg")
     return ap.parse_args(argv)
 
 
@@ -343,6 +345,84 @@ def prefill_leg(args, dev, peaks, rank, world, pg, timed, want_e2e, want_cpu):
     return out
 
 
+def model_leg(args, dev, peaks, rank, world, pg, timed):
+    """Config 4: decode step of a 32-layer Llama-7B-shaped Q4_K_M model (the 7
+    quantized projections of every layer, back to back), batch 1 and 32,
+    tensor-parallel at N > 1."""
+    import torch
+
+    from dracort_b200 import gguf_ops as G
+    from dracort_b200.parallel.decode import TPDecodeLayer
+    from dracort_b200.telemetry import ClockSampler
+    from dracort_b200.workloads import algorithmic_bytes, model_layers
+
+    specs, layers = model_layers(args.seed + 700)
+    n_layers = len(layers)
+    out = {"metric": f"{n_layers}-layer Q4_K_M decode step (config 4): linear-layer HBM GB/s and tokens/s",
+           "unit": "GB/s", "scaling": "strong", "dtype": "f32",
+           "config": {"workload": "config4_llama7b_q4_k_m_decode_step", "layers": n_layers,
+                      "weights": "per layer q,k,o,gate,up Q4_K; v,down Q6_K (Llama-7B shapes)",
+                      "parallelism": f"tp{world}" + (" (NCCL all-gather + all-reduce per layer)" if world > 1 else ""),
+                      "step": "the 7 projections of every layer (one grouped GEMV launch per layer)"},
+           "batches": {}}
+    for batch in (1, 32):
+        if world == 1:
+            tiled = [[G.repack(s.qtype, torch.from_numpy(p.reshape(-1)).to(dev), s.n_rows, s.k)
+                      for s, p in zip(specs, lay)] for lay in layers]
+            xs = [torch.randn((batch, s.k), device=dev) for s in specs]
+            ys = [torch.empty((batch, s.n_rows), device=dev) for s in specs]
+            plans = [G.GemvPlan([G.GemvProblem(s.qtype, t[i], xs[i], ys[i], s.n_rows, s.k)
+                                 for i, s in enumerate(specs)]) for t in tiled]
+
+            def step():
+                for pl in plans:
+                    pl.run()
+            launches = n_layers
+            graph = torch.cuda.CUDAGraph()
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=dev)):
+                step()
+            run = graph.replay
+        else:
+            tp = [TPDecodeLayer(specs, lay, rank, world, batch, dev, seed=args.seed, group=pg, copies=1)
+                  for lay in layers]
+
+            def run():
+                for layer in tp:
+                    layer.step(0)
+            launches = n_layers
+        for _ in range(max(3, args.warmup)):
+            run()
+        torch.cuda.synchronize()
+        K = max(1, args.model_steps)
+        sampler = ClockSampler(dev.index or 0).start()
+
+        def steps():
+            for _ in range(K):
+                run()
+
+        ms, tw0, tw1 = timed(steps)
+        clocks = sampler.summary(tw0, tw1)
+        sampler.stop()
+        ms_step = ms / K
+        gbs = n_layers * algorithmic_bytes(specs, batch) / (ms_step * 1e-3) / 1e9
+        out["batches"][str(batch)] = {
+            "ms_per_step": round(ms_step, 4), "tokens_per_s": round(batch / (ms_step * 1e-3), 1),
+            "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / (peaks["hbm_gbs"] * world), 4),
+            "gpu_launches": launches * K, "clocks": clocks}
+        if world == 1:
+            del graph, plans, tiled
+        else:
+            for layer in tp:
+                layer.close()
+            del tp
+        torch.cuda.empty_cache()
+    out["value"] = out["batches"]["1"]["gbs"]
+    return out
+
+
 def moe_leg(args, dev, peaks, rank, world, pg, timed):
     """Config 5: Mixtral-shaped MoE FFN, expert-parallel over the ranks."""
     import torch
@@ -595,6 +675,9 @@ def run_ours(args):
     moe = None
     if not args.no_moe:
         moe = moe_leg(args, dev, peaks, rank, world, pg, timed)
+    model = None
+    if not args.no_model:
+        model = model_leg(args, dev, peaks, rank, world, pg, timed)
 
     # -- CPU baseline (rank 0, N=1) --------------------------------------------
     cpu = None
@@ -657,6 +740,8 @@ def run_ours(args):
             line["prefill"] = prefill
         if moe is not None:
             line["moe"] = moe
+        if model is not None:
+            line["model"] = model
         print(json.dumps(line), flush=True)
 
     if layer is not None:

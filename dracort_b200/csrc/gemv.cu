@@ -14,14 +14,35 @@
 //    split between CTAs are combined deterministically by the last CTA to
 //    finish (arrival counter in the workspace, partials added in CTA order).
 //  * Warp 16 (producer) streams each slab into a ring of shared-memory stages
-//    with 1-D bulk copies (TMA engine) completing on mbarriers; it starts at
-//    launch, before the preceding kernel has finished (programmatic dependent
-//    launch), since weights do not depend on it.
-//  * Warps 17-19 (converters) fill each stage's activation slice: they read
-//    the slab's 256 x B activations from global memory (L2), scale each
-//    32-element group by a power of two u (max |x| / u in [2^13, 2^14)),
-//    round to an integer q and split it into two int8 digits,
-//    q = 256 * hi + lo, stored in MMA-fragment order with the group sums.
+//    with 1-D bulk copies (TMA engine) completing on the slab's ready
+//    barrier; it starts at launch, before the preceding kernel has finished
+//    (programmatic dependent launch), since weights do not depend on it.
+//  * Warps 17-19 (converters) fill each stage's activation slice (slab i by
+//    converter i % 3): they read the slab's 256 x B activations from global
+//    memory (L2), scale each 32-element group by a power of two u
+//    (max |x| / u in [2^13, 2^14)), round to an integer q and split it into
+//    two int8 digits, q = 256 * hi + lo, stored in MMA-fragment order with
+//    the group sums, and arrive on the slab's ready barrier, which completes
+//    with that arrival and the slab's weight bytes.
+//  * A barrier wait tests a phase parity, which is only sound when the waiter
+//    sees every phase of the barrier in order.  Stage st holds slabs st,
+//    st + NS, ... (round m = i / NS); the ready barriers are kept per (stage,
+//    slab parity), so each consumer warp sees every phase of its parity's
+//    barriers (phase m for an even NS, m / 2 for an odd one, where a stage's
+//    slabs alternate parities), and the producer waits for every phase of
+//    every empty barrier.  The converters see only some slabs of a stage, so
+//    they do not wait on the empty barriers: the producer, once a stage is
+//    free for round m, publishes m in the stage's generation word (release /
+//    acquire), which a full counter cannot confuse.
+//  * Every wait is bounded.  The agent whose wait runs out records
+//    DRACO_ERR_TIMEOUT and sets the CTA's abort word; the other agents' waits
+//    see it and return, nobody frees a stage after that, and the producer
+//    waits (bounded) for its last copies to land before it exits, so the CTA
+//    never ends with a bulk copy in flight (after an abort the converters
+//    still arrive, without converting, for every slab the producer issued,
+//    so that those ready phases complete with the bytes).  An aborted launch
+//    leaves the workspace's arrival counters stale: zero the workspace
+//    before reusing it.
 //  * Warps 0-15 consume: warp w owns row tile (w % 8) of the slabs whose
 //    parity is w / 8.  The quants enter the int8 tensor-core MMA
 //    (m16n8k32, u8 x s8 -> s32) as they are: Q4_K nibbles with one mask,
@@ -112,10 +133,6 @@ __device__ __forceinline__ void mma_acc(float (&d)[4], uint32_t a0, uint32_t a1,
   mma_f16_16816_acc(d, a0, a1, a2, a3, b0, b1);
 }
 
-__device__ __forceinline__ void consumers_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-}
-
 __device__ __forceinline__ int rg_tile_count(const GemvProbDev& pr, int rg) {
   const int r = pr.n_tiles - rg * kGroupTiles;
   return r < kGroupTiles ? r : kGroupTiles;
@@ -123,6 +140,48 @@ __device__ __forceinline__ int rg_tile_count(const GemvProbDev& pr, int rg) {
 
 __device__ __forceinline__ void record_error(const GemvParams& P, int code) {
   atomicCAS(reinterpret_cast<int*>(P.ws + P.status_off), 0, code);
+}
+
+// Wait for the barrier phase with the given parity.  Returns false when the CTA
+// has aborted, or when the wait ran out (then this thread records the timeout
+// and sets the abort word for the others).
+__device__ __forceinline__ bool wait_phase(const GemvParams& P, uint64_t* bar, uint32_t parity,
+                                           volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      record_error(P, DRACO_ERR_TIMEOUT);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
+// Stage generation words: the producer stores round m once the stage is free
+// for it; a converter waits until the word reaches its slab's round.
+__device__ __forceinline__ void gen_publish(int* g, int m) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(g)), "r"(m) : "memory");
+}
+__device__ __forceinline__ int gen_read(const int* g) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(g)) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool wait_generation(const GemvParams& P, const int* g, int m, volatile int* abort) {
+  const uint64_t t0 = global_timer_ns();
+  while (gen_read(g) < m) {
+    if (*abort) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      record_error(P, DRACO_ERR_TIMEOUT);
+      *abort = 1;
+      return false;
+    }
+  }
+  return true;
 }
 
 // Slab cursor: (problem, row group, super-block) of a global slab index,
@@ -557,9 +616,10 @@ struct Mailbox {
 };
 
 // Called by each consumer warp at the end of its part of a row group.
+// Returns false when the CTA aborted (the row group is then left unwritten).
 template <int G, int NT>
-__device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s_begin, int s_end, int warp, int lane,
-                                float (&acc)[NT][2], const Mailbox& mb, bool& failed) {
+__device__ bool finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s_begin, int s_end, int warp, int lane,
+                                float (&acc)[NT][2], const Mailbox& mb, volatile int* abort) {
   const GemvProbDev& pr = P.prob[p];
   const int nrt = rg_tile_count(pr, rg);
   const int rw = warp & (kRowWarps - 1), par = warp / kRowWarps;
@@ -575,20 +635,26 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s
   volatile int* tagp = mb.tag + slot * kRowWarps + rw;
   // the slot may still hold an older row group whose second warp has not
   // arrived yet (the stage ring bounds how far ahead a warp runs)
-  if (lane == 0 && !failed) {
+  int ok = 1;
+  if (lane == 0) {
     const uint64_t t0 = global_timer_ns();
     while (true) {
       const int tg = *tagp;
       if (tg == 0 || tg == L + 1) break;
+      if (*abort) {
+        ok = 0;
+        break;
+      }
       if (global_timer_ns() - t0 > kWaitLimitNs) {
         record_error(P, DRACO_ERR_TIMEOUT);
-        failed = true;
+        *abort = 1;
+        ok = 0;
         break;
       }
     }
-    atomicCAS(const_cast<int*>(tagp), 0, L + 1);
+    if (ok) atomicCAS(const_cast<int*>(tagp), 0, L + 1);
   }
-  failed = __shfl_sync(0xffffffffu, (int)failed, 0) != 0;
+  if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
   float* mine = mb.data + ((((int64_t)slot * 2 + par) * kRowWarps + rw) * 32 + lane) * (NT * 2);
   float* other = mb.data + ((((int64_t)slot * 2 + (par ^ 1)) * kRowWarps + rw) * 32 + lane) * (NT * 2);
 #pragma unroll
@@ -601,7 +667,7 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s
   int old = 0;
   if (lane == 0) old = atomicAdd(mb.cnt + slot * kRowWarps + rw, 1);
   old = __shfl_sync(0xffffffffu, old, 0);
-  if (old == 0) return;  // the partner finishes the rows
+  if (old == 0) return true;  // the partner finishes the rows
   __threadfence_block();
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
@@ -614,11 +680,11 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s
     __threadfence_block();
     *tagp = 0;
   }
-  if (rw >= nrt) return;
+  if (rw >= nrt) return true;
   const int rg_start = pr.slab0 + rg * pr.nb, rg_end = rg_start + pr.nb;
   if (s_begin <= rg_start && rg_end <= s_end) {
     write_rows<NT>(P, pr, rg, rw, lane, acc);
-    return;
+    return true;
   }
   // split row group: publish this CTA's partial of row tile rw; the last
   // contributing CTA adds them in CTA order and writes the rows
@@ -647,7 +713,7 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s
     }
   }
   last = __shfl_sync(0xffffffffu, last, 0);
-  if (!last) return;
+  if (!last) return true;
   float sum[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) sum[nt][0] = sum[nt][1] = 0.f;
@@ -662,24 +728,30 @@ __device__ void finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s
     }
   }
   write_rows<NT>(P, pr, rg, rw, lane, sum);
+  return true;
 }
 
 // ---------------------------------------------------------------------------
 // consumer side: the slabs of one row-group segment that have this warp's parity
 // ---------------------------------------------------------------------------
+// Returns false when the CTA aborted; the warp then frees no further stage.
+// ready: this parity's ready barriers, stride 2 per stage.
 template <int QT, int G, int NT>
-__device__ __forceinline__ void consume_segment(const GemvParams& P, const uint8_t* smem, uint64_t* full_bar,
+__device__ __forceinline__ bool consume_segment(const GemvParams& P, const uint8_t* smem, uint64_t* ready,
                                                 uint64_t* empty_bar, int i, int i_end, int NS, int rw, int nrt,
-                                                int cb, int lane, bool& failed, float (&acc)[NT][2]) {
-  if (i >= i_end) return;
-  int st = i % NS;
-  uint32_t ph = (uint32_t)((i / NS) & 1);
+                                                int cb, int lane, volatile int* abort, float (&acc)[NT][2]) {
+  if (i >= i_end) return true;
+  int st = i % NS, m = i / NS;
+  // phase of this slab on its parity's barriers of the stage: round m, or m / 2
+  // with an odd NS (the stage's slabs alternate parities)
+  const int sh = NS & 1;
+  uint32_t ph = (uint32_t)((m >> sh) & 1);
   for (; i < i_end; i += 2) {
-    if (!failed && !mbar_wait_bounded(&full_bar[st], ph, kWaitLimitNs)) {
-      record_error(P, DRACO_ERR_TIMEOUT);
-      failed = true;
+    // try_wait is one warp-wide test, so the branch is uniform
+    if (!mbar_try_wait(&ready[2 * st], ph)) {
+      if (!__all_sync(0xffffffffu, wait_phase(P, &ready[2 * st], ph, abort))) return false;
     }
-    if (!failed && rw < nrt) {
+    if (rw < nrt) {
       const uint8_t* stage = smem + (size_t)st * P.stage_bytes;
       const uint8_t* ch = stage + rw * cb;
       const uint8_t* xs = stage + P.w_stage;
@@ -693,9 +765,11 @@ __device__ __forceinline__ void consume_segment(const GemvParams& P, const uint8
     st += 2;
     if (st >= NS) {
       st -= NS;
-      ph ^= 1u;
+      ++m;
+      ph = (uint32_t)((m >> sh) & 1);
     }
   }
+  return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -704,9 +778,14 @@ __device__ __forceinline__ void consume_segment(const GemvParams& P, const uint8
 template <int G, int NT>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t full_bar[kMaxStages];
-  __shared__ __align__(8) uint64_t empty_bar[kMaxStages];
+  // [stage][slab parity]: the slab's weight bytes landed and its activations are converted
+  __shared__ __align__(8) uint64_t ready_bar[2 * kMaxStages];
+  __shared__ __align__(8) uint64_t empty_bar[kMaxStages];  // the stage's consumers are done with it
+  __shared__ int stage_gen[kMaxStages];                     // round the stage is free for
   __shared__ int mbox_tag[kMaxMboxSlots * kRowWarps], mbox_cnt[kMaxMboxSlots * kRowWarps];
+  __shared__ int abort_word;
+  __shared__ int prod_issued, prod_done;  // the producer's final issue count, once it is done
+  volatile int* abort = &abort_word;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cta = blockIdx.x;
@@ -724,9 +803,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   }
   for (int i = threadIdx.x; i < kMaxMboxSlots * kRowWarps; i += blockDim.x) mbox_tag[i] = mbox_cnt[i] = 0;
   if (threadIdx.x == 0) {
+    abort_word = 0;
+    prod_issued = prod_done = 0;
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&full_bar[i], 2);  // producer (with the weight bytes) + converter
+      // the producer (with the weight bytes) and the slab's converter
+      mbar_init(&ready_bar[2 * i], 2);
+      mbar_init(&ready_bar[2 * i + 1], 2);
       mbar_init(&empty_bar[i], kRowWarps);
+      stage_gen[i] = 0;
     }
     fence_mbar_init();
   }
@@ -740,23 +824,46 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     if (lane == 0) {
       SlabCursor cur;
       cur.seek(P, s_begin);
-      int st = 0;
+      int st = 0, issued = 0;
       uint32_t ph = 0;
       for (int i = 0; i < n; ++i) {
-        if (i >= NS && !mbar_wait_bounded(&empty_bar[st], ph ^ 1u, kWaitLimitNs)) {
-          record_error(P, DRACO_ERR_TIMEOUT);
-          break;
+        if (i >= NS) {
+          if (!wait_phase(P, &empty_bar[st], ph ^ 1u, abort)) break;
+          gen_publish(&stage_gen[st], i / NS);
         }
         const GemvProbDev& pr = P.prob[cur.p];
         const int nrt = rg_tile_count(pr, cur.rg);
         const uint32_t wbytes = (uint32_t)(nrt * pr.cb);
         const int64_t woff = (int64_t)cur.rg * kGroupTiles * pr.nb * pr.cb + (int64_t)cur.j * nrt * pr.cb;
-        mbar_arrive_expect_tx(&full_bar[st], wbytes);
-        bulk_g2s(smem + (size_t)st * P.stage_bytes, pr.w + woff, wbytes, &full_bar[st]);
+        uint64_t* rb = &ready_bar[2 * st + (i & 1)];
+        mbar_arrive_expect_tx(rb, wbytes);
+        bulk_g2s(smem + (size_t)st * P.stage_bytes, pr.w + woff, wbytes, rb);
+        issued = i + 1;
         cur.next(P);
         if (++st == NS) {
           st = 0;
           ph ^= 1u;
+        }
+      }
+      // tell the converters how far the producer got (they complete the ready
+      // phases of issued slabs even after an abort)
+      *reinterpret_cast<volatile int*>(&prod_issued) = issued;
+      __threadfence_block();
+      *reinterpret_cast<volatile int*>(&prod_done) = 1;
+      // Only the last copy issued into a stage can still be in flight (each
+      // earlier one was waited for before its stage was freed): wait for them,
+      // so that the CTA never exits with a copy pending, even after an abort.
+      const uint64_t t0 = global_timer_ns();
+      for (int i = max(0, issued - NS); i < issued; ++i) {
+        const int m = i / NS;
+        uint64_t* rb = &ready_bar[2 * (i % NS) + (i & 1)];
+        const uint32_t rph = (uint32_t)((m >> (NS & 1)) & 1);
+        while (!mbar_try_wait(rb, rph)) {
+          if (global_timer_ns() - t0 > kWaitLimitNs) {
+            record_error(P, DRACO_ERR_TIMEOUT);
+            *abort = 1;
+            break;
+          }
         }
       }
     }
@@ -771,16 +878,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     cur.seek(P, s_begin);
     for (int q = 0; q < c && q < n; ++q) cur.next(P);
     for (int i = c; i < n; i += kConvWarps) {
-      const int st = i % NS;
-      const uint32_t ph = (uint32_t)((i / NS) & 1);
-      if (i >= NS && !mbar_wait_bounded(&empty_bar[st], ph ^ 1u, kWaitLimitNs)) {
-        record_error(P, DRACO_ERR_TIMEOUT);
-        break;
+      const int st = i % NS, m = i / NS;
+      if (m > 0 && !__all_sync(0xffffffffu, wait_generation(P, &stage_gen[st], m, abort))) {
+        // aborted: once the producer is done, arrive for this converter's
+        // remaining slabs that it issued, so their copies' phases complete
+        const uint64_t t0 = global_timer_ns();
+        while (!*reinterpret_cast<volatile int*>(&prod_done) && global_timer_ns() - t0 < kWaitLimitNs) {
+        }
+        __threadfence_block();
+        const int issued = *reinterpret_cast<volatile int*>(&prod_issued);
+        if (lane == 0)
+          for (int r = i; r < issued; r += kConvWarps) mbar_arrive(&ready_bar[2 * (r % NS) + (r & 1)]);
+        return;
       }
       uint8_t* xs = smem + (size_t)st * P.stage_bytes + P.w_stage;
       convert_slab<G, NT>(P, P.prob[cur.p], cur.j, xs, xs + P.xs_bytes, lane);
       __syncwarp();
-      if (lane == 0) mbar_arrive(&full_bar[st]);
+      if (lane == 0) mbar_arrive(&ready_bar[2 * st + (i & 1)]);
       for (int q = 0; q < kConvWarps; ++q) cur.next(P);
     }
     return;
@@ -792,10 +906,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   float acc[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
-  // After a timed-out wait the warp stops waiting and computing but keeps
-  // walking its range, so every consumer warp still reaches each named
-  // barrier and the kernel ends.  The status word tells the host.
-  bool failed = false;
   const Mailbox mb = {reinterpret_cast<float*>(smem + P.mbox_off), mbox_tag, mbox_cnt, P.mbox_slots};
   SlabCursor cur;
   cur.seek(P, s_begin);
@@ -807,16 +917,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     const int i0 = s - s_begin;
     const int i_first = i0 + (((i0 & 1) != par) ? 1 : 0);
     const int nrt = rg_tile_count(pr, cur.rg);
+    bool ok;
     if (pr.qt == kQ4_K)
-      consume_segment<kQ4_K, G, NT>(P, smem, full_bar, empty_bar, i_first, i0 + seg, NS, rw, nrt, pr.cb, lane,
-                                    failed, acc);
+      ok = consume_segment<kQ4_K, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
+                                         pr.cb, lane, abort, acc);
     else if (pr.qt == kQ6_K)
-      consume_segment<kQ6_K, G, NT>(P, smem, full_bar, empty_bar, i_first, i0 + seg, NS, rw, nrt, pr.cb, lane,
-                                    failed, acc);
+      ok = consume_segment<kQ6_K, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
+                                         pr.cb, lane, abort, acc);
     else
-      consume_segment<kQ8_0, G, NT>(P, smem, full_bar, empty_bar, i_first, i0 + seg, NS, rw, nrt, pr.cb, lane,
-                                    failed, acc);
-    finish_rowgroup<G, NT>(P, cur.p, cur.rg, L++, s_begin, s_end, warp, lane, acc, mb, failed);
+      ok = consume_segment<kQ8_0, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
+                                         pr.cb, lane, abort, acc);
+    if (!ok || !finish_rowgroup<G, NT>(P, cur.p, cur.rg, L++, s_begin, s_end, warp, lane, acc, mb, abort)) return;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
     s += seg;

@@ -235,8 +235,14 @@ class GemvPlan:
             N.check(rc, "gemv")
 
     def status(self) -> int:
-        """Kernel-recorded status word (0 = ok).  Synchronises."""
-        return int(self.workspace[:4].view(torch.int32).item())
+        """Kernel-recorded status word (0 = ok).  Synchronises.  A nonzero status
+        means a launch aborted (its outputs are invalid) and left the
+        workspace's arrival counters stale; the workspace is zeroed here so
+        that the plan can run again."""
+        st = int(self.workspace[:4].view(torch.int32).item())
+        if st:
+            self.workspace.zero_()
+        return st
 
 
 def gemv(qtype: int, w_tiled: torch.Tensor, x: torch.Tensor, n_rows: int, k: int,

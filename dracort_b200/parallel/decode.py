@@ -31,7 +31,8 @@ class TPDecodeLayer:
 
     def __init__(self, specs: Sequence, packed: Sequence[np.ndarray], rank: int, world: int, batch: int,
                  device: torch.device, seed: int = 0, group=None, l2_bytes: int = 126 << 20,
-                 min_copies: int = 2) -> None:
+                 min_copies: int = 2, copies: int = 0) -> None:
+        """copies: weight copies to rotate through (0: enough to exceed 4x L2)."""
         import torch.distributed as dist
 
         self.rank, self.world, self.batch, self.device = rank, world, batch, device
@@ -52,7 +53,7 @@ class TPDecodeLayer:
         tiled0 = [G.repack(qt, torch.from_numpy(sh.reshape(-1)).to(device), n, k)
                   for (_, qt, n, k, sh, _, _) in self.local]
         self.local_weight_bytes = int(sum(t.numel() for t in tiled0))
-        self.n_copies = max(min_copies, math.ceil(4 * l2_bytes / max(1, self.local_weight_bytes)))
+        self.n_copies = copies or max(min_copies, math.ceil(4 * l2_bytes / max(1, self.local_weight_bytes)))
         copies = [tiled0] + [[t.clone() for t in tiled0] for _ in range(self.n_copies - 1)]
 
         # activations: full x for column shards, the rank's K slice for row shards

@@ -7,6 +7,7 @@
 * Config 3 — mixed Q4_K/Q6_K prefill dequant-GEMM, M = 2048 tokens: gate and
   up 11008x4096 in Q4_K, down 4096x11008 in Q6_K, bf16 activations.
 * Config 4 — the same projections in Q4_K_M (Q6_K for v and down).
+  Config 4's model step runs the 32 layers' projections back to back.
 * Config 5 — Mixtral-8x7B-shaped MoE FFN: 8 Q4_K experts (gate/up
   14336x4096, down 4096x14336), top-2 routing, 256 bf16 tokens.
 
@@ -83,6 +84,21 @@ def prefill_specs(mix: str = "mixed") -> List[WeightSpec]:
 
 def prefill_flops(specs: Sequence[WeightSpec], m: int = PREFILL_TOKENS) -> int:
     return sum(2 * m * s.n_rows * s.k for s in specs)
+
+
+MODEL_LAYERS = 32
+
+
+def model_layers(seed: int, n_layers: int = MODEL_LAYERS, mix: str = "q4_k_m"):
+    """Config 4: packed projections of an n-layer Llama-7B-shaped model.  One
+    layer is encoded from seeded N(0, 0.02) weights; every other layer's
+    projections are seeded row permutations of its packed rows (each row a
+    valid quantized N(0, 0.02) row).  Returns (specs, [layer][projection] packed)."""
+    specs = layer_specs(mix)
+    base = encode_specs(specs, seed)
+    rng = np.random.default_rng(seed + 1)
+    layers = [base] + [[p[rng.permutation(s.n_rows)] for s, p in zip(specs, base)] for _ in range(n_layers - 1)]
+    return specs, layers
 
 
 MOE_EXPERTS, MOE_HIDDEN, MOE_FFN, MOE_TOP_K, MOE_TOKENS = 8, 4096, 14336, 2, 256
