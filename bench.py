@@ -21,8 +21,11 @@ Usage:
   python bench.py --impl reference ...   # the reference's CPU path (oracle port) on host cores
 Multi-GPU (N > 1, under torchrun): the layer set is sharded tensor-parallel,
 column-parallel q/k/v/gate/up and row-parallel o/down (super-block aligned
-K ranges), with an NCCL all-gather after the column-parallel outputs and an
-all-reduce after the row-parallel ones.
+K ranges).  The gather of the column outputs and the sum of the row partials
+run over NVLink inside the kernels (the GEMV stores every output into every
+rank's exchange buffer; a finish kernel waits for all ranks and reduces); the
+same step with an NCCL all-gather + all-reduce is timed beside it
+("tp_nccl").
 
 The same JSON line carries the second half of the metric under "prefill":
 config 3, the mixed Q4_K/Q6_K prefill dequant-GEMM (gate and up 11008x4096
@@ -386,13 +389,23 @@ def model_leg(args, dev, peaks, rank, world, pg, timed):
                 step()
             run = graph.replay
         else:
-            tp = [TPDecodeLayer(specs, lay, rank, world, batch, dev, seed=args.seed, group=pg, copies=1)
+            tp = [TPDecodeLayer(specs, lay, rank, world, batch, dev, seed=args.seed, group=pg, copies=1, fused=True)
                   for lay in layers]
 
-            def run():
+            def step():
                 for layer in tp:
                     layer.step(0)
-            launches = n_layers
+            launches = n_layers * tp[0].launches_per_step
+            for _ in range(3):
+                step()
+            torch.cuda.synchronize()
+            bad = [layer.status() for layer in tp if layer.status()]
+            if bad:
+                raise RuntimeError(f"tensor-parallel decode step reported device status {bad[0]}")
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=dev)):
+                step()
+            run = graph.replay
         for _ in range(max(3, args.warmup)):
             run()
         torch.cuda.synchronize()
@@ -412,8 +425,9 @@ def model_leg(args, dev, peaks, rank, world, pg, timed):
             "ms_per_step": round(ms_step, 4), "tokens_per_s": round(batch / (ms_step * 1e-3), 1),
             "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / (peaks["hbm_gbs"] * world), 4),
             "gpu_launches": launches * K, "clocks": clocks}
+        del graph
         if world == 1:
-            del graph, plans, tiled
+            del plans, tiled
         else:
             for layer in tp:
                 layer.close()
@@ -513,7 +527,8 @@ def run_ours(args):
     if world > 1:
         from dracort_b200.parallel.decode import TPDecodeLayer
 
-        layer = TPDecodeLayer(specs_full, packed_full, rank, world, batch, dev, seed=args.seed, group=pg)
+        layer = TPDecodeLayer(specs_full, packed_full, rank, world, batch, dev, seed=args.seed, group=pg,
+                              fused=True)
         step_fn = layer.step
         n_copies = layer.n_copies
         gpu_launches_per_step = layer.launches_per_step
@@ -546,6 +561,8 @@ def run_ours(args):
     for i in range(max(3, args.warmup)):
         step_fn(i)
     torch.cuda.synchronize()
+    if layer is not None and layer.status():
+        raise RuntimeError(f"tensor-parallel step reported device status {layer.status()}")
     stream = torch.cuda.Stream(device=dev)
     graphs = {}
 
@@ -663,7 +680,28 @@ def run_ours(args):
     elif world > 1 and not args.no_e2e and layer is not None:
         e2e = layer.e2e(K, timed)
         e2e.update({"value": round(alg / (e2e["ms_per_step"] * 1e-3) / 1e9, 3), "unit": "GB/s",
-                    "path": "pinned host x -> cuda -> GemvPlan.run + NCCL all-gather/all-reduce -> pinned host, eager"})
+                    "path": "pinned host x -> cuda -> tensor-parallel GEMV (C ABI) with NVLink exchange + "
+                            "finish kernel -> pinned host, eager"})
+
+    # -- the same tensor-parallel step with NCCL collectives, for comparison ---
+    tp_nccl = None
+    if world > 1:
+        layer.close()
+        nl = TPDecodeLayer(specs_full, packed_full, rank, world, batch, dev, seed=args.seed, group=pg)
+        for i in range(max(3, args.warmup)):
+            nl.step(i)
+        torch.cuda.synchronize()
+        kn = min(K, 500)
+
+        def nccl_steps():
+            for i in range(kn):
+                nl.step(i)
+
+        ms_n, _, _ = timed(nccl_steps)
+        tp_nccl = {"ms_per_step": round(ms_n / kn, 5), "gbs": round(alg / (ms_n / kn * 1e-3) / 1e9, 1),
+                   "steps": kn, "path": "same shards; GemvPlan.run + NCCL all-gather + all-reduce, eager"}
+        nl.close()
+        del nl
 
     sampler.stop()
 
@@ -713,7 +751,8 @@ def run_ours(args):
                 "weights": "q,k,v,o 4096x4096; gate,up 11008x4096; down 4096x11008",
                 "l2": f"inputs larger than L2: {n_copies} layer-set copies rotated "
                       f"({n_copies * local_bytes / 1e6:.0f} MB per GPU > 4x126 MB L2)",
-                "parallelism": f"tp{world}",
+                "parallelism": f"tp{world}" + (" (in-kernel NVLink exchange: peer stores + finish kernel)"
+                                               if world > 1 else ""),
                 "graph": bool(use_graph),
             },
             "roofline": {
@@ -724,8 +763,9 @@ def run_ours(args):
                 "frac": round(achieved / (peaks["hbm_gbs"] * world), 4),
                 "traffic": traffic,
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs x {world} GPUs)",
-                "kernel": "gemv_kernel, one launch per step; algorithmic bytes "
-                          f"{alg} per step / device time per step",
+                "kernel": ("gemv_kernel, one launch per step" if world == 1 else
+                           "gemv_kernel (tensor-parallel, stores to every rank) + tp_finish_kernel per step")
+                          + f"; algorithmic bytes {alg} per step / device time per step",
             },
             "gpu_launches": gpu_launches_per_step * K,
             "clocks": clocks,
@@ -734,6 +774,8 @@ def run_ours(args):
             line["batches"] = batches
         if e2e is not None:
             line["e2e"] = e2e
+        if tp_nccl is not None:
+            line["tp_nccl"] = tp_nccl
         if cpu is not None:
             line["cpu_baseline"] = cpu
         if prefill is not None:

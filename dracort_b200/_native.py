@@ -27,6 +27,7 @@ DRACO_ERR_CUDA = 4
 DRACO_ERR_TIMEOUT = 5
 DRACO_ERR_ARG = 6
 DRACO_ERR_WORKSPACE = 7
+DRACO_ERR_PEER = 8
 
 LAYOUT_GGUF = 0
 LAYOUT_GGUF_DLAST = 1
@@ -34,6 +35,8 @@ LAYOUT_TILED = 2
 
 GEMV_MAX_PROBLEMS = 8
 GEMV_MAX_BATCH = 32
+TP_MAX_WORLD = 8
+IPC_HANDLE_BYTES = 64
 
 #: every symbol include/draco_gguf.h declares
 EXPORTED_SYMBOLS = (
@@ -51,6 +54,13 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv_grouped_noalloc",
     "draco_gguf_gemm",
     "draco_swiglu_bf16",
+    "draco_tp_buffer_alloc",
+    "draco_tp_buffer_free",
+    "draco_ipc_get_handle",
+    "draco_ipc_open",
+    "draco_ipc_close",
+    "draco_gguf_gemv_grouped_tp",
+    "draco_tp_finish",
 )
 
 DTYPE_F32 = 0
@@ -89,6 +99,20 @@ class GemmProblem(ctypes.Structure):
         ("k", ctypes.c_int64),
         ("ldx", ctypes.c_int64),
         ("ldy", ctypes.c_int64),
+    ]
+
+
+class TpExchange(ctypes.Structure):
+    """Mirror of ``draco_tp_exchange``."""
+
+    _fields_ = [
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("buffers", ctypes.c_void_p * 8),
+        ("flags_off", ctypes.c_int64),
+        ("counter_off", ctypes.c_int64),
+        ("y_off", ctypes.c_int64 * 8),
+        ("parity_stride", ctypes.c_int64 * 8),
     ]
 
 
@@ -144,6 +168,22 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_gemm.argtypes = [ctypes.POINTER(GemmProblem), c_int, vp, vp]
         lib.draco_swiglu_bf16.restype = c_int
         lib.draco_swiglu_bf16.argtypes = [vp, vp, vp, i64, vp]
+        lib.draco_tp_buffer_alloc.restype = c_int
+        lib.draco_tp_buffer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+        lib.draco_tp_buffer_free.restype = c_int
+        lib.draco_tp_buffer_free.argtypes = [vp]
+        lib.draco_ipc_get_handle.restype = c_int
+        lib.draco_ipc_get_handle.argtypes = [vp, vp]
+        lib.draco_ipc_open.restype = c_int
+        lib.draco_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
+        lib.draco_ipc_close.restype = c_int
+        lib.draco_ipc_close.argtypes = [vp]
+        lib.draco_gguf_gemv_grouped_tp.restype = c_int
+        lib.draco_gguf_gemv_grouped_tp.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int,
+                                                   ctypes.POINTER(TpExchange), vp, ctypes.c_size_t, vp]
+        lib.draco_tp_finish.restype = c_int
+        lib.draco_tp_finish.argtypes = [ctypes.POINTER(TpExchange), c_int, i64, i64, c_int, vp, i64, i64, c_int,
+                                        vp, vp, vp]
         lib.draco_gguf_gemv.restype = c_int
         lib.draco_gguf_gemv.argtypes = [c_int, vp, vp, vp, vp, c_int, i64, i64, vp, ctypes.c_size_t, vp]
         _lib = lib

@@ -23,7 +23,7 @@ LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libdraco_gguf.so"
 INCLUDE = REPO_DIR / "include"
 
-SOURCES = ["capi.cu", "dequant.cu", "gemv.cu", "gemm.cu", "act.cu"]
+SOURCES = ["capi.cu", "dequant.cu", "gemv.cu", "gemm.cu", "act.cu", "tp.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 

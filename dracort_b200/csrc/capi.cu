@@ -124,7 +124,8 @@ int draco_gguf_repack(int qtype, int src_layout, const void* src, void* dst, int
   return e == cudaSuccess ? ok() : cuda_fail(e, "repack");
 }
 
-static int check_gemv_problems(const draco_gemv_problem* probs, int n, int batch) {
+// need_y: false for the tensor-parallel form, whose outputs go to the exchange buffers
+static int check_gemv_problems(const draco_gemv_problem* probs, int n, int batch, bool need_y = true) {
   if (!probs || n < 1 || n > DRACO_GEMV_MAX_PROBLEMS)
     return fail(DRACO_ERR_ARG, "gemv: need 1..%d problems, got %d", DRACO_GEMV_MAX_PROBLEMS, n);
   if (batch < 1 || batch > DRACO_GEMV_MAX_BATCH)
@@ -133,7 +134,8 @@ static int check_gemv_problems(const draco_gemv_problem* probs, int n, int batch
     const draco_gemv_problem& q = probs[i];
     int rc = check_weight(q.qtype, DRACO_LAYOUT_TILED, q.w, q.n_rows, q.k, "gemv");
     if (rc) return rc;
-    if (q.n_rows * q.k > 0 && (!q.x || !q.y)) return fail(DRACO_ERR_ARG, "gemv: problem %d has a null x or y", i);
+    if (q.n_rows * q.k > 0 && (!q.x || (need_y && !q.y)))
+      return fail(DRACO_ERR_ARG, "gemv: problem %d has a null x or y", i);
     if (q.ldx < q.k || q.ldy < q.n_rows)
       return fail(DRACO_ERR_SHAPE, "gemv: problem %d leading dimensions too small", i);
   }
@@ -141,7 +143,8 @@ static int check_gemv_problems(const draco_gemv_problem* probs, int n, int batch
 }
 
 size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* probs, int n_problems, int batch) {
-  if (check_gemv_problems(probs, n_problems, batch)) return 0;
+  // the size does not depend on y (the tensor-parallel form has none)
+  if (check_gemv_problems(probs, n_problems, batch, false)) return 0;
   return gemv_workspace_bytes(probs, n_problems, batch);
 }
 
@@ -201,6 +204,78 @@ int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, co
   p.ldx = k;
   p.ldy = n_rows;
   return draco_gguf_gemv_grouped(&p, 1, batch, workspace, workspace_bytes, stream);
+}
+
+int draco_tp_buffer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(DRACO_ERR_ARG, "tp_buffer_alloc: null result pointer or zero size");
+  *ptr = nullptr;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "tp_buffer_alloc: cudaMalloc");
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "tp_buffer_alloc: cudaMemset");
+  }
+  *ptr = p;
+  return ok();
+}
+
+int draco_tp_buffer_free(void* ptr) {
+  if (!ptr) return ok();
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "tp_buffer_free");
+}
+
+int draco_ipc_get_handle(void* ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == DRACO_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!ptr || !handle) return fail(DRACO_ERR_ARG, "ipc_get_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "ipc_get_handle");
+  memcpy(handle, &h, sizeof(h));
+  return ok();
+}
+
+int draco_ipc_open(const void* handle, void** peer_ptr) {
+  if (!handle || !peer_ptr) return fail(DRACO_ERR_ARG, "ipc_open: null pointer");
+  *peer_ptr = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "ipc_open");
+  *peer_ptr = p;
+  return ok();
+}
+
+int draco_ipc_close(void* peer_ptr) {
+  if (!peer_ptr) return ok();
+  cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "ipc_close");
+}
+
+int draco_gguf_gemv_grouped_tp(const draco_gemv_problem* probs, int n_problems, int batch,
+                               const draco_tp_exchange* ex, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_gemv_problems(probs, n_problems, batch, false);
+  if (rc) return rc;
+  if (!ex) return fail(DRACO_ERR_ARG, "gemv_tp: null exchange description");
+  char msg[256] = {0};
+  rc = gemv_launch_tp(probs, n_problems, batch, ex, workspace, workspace_bytes, (cudaStream_t)stream, msg,
+                      sizeof(msg));
+  if (rc) return fail(rc, "%s", msg);
+  return ok();
+}
+
+int draco_tp_finish(const draco_tp_exchange* ex, int batch, int64_t gather_off, int64_t gather_stride,
+                    int gather_width, float* gather_out, int64_t reduce_off, int64_t reduce_stride,
+                    int reduce_width, float* reduce_out, int* status, void* stream) {
+  if (!ex) return fail(DRACO_ERR_ARG, "tp_finish: null exchange description");
+  char msg[256] = {0};
+  int rc = tp_finish_launch(ex, batch, gather_off, gather_stride, gather_width, gather_out, reduce_off,
+                            reduce_stride, reduce_width, reduce_out, status, (cudaStream_t)stream, msg, sizeof(msg));
+  if (rc) return fail(rc, "%s", msg);
+  return ok();
 }
 
 }  // extern "C"

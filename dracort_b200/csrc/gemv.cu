@@ -56,6 +56,12 @@
 //    sit in their own pair of MMA columns, so one accumulator collects
 //    4 (B=1) or 2 (B=2) sub-blocks and every lane owns one sub-block's sum.
 //    Batch >= 3 ("dense"): columns are (batch, digit).
+//  * Tensor-parallel form (draco_gguf_gemv_grouped_tp): each output value is
+//    stored into every rank's exchange buffer over NVLink (peer stores through
+//    CUDA IPC mappings) instead of the local y; when every CTA is done, the
+//    last one fences at system scope and stores the step's epoch into each
+//    rank's flag for this rank.  The buffers are double-buffered by the parity
+//    of the epoch, which each rank counts in its own buffer.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -83,6 +89,7 @@ struct GemvProbDev {
   int64_t ldx, ldy;
   int slab0;  // global index of the problem's first slab
   int qt, n_rows, k, nb, n_rg, n_tiles, cb;
+  int64_t tp_y_off, tp_par_stride;  // tensor-parallel output block in every rank's exchange buffer
 };
 
 struct GemvParams {
@@ -93,11 +100,15 @@ struct GemvParams {
   int n_prob, batch, nt, n_cta;
   int w_stage, xs_bytes, su_bytes, stage_bytes, n_stages;
   int mbox_slots, mbox_off;  // row-group mailbox after the stages in dynamic shared memory
+  int tp_world, tp_rank;     // tensor-parallel exchange (tp_world 0: plain outputs)
+  uint8_t* tp_buf[DRACO_TP_MAX_WORLD];
+  int64_t tp_flags_off, tp_counter_off;
   int cta_start[kMaxCta + 1];
 };
 
 // workspace layout (bytes)
 constexpr int64_t kWsStatus = 0;
+constexpr int64_t kWsGridDone = 128;  // CTAs finished (tensor-parallel form)
 constexpr int64_t kWsCounters = 256;
 constexpr int64_t kWsCountersBytes = (int64_t)kMaxCta * 2 * kRowWarps * 4;  // per (CTA, end, row tile)
 static inline int64_t align256(int64_t v) { return (v + 255) & ~(int64_t)255; }
@@ -572,9 +583,13 @@ __device__ __forceinline__ void chunk_q80(const uint8_t* ch, const uint8_t* xs, 
 // ---------------------------------------------------------------------------
 // output of one row group
 // ---------------------------------------------------------------------------
-template <int NT>
+template <int NT, bool TP>
 __device__ __forceinline__ void write_rows(const GemvParams& P, const GemvProbDev& pr, int rg, int rw, int lane,
                                            const float (&v)[NT][2]) {
+  // tensor-parallel: this step's parity (the own step counter + 1; it only
+  // changes after every CTA of this launch has finished)
+  int tp_par = 0;
+  if constexpr (TP) tp_par = (*reinterpret_cast<volatile int*>(P.tp_buf[P.tp_rank] + P.tp_counter_off) + 1) & 1;
   const int g = lane >> 2, t = lane & 3;
   const int64_t row0 = ((int64_t)rg * kGroupTiles + rw) * kChunkRows + g;
 #pragma unroll
@@ -587,7 +602,12 @@ __device__ __forceinline__ void write_rows(const GemvParams& P, const GemvProbDe
       if (row < pr.n_rows) {
         float out = v[nt][hh];
         if (pr.bias) out += pr.bias[row];
-        pr.y[(int64_t)b * pr.ldy + row] = out;
+        if constexpr (!TP) {
+          pr.y[(int64_t)b * pr.ldy + row] = out;
+        } else {
+          const int64_t off = pr.tp_y_off + (int64_t)tp_par * pr.tp_par_stride + ((int64_t)b * pr.ldy + row) * 4;
+          for (int q = 0; q < P.tp_world; ++q) *reinterpret_cast<float*>(P.tp_buf[q] + off) = out;
+        }
       }
     }
   }
@@ -617,7 +637,7 @@ struct Mailbox {
 
 // Called by each consumer warp at the end of its part of a row group.
 // Returns false when the CTA aborted (the row group is then left unwritten).
-template <int G, int NT>
+template <int G, int NT, bool TP>
 __device__ bool finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s_begin, int s_end, int warp, int lane,
                                 float (&acc)[NT][2], const Mailbox& mb, volatile int* abort) {
   const GemvProbDev& pr = P.prob[p];
@@ -683,7 +703,7 @@ __device__ bool finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s
   if (rw >= nrt) return true;
   const int rg_start = pr.slab0 + rg * pr.nb, rg_end = rg_start + pr.nb;
   if (s_begin <= rg_start && rg_end <= s_end) {
-    write_rows<NT>(P, pr, rg, rw, lane, acc);
+    write_rows<NT, TP>(P, pr, rg, rw, lane, acc);
     return true;
   }
   // split row group: publish this CTA's partial of row tile rw; the last
@@ -727,7 +747,7 @@ __device__ bool finish_rowgroup(const GemvParams& P, int p, int rg, int L, int s
       sum[nt][1] += __ldcg(q + 2 * nt + 1);
     }
   }
-  write_rows<NT>(P, pr, rg, rw, lane, sum);
+  write_rows<NT, TP>(P, pr, rg, rw, lane, sum);
   return true;
 }
 
@@ -775,7 +795,7 @@ __device__ __forceinline__ bool consume_segment(const GemvParams& P, const uint8
 // ---------------------------------------------------------------------------
 // the persistent GEMV kernel
 // ---------------------------------------------------------------------------
-template <int G, int NT>
+template <int G, int NT, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   // [stage][slab parity]: the slab's weight bytes landed and its activations are converted
@@ -903,6 +923,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
   // ---------------- consumers ----------------
   grid_dependency_wait();  // y may still be read by the preceding kernel
   const int par = warp / kRowWarps, rw = warp % kRowWarps;
+
   float acc[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
@@ -927,7 +948,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     else
       ok = consume_segment<kQ8_0, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
                                          pr.cb, lane, abort, acc);
-    if (!ok || !finish_rowgroup<G, NT>(P, cur.p, cur.rg, L++, s_begin, s_end, warp, lane, acc, mb, abort)) return;
+    if (!ok || !finish_rowgroup<G, NT, TP>(P, cur.p, cur.rg, L++, s_begin, s_end, warp, lane, acc, mb, abort))
+      break;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = 0.f;
     s += seg;
@@ -938,6 +960,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         cur.rg = 0;
         ++cur.p;
       }
+    }
+  }
+  if constexpr (!TP) return;
+  // Tensor-parallel completion.  The consumer warps meet at a named barrier;
+  // then one thread counts the CTA with a system-scope acquire-release atomic:
+  // its release orders all of the CTA's peer stores (the barrier makes them
+  // happen before it), and the last CTA's acquire sees every CTA's before it
+  // signals every rank (epoch, or -epoch when this launch aborted).  (A
+  // system-scope fence in every thread cost ~20 us per launch, one fence per
+  // CTA ~10 us; the atomic ~8.5 us.)
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  if (threadIdx.x == 0) {
+    const int tp_epoch = *reinterpret_cast<volatile int*>(P.tp_buf[P.tp_rank] + P.tp_counter_off) + 1;
+    const int tp_par = tp_epoch & 1;
+    unsigned int* grid_done = reinterpret_cast<unsigned int*>(P.ws + kWsGridDone);
+    unsigned int prev;
+    asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(grid_done) : "memory");
+    if (prev == gridDim.x - 1) {
+      *grid_done = 0u;
+      const int sig = *reinterpret_cast<volatile int*>(P.ws + P.status_off) ? -tp_epoch : tp_epoch;
+      for (int q = 0; q < P.tp_world; ++q)
+        st_release_sys(reinterpret_cast<int*>(P.tp_buf[q] + P.tp_flags_off) + tp_par * DRACO_TP_MAX_WORLD + P.tp_rank,
+                       sig);
+      *reinterpret_cast<volatile int*>(P.tp_buf[P.tp_rank] + P.tp_counter_off) = tp_epoch;
     }
   }
 }
@@ -1061,14 +1107,14 @@ size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch) {
   return local.ws_needed;
 }
 
-template <int G, int NT>
+template <int G, int NT, bool TP>
 static cudaError_t launch_gemv(const HostPlan& hp, cudaStream_t st) {
   static int attr_set[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
     cudaError_t e =
-        cudaFuncSetAttribute(gemv_kernel<G, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
+        cudaFuncSetAttribute(gemv_kernel<G, NT, TP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget);
     if (e != cudaSuccess) return e;
     attr_set[dev] = 1;
   }
@@ -1086,15 +1132,71 @@ static cudaError_t launch_gemv(const HostPlan& hp, cudaStream_t st) {
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemv_kernel<G, NT>, P);
+  return cudaLaunchKernelEx(&cfg, gemv_kernel<G, NT, TP>, P);
 }
 
-int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
-                char* msg, size_t ml) {
+template <bool TP>
+static cudaError_t dispatch_gemv(const HostPlan& hp, int batch, cudaStream_t st) {
+  if (batch == 1) return launch_gemv<4, 1, TP>(hp, st);
+  if (batch == 2) return launch_gemv<2, 1, TP>(hp, st);
+  switch (hp.P.nt) {
+    case 1: return launch_gemv<1, 1, TP>(hp, st);
+    case 2: return launch_gemv<1, 2, TP>(hp, st);
+    case 4: return launch_gemv<1, 4, TP>(hp, st);
+    default: return launch_gemv<1, 8, TP>(hp, st);
+  }
+}
+
+// Fill the tensor-parallel fields of a plan from the exchange description.
+static int set_tp(HostPlan& hp, const draco_gemv_problem* probs, int n, const draco_tp_exchange* ex, char* msg,
+                  size_t ml) {
+  GemvParams& P = hp.P;
+  if (ex->world < 2 || ex->world > DRACO_TP_MAX_WORLD || ex->rank < 0 || ex->rank >= ex->world) {
+    snprintf(msg, ml, "gemv_tp: world %d / rank %d outside 2..%d", ex->world, ex->rank, DRACO_TP_MAX_WORLD);
+    return DRACO_ERR_ARG;
+  }
+  for (int q = 0; q < ex->world; ++q) {
+    if (ex->buffers[q] == nullptr || (reinterpret_cast<uintptr_t>(ex->buffers[q]) & 255) != 0) {
+      snprintf(msg, ml, "gemv_tp: exchange buffer of rank %d is null or not 256-byte aligned", q);
+      return DRACO_ERR_ALIGN;
+    }
+    P.tp_buf[q] = static_cast<uint8_t*>(ex->buffers[q]);
+  }
+  if (ex->flags_off < 0 || (ex->flags_off & 3) || ex->counter_off < 0 || (ex->counter_off & 3)) {
+    snprintf(msg, ml, "gemv_tp: flag / counter offsets must be non-negative multiples of 4");
+    return DRACO_ERR_ALIGN;
+  }
+  for (int i = 0; i < n; ++i) {
+    if (ex->y_off[i] < 0 || (ex->y_off[i] & 3) || ex->parity_stride[i] < 0 || (ex->parity_stride[i] & 3)) {
+      snprintf(msg, ml, "gemv_tp: problem %d output offsets must be non-negative multiples of 4", i);
+      return DRACO_ERR_ALIGN;
+    }
+    P.prob[i].tp_y_off = ex->y_off[i];
+    P.prob[i].tp_par_stride = ex->parity_stride[i];
+    (void)probs;
+  }
+  P.tp_world = ex->world;
+  P.tp_rank = ex->rank;
+  P.tp_flags_off = ex->flags_off;
+  P.tp_counter_off = ex->counter_off;
+  return DRACO_OK;
+}
+
+static int gemv_launch_impl(const draco_gemv_problem* probs, int n, int batch, const draco_tp_exchange* ex, void* ws,
+                            size_t ws_bytes, cudaStream_t st, char* msg, size_t ml) {
   HostPlan hp;
   const int n_sm = device_sm_count();
   if (!build_plan(probs, n, batch, n_sm, hp, msg, ml)) return DRACO_ERR_ARG;
-  if (hp.P.total_slabs == 0) return DRACO_OK;
+  if (ex) {
+    const int rc = set_tp(hp, probs, n, ex, msg, ml);
+    if (rc != DRACO_OK) return rc;
+  }
+  // (a tensor-parallel step with no slabs would never signal its peers)
+  if (hp.P.total_slabs == 0) {
+    if (!ex) return DRACO_OK;
+    snprintf(msg, ml, "gemv_tp: the problems hold no weights");
+    return DRACO_ERR_SHAPE;
+  }
   // the plan's workspace size does not depend on the SM count
   if (ws == nullptr || ws_bytes < hp.ws_needed) {
     snprintf(msg, ml, "gemv: workspace of %zu bytes given, %zu needed", ws_bytes, hp.ws_needed);
@@ -1106,19 +1208,22 @@ int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, siz
   }
   hp.P.ws = static_cast<uint8_t*>(ws);
   cudaError_t e;
-  if (batch == 1) e = launch_gemv<4, 1>(hp, st);
-  else if (batch == 2) e = launch_gemv<2, 1>(hp, st);
-  else switch (hp.P.nt) {
-      case 1: e = launch_gemv<1, 1>(hp, st); break;
-      case 2: e = launch_gemv<1, 2>(hp, st); break;
-      case 4: e = launch_gemv<1, 4>(hp, st); break;
-      default: e = launch_gemv<1, 8>(hp, st); break;
-    }
+  e = ex ? dispatch_gemv<true>(hp, batch, st) : dispatch_gemv<false>(hp, batch, st);
   if (e != cudaSuccess) {
     snprintf(msg, ml, "gemv: launch failed: %s", cudaGetErrorString(e));
     return DRACO_ERR_CUDA;
   }
   return DRACO_OK;
+}
+
+int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
+                char* msg, size_t ml) {
+  return gemv_launch_impl(probs, n, batch, nullptr, ws, ws_bytes, st, msg, ml);
+}
+
+int gemv_launch_tp(const draco_gemv_problem* probs, int n, int batch, const draco_tp_exchange* ex, void* ws,
+                   size_t ws_bytes, cudaStream_t st, char* msg, size_t ml) {
+  return gemv_launch_impl(probs, n, batch, ex, ws, ws_bytes, st, msg, ml);
 }
 
 // ---------------------------------------------------------------------------
@@ -1183,9 +1288,9 @@ int gemv_launch_noalloc(const draco_gemv_problem* probs, int n, int batch, cudaS
     return DRACO_ERR_CUDA;
   }
   hp.P.ws = scratch;
-  if (batch == 1) e = launch_gemv<4, 1>(hp, st);
-  else if (batch == 2) e = launch_gemv<2, 1>(hp, st);
-  else e = launch_gemv<1, 1>(hp, st);  // 3 <= batch <= 4 (larger batches exceed the array)
+  if (batch == 1) e = launch_gemv<4, 1, false>(hp, st);
+  else if (batch == 2) e = launch_gemv<2, 1, false>(hp, st);
+  else e = launch_gemv<1, 1, false>(hp, st);  // 3 <= batch <= 4 (larger batches exceed the array)
   if (e != cudaSuccess) {
     snprintf(msg, ml, "gemv_noalloc: launch failed: %s", cudaGetErrorString(e));
     return DRACO_ERR_CUDA;

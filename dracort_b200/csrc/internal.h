@@ -20,6 +20,14 @@ size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch);
 int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
                 char* msg, size_t msg_len);
 
+// Tensor-parallel grouped GEMV (outputs to every rank's exchange buffer) and
+// the step's finish on this rank.
+int gemv_launch_tp(const draco_gemv_problem* probs, int n, int batch, const draco_tp_exchange* ex, void* ws,
+                   size_t ws_bytes, cudaStream_t st, char* msg, size_t msg_len);
+int tp_finish_launch(const draco_tp_exchange* ex, int batch, int64_t gather_off, int64_t gather_stride,
+                     int gather_width, float* gather_out, int64_t reduce_off, int64_t reduce_stride, int reduce_width,
+                     float* reduce_out, int* status, cudaStream_t st, char* msg, size_t msg_len);
+
 // Allocation-free grouped GEMV (scratch in a fixed device array).
 int gemv_launch_noalloc(const draco_gemv_problem* probs, int n, int batch, cudaStream_t st, char* msg,
                         size_t msg_len);

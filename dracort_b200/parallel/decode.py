@@ -3,12 +3,21 @@ gate, up, down) — the multi-GPU form of the config-2 / config-4 workload.
 
 Per rank: one grouped GEMV launch over the rank's shards of the seven weights
 (column-parallel q/k/v/gate/up: a range of output rows; row-parallel o/down: a
-super-block range of the reduction dim), writing straight into two fused
-communication buffers; then one NCCL all-gather for the five column-parallel
-outputs and one NCCL all-reduce for the two row-parallel ones.  These are the
-shard-boundary exchanges of draco/parallel/tp.py (ColumnParallelLinear /
-RowParallelLinear, whose all-reduce the reference leaves as a comment,
-tp.py:182-183), fused per layer.
+super-block range of the reduction dim).  These are the shard-boundary
+exchanges of draco/parallel/tp.py (ColumnParallelLinear / RowParallelLinear,
+whose all-reduce the reference leaves as a comment, tp.py:182-183), done per
+layer in one of two ways:
+
+* ``fused=False`` (the NCCL baseline): the GEMV writes two local
+  communication buffers, then one NCCL all-gather for the five
+  column-parallel outputs and one NCCL all-reduce for the two row-parallel
+  ones.
+* ``fused=True``: the GEMV (draco_gguf_gemv_grouped_tp) stores every output
+  value straight into every rank's exchange buffer over NVLink and signals
+  each rank when done; draco_tp_finish then waits for every rank's signal,
+  copies the gathered columns out and sums the row partials in rank order.
+  Two kernel launches per step and no host collective, so the step can be
+  captured in a CUDA graph.
 """
 
 from __future__ import annotations
@@ -19,6 +28,9 @@ from typing import List, Sequence
 import numpy as np
 import torch
 
+import ctypes
+
+from dracort_b200 import _native as N
 from dracort_b200 import gguf_ops as G
 from dracort_b200.parallel.tp import shard_k, shard_rows
 
@@ -31,8 +43,9 @@ class TPDecodeLayer:
 
     def __init__(self, specs: Sequence, packed: Sequence[np.ndarray], rank: int, world: int, batch: int,
                  device: torch.device, seed: int = 0, group=None, l2_bytes: int = 126 << 20,
-                 min_copies: int = 2, copies: int = 0) -> None:
-        """copies: weight copies to rotate through (0: enough to exceed 4x L2)."""
+                 min_copies: int = 2, copies: int = 0, fused: bool = False) -> None:
+        """copies: weight copies to rotate through (0: enough to exceed 4x L2);
+        fused: exchange over NVLink inside the kernels instead of NCCL."""
         import torch.distributed as dist
 
         self.rank, self.world, self.batch, self.device = rank, world, batch, device
@@ -78,14 +91,96 @@ class TPDecodeLayer:
             else:
                 self.y_local.append(self.rbuf[:, orr:orr + n])
                 orr += n
+        self.fused = fused
+        self.exchange = None
+        if fused:
+            self._init_fused(copies)
+            self.launches_per_step = 2  # the tensor-parallel GEMV and the finish kernel
+            self.graph_safe = True
+            return
         self.plans = [G.GemvPlan([G.GemvProblem(qt, c[i], self.x_local[i], self.y_local[i], n, k)
                                   for i, (_, qt, n, k, _, _, _) in enumerate(self.local)]) for c in copies]
         self.launches_per_step = 1  # our GEMV kernel; NCCL adds its own collective kernels
         self.graph_safe = False
 
+    def _init_fused(self, copies) -> None:
+        """Exchange buffer layout (identical on every rank): flags[2][8] int32 at
+        0, the step counter at 128, then per step parity the gathered column
+        block [world][batch][wc] and the row-partial block [world][batch][wr]."""
+        from dracort_b200.parallel.exchange import ExchangeBuffer
+
+        B, W, r = self.batch, self.world, self.rank
+
+        def a256(v):
+            return (v + 255) // 256 * 256
+
+        self.g_stride = W * B * self.wc * 4
+        self.r_stride = W * B * self.wr * 4
+        self.g_off = 256
+        self.r_off = a256(self.g_off + 2 * self.g_stride)
+        self.exchange = ExchangeBuffer(a256(self.r_off + 2 * self.r_stride), r, W, self.group)
+        ex = N.TpExchange()
+        ex.world, ex.rank = W, r
+        for q, ptr in enumerate(self.exchange.ptrs):
+            ex.buffers[q] = ptr
+        ex.flags_off, ex.counter_off = 0, 128
+        ldys = []
+        oc = orr = 0
+        for j, (_, _, n, _, _, kind, _) in enumerate(self.local):
+            if kind == "col":
+                ex.y_off[j] = self.g_off + (r * B * self.wc + oc) * 4
+                ex.parity_stride[j] = self.g_stride
+                ldys.append(self.wc)
+                oc += n
+            else:
+                ex.y_off[j] = self.r_off + (r * B * self.wr + orr) * 4
+                ex.parity_stride[j] = self.r_stride
+                ldys.append(self.wr)
+                orr += n
+        self.ex = ex
+        self._lib = N.load()
+        self.tp_status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.tp_plans = []
+        for c in copies:
+            arr = (N.GemvProblem * len(self.local))()
+            for j, ((_, qt, n, k, _, _, _), xl) in enumerate(zip(self.local, self.x_local)):
+                arr[j] = N.GemvProblem(qt, 0, c[j].data_ptr(), xl.data_ptr(), None, None, n, k, xl.stride(0),
+                                       ldys[j])
+            need = self._lib.draco_gguf_gemv_workspace_bytes(arr, len(self.local), B)
+            if need == 0:
+                N.check(N.DRACO_ERR_ARG, "gemv_tp workspace query failed")
+            ws = torch.zeros(int(need), dtype=torch.uint8, device=self.device)
+            self.tp_plans.append((arr, ws, c))
+
+    def _step_fused(self, i: int) -> None:
+        arr, ws, _ = self.tp_plans[i % len(self.tp_plans)]
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = self._lib.draco_gguf_gemv_grouped_tp(arr, len(self.local), self.batch, ctypes.byref(self.ex),
+                                                  ws.data_ptr(), ws.numel(), stream)
+        if rc:
+            N.check(rc, "gemv_tp")
+        rc = self._lib.draco_tp_finish(ctypes.byref(self.ex), self.batch, self.g_off, self.g_stride, self.wc,
+                                       self.gout.data_ptr(), self.r_off, self.r_stride, self.wr,
+                                       self.rbuf.data_ptr(), self.tp_status.data_ptr(), stream)
+        if rc:
+            N.check(rc, "tp_finish")
+
+    def status(self) -> int:
+        """First nonzero device status of the fused path (finish, then the GEMV
+        workspaces), 0 when every step succeeded.  Synchronises."""
+        if not self.fused:
+            return 0
+        st = int(self.tp_status.item())
+        for _, ws, _ in self.tp_plans:
+            st = st or int(ws[:4].view(torch.int32).item())
+        return st
+
     def step(self, i: int) -> None:
         import torch.distributed as dist
 
+        if self.fused:
+            self._step_fused(i)
+            return
         self.plans[i % self.n_copies].run()
         dist.all_gather_into_tensor(self.gout, self.gbuf, group=self.group)
         dist.all_reduce(self.rbuf, group=self.group)
@@ -125,4 +220,10 @@ class TPDecodeLayer:
                 "d2h_bytes_per_step": (self.gout.numel() + self.rbuf.numel()) * 4}
 
     def close(self) -> None:
+        if self.fused:
+            self.tp_plans.clear()
+            if self.exchange is not None:
+                self.exchange.close()
+                self.exchange = None
+            return
         self.plans.clear()

@@ -66,6 +66,7 @@ extern "C" {
 #define DRACO_ERR_TIMEOUT 5   /* a bounded device wait ran out           */
 #define DRACO_ERR_ARG 6       /* null pointer, bad batch, too many problems */
 #define DRACO_ERR_WORKSPACE 7 /* workspace missing or too small          */
+#define DRACO_ERR_PEER 8      /* another rank reported a failed step     */
 
 /* Output element types for the GEMM. */
 #define DRACO_DTYPE_F32 0
@@ -176,6 +177,70 @@ int draco_gguf_gemv_grouped(const draco_gemv_problem* problems, int n_problems, 
  * serialised by the caller. */
 int draco_gguf_gemv_grouped_noalloc(const draco_gemv_problem* problems, int n_problems, int batch,
                                     void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Tensor-parallel decode over NVLink: one process per GPU, ranks on one box.
+ *
+ * Replaces the shard-boundary collectives of draco/parallel/tp.py
+ * (ColumnParallelLinear's gather of the output shards, RowParallelLinear's
+ * sum of the partial outputs; the reference leaves that all-reduce as a
+ * comment at tp.py:182-183).  Every rank allocates an exchange buffer of the
+ * same size and layout and maps the others' with CUDA IPC.  The GEMV stores
+ * its outputs straight into every rank's buffer and signals each rank;
+ * draco_tp_finish, on each rank, waits for every rank's signal of the step,
+ * then copies the gathered columns out and sums the row partials.
+ * ------------------------------------------------------------------------- */
+#define DRACO_TP_MAX_WORLD 8
+#define DRACO_IPC_HANDLE_BYTES 64
+
+/* Exchange buffer: cudaMalloc'd (256-byte aligned) and zero-filled, as the
+ * flags and the step counter in it must start at zero. */
+int draco_tp_buffer_alloc(size_t bytes, void** ptr);
+int draco_tp_buffer_free(void* ptr);
+/* The CUDA IPC handle (DRACO_IPC_HANDLE_BYTES bytes) of a buffer from
+ * draco_tp_buffer_alloc; the mapping of another process's handle into this
+ * one (on the current device) and its release. */
+int draco_ipc_get_handle(void* ptr, void* handle);
+int draco_ipc_open(const void* handle, void** peer_ptr);
+int draco_ipc_close(void* peer_ptr);
+
+typedef struct draco_tp_exchange {
+  int world; /* 2..DRACO_TP_MAX_WORLD */
+  int rank;
+  void* buffers[DRACO_TP_MAX_WORLD]; /* every rank's buffer as mapped here; [rank] is the own one */
+  int64_t flags_off;   /* int32 flags[2][DRACO_TP_MAX_WORLD] in every buffer */
+  int64_t counter_off; /* int32 step counter in every buffer */
+  /* per GEMV problem: byte offset of this rank's output block (step parity
+   * 0) in every buffer, and the bytes from the parity-0 to the parity-1 block */
+  int64_t y_off[DRACO_GEMV_MAX_PROBLEMS];
+  int64_t parity_stride[DRACO_GEMV_MAX_PROBLEMS];
+} draco_tp_exchange;
+
+/* Grouped GEMV of this rank's shards whose outputs go to every rank: the
+ * value y[b][row] of problem i is stored at
+ *   (float*)(buffers[q] + y_off[i] + parity * parity_stride[i])[b * ldy + row]
+ * for every rank q (problems[i].y is not used and may be NULL).  The step's
+ * epoch is the own buffer's step counter + 1 and its parity the epoch's.
+ * When every CTA is done, the last one stores the epoch (negated if the
+ * launch aborted) into flags[parity][rank] of every buffer and the epoch
+ * into the own counter.  Workspace as for draco_gguf_gemv_grouped. */
+int draco_gguf_gemv_grouped_tp(const draco_gemv_problem* problems, int n_problems, int batch,
+                               const draco_tp_exchange* ex, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* The end of the step on this rank.  Waits (bounded, 1 s) until every
+ * rank's flag for the step holds the step's epoch, then, over the own buffer
+ * at the step's parity,
+ *   gather_out[q][b][j] = buffer[gather_off + parity * gather_stride][q][b][j]
+ *   reduce_out[b][j]    = sum over q of buffer[reduce_off + parity * reduce_stride][q][b][j]
+ * (fp32; q < world, b < batch, j < the width; a width of 0 skips that part).
+ * Launch it after the step's draco_gguf_gemv_grouped_tp on the same stream:
+ * it waits only for the other GPUs.  *status (device int32, may be NULL)
+ * becomes DRACO_ERR_TIMEOUT when a rank's signal did not come and
+ * DRACO_ERR_PEER when a rank reported an aborted step. */
+int draco_tp_finish(const draco_tp_exchange* ex, int batch, int64_t gather_off, int64_t gather_stride,
+                    int gather_width, float* gather_out, int64_t reduce_off, int64_t reduce_stride,
+                    int reduce_width, float* reduce_out, int* status, void* stream);
 
 /* One weight of a prefill GEMM launch: Y = X @ dequant(W)^T.
  *   w      : TILED weight [n_rows, k] of type qtype (16-byte aligned)
