@@ -9,11 +9,14 @@
 // all ranks' signals of the step, copies the gathered column outputs out and
 // sums the row-parallel partials.
 //
-// Launched after the step's GEMV on the same stream and without programmatic
-// dependent launch, so it never waits for a kernel of its own GPU: the only
-// waits are on flags written by the other GPUs' kernels, bounded by
-// kTpWaitNs, after which the status word records the failure and the kernel
-// returns.
+// Launched after the step's GEMV on the same stream with programmatic
+// dependent launch: it may be scheduled early, but griddepcontrol.wait holds
+// it until that GEMV has completed, so it never spins on a kernel of its own
+// GPU: the only waits are on flags written by the other GPUs' kernels,
+// bounded by kTpWaitNs, after which the status word records the failure and
+// the kernel returns.  It lets the next kernel in the stream (the next step's
+// GEMV) launch at once: that GEMV streams weights meanwhile and waits for
+// this kernel's completion before it reads activations or writes outputs.
 #include <algorithm>
 #include <cstdio>
 
@@ -41,6 +44,8 @@ struct TpFinishParams {
 
 __global__ void __launch_bounds__(kTpThreads) tp_finish_kernel(const __grid_constant__ TpFinishParams F) {
   __shared__ int failed;
+  grid_dependency_wait();    // this rank's GEMV of the step is complete
+  grid_launch_dependents();  // the next step's GEMV may start streaming weights
   // the step's epoch, counted by this rank's GEMV (complete: it precedes us in the stream)
   const int epoch = *reinterpret_cast<const volatile int*>(F.own + F.counter_off);
   const int par = epoch & 1;
@@ -119,8 +124,17 @@ int tp_finish_launch(const draco_tp_exchange* ex, int batch, int64_t gather_off,
   const int64_t work = std::max<int64_t>((int64_t)ex->world * batch * gather_width, (int64_t)batch * reduce_width);
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(2 * device_sm_count(),
                                                                  (work + kTpThreads - 1) / kTpThreads));
-  tp_finish_kernel<<<blocks, kTpThreads, 0, st>>>(F);
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(kTpThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, tp_finish_kernel, F);
   if (e != cudaSuccess) {
     snprintf(msg, ml, "tp_finish: launch failed: %s", cudaGetErrorString(e));
     return DRACO_ERR_CUDA;

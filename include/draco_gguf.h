@@ -235,7 +235,8 @@ int draco_gguf_gemv_grouped_tp(const draco_gemv_problem* problems, int n_problem
  *   reduce_out[b][j]    = sum over q of buffer[reduce_off + parity * reduce_stride][q][b][j]
  * (fp32; q < world, b < batch, j < the width; a width of 0 skips that part).
  * Launch it after the step's draco_gguf_gemv_grouped_tp on the same stream:
- * it waits only for the other GPUs.  *status (device int32, may be NULL)
+ * it first waits (griddepcontrol.wait) for that launch to complete and then
+ * spins only on the other GPUs' flags.  *status (device int32, may be NULL)
  * becomes DRACO_ERR_TIMEOUT when a rank's signal did not come and
  * DRACO_ERR_PEER when a rank reported an aborted step. */
 int draco_tp_finish(const draco_tp_exchange* ex, int batch, int64_t gather_off, int64_t gather_stride,
