@@ -54,6 +54,7 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv_grouped_noalloc",
     "draco_gguf_gemm",
     "draco_swiglu_bf16",
+    "draco_swiglu_f32",
     "draco_tp_buffer_alloc",
     "draco_tp_buffer_free",
     "draco_ipc_get_handle",
@@ -168,6 +169,8 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_gemm.argtypes = [ctypes.POINTER(GemmProblem), c_int, vp, vp]
         lib.draco_swiglu_bf16.restype = c_int
         lib.draco_swiglu_bf16.argtypes = [vp, vp, vp, i64, vp]
+        lib.draco_swiglu_f32.restype = c_int
+        lib.draco_swiglu_f32.argtypes = [vp, vp, vp, i64, vp]
         lib.draco_tp_buffer_alloc.restype = c_int
         lib.draco_tp_buffer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
         lib.draco_tp_buffer_free.restype = c_int

@@ -1,8 +1,10 @@
-// act.cu — SwiGLU product of a gated MLP, out = bf16(silu(gate) * up), computed
-// in fp32 from bf16 inputs with one rounding.  Sits between the gate/up and
-// the down dequant-GEMMs of an expert or decoder MLP: the reference's
-// Expert.forward (draco/models/moe/expert.py:47-49) and the Llama MLP apply
-// act_fn(gate_proj(x)) * up_proj(x) there.  HBM-bound: 6 bytes per element.
+// act.cu — SwiGLU product of a gated MLP, out = silu(gate) * up, computed in
+// fp32: from bf16 inputs with one rounding to bf16 (prefill / experts), or on
+// fp32 vectors (decode).  Sits between the gate/up and the down dequant
+// kernels of an expert or decoder MLP: the reference's Expert.forward
+// (draco/models/moe/expert.py:47-49), fused_swiGLU (draco/kernels/ops.py:
+// 114-137) and the Llama MLP apply act_fn(gate_proj(x)) * up_proj(x) there.
+// HBM-bound: 6 (bf16) or 12 (fp32) bytes per element.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -47,6 +49,31 @@ cudaError_t launch_swiglu_bf16(const void* gate, const void* up, void* out, int6
   const int grid = (int)(want < 1 ? 1 : (want > 8 * device_sm_count() ? 8 * device_sm_count() : want));
   swiglu_bf16_kernel<<<grid, threads, 0, st>>>(static_cast<const uint16_t*>(gate), static_cast<const uint16_t*>(up),
                                                 static_cast<uint16_t*>(out), n);
+  return cudaGetLastError();
+}
+
+// fp32: 4 elements per thread and iteration on 16-byte vectors, the last n % 4
+// by single threads
+__global__ void swiglu_f32_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ o,
+                                  int64_t n) {
+  const int64_t n4 = n >> 2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float4* g4 = reinterpret_cast<const float4*>(g);
+  const float4* u4 = reinterpret_cast<const float4*>(u);
+  float4* o4 = reinterpret_cast<float4*>(o);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 a = __ldg(g4 + i), b = __ldg(u4 + i);
+    o4[i] = make_float4(silu_mul(a.x, b.x), silu_mul(a.y, b.y), silu_mul(a.z, b.z), silu_mul(a.w, b.w));
+  }
+  const int64_t t = (n4 << 2) + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < n) o[t] = silu_mul(g[t], u[t]);
+}
+
+cudaError_t launch_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, cudaStream_t st) {
+  const int threads = 256;
+  const int64_t want = ((n >> 2) + threads - 1) / threads;
+  const int grid = (int)(want < 1 ? 1 : (want > 8 * device_sm_count() ? 8 * device_sm_count() : want));
+  swiglu_f32_kernel<<<grid, threads, 0, st>>>(gate, up, out, n);
   return cudaGetLastError();
 }
 

@@ -289,3 +289,13 @@ int draco_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, vo
   cudaError_t e = draco::launch_swiglu_bf16(gate, up, out, n, (cudaStream_t)stream);
   return e == cudaSuccess ? ok() : cuda_fail(e, "swiglu");
 }
+
+int draco_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, void* stream) {
+  if (n < 0) return fail(DRACO_ERR_SHAPE, "swiglu_f32: negative length");
+  if (n == 0) return ok();
+  if (!gate || !up || !out) return fail(DRACO_ERR_ARG, "swiglu_f32: null pointer");
+  if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(DRACO_ERR_ALIGN, "swiglu_f32: gate, up and out must be 16-byte aligned");
+  cudaError_t e = draco::launch_swiglu_f32(gate, up, out, n, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "swiglu_f32");
+}

@@ -39,6 +39,8 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
 
 // out = bf16(silu(gate) * up) over n bf16 elements (16-byte aligned).
 cudaError_t launch_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, cudaStream_t st);
+// out = silu(gate) * up over n fp32 elements (16-byte aligned).
+cudaError_t launch_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, cudaStream_t st);
 
 // Number of SMs of the current device (cached per device).
 int device_sm_count();

@@ -343,6 +343,24 @@ def swiglu_bf16(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor
     return out
 
 
+def swiglu(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(gate) * up on the GPU for bf16 (one rounding, draco_swiglu_bf16) or
+    fp32 (draco_swiglu_f32) contiguous CUDA tensors of one shape; `out` may be
+    `gate`.  Pointers must be 16-byte aligned (fresh allocations are)."""
+    if gate.dtype == torch.bfloat16:
+        return swiglu_bf16(gate, up, out)
+    for t, nm in ((gate, "gate"), (up, "up")):
+        _require_cuda(t, nm)
+        if t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError(f"swiglu: {nm} must be a contiguous float32 or bfloat16 CUDA tensor")
+    if gate.shape != up.shape:
+        raise DracoFormatError(f"swiglu: gate {tuple(gate.shape)} and up {tuple(up.shape)} differ")
+    out = out if out is not None else torch.empty_like(gate)
+    N.check(N.load().draco_swiglu_f32(gate.data_ptr(), up.data_ptr(), out.data_ptr(), gate.numel(),
+                                      _stream_ptr(gate.device)), "swiglu")
+    return out
+
+
 def gemm(qtype: int, w_tiled: torch.Tensor, x: torch.Tensor, n_rows: int, k: int,
          out_dtype: torch.dtype = torch.bfloat16, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Y = X @ dequant(W)^T with X cast to bf16; returns [m, n_rows] of out_dtype."""

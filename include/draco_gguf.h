@@ -280,6 +280,12 @@ int draco_gguf_gemm(const draco_gemm_problem* problems, int n_problems, int* sta
  * Expert.forward (draco/models/moe/expert.py:47-49). */
 int draco_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, void* stream);
 
+/* fp32 form for decode activations: out = silu(gate) * up over n fp32
+ * values (expf as CUDA provides it), 16-byte aligned, out may alias gate.
+ * Replaces the activation step of draco/kernels/ops.py:114-137
+ * (fused_swiGLU) between the gate/up and down GEMVs. */
+int draco_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, void* stream);
+
 /* Single-weight convenience form of draco_gguf_gemv_grouped. */
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias,
                     int batch, int64_t n_rows, int64_t k, void* workspace,
