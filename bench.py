@@ -67,7 +67,8 @@ def parse_args(argv=None):
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
-    ap.add_argument("--sweep", action="store_true", help="also time batch 4 and 16 (reported under 'batches')")
+    ap.add_argument("--no-sweep", dest="sweep", action="store_false",
+                    help="skip timing batch 4 and 16 (reported under 'batches')")
     ap.add_argument("--prefill-steps", type=int, default=200, help="timed steps of the prefill GEMM leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill GEMM leg")
     ap.add_argument("--moe-steps", type=int, default=50, help="timed steps of the MoE (config 5) leg")
@@ -240,6 +241,60 @@ def cpu_prefill_leg(specs, packed, seed, tokens=64):
     flops = sum(2 * tokens * s.n_rows * s.k for s in specs)
     return {"tflops": flops / sum(best) / 1e12, "tokens": tokens, "dequant_s": t_dequant,
             "step_s": sum(best)}
+
+
+def cpu_model_leg(specs, layer_packed, seed, n_layers, batches=(1, 32)):
+    """Config 4 on the host (the reference's path): one layer's seven projections
+    dequantized to the fp32 cache, then x @ W.T per projection (median of 3),
+    times the number of layers."""
+    from oracle import gguf_oracle as O
+
+    rng = np.random.default_rng(seed + 13)
+    t0 = time.perf_counter()
+    weights = [O.dequantize_matrix(s.qtype, p, s.n_rows, s.k) for s, p in zip(specs, layer_packed)]
+    t_dequant = time.perf_counter() - t0
+    out = {"dequant_layer_s": round(t_dequant, 3)}
+    for b in batches:
+        xs = [rng.standard_normal((b, s.k)).astype(np.float32) for s in specs]
+        layer_s = 0.0
+        for x, w in zip(xs, weights):
+            O.matmul_f32(x, w)
+            ts = []
+            for _ in range(3):
+                t = time.perf_counter()
+                O.matmul_f32(x, w)
+                ts.append(time.perf_counter() - t)
+            layer_s += float(np.median(ts))
+        out[str(b)] = {"ms_per_step": round(layer_s * n_layers * 1e3, 3),
+                       "tokens_per_s": round(b / (layer_s * n_layers), 2)}
+    return out
+
+
+def cpu_moe_leg(expert, hidden, ffn, tokens_per_expert, n_experts, seed):
+    """Config 5 on the host (the reference's ExpertGroup path on fp32
+    dequantized weights, torch CPU): one expert's gate/up/down MLP on its share
+    of the routed tokens, median of 3, times the number of experts."""
+    import torch
+    import torch.nn.functional as F
+
+    from oracle import gguf_oracle as O
+
+    qt, g, u, d = expert
+    t0 = time.perf_counter()
+    wg = torch.from_numpy(O.dequantize_matrix(qt, g, ffn, hidden))
+    wu = torch.from_numpy(O.dequantize_matrix(qt, u, ffn, hidden))
+    wd = torch.from_numpy(O.dequantize_matrix(qt, d, hidden, ffn))
+    t_dequant = time.perf_counter() - t0
+    x = torch.from_numpy(np.random.default_rng(seed + 17).standard_normal((tokens_per_expert, hidden))
+                         .astype(np.float32))
+    ts = []
+    for _ in range(4):
+        t = time.perf_counter()
+        (F.silu(x @ wg.T) * (x @ wu.T)) @ wd.T
+        ts.append(time.perf_counter() - t)
+    expert_s = float(np.median(ts[1:]))
+    return {"step_s": expert_s * n_experts, "expert_s": expert_s, "dequant_expert_s": t_dequant,
+            "threads": torch.get_num_threads()}
 
 
 def prefill_leg(args, dev, peaks, rank, world, pg, timed, want_e2e, want_cpu):
@@ -434,6 +489,15 @@ def model_leg(args, dev, peaks, rank, world, pg, timed):
             del tp
         torch.cuda.empty_cache()
     out["value"] = out["batches"]["1"]["gbs"]
+    if rank == 0 and world == 1 and not args.no_cpu:
+        res = cpu_model_leg(specs, layers[0], args.seed, n_layers)
+        out["cpu_baseline"] = {
+            "value": res["1"]["tokens_per_s"], "unit": "tokens/s (batch 1)", "cores": os.cpu_count(), "kind": "port",
+            "batches": {b: res[b] for b in ("1", "32")},
+            "sample": (f"reference path (oracle port of gguf._dequantize + GenericGemmKernel.matmul_f32): one "
+                       f"layer's 7 projections on the warm fp32 cache, median of 3 per projection, x {n_layers} "
+                       f"layers; first-touch dequant of one layer {res['dequant_layer_s']:.1f} s; numpy/OpenBLAS "
+                       f"default threads")}
     return out
 
 
@@ -492,9 +556,25 @@ def moe_leg(args, dev, peaks, rank, world, pg, timed):
                      "frac": round(gbs / (peaks["hbm_gbs"] * world), 4),
                      "note": f"{wbytes} B of packed expert weights per step (each expert read once) over the "
                              f"whole step time incl. routing and collectives"},
-        "gpu_launches": 2 * K,
+        "gpu_launches": 3 * K * max(1, -(-2 * (n_exp // world) // 16)),
         "clocks": clocks,
+        **({"cpu_baseline": _moe_cpu_baseline(experts, n_exp)} if rank == 0 and world == 1 and not args.no_cpu
+           else {}),
     }
+
+
+def _moe_cpu_baseline(experts, n_exp):
+    from dracort_b200.workloads import MOE_FFN, MOE_HIDDEN, MOE_TOKENS, MOE_TOP_K
+
+    per_expert = MOE_TOKENS * MOE_TOP_K // n_exp
+    res = cpu_moe_leg(experts[0], MOE_HIDDEN, MOE_FFN, per_expert, n_exp, 0)
+    flops = 2 * 3 * MOE_HIDDEN * MOE_FFN * MOE_TOKENS * MOE_TOP_K
+    return {"value": round(flops / res["step_s"] / 1e12, 5), "unit": "TFLOP/s", "cores": os.cpu_count(),
+            "kind": "port", "ms_per_step": round(res["step_s"] * 1e3, 2),
+            "sample": (f"reference ExpertGroup math (down(silu(gate(x)) * up(x))) on the oracle's fp32 dequantized "
+                       f"weights, torch CPU ({res['threads']} threads): one expert on {per_expert} tokens (the "
+                       f"mean routed share), median of 3, x {n_exp} experts; first-touch dequant of one expert "
+                       f"{res['dequant_expert_s']:.1f} s")}
 
 
 # ---------------------------------------------------------------------------
