@@ -329,6 +329,24 @@ def gemm_grouped_unchecked(entries: Sequence[tuple], device: torch.device,
     N.check(lib.draco_gguf_gemm(arr, len(entries), st, _stream_ptr(device)), "gemm")
 
 
+def gemm_grouped_raw(entries: Sequence[tuple], device: torch.device, status: Optional[torch.Tensor] = None) -> None:
+    """gemm_grouped on raw device pointers for internal callers that slice one
+    buffer into many problems (the MoE experts' row blocks) and would otherwise
+    pay for a tensor view per problem: entries are (qtype, w_ptr, x_ptr, y_ptr,
+    m, n_rows, k, ldx, ldy, ydtype) with ydtype N.DTYPE_BF16 or N.DTYPE_F32, at
+    most GEMM_MAX_PROBLEMS; only the C ABI's own checks run."""
+    if not entries:
+        return
+    arr = (N.GemmProblem * len(entries))()
+    for s, (qt, w, x, y, m, n, k, ldx, ldy, ydt) in zip(arr, entries):
+        s.qtype, s.ydtype = qt, ydt
+        s.w, s.x, s.y = w, x, y
+        s.m, s.n_rows, s.k = m, n, k
+        s.ldx, s.ldy = ldx, ldy
+    st = status.data_ptr() if status is not None else None
+    N.check(N.load().draco_gguf_gemm(arr, len(entries), st, _stream_ptr(device)), "gemm")
+
+
 def swiglu_bf16(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """bf16(silu(gate) * up) in fp32 with one rounding (C ABI draco_swiglu_bf16)."""
     for t, nm in ((gate, "gate"), (up, "up")):

@@ -73,6 +73,7 @@ class GGUFExpertGroup:
             def tiled(p, n, k, qt=qt):
                 return G.repack(qt, torch.from_numpy(np.ascontiguousarray(p).reshape(-1)).to(device), n, k)
             self.w.append((qt, tiled(g, ffn, hidden), tiled(u, ffn, hidden), tiled(d, hidden, ffn)))
+        self.w_ptrs = [(qt, a.data_ptr(), b.data_ptr(), c.data_ptr()) for qt, a, b, c in self.w]
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
 
     @property
@@ -90,20 +91,25 @@ class GGUFExpertGroup:
             x = x.to(torch.bfloat16).contiguous()
         gate = torch.empty((rows, self.ffn), dtype=torch.bfloat16, device=self.device)
         up = torch.empty_like(gate)
+        # each expert's rows are a block of x / gate / up / out: pass pointers
+        # into the buffers rather than a tensor view per block
+        H, Fn, bf = self.hidden, self.ffn, G.N.DTYPE_BF16
+        px, pg, pu, po = x.data_ptr(), gate.data_ptr(), up.data_ptr(), out.data_ptr()
         gu, down, r0 = [], [], 0
         for i, c in enumerate(counts):
             if c:
-                qt, wg, wu, wd = self.w[i]
-                gu.append((qt, wg, x[r0:r0 + c], gate[r0:r0 + c], self.ffn, self.hidden))
-                gu.append((qt, wu, x[r0:r0 + c], up[r0:r0 + c], self.ffn, self.hidden))
-                down.append((qt, wd, gate[r0:r0 + c], out[r0:r0 + c], self.hidden, self.ffn))
+                qt, wg, wu, wd = self.w_ptrs[i]
+                xr, fr = px + 2 * r0 * H, 2 * r0 * Fn
+                gu.append((qt, wg, xr, pg + fr, c, Fn, H, H, Fn, bf))
+                gu.append((qt, wu, xr, pu + fr, c, Fn, H, H, Fn, bf))
+                down.append((qt, wd, pg + fr, po + 2 * r0 * H, c, H, Fn, Fn, H, bf))
             r0 += c
         mx = G.N.GEMM_MAX_PROBLEMS
         for i in range(0, len(gu), mx):
-            G.gemm_grouped_unchecked(gu[i:i + mx], self.device, self.status)
+            G.gemm_grouped_raw(gu[i:i + mx], self.device, self.status)
         G.swiglu_bf16(gate, up, out=gate)  # the SwiGLU product overwrites gate, the down input
         for i in range(0, len(down), mx):
-            G.gemm_grouped_unchecked(down[i:i + mx], self.device, self.status)
+            G.gemm_grouped_raw(down[i:i + mx], self.device, self.status)
         return out
 
 
