@@ -279,18 +279,32 @@ __device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProb
   const int m = lane >> 2, r = lane & 3, kap = r >> 1, t0 = 2 * (r & 1);
   const int kk0 = 256 * j + 32 * m + 8 * r;
   const bool q6 = pr.qt == kQ6_K;
-  for (int b = 0; b < P.batch; ++b) {
-    const float* xp = pr.x + (int64_t)b * pr.ldx + kk0;
-    float v[8];
-    if (kk0 + 8 <= pr.k && (reinterpret_cast<uintptr_t>(xp) & 15) == 0) {
-      const float4 lo4 = __ldg(reinterpret_cast<const float4*>(xp));
-      const float4 hi4 = __ldg(reinterpret_cast<const float4*>(xp) + 1);
-      v[0] = lo4.x, v[1] = lo4.y, v[2] = lo4.z, v[3] = lo4.w;
-      v[4] = hi4.x, v[5] = hi4.y, v[6] = hi4.z, v[7] = hi4.w;
-    } else {
+  // Dense layouts (batch >= 3): the x values of kPre batch rows are loaded
+  // before any of them is converted, so a slab's L2 round trips overlap
+  // instead of following one another, one per row.
+  constexpr int kPre = kDiag ? 1 : 4;
+  for (int b0 = 0; b0 < P.batch; b0 += kPre) {
+    float vv[kPre][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = (kk0 + i < pr.k) ? __ldg(xp + i) : 0.f;
+    for (int q = 0; q < kPre; ++q) {
+      const int b = b0 + q;
+      if (b >= P.batch) break;
+      const float* xp = pr.x + (int64_t)b * pr.ldx + kk0;
+      if (kk0 + 8 <= pr.k && (reinterpret_cast<uintptr_t>(xp) & 15) == 0) {
+        const float4 lo4 = __ldg(reinterpret_cast<const float4*>(xp));
+        const float4 hi4 = __ldg(reinterpret_cast<const float4*>(xp) + 1);
+        vv[q][0] = lo4.x, vv[q][1] = lo4.y, vv[q][2] = lo4.z, vv[q][3] = lo4.w;
+        vv[q][4] = hi4.x, vv[q][5] = hi4.y, vv[q][6] = hi4.z, vv[q][7] = hi4.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vv[q][i] = (kk0 + i < pr.k) ? __ldg(xp + i) : 0.f;
+      }
     }
+#pragma unroll
+    for (int q = 0; q < kPre; ++q) {
+    const int b = b0 + q;
+    if (b >= P.batch) break;  // uniform across the warp
+    const float (&v)[8] = vv[q];
     float amax = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -350,6 +364,7 @@ __device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProb
 #pragma unroll
         for (int tt = 0; tt < 2; ++tt)
           *reinterpret_cast<uint32_t*>(base + (2 * b + dg) * 32 + tt * 8) = dg ? dl[tt] : dh[tt];
+    }
     }
   }
 }
