@@ -23,7 +23,13 @@
 //    (max |x| / u in [2^13, 2^14)), round to an integer q and split it into
 //    two int8 digits, q = 256 * hi + lo, stored in MMA-fragment order with
 //    the group sums, and arrive on the slab's ready barrier, which completes
-//    with that arrival and the slab's weight bytes.
+//    with that arrival and the slab's weight bytes.  From batch 5 on (two or
+//    more MMA column tiles) the activations are converted once per launch
+//    instead, by gemv_convert_kernel, into per-(problem, super-block) slices
+//    of the workspace laid out as a stage's slice; the converter warps then
+//    fill a stage with one bulk copy of that slice (arrive.expect_tx on the
+//    same ready barrier).  Converting per slab in every CTA repeated the work
+//    for every row group, which dominated at batch 32.
 //  * A barrier wait tests a phase parity, which is only sound when the waiter
 //    sees every phase of the barrier in order.  Stage st holds slabs st,
 //    st + NS, ... (round m = i / NS); the ready barriers are kept per (stage,
@@ -90,6 +96,7 @@ struct GemvProbDev {
   int slab0;  // global index of the problem's first slab
   int qt, n_rows, k, nb, n_rg, n_tiles, cb;
   int64_t tp_y_off, tp_par_stride;  // tensor-parallel output block in every rank's exchange buffer
+  int64_t xcv_off;                   // workspace offset of the pre-converted activation slices
 };
 
 struct GemvParams {
@@ -100,6 +107,7 @@ struct GemvParams {
   int n_prob, batch, nt, n_cta;
   int w_stage, xs_bytes, su_bytes, stage_bytes, n_stages;
   int mbox_slots, mbox_off;  // row-group mailbox after the stages in dynamic shared memory
+  int precvt;                // activations converted by gemv_convert_kernel before the launch
   int tp_world, tp_rank;     // tensor-parallel exchange (tp_world 0: plain outputs)
   uint8_t* tp_buf[DRACO_TP_MAX_WORLD];
   int64_t tp_flags_off, tp_counter_off;
@@ -808,6 +816,27 @@ __device__ __forceinline__ bool consume_segment(const GemvParams& P, const uint8
 }
 
 // ---------------------------------------------------------------------------
+// activation conversion once per launch (batch >= 5): one warp per
+// (problem, super-block) slice, written in the stage layout (digits in
+// MMA-fragment order, then the group sums), padded batch slots zero
+// ---------------------------------------------------------------------------
+constexpr int kConvertWarpsPerBlock = 4;
+
+template <int NT>
+__global__ void __launch_bounds__(kConvertWarpsPerBlock * 32) gemv_convert_kernel(const __grid_constant__ GemvParams P) {
+  grid_launch_dependents();  // the GEMV may start streaming weights at once
+  const int lane = threadIdx.x & 31;
+  int u = blockIdx.x * kConvertWarpsPerBlock + (threadIdx.x >> 5), p = 0;
+  while (p < P.n_prob && u >= P.prob[p].nb) u -= P.prob[p].nb, ++p;
+  if (p >= P.n_prob) return;
+  const int xb = P.xs_bytes + P.su_bytes;
+  uint8_t* dst = P.ws + P.prob[p].xcv_off + (int64_t)u * xb;
+  for (int i = lane; i < (xb >> 4); i += 32) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
+  __syncwarp();
+  convert_slab<1, NT>(P, P.prob[p], u, dst, dst + P.xs_bytes, lane);
+}
+
+// ---------------------------------------------------------------------------
 // the persistent GEMV kernel
 // ---------------------------------------------------------------------------
 template <int G, int NT, bool TP>
@@ -927,9 +956,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         return;
       }
       uint8_t* xs = smem + (size_t)st * P.stage_bytes + P.w_stage;
-      convert_slab<G, NT>(P, P.prob[cur.p], cur.j, xs, xs + P.xs_bytes, lane);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ready_bar[2 * st + (i & 1)]);
+      if (G == 1 && NT >= 2 && P.precvt) {
+        // the slice was converted before the launch: one bulk copy, which the
+        // stage's ready phase waits for along with the weight bytes
+        if (lane == 0) {
+          const uint32_t xb = (uint32_t)(P.xs_bytes + P.su_bytes);
+          uint64_t* rb = &ready_bar[2 * st + (i & 1)];
+          mbar_arrive_expect_tx(rb, xb);
+          bulk_g2s(xs, P.ws + P.prob[cur.p].xcv_off + (int64_t)cur.j * xb, xb, rb);
+        }
+      } else {
+        convert_slab<G, NT>(P, P.prob[cur.p], cur.j, xs, xs + P.xs_bytes, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ready_bar[2 * st + (i & 1)]);
+      }
       for (int q = 0; q < kConvWarps; ++q) cur.next(P);
     }
     return;
@@ -1058,6 +1098,15 @@ static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_
   int64_t off = align256(kWsCounters + kWsCountersBytes);
   P.part_off = off;
   off = align256(off + (int64_t)kMaxCta * 2 * kRowWarps * 32 * NT * 2 * 4);
+  // batch >= 5: slices of the activations converted once per launch
+  P.precvt = (NT >= 2) ? 1 : 0;
+  for (int p = 0; p < n; ++p) {
+    P.prob[p].xcv_off = -1;
+    if (P.precvt) {
+      P.prob[p].xcv_off = off;
+      off = align256(off + (int64_t)P.prob[p].nb * (P.xs_bytes + P.su_bytes));
+    }
+  }
   P.status_off = kWsStatus;
   P.cnt_off = kWsCounters;
   P.total_slabs = (int)slab0;
@@ -1222,6 +1271,20 @@ static int gemv_launch_impl(const draco_gemv_problem* probs, int n, int batch, c
     return DRACO_ERR_ALIGN;
   }
   hp.P.ws = static_cast<uint8_t*>(ws);
+  if (hp.P.precvt) {
+    int units = 0;
+    for (int p = 0; p < n; ++p) units += hp.P.prob[p].nb;
+    const int blocks = (units + kConvertWarpsPerBlock - 1) / kConvertWarpsPerBlock;
+    const dim3 grid(blocks), block(kConvertWarpsPerBlock * 32);
+    if (hp.P.nt == 2) gemv_convert_kernel<2><<<grid, block, 0, st>>>(hp.P);
+    else if (hp.P.nt == 4) gemv_convert_kernel<4><<<grid, block, 0, st>>>(hp.P);
+    else gemv_convert_kernel<8><<<grid, block, 0, st>>>(hp.P);
+    const cudaError_t ce = cudaGetLastError();
+    if (ce != cudaSuccess) {
+      snprintf(msg, ml, "gemv: activation conversion launch failed: %s", cudaGetErrorString(ce));
+      return DRACO_ERR_CUDA;
+    }
+  }
   cudaError_t e;
   e = ex ? dispatch_gemv<true>(hp, batch, st) : dispatch_gemv<false>(hp, batch, st);
   if (e != cudaSuccess) {
