@@ -123,7 +123,7 @@ def _rel(a, b):
     return float((a - b).norm() / b.norm())
 
 
-@pytest.mark.parametrize("batch", [1, 3])
+@pytest.mark.parametrize("batch", [1, 3, 8])  # 8: activations converted once per launch
 def test_emulated_two_rank_exchange_matches_unsharded_gemv(batch):
     em = _Emulated(batch, seed=batch)
     try:
