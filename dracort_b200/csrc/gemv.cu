@@ -23,8 +23,8 @@
 //    (max |x| / u in [2^13, 2^14)), round to an integer q and split it into
 //    two int8 digits, q = 256 * hi + lo, stored in MMA-fragment order with
 //    the group sums, and arrive on the slab's ready barrier, which completes
-//    with that arrival and the slab's weight bytes.  From batch 5 on (two or
-//    more MMA column tiles) the activations are converted once per launch
+//    with that arrival and the slab's weight bytes.  From batch 3 on (the
+//    dense layouts) the activations are converted once per launch
 //    instead, by gemv_convert_kernel, into per-(problem, super-block) slices
 //    of the workspace laid out as a stage's slice; the converter warps then
 //    fill a stage with one bulk copy of that slice (arrive.expect_tx on the
@@ -816,7 +816,7 @@ __device__ __forceinline__ bool consume_segment(const GemvParams& P, const uint8
 }
 
 // ---------------------------------------------------------------------------
-// activation conversion once per launch (batch >= 5): one warp per
+// activation conversion once per launch (batch >= 3): one warp per
 // (problem, super-block) slice, written in the stage layout (digits in
 // MMA-fragment order, then the group sums), padded batch slots zero
 // ---------------------------------------------------------------------------
@@ -956,7 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         return;
       }
       uint8_t* xs = smem + (size_t)st * P.stage_bytes + P.w_stage;
-      if (G == 1 && NT >= 2 && P.precvt) {
+      if (G == 1 && P.precvt) {
         // the slice was converted before the launch: one bulk copy, which the
         // stage's ready phase waits for along with the weight bytes
         if (lane == 0) {
@@ -1058,8 +1058,11 @@ static int nt_of_batch(int batch) { return batch <= 4 ? 1 : batch <= 8 ? 2 : bat
 // mailbox); static shared memory (barriers, mailbox tags) comes on top.
 constexpr int kSmemBudget = 216 * 1024;
 
+// convert_once: convert the activations once per launch in the dense
+// layouts (batch >= 3); the allocation-free entry keeps the in-kernel
+// conversion, whose scratch needs no activation slices.
 static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, HostPlan& hp, char* msg,
-                       size_t ml) {
+                       size_t ml, bool convert_once = true) {
   GemvParams& P = hp.P;
   memset(&P, 0, sizeof(P));
   P.n_prob = n;
@@ -1098,8 +1101,8 @@ static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_
   int64_t off = align256(kWsCounters + kWsCountersBytes);
   P.part_off = off;
   off = align256(off + (int64_t)kMaxCta * 2 * kRowWarps * 32 * NT * 2 * 4);
-  // batch >= 5: slices of the activations converted once per launch
-  P.precvt = (NT >= 2) ? 1 : 0;
+  // dense layouts (batch >= 3): slices of the activations converted once per launch
+  P.precvt = (convert_once && batch >= 3) ? 1 : 0;
   for (int p = 0; p < n; ++p) {
     P.prob[p].xcv_off = -1;
     if (P.precvt) {
@@ -1276,7 +1279,8 @@ static int gemv_launch_impl(const draco_gemv_problem* probs, int n, int batch, c
     for (int p = 0; p < n; ++p) units += hp.P.prob[p].nb;
     const int blocks = (units + kConvertWarpsPerBlock - 1) / kConvertWarpsPerBlock;
     const dim3 grid(blocks), block(kConvertWarpsPerBlock * 32);
-    if (hp.P.nt == 2) gemv_convert_kernel<2><<<grid, block, 0, st>>>(hp.P);
+    if (hp.P.nt == 1) gemv_convert_kernel<1><<<grid, block, 0, st>>>(hp.P);
+    else if (hp.P.nt == 2) gemv_convert_kernel<2><<<grid, block, 0, st>>>(hp.P);
     else if (hp.P.nt == 4) gemv_convert_kernel<4><<<grid, block, 0, st>>>(hp.P);
     else gemv_convert_kernel<8><<<grid, block, 0, st>>>(hp.P);
     const cudaError_t ce = cudaGetLastError();
@@ -1346,7 +1350,7 @@ int gemv_launch_noalloc(const draco_gemv_problem* probs, int n, int batch, cudaS
                         size_t ml) {
   HostPlan hp;
   const int n_sm = device_sm_count();
-  if (!build_plan(probs, n, batch, n_sm, hp, msg, ml)) return DRACO_ERR_ARG;
+  if (!build_plan(probs, n, batch, n_sm, hp, msg, ml, /*convert_once=*/false)) return DRACO_ERR_ARG;
   if (hp.P.total_slabs == 0) return DRACO_OK;
   if (hp.ws_needed > kStaticScratchBytes) {
     snprintf(msg, ml,
