@@ -75,6 +75,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE expert-parallel leg")
     ap.add_argument("--model-steps", type=int, default=20, help="timed steps of the 32-layer decode leg")
     ap.add_argument("--no-model", action="store_true", help="skip the 32-layer decode (config 4) leg")
+    ap.add_argument("--q8-steps", type=int, default=2000, help="timed steps of the Q8_0 (config 1) leg")
+    ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0 GEMV (config 1) leg")
     return ap.parse_args(argv)
 
 
@@ -114,49 +116,72 @@ def dist_env():
 # CPU leg: the reference's own algorithm (oracle port of gguf._dequantize +
 # GenericGemmKernel.matmul_f32) on the host cores
 # ---------------------------------------------------------------------------
-def cpu_reference_leg(specs, packed, batch, seed, budget_s=12.0, steps=None):
+def host_cpu_info():
+    """Logical and physical core counts and the BLAS thread pools numpy uses."""
+    info = {"logical_cores": os.cpu_count()}
+    try:
+        import psutil
+
+        info["physical_cores"] = psutil.cpu_count(logical=False)
+    except Exception:  # pragma: no cover - psutil is in the image
+        info["physical_cores"] = None
+    try:
+        from threadpoolctl import threadpool_info
+
+        info["blas"] = [{"api": p.get("internal_api"), "threads": p.get("num_threads")} for p in threadpool_info()
+                        if p.get("user_api") == "blas"]
+    except Exception:  # pragma: no cover
+        info["blas"] = []
+    return info
+
+
+def blas_threads(info):
+    return max([b["threads"] or 0 for b in info.get("blas", [])] or [0]) or None
+
+
+def workload_config(mix, batch, world):
+    """The config keys that name the workload; both arms report them."""
+    return {"workload": f"config2_{mix}_layer_decode_gemv", "batch": batch,
+            "weights": "q,k,v,o 4096x4096; gate,up 11008x4096; down 4096x11008"
+                       + (" (Q6_K v and down)" if mix == "q4_k_m" else ""),
+            "step": "the 7 projections of one decoder layer, one pass each",
+            "parallelism": f"tp{world}"}
+
+
+def cpu_layer_steps(specs, packed, batch, seed, warmup, steps, threads=None, budget_s=None):
+    """The reference's decode path on the host for whole layer-set steps: the
+    fp32 cache from gguf._dequantize (first touch, timed once), then per step
+    the 7 projections' matmul_f32 (executor._linear, executor.py:47-79).
+    Returns per-step seconds and the first-touch dequant time."""
     from oracle import gguf_oracle as O
 
-    rng = np.random.default_rng(seed + 7)
-    t0 = time.perf_counter()
-    weights = [O.dequantize_matrix(s.qtype, p, s.n_rows, s.k) for s, p in zip(specs, packed)]
-    t_dequant = time.perf_counter() - t0
-    xs = [rng.standard_normal((batch, s.k)).astype(np.float32) for s in specs]
-    # warm (steady-state) path of the reference: fp32 cache @ x per projection
-    for x, w in zip(xs, weights):
-        O.matmul_f32(x, w)
-    per = []
-    n = 0
-    t_start = time.perf_counter()
-    i = 0
-    while True:
-        j = i % len(specs)
-        t = time.perf_counter()
-        O.matmul_f32(xs[j], weights[j])
-        per.append((j, time.perf_counter() - t))
-        i += 1
-        n += 1
-        if steps is not None and n >= steps:
-            break
-        if steps is None and time.perf_counter() - t_start > budget_s and i % len(specs) == 0:
-            break
-    by = {}
-    for j, dt in per:
-        by.setdefault(j, []).append(dt)
-    layer_s = sum(float(np.median(v)) for v in by.values())
-    from dracort_b200.workloads import algorithmic_bytes
+    import contextlib
 
-    gbs = algorithmic_bytes(specs, batch) / layer_s / 1e9
-    cold_s = t_dequant + layer_s
-    return {
-        "layer_warm_s": layer_s,
-        "layer_cold_s": cold_s,
-        "dequant_s": t_dequant,
-        "value_warm_gbs": gbs,
-        "value_cold_gbs": algorithmic_bytes(specs, batch) / cold_s / 1e9,
-        "matmuls_timed": n,
-        "per_step": per,
-    }
+    ctx = contextlib.nullcontext()
+    if threads:
+        from threadpoolctl import threadpool_limits
+
+        ctx = threadpool_limits(limits=threads, user_api="blas")
+    with ctx:
+        rng = np.random.default_rng(seed + 7)
+        t0 = time.perf_counter()
+        weights = [O.dequantize_matrix(s.qtype, p, s.n_rows, s.k) for s, p in zip(specs, packed)]
+        t_dequant = time.perf_counter() - t0
+        xs = [rng.standard_normal((batch, s.k)).astype(np.float32) for s in specs]
+
+        def step():
+            for x, w in zip(xs, weights):
+                O.matmul_f32(x, w)
+
+        for _ in range(max(0, warmup)):
+            step()
+        per = []
+        t_end = None if budget_s is None else time.perf_counter() + budget_s
+        while len(per) < max(1, steps) and (t_end is None or time.perf_counter() < t_end or not per):
+            t = time.perf_counter()
+            step()
+            per.append(time.perf_counter() - t)
+        return per, t_dequant
 
 
 def run_reference(args):
@@ -167,41 +192,34 @@ def run_reference(args):
 
     specs = layer_specs(args.mix)
     packed = encode_specs(specs, args.seed)
-    for _ in range(max(0, args.warmup)):
-        pass
-    # each step: one projection's matmul on the fp32 cache (rotating through the
-    # seven), i.e. a bounded sample of the layer-set workload
-    res = cpu_reference_leg(specs, packed, args.batch, args.seed, steps=max(1, args.steps))
-    step_bytes = []
-    total_t = 0.0
-    total_b = 0
-    for j, dt in res["per_step"]:
-        s = specs[j]
-        total_b += s.nbytes + 4 * args.batch * (s.k + s.n_rows)
-        total_t += dt
-    value = total_b / total_t / 1e9
-    cores = os.cpu_count()
+    info = host_cpu_info()
+    # a step is one pass over the layer set (the same step as the GPU arm's);
+    # the run is bounded to a few minutes of host time
+    per, t_dequant = cpu_layer_steps(specs, packed, args.batch, args.seed, args.warmup, args.steps)
+    alg = algorithmic_bytes(specs, args.batch)
+    total_t = float(sum(per))
+    value = alg * len(per) / total_t / 1e9
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": round(value, 3),
         "unit": "GB/s",
         "n_gpus": world,
-        "steps": args.steps,
+        "steps": len(per),
         "warmup": args.warmup,
-        "ms_per_step": round(1e3 * total_t / max(1, len(res["per_step"])), 4),
+        "ms_per_step": round(1e3 * total_t / len(per), 4),
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded N(0,0.02) weights, GGUF-encoded; N(0,1) activations)",
-        "config": {"workload": f"config2_{args.mix}_layer_decode_gemv", "batch": args.batch,
-                   "step": "one projection matmul of the layer set, rotating q,k,v,o,gate,up,down",
-                   "parallelism": "host"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-                         "sample": f"{len(res['per_step'])} projection matmuls on the fp32 dequant cache "
-                                   f"(reference steady state, numpy/OpenBLAS default threads); "
-                                   f"first-touch dequant of the layer set took {res['dequant_s']:.2f} s"},
+        "config": workload_config(args.mix, args.batch, world),
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": blas_threads(info) or os.cpu_count(),
+                         "kind": "port", **info,
+                         "sample": f"{len(per)} layer-set steps after {args.warmup} warm-up steps: the 7 "
+                                   f"projections' matmul_f32 on the fp32 dequant cache (reference steady "
+                                   f"state, numpy/OpenBLAS default threads); first-touch dequant of the layer "
+                                   f"set {t_dequant:.2f} s"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     if not args.no_prefill:
@@ -212,7 +230,8 @@ def run_reference(args):
         line["prefill"] = {
             "metric": "prefill dequant-GEMM TFLOP/s", "value": round(pres["tflops"], 5), "unit": "TFLOP/s",
             "config": {"workload": "config3_mixed_q4k_q6k_prefill_gemm", "tokens_sampled": pres["tokens"]},
-            "cpu_baseline": {"value": round(pres["tflops"], 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": round(pres["tflops"], 5), "unit": "TFLOP/s",
+                             "cores": blas_threads(info) or os.cpu_count(), "kind": "port",
                              "sample": f"{pres['tokens']} tokens through gate, up, down on the fp32 dequant cache"},
         }
     print(json.dumps(line), flush=True)
@@ -295,6 +314,98 @@ def cpu_moe_leg(expert, hidden, ffn, tokens_per_expert, n_experts, seed):
     expert_s = float(np.median(ts[1:]))
     return {"step_s": expert_s * n_experts, "expert_s": expert_s, "dequant_expert_s": t_dequant,
             "threads": torch.get_num_threads()}
+
+
+def q8_0_leg(args, dev, peaks, timed, want_e2e, want_cpu):
+    """Config 1: the Q8_0 GEMV, W 4096x4096 (fp16 d = max|w|/127, int8 rint(w/d)
+    per 32-element block, as the reference test encoder), x fp32 [1, 4096],
+    y fp32, one GEMV launch per step; distinct weight copies rotated so no
+    step finds its weight in L2.  N = 1 only (the weight is one GPU's work)."""
+    import torch
+
+    from dracort_b200 import gguf_ops as G
+    from dracort_b200.telemetry import ClockSampler
+    from dracort_b200.workloads import algorithmic_bytes, encode_specs, q8_0_spec
+
+    specs = q8_0_spec()
+    s = specs[0]
+    packed = encode_specs(specs, args.seed + 300)[0]
+    t0 = G.repack(s.qtype, torch.from_numpy(packed.reshape(-1)).to(dev), s.n_rows, s.k)
+    n_copies = max(2, math.ceil(4 * L2_BYTES / t0.numel()))
+    copies = [t0] + [t0.clone() for _ in range(n_copies - 1)]
+    g = torch.Generator().manual_seed(args.seed + 301)
+    x = torch.randn((1, s.k), generator=g).to(dev)
+    y = torch.empty((1, s.n_rows), device=dev)
+    plans = [G.GemvPlan([G.GemvProblem(s.qtype, c, x, y, s.n_rows, s.k)]) for c in copies]
+    for i in range(max(3, args.warmup)):
+        plans[i % n_copies].run()
+    torch.cuda.synchronize()
+    if plans[0].status():
+        raise RuntimeError(f"Q8_0 GEMV reported device status {plans[0].status()}")
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=torch.cuda.Stream(device=dev)):
+        for pl in plans:
+            pl.run()
+    graph.replay()
+    torch.cuda.synchronize()
+    reps = max(1, args.q8_steps // n_copies)
+    K = reps * n_copies
+    sampler = ClockSampler(dev.index or 0).start()
+
+    def steps():
+        for _ in range(reps):
+            graph.replay()
+
+    ms, tw0, tw1 = timed(steps)
+    clocks = sampler.summary(tw0, tw1)
+    sampler.stop()
+    ms_step = ms / K
+    alg = algorithmic_bytes(specs, 1)
+    gbs = alg / (ms_step * 1e-3) / 1e9
+    out = {
+        "metric": "Q8_0 dequant-GEMV HBM GB/s (config 1)", "value": round(gbs, 2), "unit": "GB/s",
+        "ms_per_step": round(ms_step, 6), "steps": K, "higher_is_better": True, "dtype": "f32",
+        "config": {"workload": "config1_q8_0_gemv", "batch": 1, "weights": "4096x4096 Q8_0",
+                   "l2": f"{n_copies} weight copies rotated ({n_copies * t0.numel() / 1e6:.0f} MB > 4x126 MB L2)",
+                   "graph": True},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "traffic": profiled_traffic("gemv_q8_0_config1"),
+                     "peak_source": f"{peaks['source']} MEASURED_PEAKS.json hbm_gbs",
+                     "kernel": f"gemv_kernel, one launch per step; algorithmic bytes {alg} per step"},
+        "gpu_launches": K,
+        "clocks": clocks,
+    }
+    if want_e2e:
+        xh = torch.randn((1, s.k), generator=g).pin_memory()
+        yh = torch.empty((1, s.n_rows)).pin_memory()
+
+        def e2e_steps(n):
+            for i in range(n):
+                x.copy_(xh, non_blocking=True)
+                plans[i % n_copies].run()
+                yh.copy_(y, non_blocking=True)
+
+        e2e_steps(max(3, args.warmup))
+        torch.cuda.synchronize()
+        ms_e, _, _ = timed(lambda: e2e_steps(K))
+        out["e2e"] = {"value": round(alg / (ms_e / K * 1e-3) / 1e9, 3), "unit": "GB/s",
+                      "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": yh.numel() * 4,
+                      "ms_per_step": round(ms_e / K, 6),
+                      "path": "pinned host x -> cuda -> GemvPlan.run (C ABI) -> pinned host y, eager"}
+    if want_cpu:
+        per, t_dq = cpu_layer_steps(specs, [packed], 1, args.seed, 3, 200)
+        cpu_gbs = alg * len(per) / sum(per) / 1e9
+        info = host_cpu_info()
+        out["cpu_baseline"] = {
+            "value": round(cpu_gbs, 3), "unit": "GB/s", "cores": blas_threads(info) or os.cpu_count(),
+            "kind": "port", **info,
+            "sample": (f"{len(per)} matmul_f32 steps on the fp32 cache after 3 warm-up steps (oracle port of "
+                       f"gguf._dequantize + GenericGemmKernel.matmul_f32, numpy/OpenBLAS default threads), "
+                       f"{np.median(per) * 1e3:.3f} ms median; first-touch dequant {t_dq * 1e3:.0f} ms")}
+    del graph, plans, copies
+    torch.cuda.empty_cache()
+    return out
 
 
 def prefill_leg(args, dev, peaks, rank, world, pg, timed, want_e2e, want_cpu):
@@ -420,7 +531,8 @@ def model_leg(args, dev, peaks, rank, world, pg, timed):
            "unit": "GB/s", "scaling": "strong", "dtype": "f32",
            "config": {"workload": "config4_llama7b_q4_k_m_decode_step", "layers": n_layers,
                       "weights": "per layer q,k,o,gate,up Q4_K; v,down Q6_K (Llama-7B shapes)",
-                      "parallelism": f"tp{world}" + (" (NCCL all-gather + all-reduce per layer)" if world > 1 else ""),
+                      "parallelism": f"tp{world}" + (" (in-kernel NVLink exchange + finish kernel per layer)"
+                                                     if world > 1 else ""),
                       "step": "the 7 projections of every layer (one grouped GEMV launch per layer)"},
            "batches": {}}
     for batch in (1, 32):
@@ -627,8 +739,16 @@ def run_ours(args):
         n_copies = max(2, math.ceil(4 * L2_BYTES / set_bytes))
         copies = [tiled0] + [[t.clone() for t in tiled0] for _ in range(n_copies - 1)]
         rng = torch.Generator(device="cpu").manual_seed(args.seed + 1)
-        xs = [torch.randn((batch, s.k), generator=rng).to(dev) for s in specs_full]
-        ys = [torch.empty((batch, s.n_rows), device=dev) for s in specs_full]
+        # every projection's x [batch, k] and y [batch, n] is a block of one
+        # buffer, so the end-to-end leg moves each with one copy
+        xbuf = torch.randn(batch * sum(s.k for s in specs_full), generator=rng).to(dev)
+        ybuf = torch.empty(batch * sum(s.n_rows for s in specs_full), device=dev)
+        xs, ys, ox, oy = [], [], 0, 0
+        for s in specs_full:
+            xs.append(xbuf[ox:ox + batch * s.k].view(batch, s.k))
+            ys.append(ybuf[oy:oy + batch * s.n_rows].view(batch, s.n_rows))
+            ox += batch * s.k
+            oy += batch * s.n_rows
         plans = [G.GemvPlan([G.GemvProblem(s.qtype, c[i], xs[i], ys[i], s.n_rows, s.k)
                              for i, s in enumerate(specs_full)]) for c in copies]
         local_bytes = set_bytes
@@ -737,26 +857,24 @@ def run_ours(args):
     # -- end to end through the public API, host buffers -----------------------
     e2e = None
     if not args.no_e2e and world == 1:
-        xh = [torch.randn((batch, s.k)).pin_memory() for s in specs_full]
-        yh = [torch.empty((batch, s.n_rows)).pin_memory() for s in specs_full]
-        h2d = sum(t.numel() * 4 for t in xh)
-        d2h = sum(t.numel() * 4 for t in yh)
+        xh = torch.randn(xbuf.shape).pin_memory()
+        yh = torch.empty(ybuf.shape).pin_memory()
+        h2d, d2h = xh.numel() * 4, yh.numel() * 4
 
-        def e2e_steps():
-            for i in range(K):
-                for a, b in zip(xs, xh):
-                    a.copy_(b, non_blocking=True)
+        def e2e_steps(n):
+            for i in range(n):
+                xbuf.copy_(xh, non_blocking=True)
                 plans[i % n_copies].run()
-                for a, b in zip(yh, ys):
-                    a.copy_(b, non_blocking=True)
+                yh.copy_(ybuf, non_blocking=True)
 
-        for _ in range(3):
-            pass
-        ms_e2e, _, _ = timed(e2e_steps)
+        e2e_steps(max(3, args.warmup))
+        torch.cuda.synchronize()
+        ms_e2e, _, _ = timed(lambda: e2e_steps(K))
         e2e = {"value": round(alg / (ms_e2e / K * 1e-3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(ms_e2e / K, 5),
-               "path": "pinned host x -> cuda (7 copies) -> GemvPlan.run (C ABI) -> pinned host y (7 copies), eager"}
+               "path": "pinned host x (one buffer, one copy) -> cuda -> GemvPlan.run (C ABI) -> pinned host y "
+                       "(one buffer, one copy), eager"}
     elif world > 1 and not args.no_e2e and layer is not None:
         e2e = layer.e2e(K, timed)
         e2e.update({"value": round(alg / (e2e["ms_per_step"] * 1e-3) / 1e9, 3), "unit": "GB/s",
@@ -790,6 +908,10 @@ def run_ours(args):
     if not args.no_prefill:
         prefill = prefill_leg(args, dev, peaks, rank, world, pg, timed, not args.no_e2e, not args.no_cpu)
 
+    q8 = None
+    if not args.no_q8 and world == 1:
+        q8 = q8_0_leg(args, dev, peaks, timed, not args.no_e2e, rank == 0 and not args.no_cpu)
+
     moe = None
     if not args.no_moe:
         moe = moe_leg(args, dev, peaks, rank, world, pg, timed)
@@ -800,14 +922,21 @@ def run_ours(args):
     # -- CPU baseline (rank 0, N=1) --------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        res = cpu_reference_leg(specs_full, packed_full, batch, args.seed, budget_s=10.0)
-        cpu = {"value": round(res["value_warm_gbs"], 3), "unit": "GB/s", "cores": os.cpu_count(),
-               "kind": "port",
+        info = host_cpu_info()
+        per, t_dq = cpu_layer_steps(specs_full, packed_full, batch, args.seed, 3, 100000, budget_s=8.0)
+        warm = alg * len(per) / sum(per) / 1e9
+        phys = info.get("physical_cores")
+        per_p, _ = (cpu_layer_steps(specs_full, packed_full, batch, args.seed, 3, 100000, threads=phys, budget_s=4.0)
+                    if phys else (None, None))
+        cpu = {"value": round(warm, 3), "unit": "GB/s", "cores": blas_threads(info) or os.cpu_count(),
+               "kind": "port", **info,
+               "value_physical_threads": round(alg * len(per_p) / sum(per_p) / 1e9, 3) if per_p else None,
+               "value_cold": round(alg / (t_dq + float(np.median(per))) / 1e9, 4),
                "sample": (f"reference path (oracle port of gguf._dequantize + GenericGemmKernel.matmul_f32) over "
-                          f"the same layer set at batch {batch}: {res['matmuls_timed']} projection matmuls on the "
-                          f"fp32 cache, median per projection summed = {res['layer_warm_s'] * 1e3:.2f} ms/layer "
-                          f"(warm); cold first touch incl. dequant = {res['layer_cold_s']:.2f} s/layer "
-                          f"({res['value_cold_gbs']:.4f} GB/s); numpy/OpenBLAS default threads")}
+                          f"the same layer set at batch {batch}: {len(per)} layer-set steps on the fp32 cache "
+                          f"after 3 warm-up steps, {float(np.median(per)) * 1e3:.2f} ms median (warm, BLAS default "
+                          f"threads); value_physical_threads with BLAS limited to the physical cores; cold first "
+                          f"touch incl. dequant {t_dq:.2f} s per layer set")}
 
     if rank == 0:
         achieved = value
@@ -826,13 +955,10 @@ def run_ours(args):
             "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights, GGUF-encoded; N(0,1) fp32 activations)",
             "config": {
-                "workload": f"config2_{args.mix}_layer_decode_gemv",
-                "batch": batch,
-                "weights": "q,k,v,o 4096x4096; gate,up 11008x4096; down 4096x11008",
+                **workload_config(args.mix, batch, world),
                 "l2": f"inputs larger than L2: {n_copies} layer-set copies rotated "
                       f"({n_copies * local_bytes / 1e6:.0f} MB per GPU > 4x126 MB L2)",
-                "parallelism": f"tp{world}" + (" (in-kernel NVLink exchange: peer stores + finish kernel)"
-                                               if world > 1 else ""),
+                "exchange": ("in-kernel NVLink exchange: peer stores + finish kernel" if world > 1 else None),
                 "graph": bool(use_graph),
             },
             "roofline": {
@@ -858,6 +984,8 @@ def run_ours(args):
             line["tp_nccl"] = tp_nccl
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if q8 is not None:
+            line["q8_0"] = q8
         if prefill is not None:
             line["prefill"] = prefill
         if moe is not None:

@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv_grouped",
     "draco_gguf_gemv",
     "draco_gguf_gemv_grouped_noalloc",
+    "draco_gguf_gemv_noalloc_status",
     "draco_gguf_gemm",
     "draco_swiglu_bf16",
     "draco_swiglu_f32",
@@ -165,6 +166,8 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_gemv_grouped.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp, ctypes.c_size_t, vp]
         lib.draco_gguf_gemv_grouped_noalloc.restype = c_int
         lib.draco_gguf_gemv_grouped_noalloc.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp]
+        lib.draco_gguf_gemv_noalloc_status.restype = c_int
+        lib.draco_gguf_gemv_noalloc_status.argtypes = [ctypes.POINTER(c_int), vp]
         lib.draco_gguf_gemm.restype = c_int
         lib.draco_gguf_gemm.argtypes = [ctypes.POINTER(GemmProblem), c_int, vp, vp]
         lib.draco_swiglu_bf16.restype = c_int

@@ -4,12 +4,16 @@ Usage:  python -m dracort_b200.build [--force]
 
 The library lands in ``dracort_b200/_lib/libdraco_gguf.so`` next to the
 sources, so it travels with the repository snapshot (no JIT cache).  A rebuild
-happens only when a source or header is newer than the library.
+is skipped only when the library was built from exactly the current sources,
+headers and flags: their SHA-256 is recorded beside the library
+(``_lib/build.stamp``) and compared, so a library left over from other
+sources (file times are not trusted) is always rebuilt.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -21,6 +25,7 @@ REPO_DIR = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libdraco_gguf.so"
+STAMP_PATH = LIB_DIR / "build.stamp"
 INCLUDE = REPO_DIR / "include"
 
 SOURCES = ["capi.cu", "dequant.cu", "gemv.cu", "gemm.cu", "act.cu", "tp.cu"]
@@ -41,17 +46,27 @@ def _inputs() -> list[Path]:
     return files
 
 
+def source_hash() -> str:
+    """SHA-256 over the compiler flags and every source and header (name and bytes)."""
+    h = hashlib.sha256()
+    h.update(" ".join(ARCH_FLAGS + NVCC_FLAGS + SOURCES).encode())
+    for f in _inputs():
+        h.update(f.name.encode() + b"\0")
+        h.update(f.read_bytes())
+    return h.hexdigest()
+
+
 def needs_build() -> bool:
-    if not LIB_PATH.exists():
+    if not LIB_PATH.exists() or not STAMP_PATH.exists():
         return True
-    t = LIB_PATH.stat().st_mtime
-    return any(f.stat().st_mtime > t for f in _inputs())
+    return STAMP_PATH.read_text().strip() != source_hash()
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
     """Compile every .cu into object files (in parallel) and link the .so."""
     if not force and not needs_build():
         return LIB_PATH
+    digest = source_hash()
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     obj_dir = LIB_DIR / "obj"
     obj_dir.mkdir(parents=True, exist_ok=True)
@@ -82,6 +97,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if r.returncode != 0:
         raise RuntimeError("link failed:\n" + r.stdout.decode(errors="replace"))
     os.replace(tmp, LIB_PATH)
+    STAMP_PATH.write_text(digest + "\n")
     return LIB_PATH
 
 

@@ -167,6 +167,14 @@ int draco_gguf_gemv_grouped_noalloc(const draco_gemv_problem* probs, int n_probl
   return ok();
 }
 
+int draco_gguf_gemv_noalloc_status(int* status, void* stream) {
+  if (!status) return fail(DRACO_ERR_ARG, "gemv_noalloc_status: null status pointer");
+  char msg[256] = {0};
+  const int rc = gemv_noalloc_status(status, (cudaStream_t)stream, msg, sizeof(msg));
+  if (rc) return fail(rc, "%s", msg);
+  return ok();
+}
+
 int draco_gguf_gemm(const draco_gemm_problem* probs, int n_problems, int* status, void* stream) {
   if (!probs || n_problems < 1 || n_problems > DRACO_GEMM_MAX_PROBLEMS)
     return fail(DRACO_ERR_ARG, "gemm: need 1..%d problems, got %d", DRACO_GEMM_MAX_PROBLEMS, n_problems);

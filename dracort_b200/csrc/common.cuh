@@ -220,6 +220,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       : "memory");
 }
 
+// L2 prefetch of a contiguous global range by the TMA engine (no completion
+// to wait for).  Address 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Programmatic dependent launch: wait for the preceding kernel in the stream
 // (no-op when the launch did not use the attribute).
 __device__ __forceinline__ void grid_dependency_wait() {

@@ -123,11 +123,6 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
 // tcgen05.commit).  A cluster-scope acquire on every poll costs a few hundred
 // cycles, which the MMA issue loop cannot afford three times per k-block.
 
-// L2 prefetch of a contiguous global range by the TMA engine (no completion
-// tracking; 16-byte aligned address, size a multiple of 16)
-__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 // TMA 2-D tile load into this CTA's shared memory; the transaction bytes are
 // counted on `bar_cluster` (a barrier of the leader CTA of the pair).

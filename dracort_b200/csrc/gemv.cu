@@ -86,6 +86,13 @@ constexpr int kConvWarps = 3;
 constexpr int kThreads = (kConsumerWarps + 1 + kConvWarps) * 32;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
 constexpr int kMaxMboxSlots = 4;
+// Back-off (ns) between polls of a stage's generation word by a converter
+// warp: the converters run ahead of the consumers and mostly wait, and a
+// tight poll loop takes issue slots from the consumer warps of their SMSP.
+#ifndef DRACO_GEMV_GEN_SLEEP_NS
+#define DRACO_GEMV_GEN_SLEEP_NS 0
+#endif
+constexpr int kGenSleepNs = DRACO_GEMV_GEN_SLEEP_NS;
 
 struct GemvProbDev {
   const uint8_t* w;
@@ -191,8 +198,10 @@ __device__ __forceinline__ int gen_read(const int* g) {
   return v;
 }
 __device__ __forceinline__ bool wait_generation(const GemvParams& P, const int* g, int m, volatile int* abort) {
+  if (gen_read(g) >= m) return true;
   const uint64_t t0 = global_timer_ns();
   while (gen_read(g) < m) {
+    if (kGenSleepNs > 0) __nanosleep(kGenSleepNs);
     if (*abort) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) {
       record_error(P, DRACO_ERR_TIMEOUT);
@@ -1377,6 +1386,25 @@ int gemv_launch_noalloc(const draco_gemv_problem* probs, int n, int batch, cudaS
     snprintf(msg, ml, "gemv_noalloc: launch failed: %s", cudaGetErrorString(e));
     return DRACO_ERR_CUDA;
   }
+  return DRACO_OK;
+}
+
+// Status word of the last allocation-free call on the current device: the
+// first int32 of the fixed array (0, or the DRACO_* code a device-side wait
+// recorded).  Copied on `st` after the work queued there, into host memory
+// owned by the caller; the host waits for the stream.  No allocation.
+int gemv_noalloc_status(int* out, cudaStream_t st, char* msg, size_t ml) {
+  uint8_t* scratch = nullptr;
+  int rc = static_scratch_address(&scratch, msg, ml);
+  if (rc != DRACO_OK) return rc;
+  int v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, scratch + kWsStatus, sizeof(int), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) {
+    snprintf(msg, ml, "gemv_noalloc_status: reading the status word failed: %s", cudaGetErrorString(e));
+    return DRACO_ERR_CUDA;
+  }
+  *out = v;
   return DRACO_OK;
 }
 

@@ -32,6 +32,7 @@ int tp_finish_launch(const draco_tp_exchange* ex, int batch, int64_t gather_off,
 int gemv_launch_noalloc(const draco_gemv_problem* probs, int n, int batch, cudaStream_t st, char* msg,
                         size_t msg_len);
 size_t gemv_static_scratch_bytes();
+int gemv_noalloc_status(int* out, cudaStream_t st, char* msg, size_t msg_len);
 
 // Prefill dequant-GEMM (tcgen05).  `status` is an optional device int the
 // kernel sets to a DRACO_* code on a device-side failure.

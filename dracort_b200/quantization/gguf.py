@@ -26,12 +26,12 @@ MoE ``Expert`` (draco/models/moe/expert.py:34-36).
 from __future__ import annotations
 
 import threading
-from collections import OrderedDict
 from typing import Any, Dict, List, Optional, Tuple
 
 import numpy as np
 import torch
 import torch.nn as nn
+from torch.utils.weak import WeakIdKeyDictionary
 
 from dracort_b200 import _native as N
 from dracort_b200 import gguf_ops as G
@@ -72,26 +72,33 @@ def _as_cuda_u8(payload, device) -> torch.Tensor:
 
 
 class _TiledCache:
-    """Small LRU cache: packed GGUF weight tensor -> TILED device copy."""
+    """Packed GGUF weight tensor -> its TILED device copy.
 
-    def __init__(self, capacity: int = 512) -> None:
-        self.capacity = capacity
-        self._d: "OrderedDict[Tuple, torch.Tensor]" = OrderedDict()
+    Entries are keyed on the weight tensor object itself (held weakly) plus its
+    in-place version counter, never on its device address: a weight that is
+    freed drops its entry, and a new tensor that the caching allocator places
+    at the freed address is a different object, so it can never be served the
+    old weight's copy.  An in-place write to the weight bumps its version and
+    forces a fresh repack."""
+
+    def __init__(self) -> None:
+        self._d = WeakIdKeyDictionary()
         self._lock = threading.Lock()
 
     def get(self, w: torch.Tensor, qtype: int, layout: str, n_rows: int, k: int) -> torch.Tensor:
-        key = (w.data_ptr(), w.numel(), w.device.index, getattr(w, "_version", 0), qtype, layout, n_rows, k)
+        params = (w._version, qtype, layout, n_rows, k)
         with self._lock:
-            t = self._d.get(key)
-            if t is not None:
-                self._d.move_to_end(key)
-                return t
+            hit = self._d.get(w)
+            if hit is not None and hit[0] == params:
+                return hit[1]
         t = G.repack(qtype, w, n_rows, k, layout=layout)
         with self._lock:
-            self._d[key] = t
-            while len(self._d) > self.capacity:
-                self._d.popitem(last=False)
+            self._d[w] = (params, t)
         return t
+
+    def __len__(self) -> int:
+        with self._lock:
+            return len(self._d)
 
     def clear(self) -> None:
         with self._lock:

@@ -1,68 +1,79 @@
-"""Quantization registry — same contract as draco/quantization/registry.py.
+"""Name -> backend lookup for the quantization plugins.
 
-``QuantizationRegistry`` (registry.py:21-86) maps lower-cased method names to
-backend instances: ``register`` warns when a name is re-registered (:31-42),
-``get`` raises ValueError listing the available methods (:44-52), plus
-``has``/``list_methods``/``list_backends``/``detect_from_config`` and the
-container dunders.  ``QUANT_REGISTRY`` is the process-wide singleton (:90).
+Callers of draco/quantization/registry.py rely on a few behaviours, which
+this table provides: names are case-insensitive (stored lower-cased),
+registering a taken name replaces the entry and logs a warning, an unknown
+name raises ValueError naming what is available, and a model's
+``quantization_config`` can be matched to a registered name.  The public
+method names are the ones the reference's callers use (register, get, has,
+list_methods, list_backends, detect_from_config, ``in``, ``len``), so the
+GGUF backends can be registered here or in the reference's own registry
+(``register_into`` in this package).
 """
 
 from __future__ import annotations
 
 import logging
-from typing import Any, Dict, List, Optional
+from typing import Any, Dict, List, Mapping, Optional
 
 from dracort_b200.quantization.base import QuantizationBackend
 
-logger = logging.getLogger("dracort_b200.quantization.registry")
+_log = logging.getLogger(__name__)
+
+# keys a quantization_config may name its method under, in lookup order
+_CONFIG_KEYS = ("quant_method", "quantization_method")
+
+
+def _key(name: str) -> str:
+    return str(name).lower()
 
 
 class QuantizationRegistry:
-    """Central registry for quantization backends."""
+    """A case-insensitive table of quantization backends."""
 
     def __init__(self) -> None:
-        self._backends: Dict[str, QuantizationBackend] = {}
+        self._table: Dict[str, QuantizationBackend] = {}
 
     def register(self, name: str, backend: QuantizationBackend) -> None:
-        name = name.lower()
-        if name in self._backends:
-            logger.warning(
-                "Re-registering quantization backend '%s': %s -> %s",
-                name,
-                type(self._backends[name]).__name__,
-                type(backend).__name__,
-            )
-        self._backends[name] = backend
+        key = _key(name)
+        previous = self._table.get(key)
+        if previous is not None:
+            _log.warning("quantization backend %r replaced (%s by %s)", key, type(previous).__name__,
+                         type(backend).__name__)
+        self._table[key] = backend
 
     def get(self, name: str) -> QuantizationBackend:
-        name = name.lower()
-        if name not in self._backends:
-            raise ValueError(f"Unknown quantization method: {name!r}. Available: {self.list_methods()}")
-        return self._backends[name]
+        try:
+            return self._table[_key(name)]
+        except KeyError:
+            raise ValueError(f"no quantization backend named {_key(name)!r}; "
+                             f"registered: {', '.join(self.list_methods()) or 'none'}") from None
 
     def has(self, name: str) -> bool:
-        return name.lower() in self._backends
+        return _key(name) in self._table
 
     def list_methods(self) -> List[str]:
-        return sorted(self._backends.keys())
+        return sorted(self._table)
 
     def list_backends(self) -> Dict[str, QuantizationBackend]:
-        return dict(self._backends)
+        return self._table.copy()
 
-    def detect_from_config(self, quantization_config: Dict[str, Any]) -> Optional[str]:
-        method = quantization_config.get("quant_method", quantization_config.get("quantization_method"))
-        if method and method.lower() in self._backends:
-            return method.lower()
+    def detect_from_config(self, quantization_config: Mapping[str, Any]) -> Optional[str]:
+        """The registered name a model's quantization_config asks for, or None."""
+        for field in _CONFIG_KEYS:
+            method = quantization_config.get(field)
+            if method:
+                return _key(method) if self.has(method) else None
         return None
 
-    def __contains__(self, name: str) -> bool:
-        return self.has(name)
+    __contains__ = has
 
     def __len__(self) -> int:
-        return len(self._backends)
+        return len(self._table)
 
     def __repr__(self) -> str:
-        return f"QuantizationRegistry(methods={self.list_methods()})"
+        return f"{type(self).__name__}({self.list_methods()})"
 
 
+#: the process-wide table the GGUF backends register into at import
 QUANT_REGISTRY = QuantizationRegistry()

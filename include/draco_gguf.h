@@ -22,8 +22,10 @@
  *     failure on the calling host thread is available from
  *     draco_last_error_string().
  *   - The library holds no mutable global state except the thread-local error
- *     string and per-device attribute caches; calls on different streams are
- *     independent.
+ *     string, per-device attribute caches and one shared device array: the
+ *     fixed scratch of draco_gguf_gemv_grouped_noalloc, whose calls race when
+ *     they overlap on the GPU (see there).  Every other call works on
+ *     caller-owned buffers, and calls on different streams are independent.
  */
 #ifndef DRACO_GGUF_H
 #define DRACO_GGUF_H
@@ -174,9 +176,20 @@ int draco_gguf_gemv_grouped(const draco_gemv_problem* problems, int n_problems, 
  * Each call clears the counters it relies on (cudaMemsetAsync on `stream`).
  * All calls share the one array: calls that overlap on the GPU (different
  * streams, or different host threads on one device) race and must be
- * serialised by the caller. */
+ * serialised by the caller.
+ * A device-side failure (a bounded wait that ran out) is not visible in the
+ * return code, which only covers the launch: read it with
+ * draco_gguf_gemv_noalloc_status before the next call, which clears it. */
 int draco_gguf_gemv_grouped_noalloc(const draco_gemv_problem* problems, int n_problems, int batch,
                                     void* stream);
+
+/* Status of the last draco_gguf_gemv_grouped_noalloc call on the current
+ * device: *status (host int) becomes 0 or the DRACO_* code the kernel
+ * recorded (DRACO_ERR_TIMEOUT when a device wait ran out; the outputs of that
+ * call are then invalid).  Reads the fixed array after the work queued on
+ * `stream` and waits for it (host synchronisation); allocates nothing.  No
+ * counterpart in the reference (its numpy path has no device status). */
+int draco_gguf_gemv_noalloc_status(int* status, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Tensor-parallel decode over NVLink: one process per GPU, ranks on one box.

@@ -2,7 +2,8 @@
 
 Run in a container where the reference (sadrasa97/DracoRT) is checked out:
 
-    DRACO_REFERENCE=/path/to/DracoRT python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --reference /path/to/DracoRT
+    (or DRACO_REFERENCE=/path/to/DracoRT python tests/golden/make_golden.py)
 
 The reference is imported the way its own tests do it (tests/conftest.py:18-29
 stubs the top-level packages so that draco/__init__.py, which pulls in torch,
@@ -32,7 +33,7 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("DRACO_REFERENCE", "/root/reference"))
+REF = None  # the reference checkout, from --reference or DRACO_REFERENCE (required)
 
 
 def _stub(name: str, path: Path) -> None:
@@ -43,6 +44,8 @@ def _stub(name: str, path: Path) -> None:
 
 
 def load_reference():
+    if REF is None:
+        raise SystemExit("give the reference checkout: --reference PATH or DRACO_REFERENCE=PATH")
     d = REF / "draco"
     if not d.is_dir():
         raise SystemExit(f"reference not found at {REF}")
@@ -150,4 +153,10 @@ def main() -> None:
 
 
 if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser(description="regenerate tests/golden/gguf_golden.npz from the reference")
+    ap.add_argument("--reference", default=os.environ.get("DRACO_REFERENCE"),
+                    help="path of the DracoRT checkout (default: $DRACO_REFERENCE)")
+    REF = Path(ap.parse_args().reference) if ap.parse_args().reference else None
     main()

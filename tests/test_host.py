@@ -108,8 +108,10 @@ def test_registry_contract():
     assert {"gguf_q8_0", "gguf_q4_k", "gguf_q6_k", "gguf_q6_k_dlast"} <= set(QUANT_REGISTRY.list_methods())
     assert QUANT_REGISTRY.get("GGUF_Q4_K").name == "gguf_q4_k"
     assert "gguf_q8_0" in QUANT_REGISTRY and len(QUANT_REGISTRY) >= 4
-    with pytest.raises(ValueError, match="Unknown quantization method"):
+    with pytest.raises(ValueError, match="gguf_q4_k"):  # names what is registered
         QUANT_REGISTRY.get("nope")
+    assert QUANT_REGISTRY.detect_from_config({"quant_method": "awq"}) is None
+    assert QUANT_REGISTRY.detect_from_config({}) is None
     assert QUANT_REGISTRY.detect_from_config({"quant_method": "GGUF_Q6_K"}) == "gguf_q6_k"
 
     class Foreign:  # any registry with register(name, backend), e.g. draco's QUANT_REGISTRY
@@ -124,6 +126,10 @@ def test_registry_contract():
     r = QuantizationRegistry()
     register_into(r)
     assert r.get("gguf_q6_k_dlast").q6k_order == "d_last"
+    # re-registering replaces the entry (with a warning), case-insensitively
+    first = r.get("gguf_q8_0")
+    register_into(r)
+    assert r.get("GGUF_Q8_0") is not first and len(r) == 4
 
 
 def test_backend_host_logic():

@@ -101,3 +101,34 @@ def test_gemm_kernel_matmul_matches_oracle(qtype, name):
         y = kern.matmul(a, info, p.tobytes())
         assert O.rel_l2(y, O.linear(a, qtype, p, n, k)) < 1e-3
     assert len(kern._cache) == 1  # the named tensor only
+
+
+@gpu
+@needs_cuda
+def test_backend_cache_never_serves_a_freed_weight_at_a_reused_address():
+    """quantized_linear keeps a TILED copy per weight.  A weight that is freed,
+    followed by a new weight of the same size placed at the same address by
+    the caching allocator, must be repacked, not served the old copy."""
+    from dracort_b200.format import quantize as Q
+    from dracort_b200.quantization import GGUFBackend
+
+    be = GGUFBackend(12)
+    rng = np.random.default_rng(5)
+    n, k = 128, 512
+    x = rng.standard_normal((2, k)).astype(np.float32)
+    xt = torch.from_numpy(x).cuda()
+    pa = Q.encode(12, Q.random_weight(rng, n, k))
+    pb = Q.encode(12, Q.random_weight(rng, n, k))
+    wa = torch.from_numpy(pa).cuda()
+    ya = be.quantized_linear(xt, wa, None).cpu().numpy()
+    assert O.rel_l2(ya, O.linear(x, 12, pa, n, k)) < 1e-3
+    addr = wa.data_ptr()
+    del wa
+    wb = torch.empty(pb.shape, dtype=torch.uint8, device="cuda")
+    assert wb.data_ptr() == addr  # the allocator reused the block (same size class)
+    wb.copy_(torch.from_numpy(pb))
+    yb = be.quantized_linear(xt, wb, None).cpu().numpy()
+    assert O.rel_l2(yb, O.linear(x, 12, pb, n, k)) < 1e-3
+    # an in-place rewrite of a live weight is seen as well
+    wb.copy_(torch.from_numpy(pa))
+    assert O.rel_l2(be.quantized_linear(xt, wb, None).cpu().numpy(), O.linear(x, 12, pa, n, k)) < 1e-3

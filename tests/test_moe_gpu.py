@@ -82,3 +82,46 @@ def test_swiglu_bf16_matches_fp32_formula(n):
     inplace = gate.clone()
     G.swiglu_bf16(inplace, up, out=inplace)
     assert torch.equal(inplace, out)
+
+
+def _numpy_route(logits, top_k):
+    """TopKRouter.forward (router.py:81-120) restated in numpy, independent of
+    the product's router: top-k of the logits, softmax over the k selected,
+    renormalised (router.py:106-111)."""
+    idx = np.argsort(-logits, axis=-1, kind="stable")[:, :top_k]
+    sel = np.take_along_axis(logits, idx, axis=-1).astype(np.float64)
+    w = np.exp(sel - sel.max(axis=-1, keepdims=True))
+    w /= w.sum(axis=-1, keepdims=True)
+    w /= w.sum(axis=-1, keepdims=True)
+    return idx, w.astype(np.float32)
+
+
+def test_moe_layer_at_config5_shapes_matches_expert_group_math():
+    """Config 5 in full: 8 Q4_K experts (gate/up 14336x4096, down 4096x14336),
+    256 bf16 tokens, top-2, against ExpertGroup.forward's math
+    (expert.py:77-116: per expert down(silu(gate(x)) * up(x)), outputs added
+    with the routing weights) on the oracle's fp32 weights, routed in numpy."""
+    from dracort_b200.workloads import MOE_FFN, MOE_HIDDEN, MOE_TOKENS, MOE_TOP_K, moe_experts
+
+    experts = moe_experts(2024)
+    rng = np.random.default_rng(2025)
+    x = torch.from_numpy(rng.standard_normal((MOE_TOKENS, MOE_HIDDEN)).astype(np.float32)).to(torch.bfloat16)
+    logits = rng.standard_normal((MOE_TOKENS, len(experts))).astype(np.float32)
+    layer = EPMoELayer(experts, MOE_HIDDEN, MOE_FFN, MOE_TOP_K, 0, 1, torch.device("cuda"))
+    y = layer.forward(x.cuda(), torch.from_numpy(logits).cuda()).cpu().numpy()
+    torch.cuda.synchronize()
+    assert layer.check_status() == 0
+
+    idx, w = _numpy_route(logits, MOE_TOP_K)
+    xf = x.float().numpy()
+    ref = np.zeros((MOE_TOKENS, MOE_HIDDEN), dtype=np.float32)
+    for e, (qt, g, u, d) in enumerate(experts):
+        rows, slot = np.nonzero(idx == e)
+        if rows.size == 0:
+            continue
+        xe = xf[rows]
+        h = xe @ O.dequantize_matrix(qt, g, MOE_FFN, MOE_HIDDEN).T
+        h = h / (1.0 + np.exp(-h)) * (xe @ O.dequantize_matrix(qt, u, MOE_FFN, MOE_HIDDEN).T)
+        ye = h @ O.dequantize_matrix(qt, d, MOE_HIDDEN, MOE_FFN).T
+        np.add.at(ref, rows, ye * w[rows, slot][:, None])
+    assert O.rel_l2(y, ref) < PREFILL_TOL

@@ -1,5 +1,6 @@
 """Tensor-parallel decode on 2 GPUs (NCCL): sharded GEMV + all-gather / all-reduce
-must reproduce the single-GPU GEMV of the unsharded layer set."""
+must reproduce the CPU oracle's fp32 linear layers of the unsharded layer set
+(the GEMV bar, 1e-3 relative L2)."""
 
 import os
 import socket
@@ -25,7 +26,6 @@ def _worker(rank, world, port, q):
 
     import torch.distributed as dist
 
-    from dracort_b200 import gguf_ops as G
     from dracort_b200.parallel.decode import TPDecodeLayer
     from dracort_b200.workloads import encode_specs, layer_specs
 
@@ -42,21 +42,15 @@ def _worker(rank, world, port, q):
         layer = TPDecodeLayer(specs, packed, rank, world, 2, dev, seed=3, min_copies=1, l2_bytes=0)
         layer.step(0)
         torch.cuda.synchronize()
-        outs = layer.outputs()
-        errs = {}
-        for s, p in zip(specs, packed):
-            t = G.repack(s.qtype, torch.from_numpy(p.reshape(-1)).to(dev), s.n_rows, s.k)
-            ref = G.gemv(s.qtype, t, layer.x_full[s.name], s.n_rows, s.k)
-            got = outs[s.name]
-            errs[s.name] = float((got - ref).norm() / ref.norm())
-        q.put((rank, errs))
+        outs = {k: v.cpu().numpy() for k, v in layer.outputs().items()}
+        q.put((rank, outs, {k: v.cpu().numpy() for k, v in layer.x_full.items()}))
         layer.close()
     finally:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def test_tp2_decode_layer_matches_single_gpu():
+def test_tp2_decode_layer_matches_oracle():
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
@@ -69,8 +63,14 @@ def test_tp2_decode_layer_matches_single_gpu():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, errs in res:
-        for name, e in errs.items():
-            # sharding changes only the k ranges of the activation groups and the
-            # summation order: both results are within the GEMV error budget
-            assert e < 5e-4, (rank, name, e)
+    from dracort_b200.workloads import encode_specs, layer_specs
+    from oracle import gguf_oracle as O
+
+    specs = layer_specs("q4_k_m")
+    packed = encode_specs(specs, 77)
+    _, _, xs0 = res[0]
+    for rank, outs, xs in res:
+        for s, p in zip(specs, packed):
+            assert np.array_equal(xs[s.name], xs0[s.name])
+            want = O.linear(xs[s.name], s.qtype, p, s.n_rows, s.k)
+            assert O.rel_l2(outs[s.name], want) < 1e-3, (rank, s.name)
