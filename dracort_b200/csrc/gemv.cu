@@ -86,13 +86,6 @@ constexpr int kConvWarps = 3;
 constexpr int kThreads = (kConsumerWarps + 1 + kConvWarps) * 32;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
 constexpr int kMaxMboxSlots = 4;
-// Back-off (ns) between polls of a stage's generation word by a converter
-// warp: the converters run ahead of the consumers and mostly wait, and a
-// tight poll loop takes issue slots from the consumer warps of their SMSP.
-#ifndef DRACO_GEMV_GEN_SLEEP_NS
-#define DRACO_GEMV_GEN_SLEEP_NS 0
-#endif
-constexpr int kGenSleepNs = DRACO_GEMV_GEN_SLEEP_NS;
 
 struct GemvProbDev {
   const uint8_t* w;
@@ -201,7 +194,6 @@ __device__ __forceinline__ bool wait_generation(const GemvParams& P, const int* 
   if (gen_read(g) >= m) return true;
   const uint64_t t0 = global_timer_ns();
   while (gen_read(g) < m) {
-    if (kGenSleepNs > 0) __nanosleep(kGenSleepNs);
     if (*abort) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) {
       record_error(P, DRACO_ERR_TIMEOUT);
@@ -261,7 +253,32 @@ __device__ __forceinline__ void imma_u8_k16(int (&d)[4], uint32_t a0, uint32_t a
                : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
                : "r"(a0), "r"(a1), "r"(b0));
 }
-__device__ __forceinline__ void zero4(int (&d)[4]) { d[0] = d[1] = d[2] = d[3] = 0; }
+// first MMA of an accumulation chain: zero accumulator input (no register moves)
+__device__ __forceinline__ void imma_u8_k32_first(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                  uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void imma_s8_k32_first(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                  uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void imma_u8_k16_first(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+               : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+               : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+// x * v for a 6-bit integer v given as the float bits of 2^23 + v: one FMA
+// whose exact result x * v (at most 17 significant bits for an fp16 x) is
+// representable, so the single rounding returns it exactly.
+__device__ __forceinline__ float mul_small(float x, uint32_t v_bits, float neg_x_2p23) {
+  return fmaf(x, __uint_as_float(v_bits), neg_x_2p23);
+}
 // the two activation digits of one row: x / u = 256 * hi + lo
 __device__ __forceinline__ float digits(int hi, int lo) { return __int2float_rn(hi * 256 + lo); }
 
@@ -280,7 +297,7 @@ constexpr uint32_t kNibHi = 0xF0F0F0F0u;
 //         diagonal: ((sub-block mod G) * Bp + b) * 2 + digit,  G = 4 / Bp,
 //       a Q4_K / Q8_0 sub-block being the group and a Q6_K sub-block one half
 //       (the halves then go to different columns); unused slots hold zeros;
-//   su[m][b] = (S_half0, S_half1, u, 0).
+//   su[m][b] = (S_half0, S_half1, u, S_half0 + S_half1) (all exact).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -345,7 +362,7 @@ __device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProb
     const int qs_other = __shfl_xor_sync(0xffffffffu, qs, 2);  // the group's other half
     if (r == 0)
       *reinterpret_cast<float4*>(su + (m * kSlots + b) * 16) =
-          make_float4(__int2float_rn(qs) * u, __int2float_rn(qs_other) * u, u, 0.f);
+          make_float4(__int2float_rn(qs) * u, __int2float_rn(qs_other) * u, u, __int2float_rn(qs + qs_other) * u);
     uint32_t dh[2], dl[2];
 #pragma unroll
     for (int tt = 0; tt < 2; ++tt) {
@@ -427,28 +444,50 @@ __device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, 
     constexpr int Bp = 4 / G, NF = 8 / G;
     int fr[NF][4];
 #pragma unroll
-    for (int f = 0; f < NF; ++f) zero4(fr[f]);
-#pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint4 v = lds128(ch + 512 * q + 16 * lane);
       const uint2 bl = lds64(xs + (2 * q) * kColBytes + lane * 8);
       const uint2 bh = lds64(xs + (2 * q + 1) * kColBytes + lane * 8);
-      imma_u8_k32(fr[(2 * q) / G], v.x & kNib, v.z & kNib, v.y & kNib, v.w & kNib, bl.x, bl.y);
+      if ((2 * q) % G == 0)
+        imma_u8_k32_first(fr[(2 * q) / G], v.x & kNib, v.z & kNib, v.y & kNib, v.w & kNib, bl.x, bl.y);
+      else
+        imma_u8_k32(fr[(2 * q) / G], v.x & kNib, v.z & kNib, v.y & kNib, v.w & kNib, bl.x, bl.y);
       // high nibbles in place: 16 x the quant (exact in the int32 sum)
       imma_u8_k32(fr[(2 * q + 1) / G], v.x & kNibHi, v.z & kNibHi, v.y & kNibHi, v.w & kNibHi, bh.x, bh.y);
     }
     const int b = t % Bp;
+    // this lane's sub-blocks j = f * G + t / Bp all have the same parity: odd
+    // sub-blocks were entered as 16 x the quant, so fold 1/16 into d
+    const float h = ((t / Bp) & 1) ? 0.0625f : 1.f;
+    const float dq0 = d0 * h, dq1 = d1 * h;
+    const float ndq0 = dq0 * -8388608.f, ndq1 = dq1 * -8388608.f;
+    const float nm0 = m0 * -8388608.f, nm1 = m1 * -8388608.f;
+    constexpr uint32_t kMag = 0x4B000000u;  // float bits of 2^23
 #pragma unroll
     for (int f = 0; f < NF; ++f) {
       const int j = f * G + t / Bp;  // this lane's sub-block in accumulator f
-      float ds0, mm0, ds1, mm1;
-      q4k_sm(A0, B0, C0, d0, m0, j, f * G >= 4, ds0, mm0);
-      q4k_sm(A1, B1, C1, d1, m1, j, f * G >= 4, ds1, mm1);
-      const float4 s = lds128f(su + (j * 4 + b) * 16);
-      const float S = s.x + s.y;
-      const float us = (j & 1) ? s.z * 0.0625f : s.z;  // odd sub-blocks: high nibbles entered as 16 x q
-      acc[0][0] = fmaf(ds0 * us, digits(fr[f][0], fr[f][1]), fmaf(-mm0, S, acc[0][0]));
-      acc[0][1] = fmaf(ds1 * us, digits(fr[f][2], fr[f][3]), fmaf(-mm1, S, acc[0][1]));
+      uint32_t sc0, mn0, sc1, mn1;   // float bits of 2^23 + the 6-bit scale / min (gguf.py:436-442)
+      if (f * G < 4) {
+        const uint32_t sel = 0x7440u | (uint32_t)j;  // byte j, two zero bytes, 0x4B
+        sc0 = __byte_perm(A0, kMag, sel) & 0x4B00003Fu;
+        mn0 = __byte_perm(B0, kMag, sel) & 0x4B00003Fu;
+        sc1 = __byte_perm(A1, kMag, sel) & 0x4B00003Fu;
+        mn1 = __byte_perm(B1, kMag, sel) & 0x4B00003Fu;
+      } else {
+        const uint32_t sel = 0x0040u | (uint32_t)(j - 4) | ((uint32_t)(j - 4) << 4);  // {C[i], X[i], 0, 0}
+        const uint32_t xa0 = __byte_perm(C0, A0, sel), xb0 = __byte_perm(C0, B0, sel);
+        const uint32_t xa1 = __byte_perm(C1, A1, sel), xb1 = __byte_perm(C1, B1, sel);
+        // scale: C[i] & 15 | (A[i] >> 6) << 4;  min: C[i] >> 4 | (B[i] >> 6) << 4
+        sc0 = ((xa0 & 15u) | kMag) | ((xa0 >> 10) & 0x30u);
+        mn0 = (((xb0 >> 4) & 15u) | kMag) | ((xb0 >> 10) & 0x30u);
+        sc1 = ((xa1 & 15u) | kMag) | ((xa1 >> 10) & 0x30u);
+        mn1 = (((xb1 >> 4) & 15u) | kMag) | ((xb1 >> 10) & 0x30u);
+      }
+      const float4 s = lds128f(su + (j * 4 + b) * 16);  // (S_half0, S_half1, u, S)
+      const float ds0 = mul_small(dq0, sc0, ndq0), ds1 = mul_small(dq1, sc1, ndq1);
+      const float mm0 = mul_small(m0, mn0, nm0), mm1 = mul_small(m1, mn1, nm1);
+      acc[0][0] = fmaf(ds0, s.z * digits(fr[f][0], fr[f][1]), fmaf(-mm0, s.w, acc[0][0]));
+      acc[0][1] = fmaf(ds1, s.z * digits(fr[f][2], fr[f][3]), fmaf(-mm1, s.w, acc[0][1]));
     }
   } else {
 #pragma unroll
@@ -466,17 +505,15 @@ __device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, 
         const uint2 bl = lds64(xs + (2 * q) * kColBytes + nt * 256 + lane * 8);
         const uint2 bh = lds64(xs + (2 * q + 1) * kColBytes + nt * 256 + lane * 8);
         int c[4], e[4];
-        zero4(c);
-        zero4(e);
-        imma_u8_k32(c, l0, l1, l2, l3, bl.x, bl.y);
-        imma_u8_k32(e, h0, h1, h2, h3, bh.x, bh.y);
+        imma_u8_k32_first(c, l0, l1, l2, l3, bl.x, bl.y);
+        imma_u8_k32_first(e, h0, h1, h2, h3, bh.x, bh.y);
         const float4 sl = lds128f(su + ((2 * q) * 4 * NT + 4 * nt + t) * 16);
         const float4 sh = lds128f(su + ((2 * q + 1) * 4 * NT + 4 * nt + t) * 16);
         float r0 = acc[nt][0], r1 = acc[nt][1];
-        r0 = fmaf(dsl0 * sl.z, digits(c[0], c[1]), fmaf(-mml0, sl.x + sl.y, r0));
-        r1 = fmaf(dsl1 * sl.z, digits(c[2], c[3]), fmaf(-mml1, sl.x + sl.y, r1));
-        r0 = fmaf(dsh0 * sh.z, digits(e[0], e[1]), fmaf(-mmh0, sh.x + sh.y, r0));
-        r1 = fmaf(dsh1 * sh.z, digits(e[2], e[3]), fmaf(-mmh1, sh.x + sh.y, r1));
+        r0 = fmaf(dsl0 * sl.z, digits(c[0], c[1]), fmaf(-mml0, sl.w, r0));
+        r1 = fmaf(dsl1 * sl.z, digits(c[2], c[3]), fmaf(-mml1, sl.w, r1));
+        r0 = fmaf(dsh0 * sh.z, digits(e[0], e[1]), fmaf(-mmh0, sh.w, r0));
+        r1 = fmaf(dsh1 * sh.z, digits(e[2], e[3]), fmaf(-mmh1, sh.w, r1));
         acc[nt][0] = r0;
         acc[nt][1] = r1;
       }
@@ -510,8 +547,6 @@ __device__ __forceinline__ void chunk_q6k(const uint8_t* ch, const uint8_t* xs, 
     constexpr int Bp = 4 / G, NF = 16 / G;
     int fr[NF][4];
 #pragma unroll
-    for (int f = 0; f < NF; ++f) zero4(fr[f]);
-#pragma unroll
     for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -522,7 +557,8 @@ __device__ __forceinline__ void chunk_q6k(const uint8_t* ch, const uint8_t* xs, 
         const uint32_t a1 = q6_bytes(W[w0 + 3 + (i & 1)], W[w0 + 5], i);
         const uint32_t a2 = q6_bytes(W[w1 + (i & 1)], W[w1 + 2], i);
         const uint32_t a3 = q6_bytes(W[w1 + 3 + (i & 1)], W[w1 + 5], i);
-        imma_u8_k32(fr[(2 * m) / G], a0, a1, a2, a3, bx.x, bx.y);
+        if ((2 * m) % G == 0) imma_u8_k32_first(fr[(2 * m) / G], a0, a1, a2, a3, bx.x, bx.y);
+        else imma_u8_k32(fr[(2 * m) / G], a0, a1, a2, a3, bx.x, bx.y);
       }
     const int b = t % Bp;
 #pragma unroll
@@ -556,8 +592,7 @@ __device__ __forceinline__ void chunk_q6k(const uint8_t* ch, const uint8_t* xs, 
             const uint2 bx = lds64(xs + m * kColBytes + nt * 256 + lane * 8);
             const float4 sv = lds128f(su + (m * 4 * NT + 4 * nt + t) * 16);
             int c[4];
-            zero4(c);
-            imma_u8_k16(c, a0, a1, is ? bx.y : bx.x);
+            imma_u8_k16_first(c, a0, a1, is ? bx.y : bx.x);
             const float S = is ? sv.y : sv.x;
             acc[nt][0] = fmaf(al0, fmaf(-32.f, S, sv.z * digits(c[0], c[1])), acc[nt][0]);
             acc[nt][1] = fmaf(al1, fmaf(-32.f, S, sv.z * digits(c[2], c[3])), acc[nt][1]);
@@ -577,12 +612,11 @@ __device__ __forceinline__ void chunk_q80(const uint8_t* ch, const uint8_t* xs, 
     constexpr int Bp = 4 / G, NF = 8 / G;
     int fr[NF][4];
 #pragma unroll
-    for (int f = 0; f < NF; ++f) zero4(fr[f]);
-#pragma unroll
     for (int bk = 0; bk < 8; ++bk) {
       const uint4 v = lds128(ch + 512 * bk + 16 * lane);
       const uint2 bx = lds64(xs + bk * kColBytes + lane * 8);
-      imma_s8_k32(fr[bk / G], v.x, v.z, v.y, v.w, bx.x, bx.y);
+      if (bk % G == 0) imma_s8_k32_first(fr[bk / G], v.x, v.z, v.y, v.w, bx.x, bx.y);
+      else imma_s8_k32(fr[bk / G], v.x, v.z, v.y, v.w, bx.x, bx.y);
     }
     const int b = t % Bp;
 #pragma unroll
@@ -603,8 +637,7 @@ __device__ __forceinline__ void chunk_q80(const uint8_t* ch, const uint8_t* xs, 
         const uint2 bx = lds64(xs + bk * kColBytes + nt * 256 + lane * 8);
         const float u = lds128f(su + (bk * 4 * NT + 4 * nt + t) * 16).z;
         int c[4];
-        zero4(c);
-        imma_s8_k32(c, v.x, v.z, v.y, v.w, bx.x, bx.y);
+        imma_s8_k32_first(c, v.x, v.z, v.y, v.w, bx.x, bx.y);
         acc[nt][0] = fmaf(dg * u, digits(c[0], c[1]), acc[nt][0]);
         acc[nt][1] = fmaf(dg8 * u, digits(c[2], c[3]), acc[nt][1]);
       }
@@ -842,7 +875,9 @@ __global__ void __launch_bounds__(kConvertWarpsPerBlock * 32) gemv_convert_kerne
   uint8_t* dst = P.ws + P.prob[p].xcv_off + (int64_t)u * xb;
   for (int i = lane; i < (xb >> 4); i += 32) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
   __syncwarp();
-  convert_slab<1, NT>(P, P.prob[p], u, dst, dst + P.xs_bytes, lane);
+  if (P.batch == 1) convert_slab<4, 1>(P, P.prob[p], u, dst, dst + P.xs_bytes, lane);
+  else if (P.batch == 2) convert_slab<2, 1>(P, P.prob[p], u, dst, dst + P.xs_bytes, lane);
+  else convert_slab<1, NT>(P, P.prob[p], u, dst, dst + P.xs_bytes, lane);
 }
 
 // ---------------------------------------------------------------------------
@@ -965,7 +1000,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         return;
       }
       uint8_t* xs = smem + (size_t)st * P.stage_bytes + P.w_stage;
-      if (G == 1 && P.precvt) {
+      if (P.precvt) {
         // the slice was converted before the launch: one bulk copy, which the
         // stage's ready phase waits for along with the weight bytes
         if (lane == 0) {
@@ -1111,7 +1146,10 @@ static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_
   P.part_off = off;
   off = align256(off + (int64_t)kMaxCta * 2 * kRowWarps * 32 * NT * 2 * 4);
   // dense layouts (batch >= 3): slices of the activations converted once per launch
-  P.precvt = (convert_once && batch >= 3) ? 1 : 0;
+#ifndef DRACO_GEMV_PRECVT_MIN_BATCH
+#define DRACO_GEMV_PRECVT_MIN_BATCH 2
+#endif
+  P.precvt = (convert_once && batch >= DRACO_GEMV_PRECVT_MIN_BATCH) ? 1 : 0;
   for (int p = 0; p < n; ++p) {
     P.prob[p].xcv_off = -1;
     if (P.precvt) {
