@@ -141,27 +141,60 @@ class GGUFBackend(QuantizationBackend):
                                device: torch.device) -> nn.Module:
         """Replace nn.Linear submodules with GGUFLinear from packed GGUF tensors.
 
-        ``config["tensors"]`` maps a module's ``<name>.weight`` to
-        ``(ggml_type, payload)`` where payload is the packed uint8 array of a
-        [out_features, in_features] tensor; tensors of another type than this
-        backend's are loaded with their own type.  ``model_path`` is recorded
-        only (GGUF container parsing is done by the caller's reader).
+        Two sources, in this order:
+        * ``model_path`` naming a .gguf file: its quantized tensors are loaded
+          onto ``device`` by dracort_b200.gguf_loader (pinned staging, on-device
+          regroup) and matched to modules by their llama-family canonical names
+          (``blk.N.attn_q.weight`` -> ``model.layers.N.self_attn.q_proj.weight``,
+          the naming of draco/format/gguf.py:104-171) or their own names;
+          ``config["q6k_order"]`` (default "d_last", llama.cpp's order) gives
+          the Q6_K byte order of the file;
+        * ``config["tensors"]`` mapping ``<module>.weight`` to
+          ``(ggml_type, payload)`` (packed uint8 [out_features, row_bytes]).
+        Tensors of another type than this backend's keep their own type.
         """
-        tensors = config.get("tensors") or {}
         replaced = 0
-        for mod_name, mod in list(target_model.named_modules()):
-            if not isinstance(mod, nn.Linear):
-                continue
+        device = torch.device(device)
+
+        def swap(mod_name: str, new: nn.Module) -> None:
+            parent_name, _, child = mod_name.rpartition(".")
+            parent = target_model.get_submodule(parent_name) if parent_name else target_model
+            setattr(parent, child, new)
+
+        linears = {n: m for n, m in target_model.named_modules() if isinstance(m, nn.Linear)}
+        if isinstance(model_path, str) and model_path.endswith(".gguf"):
+            from dracort_b200.format.gguf_file import GGUFFile, canonical_name
+            from dracort_b200.gguf_loader import load_gguf
+
+            with GGUFFile(model_path) as gf:
+                plan = {}
+                for t in gf:
+                    for cand in (canonical_name(t.name), t.name):
+                        mod = cand[:-len(".weight")] if cand.endswith(".weight") else None
+                        if t.is_quantized and mod in linears and mod not in plan:
+                            plan[mod] = t
+                            break
+                for mod_name, t in plan.items():
+                    m = linears[mod_name]
+                    if (t.n_rows, t.k) != (m.out_features, m.in_features):
+                        raise DracoFormatError(f"GGUF tensor '{t.name}' has shape {t.shape}, module '{mod_name}' "
+                                               f"expects [{m.out_features}, {m.in_features}]")
+                loaded = load_gguf(gf, device, names=[t.name for t in plan.values()],
+                                   q6k_order=config.get("q6k_order", Q6K_D_LAST))
+                for mod_name, t in plan.items():
+                    m, dw = linears[mod_name], loaded[t.name]
+                    bias = m.bias.detach().to(device) if m.bias is not None else None
+                    swap(mod_name, GGUFLinear(m.in_features, m.out_features, dw.qtype, dw.tiled, bias))
+                    replaced += 1
+        tensors = config.get("tensors") or {}
+        for mod_name, mod in linears.items():
             entry = tensors.get(f"{mod_name}.weight")
             if entry is None:
                 continue
             qtype, payload = entry
             bias = mod.bias.detach() if mod.bias is not None else None
-            new = GGUFLinear.from_packed(qtype, payload, mod.in_features, mod.out_features, bias=bias,
-                                         q6k_order=self.q6k_order, device=device)
-            parent_name, _, child = mod_name.rpartition(".")
-            parent = target_model.get_submodule(parent_name) if parent_name else target_model
-            setattr(parent, child, new)
+            swap(mod_name, GGUFLinear.from_packed(qtype, payload, mod.in_features, mod.out_features, bias=bias,
+                                                  q6k_order=self.q6k_order, device=device))
             replaced += 1
         target_model._gguf_replaced = replaced  # type: ignore[attr-defined]
         return target_model.to(device)
