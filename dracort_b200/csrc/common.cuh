@@ -183,17 +183,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// try_wait with an explicit suspend-time hint (ns): a waiting thread is
-// suspended until the phase completes or the hint expires instead of polling.
-__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
 // 32-bit flag store / load ordered at system scope (flags that other GPUs
 // write into this GPU's memory, or this GPU into theirs, over NVLink).
 __device__ __forceinline__ void st_release_sys(int* p, int v) {

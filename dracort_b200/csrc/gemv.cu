@@ -86,9 +86,6 @@ constexpr int kConvWarps = 3;
 constexpr int kThreads = (kConsumerWarps + 1 + kConvWarps) * 32;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
 constexpr int kMaxMboxSlots = 4;
-#ifndef DRACO_GEMV_SUSPEND_NS
-#define DRACO_GEMV_SUSPEND_NS 0
-#endif
 
 struct GemvProbDev {
   const uint8_t* w;
@@ -172,12 +169,8 @@ __device__ __forceinline__ bool wait_phase(const GemvParams& P, uint64_t* bar, u
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
-#if DRACO_GEMV_SUSPEND_NS > 0
-    if (mbar_try_wait_hint(bar, parity, DRACO_GEMV_SUSPEND_NS)) return true;
-#else
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-#endif
     if (*abort) return false;
     if (global_timer_ns() - t0 > kWaitLimitNs) {
       record_error(P, DRACO_ERR_TIMEOUT);
