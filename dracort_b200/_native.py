@@ -54,6 +54,8 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv_grouped_noalloc",
     "draco_gguf_gemv_noalloc_status",
     "draco_gguf_gemm",
+    "draco_gguf_gemm_rows",
+    "draco_swiglu_bf16_rows",
     "draco_swiglu_bf16",
     "draco_swiglu_f32",
     "draco_tp_buffer_alloc",
@@ -170,6 +172,10 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_gemv_noalloc_status.argtypes = [ctypes.POINTER(c_int), vp]
         lib.draco_gguf_gemm.restype = c_int
         lib.draco_gguf_gemm.argtypes = [ctypes.POINTER(GemmProblem), c_int, vp, vp]
+        lib.draco_gguf_gemm_rows.restype = c_int
+        lib.draco_gguf_gemm_rows.argtypes = [ctypes.POINTER(GemmProblem), c_int, vp, vp, vp]
+        lib.draco_swiglu_bf16_rows.restype = c_int
+        lib.draco_swiglu_bf16_rows.argtypes = [vp, vp, vp, c_int, i64, i64, vp, vp]
         lib.draco_swiglu_bf16.restype = c_int
         lib.draco_swiglu_bf16.argtypes = [vp, vp, vp, i64, vp]
         lib.draco_swiglu_f32.restype = c_int

@@ -52,6 +52,37 @@ cudaError_t launch_swiglu_bf16(const void* gate, const void* up, void* out, int6
   return cudaGetLastError();
 }
 
+// Row-counted form: `groups` blocks of [cap_rows, width] bf16 (row-major,
+// block g at g * cap_rows * width); only the first rows[g] rows of block g
+// (device count, clamped to cap_rows) are computed.  width % 8 == 0.
+__global__ void swiglu_bf16_rows_kernel(const uint16_t* __restrict__ g, const uint16_t* __restrict__ u,
+                                        uint16_t* __restrict__ o, int64_t cap_rows, int64_t width,
+                                        const int* __restrict__ rows) {
+  const int grp = blockIdx.y;
+  const int64_t r = min((int64_t)max(rows[grp], 0), cap_rows);
+  const int64_t n8 = r * (width >> 3);
+  const int64_t base = (int64_t)grp * cap_rows * (width >> 3);
+  const uint4* g4 = reinterpret_cast<const uint4*>(g) + base;
+  const uint4* u4 = reinterpret_cast<const uint4*>(u) + base;
+  uint4* o4 = reinterpret_cast<uint4*>(o) + base;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 a = g4[i], b = u4[i];
+    o4[i] = make_uint4(swiglu2(a.x, b.x), swiglu2(a.y, b.y), swiglu2(a.z, b.z), swiglu2(a.w, b.w));
+  }
+}
+
+cudaError_t launch_swiglu_bf16_rows(const void* gate, const void* up, void* out, int groups, int64_t cap_rows,
+                                    int64_t width, const int* rows, cudaStream_t st) {
+  const int threads = 256;
+  const int64_t want = (cap_rows * (width >> 3) + threads - 1) / threads;
+  const int per = (8 * device_sm_count() + groups - 1) / groups;
+  const dim3 grid((unsigned)(want < 1 ? 1 : (want > per ? per : want)), (unsigned)groups);
+  swiglu_bf16_rows_kernel<<<grid, threads, 0, st>>>(static_cast<const uint16_t*>(gate),
+                                                     static_cast<const uint16_t*>(up), static_cast<uint16_t*>(out),
+                                                     cap_rows, width, rows);
+  return cudaGetLastError();
+}
+
 // fp32: 4 elements per thread and iteration on 16-byte vectors, the last n % 4
 // by single threads
 __global__ void swiglu_f32_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ o,

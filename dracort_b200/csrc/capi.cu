@@ -175,7 +175,7 @@ int draco_gguf_gemv_noalloc_status(int* status, void* stream) {
   return ok();
 }
 
-int draco_gguf_gemm(const draco_gemm_problem* probs, int n_problems, int* status, void* stream) {
+static int check_gemm_problems(const draco_gemm_problem* probs, int n_problems) {
   if (!probs || n_problems < 1 || n_problems > DRACO_GEMM_MAX_PROBLEMS)
     return fail(DRACO_ERR_ARG, "gemm: need 1..%d problems, got %d", DRACO_GEMM_MAX_PROBLEMS, n_problems);
   for (int i = 0; i < n_problems; ++i) {
@@ -192,8 +192,26 @@ int draco_gguf_gemm(const draco_gemm_problem* probs, int n_problems, int* status
       return fail(DRACO_ERR_ALIGN, "gemm: problem %d: x must be 16-byte aligned with ldx a multiple of 8", i);
     if (q.m > (int64_t)1 << 30) return fail(DRACO_ERR_SHAPE, "gemm: problem %d m too large", i);
   }
+  return DRACO_OK;
+}
+
+int draco_gguf_gemm(const draco_gemm_problem* probs, int n_problems, int* status, void* stream) {
+  int rc = check_gemm_problems(probs, n_problems);
+  if (rc) return rc;
   char msg[256] = {0};
-  int rc = gemm_launch(probs, n_problems, status, (cudaStream_t)stream, msg, sizeof(msg));
+  rc = gemm_launch(probs, n_problems, nullptr, status, (cudaStream_t)stream, msg, sizeof(msg));
+  if (rc) return fail(rc, "%s", msg);
+  return ok();
+}
+
+int draco_gguf_gemm_rows(const draco_gemm_problem* probs, int n_problems, const int* rows, int* status,
+                         void* stream) {
+  if (!rows) return fail(DRACO_ERR_ARG, "gemm_rows: null row counts");
+  if (reinterpret_cast<uintptr_t>(rows) & 3) return fail(DRACO_ERR_ALIGN, "gemm_rows: row counts not 4-byte aligned");
+  int rc = check_gemm_problems(probs, n_problems);
+  if (rc) return rc;
+  char msg[256] = {0};
+  rc = gemm_launch(probs, n_problems, rows, status, (cudaStream_t)stream, msg, sizeof(msg));
   if (rc) return fail(rc, "%s", msg);
   return ok();
 }
@@ -296,6 +314,20 @@ int draco_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, vo
     return fail(DRACO_ERR_ALIGN, "swiglu: gate, up and out must be 16-byte aligned");
   cudaError_t e = draco::launch_swiglu_bf16(gate, up, out, n, (cudaStream_t)stream);
   return e == cudaSuccess ? ok() : cuda_fail(e, "swiglu");
+}
+
+int draco_swiglu_bf16_rows(const void* gate, const void* up, void* out, int groups, int64_t cap_rows,
+                           int64_t width, const int* rows, void* stream) {
+  if (groups < 0 || groups > 65535 || cap_rows < 0 || width < 0)
+    return fail(DRACO_ERR_SHAPE, "swiglu_rows: bad groups / rows / width");
+  if (groups == 0 || cap_rows == 0 || width == 0) return ok();
+  if (!gate || !up || !out || !rows) return fail(DRACO_ERR_ARG, "swiglu_rows: null pointer");
+  if (width % 8) return fail(DRACO_ERR_SHAPE, "swiglu_rows: width must be a multiple of 8");
+  if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return fail(DRACO_ERR_ALIGN, "swiglu_rows: gate, up and out must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(rows) & 3) return fail(DRACO_ERR_ALIGN, "swiglu_rows: rows not 4-byte aligned");
+  cudaError_t e = draco::launch_swiglu_bf16_rows(gate, up, out, groups, cap_rows, width, rows, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "swiglu_rows");
 }
 
 int draco_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, void* stream) {

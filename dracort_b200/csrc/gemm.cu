@@ -68,6 +68,7 @@ struct GemmProbDev {
   void* y;
   int64_t ldy;
   int qt, ydtype, m, n, k, nb, n_rg, n_tiles, cb, tblocks, tile0, vec, ymode;
+  int src;  // index of the problem in the caller's array (device row counts are in that order)
 };
 constexpr int kYDirect = 0, kYTma = 1;  // epilogue: direct stores or staged TMA stores
 
@@ -79,6 +80,7 @@ struct __align__(64) GemmParams {
   CUtensorMap ymap[kGemmMaxProblems];
   GemmProbDev prob[kGemmMaxProblems];
   int* status;
+  const int* rows;  // optional device row counts per problem (caller's order); m is then the capacity
   int n_prob, total_tiles;
   int sched_ok;                       // 1: pair p runs tiles sched[off[p] .. off[p+1]); 0: strided
   uint16_t off[kMaxPairs + 1];
@@ -450,9 +452,9 @@ __device__ __forceinline__ int tile_at(const GemmParams& P, int pair, int i, int
   return t < P.total_tiles ? t : -1;
 }
 
-// pair tile t -> (problem, row pair, 512-token block)
+// pair tile t -> (problem, row pair, 512-token block, the problem's token count)
 struct TileCursor {
-  int p, rp, tb, nkb;
+  int p, rp, tb, nkb, m;
   __device__ void at(const GemmParams& P, int t) {
     p = 0;
     for (int q = 1; q < P.n_prob; ++q)
@@ -461,11 +463,15 @@ struct TileCursor {
     rp = local / P.prob[p].tblocks;
     tb = local - rp * P.prob[p].tblocks;
     nkb = P.prob[p].nb * 4;
+    m = P.prob[p].m;
+    // rows counted on the device by a preceding kernel (read after the grid
+    // dependency wait): tokens past them are neither loaded, multiplied nor stored
+    if (P.rows) m = min(m, max(0, P.rows[P.prob[p].src]));
   }
 };
 
-__device__ __forceinline__ void store_rows(const GemmProbDev& pr, int tok, int row0, const uint32_t (&v)[32]) {
-  if (tok >= pr.m || row0 >= pr.n) return;
+__device__ __forceinline__ void store_rows(const GemmProbDev& pr, int m, int tok, int row0, const uint32_t (&v)[32]) {
+  if (tok >= m || row0 >= pr.n) return;
   if (pr.ydtype == DRACO_DTYPE_BF16) {
     __nv_bfloat16* y = static_cast<__nv_bfloat16*>(pr.y) + (int64_t)tok * pr.ldy + row0;
     if (pr.vec && row0 + 32 <= pr.n) {
@@ -635,7 +641,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
           // an expert's few tokens leave the upper ones empty): both CTAs
           // count the same boxes, the leader expects their bytes
           const int tok_tile = c.tb * kTileTok;
-          const int m = P.prob[c.p].m;
+          const int m = c.m;
           if (rank == 0) {
             int nbox = 0;
 #pragma unroll
@@ -666,7 +672,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         TileCursor c;
         c.at(P, t);
         // accumulators whose 256 tokens all lie at or past M get no MMAs
-        const int nh_live = c.tb * kTileTok + kUmmaM < P.prob[c.p].m ? 2 : 1;
+        const int tok_tile = c.tb * kTileTok;
+        const int nh_live = tok_tile + kUmmaM < c.m ? 2 : (tok_tile < c.m ? 1 : 0);
         for (int kb = 0; kb < c.nkb && ok; ++kb) {
           // one wait per k-block: X boxes of both CTAs landed, both weight tiles dequantized
           if (!mbar_wait_bounded(&full_kb[rs.s], rs.ph, kGemmWaitNs)) {
@@ -731,7 +738,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         tc_fence_after();
         const int tok0 = c.tb * kTileTok + hh * kUmmaM + (int)rank * kTokCta + 32 * e;
         const uint32_t tbase = tmem + ((uint32_t)(32 * e) << 16) + hh * kUmmaN;
-        if (tok0 < pr.m) {
+        if (tok0 < c.m) {
 #pragma unroll 1
           for (int cc = 0; cc < kUmmaN / 32; cc += 2) {
             uint32_t v0[32], v1[32];
@@ -764,8 +771,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
                 ++nst;
               }
             } else {
-              store_rows(pr, tok0 + lane, row0, v0);
-              store_rows(pr, tok0 + lane, row0 + 32, v1);
+              store_rows(pr, c.m, tok0 + lane, row0, v0);
+              store_rows(pr, c.m, tok0 + lane, row0 + 32, v1);
             }
           }
         }
@@ -966,7 +973,8 @@ static void build_schedule(GemmParams& P, int pairs) {
   P.sched_ok = 1;
 }
 
-int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_t st, char* msg, size_t ml) {
+int gemm_launch(const draco_gemm_problem* probs, int n, const int* rows, int* status, cudaStream_t st, char* msg,
+                size_t ml) {
   if (n < 1 || n > kGemmMaxProblems) {
     snprintf(msg, ml, "gemm: need 1..%d problems, got %d", kGemmMaxProblems, n);
     return DRACO_ERR_ARG;
@@ -996,6 +1004,7 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
     d.qt = q.qtype;
     d.ydtype = q.ydtype;
     d.m = (int)q.m;
+    d.src = order[p];
     d.n = (int)q.n_rows;
     d.k = (int)q.k;
     d.nb = (int)g.nb;
@@ -1036,6 +1045,7 @@ int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_
   P.n_prob = n;
   P.total_tiles = tiles;
   P.status = status;
+  P.rows = rows;
   if (tiles == 0) return DRACO_OK;
   int dyn_smem = 0;
   const int max_pairs = gemm_max_pairs(&dyn_smem, msg, ml);

@@ -36,10 +36,15 @@ int gemv_noalloc_status(int* out, cudaStream_t st, char* msg, size_t msg_len);
 
 // Prefill dequant-GEMM (tcgen05).  `status` is an optional device int the
 // kernel sets to a DRACO_* code on a device-side failure.
-int gemm_launch(const draco_gemm_problem* probs, int n, int* status, cudaStream_t st, char* msg, size_t msg_len);
+// `rows` (optional, device): tokens actually present per problem, each m the capacity.
+int gemm_launch(const draco_gemm_problem* probs, int n, const int* rows, int* status, cudaStream_t st, char* msg,
+                size_t msg_len);
 
 // out = bf16(silu(gate) * up) over n bf16 elements (16-byte aligned).
 cudaError_t launch_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, cudaStream_t st);
+// Row-counted bf16 form over groups of [cap_rows, width] blocks (rows: device counts).
+cudaError_t launch_swiglu_bf16_rows(const void* gate, const void* up, void* out, int groups, int64_t cap_rows,
+                                    int64_t width, const int* rows, cudaStream_t st);
 // out = silu(gate) * up over n fp32 elements (16-byte aligned).
 cudaError_t launch_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, cudaStream_t st);
 

@@ -347,6 +347,45 @@ def gemm_grouped_raw(entries: Sequence[tuple], device: torch.device, status: Opt
     N.check(N.load().draco_gguf_gemm(arr, len(entries), st, _stream_ptr(device)), "gemm")
 
 
+def gemm_rows_raw(entries: Sequence[tuple], rows: torch.Tensor, device: torch.device,
+                  status: Optional[torch.Tensor] = None) -> None:
+    """gemm_grouped_raw whose problems' token counts live on the device: each
+    entry's m is the capacity of its x / y blocks, rows (CUDA int32, one per
+    entry, in entry order) the tokens present (draco_gguf_gemm_rows).  No host
+    synchronisation; rows of y past the count up to the next 32 may be
+    written with values of no meaning."""
+    if not entries:
+        return
+    if rows.dtype != torch.int32 or not rows.is_cuda or rows.numel() < len(entries) or not rows.is_contiguous():
+        raise ValueError("gemm_rows: rows must be a contiguous CUDA int32 tensor with one count per problem")
+    arr = (N.GemmProblem * len(entries))()
+    for s, (qt, w, x, y, m, n, k, ldx, ldy, ydt) in zip(arr, entries):
+        s.qtype, s.ydtype = qt, ydt
+        s.w, s.x, s.y = w, x, y
+        s.m, s.n_rows, s.k = m, n, k
+        s.ldx, s.ldy = ldx, ldy
+    st = status.data_ptr() if status is not None else None
+    N.check(N.load().draco_gguf_gemm_rows(arr, len(entries), rows.data_ptr(), st, _stream_ptr(device)), "gemm_rows")
+
+
+def swiglu_bf16_rows(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
+    """out[g, r] = bf16(silu(gate[g, r]) * up[g, r]) for r < rows[g] over
+    [groups, cap_rows, width] bf16 blocks; rows is a CUDA int32 [groups]
+    (draco_swiglu_bf16_rows).  out may be gate."""
+    for t, nm in ((gate, "gate"), (up, "up"), (out, "out")):
+        _require_cuda(t, nm)
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.dim() != 3:
+            raise ValueError(f"swiglu_rows: {nm} must be a contiguous [groups, rows, width] bfloat16 CUDA tensor")
+    if gate.shape != up.shape or gate.shape != out.shape:
+        raise DracoFormatError(f"swiglu_rows: shapes {tuple(gate.shape)}, {tuple(up.shape)}, {tuple(out.shape)} differ")
+    if rows.dtype != torch.int32 or not rows.is_cuda or rows.numel() != gate.shape[0]:
+        raise ValueError("swiglu_rows: rows must be a CUDA int32 tensor with one count per group")
+    g, c, w = gate.shape
+    N.check(N.load().draco_swiglu_bf16_rows(gate.data_ptr(), up.data_ptr(), out.data_ptr(), g, c, w,
+                                            rows.data_ptr(), _stream_ptr(gate.device)), "swiglu_rows")
+    return out
+
+
 def swiglu_bf16(gate: torch.Tensor, up: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """bf16(silu(gate) * up) in fp32 with one rounding (C ABI draco_swiglu_bf16)."""
     for t, nm in ((gate, "gate"), (up, "up")):

@@ -8,18 +8,23 @@ Mirrors draco/models/moe:
   up(x)); ``ExpertGroup.forward``: every routed token's expert outputs summed
   with its routing weights) over TILED GGUF weights: the gate and up
   projections of all local experts go through one grouped tcgen05
-  dequant-GEMM launch, the down projections through a second.
+  dequant-GEMM launch, the SwiGLU product through one kernel, the down
+  projections through a second GEMM launch.
 * ``EPMoELayer`` — the dispatch/combine of dispatch.py:17-79 made
   expert-parallel: rank r owns experts [r*E/W, (r+1)*E/W); each rank routes
   its own tokens, sends every (token, expert) copy to the expert's rank with
-  one NCCL all-to-all (the variable split sizes are exchanged first), runs
-  its experts on what it received, and returns the outputs with a second
-  all-to-all; the source rank adds them with the routing weights.  At world
-  size 1 there is no collective.
+  one NCCL all-to-all, runs its experts on what it received, and returns the
+  outputs with a second all-to-all; the source rank adds them with the
+  routing weights.  At world size 1 there is no collective.
 
-The hot path is the quantized linear (the GEMM kernel) and the SwiGLU product
-between gate/up and down (draco_swiglu_bf16); routing and the token
-permutation are small tensor ops around them.
+The step never waits for the host.  Routing positions and per-expert token
+counts are computed on the device; tokens travel in fixed-capacity blocks
+(an expert receives at most one row per token of each rank, so a block of
+the rank's token count always suffices), every all-to-all has equal splits,
+and the GEMM and SwiGLU kernels read the counts from device memory
+(draco_gguf_gemm_rows, draco_swiglu_bf16_rows) and skip the empty rows.  The
+layer can therefore be captured in a CUDA graph.  The combine sums each
+token's k expert outputs in slot order: the result is deterministic.
 """
 
 from __future__ import annotations
@@ -80,36 +85,31 @@ class GGUFExpertGroup:
     def n_local(self) -> int:
         return len(self.w)
 
-    def run(self, x: torch.Tensor, counts: Sequence[int]) -> torch.Tensor:
-        """x: (rows, hidden) bf16 grouped by local expert (counts[i] rows for
-        expert i, in order) -> (rows, hidden) bf16 expert outputs."""
-        rows = x.shape[0]
-        out = torch.empty((rows, self.hidden), dtype=torch.bfloat16, device=self.device)
-        if rows == 0:
-            return out
+    def run_padded(self, x: torch.Tensor, rows: torch.Tensor, cap: int) -> torch.Tensor:
+        """x: [n_local, cap, hidden] bf16, expert i's tokens in the first rows[i]
+        rows of block i; rows: CUDA int32 [n_local].  Returns [n_local, cap,
+        hidden] bf16 expert outputs (rows past rows[i] hold no meaning)."""
+        n, H, Fn, bf = self.n_local, self.hidden, self.ffn, G.N.DTYPE_BF16
         if x.dtype != torch.bfloat16 or not x.is_contiguous():
             x = x.to(torch.bfloat16).contiguous()
-        gate = torch.empty((rows, self.ffn), dtype=torch.bfloat16, device=self.device)
+        gate = torch.empty((n, cap, Fn), dtype=torch.bfloat16, device=self.device)
         up = torch.empty_like(gate)
-        # each expert's rows are a block of x / gate / up / out: pass pointers
-        # into the buffers rather than a tensor view per block
-        H, Fn, bf = self.hidden, self.ffn, G.N.DTYPE_BF16
+        out = torch.empty((n, cap, H), dtype=torch.bfloat16, device=self.device)
         px, pg, pu, po = x.data_ptr(), gate.data_ptr(), up.data_ptr(), out.data_ptr()
-        gu, down, r0 = [], [], 0
-        for i, c in enumerate(counts):
-            if c:
-                qt, wg, wu, wd = self.w_ptrs[i]
-                xr, fr = px + 2 * r0 * H, 2 * r0 * Fn
-                gu.append((qt, wg, xr, pg + fr, c, Fn, H, H, Fn, bf))
-                gu.append((qt, wu, xr, pu + fr, c, Fn, H, H, Fn, bf))
-                down.append((qt, wd, pg + fr, po + 2 * r0 * H, c, H, Fn, Fn, H, bf))
-            r0 += c
+        gu, down = [], []
+        for i, (qt, wg, wu, wd) in enumerate(self.w_ptrs):
+            xr, fr = px + 2 * i * cap * H, 2 * i * cap * Fn
+            gu.append((qt, wg, xr, pg + fr, cap, Fn, H, H, Fn, bf))
+            gu.append((qt, wu, xr, pu + fr, cap, Fn, H, H, Fn, bf))
+            down.append((qt, wd, pg + fr, po + 2 * i * cap * H, cap, H, Fn, Fn, H, bf))
+        rows = rows.to(torch.int32).contiguous()
+        rows2 = rows.repeat_interleave(2)  # gate and up of each expert
         mx = G.N.GEMM_MAX_PROBLEMS
         for i in range(0, len(gu), mx):
-            G.gemm_grouped_raw(gu[i:i + mx], self.device, self.status)
-        G.swiglu_bf16(gate, up, out=gate)  # the SwiGLU product overwrites gate, the down input
+            G.gemm_rows_raw(gu[i:i + mx], rows2[i:i + mx], self.device, self.status)
+        G.swiglu_bf16_rows(gate, up, gate, rows)  # the SwiGLU product overwrites gate, the down input
         for i in range(0, len(down), mx):
-            G.gemm_grouped_raw(down[i:i + mx], self.device, self.status)
+            G.gemm_rows_raw(down[i:i + mx], rows[i:i + mx], self.device, self.status)
         return out
 
 
@@ -120,11 +120,12 @@ class EPMoELayer:
                  device: torch.device, group=None, expert_group_factory=None) -> None:
         """experts: per expert (qtype, gate, up, down) packed payloads, or whatever
         `expert_group_factory(experts_of_this_rank, hidden, ffn, device, e0)`
-        takes (default: GGUFExpertGroup)."""
+        takes (default: GGUFExpertGroup); the group's run_padded(x, rows, cap)
+        computes its experts on fixed-capacity blocks."""
         n_exp = len(experts)
         if n_exp % world:
             raise ValueError(f"{n_exp} experts do not split evenly over {world} ranks")
-        self.n_exp, self.hidden, self.ffn = n_exp, hidden, ffn
+        self.n_exp, self.hidden, self.ffn, self.top_k = n_exp, hidden, ffn, top_k
         self.rank, self.world, self.device = rank, world, device
         self.per_rank = n_exp // world
         self.group = group
@@ -137,53 +138,54 @@ class EPMoELayer:
         factory = expert_group_factory or GGUFExpertGroup
         self.local = factory(experts[e0:e0 + self.per_rank], hidden, ffn, device, e0)
 
+    def dispatch_plan(self, router_logits: torch.Tensor):
+        """Device-side routing: expert index and weight of every (token, slot),
+        its row in the [n_exp, cap] block layout (cap = tokens of this rank;
+        rows of an expert in token order) and the per-expert counts."""
+        T = router_logits.shape[0]
+        idx, wts = self.router.route(router_logits)
+        flat_e = idx.reshape(-1)
+        csum = F.one_hot(flat_e, self.n_exp).to(torch.int32).cumsum(0)
+        pos = csum.gather(1, flat_e[:, None]).squeeze(1) - 1
+        counts = csum[-1].contiguous() if T else torch.zeros(self.n_exp, dtype=torch.int32, device=flat_e.device)
+        return flat_e * T + pos, wts, counts
+
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         """x (tokens, hidden) and router logits (tokens, E) of this rank's tokens
         -> (tokens, hidden) fp32 MoE output."""
-        T = x.shape[0]
-        idx, wts = self.router.route(router_logits)
-        k = idx.shape[1]
-        flat_e = idx.reshape(-1)
-        flat_t = torch.arange(T, device=x.device).repeat_interleave(k)
-        order = torch.argsort(flat_e, stable=True)  # by expert, hence by owner rank
-        send_e = flat_e[order]
-        send_t = flat_t[order]
-        send_x = x.index_select(0, send_t)
-        per_exp = torch.bincount(send_e, minlength=self.n_exp)
-        if self.world == 1:
-            y_rows = self.local.run(send_x, per_exp.tolist())
+        T, H, k, E, W, El = x.shape[0], self.hidden, self.top_k, self.n_exp, self.world, self.per_rank
+        dst, wts, counts = self.dispatch_plan(router_logits)
+        cap = T
+        send = x.new_empty((E * cap, H))
+        send.index_copy_(0, dst, x.repeat_interleave(k, dim=0))
+        if W == 1:
+            back = self.local.run_padded(send.view(E, cap, H), counts, cap).view(E * cap, H)
         else:
             import torch.distributed as dist
 
-            send_counts = per_exp.view(self.world, self.per_rank).contiguous()  # [dest rank, local expert]
-            recv_counts = torch.empty_like(send_counts)
-            dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-            send_split = send_counts.sum(1).tolist()
-            recv_split = recv_counts.sum(1).tolist()
-            recv_x = torch.empty((sum(recv_split), self.hidden), dtype=x.dtype, device=x.device)
-            dist.all_to_all_single(recv_x, send_x, recv_split, send_split, group=self.group)
-            # rows arrive grouped by source rank, each block sorted by local
-            # expert: regroup them by local expert for the grouped GEMM
-            rc = recv_counts.tolist()
-            src_off = np.concatenate([[0], np.cumsum(recv_split)])
-            perm, counts = [], []
-            for e in range(self.per_rank):
-                c = 0
-                for s in range(self.world):
-                    start = int(src_off[s]) + sum(rc[s][:e])
-                    perm.extend(range(start, start + rc[s][e]))
-                    c += rc[s][e]
-                counts.append(c)
-            perm_t = torch.tensor(perm, dtype=torch.long, device=x.device)
-            out_rows = self.local.run(recv_x.index_select(0, perm_t), counts)
-            back = torch.empty_like(out_rows)
-            back.index_copy_(0, perm_t, out_rows)  # source-rank order again
-            y_rows = torch.empty((sum(send_split), self.hidden), dtype=out_rows.dtype, device=x.device)
-            dist.all_to_all_single(y_rows, back, send_split, recv_split, group=self.group)
-        w_rows = wts.reshape(-1)[order]
-        out = torch.zeros((T, self.hidden), dtype=torch.float32, device=x.device)
-        out.index_add_(0, send_t, y_rows.float() * w_rows[:, None])
-        return out
+            recv = torch.empty_like(send)  # [source rank][local expert][cap]
+            dist.all_to_all_single(recv, send, group=self.group)
+            rc = torch.empty_like(counts)
+            dist.all_to_all_single(rc, counts, group=self.group)
+            rc = rc.view(W, El)
+            # regroup each local expert's rows from every source into one block
+            # of capacity W * cap; unused rows of a source block go to a spare row
+            cap2 = W * cap
+            off = rc.cumsum(0) - rc
+            i = torch.arange(cap, device=x.device)
+            valid = i[None, None, :] < rc[:, :, None]
+            el = torch.arange(El, device=x.device)
+            dest = (el[None, :, None] * cap2 + off[:, :, None] + i[None, None, :]).to(torch.int64)
+            dest = torch.where(valid, dest, torch.full_like(dest, El * cap2)).reshape(-1)
+            xin = x.new_empty((El * cap2 + 1, H))
+            xin.index_copy_(0, dest, recv)
+            y = self.local.run_padded(xin[:El * cap2].view(El, cap2, H), rc.sum(0).to(torch.int32), cap2)
+            y = torch.cat([y.view(El * cap2, H), y.new_zeros((1, H))])
+            y_send = y.index_select(0, dest)  # back in [destination rank][local expert][cap] order
+            back = torch.empty_like(y_send)
+            dist.all_to_all_single(back, y_send, group=self.group)
+        rows = back.index_select(0, dst).view(T, k, H).float()
+        return (rows * wts[..., None]).sum(dim=1)
 
     def check_status(self) -> int:
         st = getattr(self.local, "status", None)

@@ -286,12 +286,35 @@ typedef struct draco_gemm_problem {
  * a device-side wait runs out (it never traps).  `problems` is a host array. */
 int draco_gguf_gemm(const draco_gemm_problem* problems, int n_problems, int* status, void* stream);
 
+/* draco_gguf_gemm with the tokens of each problem counted on the device:
+ * problems[i].m is the CAPACITY (rows x and y hold), rows[i] (device int32,
+ * in the caller's problem order, written by an earlier kernel on the stream)
+ * the tokens actually present (clamped to 0..m).  Tokens past rows[i] are not
+ * multiplied; their rows of y up to the next multiple of 32 may be written
+ * with values of no meaning, so y must hold the capacity.  Lets a
+ * mixture-of-experts layer run its experts' GEMMs on device-computed routing
+ * without a host synchronisation.  Replaces the per-expert loop of
+ * ExpertGroup.forward (draco/models/moe/expert.py:77-116), whose token counts
+ * are host values. */
+int draco_gguf_gemm_rows(const draco_gemm_problem* problems, int n_problems, const int* rows, int* status,
+                         void* stream);
+
 /* SwiGLU product of a gated MLP between its gate/up and down projections:
  * out[i] = bf16(silu(gate[i]) * up[i]) in fp32 with one rounding, n bf16
  * elements, all three pointers 16-byte aligned (out may alias gate or up).
  * Replaces act_fn(gate_proj(x)) * up_proj(x) of the reference's
  * Expert.forward (draco/models/moe/expert.py:47-49). */
 int draco_swiglu_bf16(const void* gate, const void* up, void* out, int64_t n, void* stream);
+
+/* Row-counted bf16 form for experts whose token counts live on the device:
+ * gate, up and out are `groups` blocks of [cap_rows, width] bf16 (row-major,
+ * block g at element g * cap_rows * width); only the first rows[g] rows of
+ * block g are computed (rows: device int32 [groups], clamped to cap_rows).
+ * width % 8 == 0, pointers 16-byte aligned, out may alias gate or up.
+ * Replaces the same step of Expert.forward (draco/models/moe/expert.py:47-49)
+ * for all experts of a layer at once. */
+int draco_swiglu_bf16_rows(const void* gate, const void* up, void* out, int groups, int64_t cap_rows,
+                           int64_t width, const int* rows, void* stream);
 
 /* fp32 form for decode activations: out = silu(gate) * up over n fp32
  * values (expf as CUDA provides it), 16-byte aligned, out may alias gate.

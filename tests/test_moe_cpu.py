@@ -30,13 +30,12 @@ class OracleExperts:
         self.w = [tuple(torch.from_numpy(O.dequantize_matrix(qt, p, n, k)) for p, n, k in
                         ((g, ffn, hidden), (u, ffn, hidden), (d, hidden, ffn))) for qt, g, u, d in experts]
 
-    def run(self, x, counts):
-        out, r = [], 0
-        for (wg, wu, wd), c in zip(self.w, counts):
-            xe = x[r:r + c].float()
-            out.append((F.silu(xe @ wg.T) * (xe @ wu.T)) @ wd.T)
-            r += c
-        return torch.cat(out) if out else x.new_zeros((0, x.shape[1]))
+    def run_padded(self, x, rows, cap):
+        out = torch.full((len(self.w), cap, x.shape[-1]), float("nan"))  # unused rows hold no meaning
+        for e, ((wg, wu, wd), c) in enumerate(zip(self.w, rows.tolist())):
+            xe = x[e, :c].float()
+            out[e, :c] = (F.silu(xe @ wg.T) * (xe @ wu.T)) @ wd.T
+        return out
 
 
 def make_experts(seed):
@@ -55,7 +54,10 @@ def reference_moe(x, logits, experts):
         if not mask.any():
             continue
         t = mask.nonzero(as_tuple=True)[0]
-        ye = ex.run(x[t], [0] * e + [len(t)] + [0] * (E - e - 1))
+        xe = torch.zeros((E, len(t), HIDDEN))
+        xe[e] = x[t]
+        ye = ex.run_padded(xe, torch.tensor([len(t) if j == e else 0 for j in range(E)], dtype=torch.int32),
+                           len(t))[e]
         we = (w[t] * (idx[t] == e).float()).sum(dim=-1, keepdim=True)
         out.index_add_(0, t, ye * we)
     return out
@@ -75,6 +77,22 @@ def test_router_top2_softmax_renormalised():
     np.testing.assert_allclose(w.sum(-1).numpy(), 1.0, rtol=1e-6)
     with pytest.raises(ValueError):
         TopKRouter(4, 5)
+
+
+def test_dispatch_plan_positions_and_counts():
+    g = torch.Generator().manual_seed(8)
+    logits = torch.randn((23, E), generator=g)
+    layer = EPMoELayer(make_experts(2), HIDDEN, FFN, TOP_K, 0, 1, torch.device("cpu"),
+                       expert_group_factory=OracleExperts)
+    dst, w, counts = layer.dispatch_plan(logits)
+    idx, _ = TopKRouter(E, TOP_K).route(logits)
+    flat = idx.reshape(-1).tolist()
+    assert counts.tolist() == [flat.count(e) for e in range(E)]
+    seen = [0] * E
+    for p, e in enumerate(flat):  # rows of an expert in token order, from row 0 of its block
+        assert dst[p].item() == e * 23 + seen[e]
+        seen[e] += 1
+    assert len(set(dst.tolist())) == len(flat)
 
 
 def test_ep_single_rank_matches_expert_group():

@@ -65,6 +65,15 @@ def test_moe_layer_matches_expert_group(qtypes):
     assert layer.check_status() == 0
     ref = _reference(x.float(), logits, experts, hidden, ffn, top_k)
     assert O.rel_l2(y.cpu().numpy(), ref.numpy()) < PREFILL_TOL
+    # no host synchronisation inside the step: it replays from a CUDA graph,
+    # bit-identically
+    xc, lc = x.cuda(), logits.cuda()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        yg = layer.forward(xc, lc)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(yg, y)
 
 
 @pytest.mark.parametrize("n", [8 * 1000, 8 * 1000 + 5, 3])
