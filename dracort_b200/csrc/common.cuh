@@ -18,11 +18,12 @@ namespace draco {
 // ---------------------------------------------------------------------------
 constexpr int kQ8_0 = DRACO_GGML_TYPE_Q8_0;
 constexpr int kQ4_K = DRACO_GGML_TYPE_Q4_K;
+constexpr int kQ5_K = DRACO_GGML_TYPE_Q5_K;
 constexpr int kQ6_K = DRACO_GGML_TYPE_Q6_K;
 
 __host__ __device__ inline int block_size_of(int qt) { return qt == kQ8_0 ? 32 : 256; }
 __host__ __device__ inline int block_bytes_of(int qt) {
-  return qt == kQ8_0 ? 34 : (qt == kQ4_K ? 144 : 210);
+  return qt == kQ8_0 ? 34 : qt == kQ4_K ? 144 : qt == kQ5_K ? 176 : 210;
 }
 
 // Field offsets inside one Q6_K block for the two byte orders.  GGUF (the
@@ -98,6 +99,14 @@ __host__ __device__ inline int q4k_qs_pos(int rr, int p) {
 }
 __host__ __device__ inline int q4k_sc_pos(int rr, int s) { return 2048 + 24 * (rr & 7) + 12 * (rr >> 3) + s; }
 __host__ __device__ inline int q4k_d_pos(int rr) { return 2240 + 8 * (rr & 7) + 4 * (rr >> 3); }  // +2 = dmin
+
+// Q5_K: qs as Q4_K -> [0,2048); qh[32] -> [2048,2560), in the same lane units
+// as one group of qs (byte u of row rr where qs byte u of a group sits), so a
+// lane's 16-byte qh unit holds the fifth bits of all its quants;
+// scales[12] -> [2560,2752), d,dmin -> [2752,2816).
+__host__ __device__ inline int q5k_qh_pos(int rr, int u) { return 2048 + q4k_qs_pos(rr, u); }
+__host__ __device__ inline int q5k_sc_pos(int rr, int s) { return 2560 + 24 * (rr & 7) + 12 * (rr >> 3) + s; }
+__host__ __device__ inline int q5k_d_pos(int rr) { return 2752 + 8 * (rr & 7) + 4 * (rr >> 3); }  // +2 = dmin
 
 // Q6_K fields: ql[128]/qh[64] -> [0,3072), sc[16] -> [3072,3328), d -> [3328,3360).
 // Lane data: 24 words; group nu = 2*n + is (n = half of the super-block,

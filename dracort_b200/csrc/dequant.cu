@@ -1,4 +1,4 @@
-// dequant.cu — GGUF block dequantization (Q8_0, Q4_K, Q6_K) to fp32 / bf16,
+// dequant.cu — GGUF block dequantization (Q8_0, Q4_K, Q5_K, Q6_K) to fp32 / bf16,
 // and the GGUF -> TILED repack.
 //
 // Parity target: draco/format/gguf.py:_dequantize.  Each output element is
@@ -6,6 +6,8 @@
 //   Q8_0 (gguf.py:300-303): q * d                       (exact)
 //   Q4_K (gguf.py:425-456): (d*sc)*q - (dmin*m)          (products exact, one
 //                                                         rounding in the subtract)
+//   Q5_K (gguf.py:425-468): the same with q = nibble + 16 * fifth bit (the
+//                           reference forms it in float64: the same value)
 //   Q6_K (gguf.py:470-495): (d*sc) * (q6 - 32)           (d*sc exact, one rounding)
 // The multiplies and the subtract are written with explicit _rn intrinsics so
 // that no FMA contraction can change a bit.
@@ -37,6 +39,30 @@ struct TiledQ4K {
   __device__ float d() const { return ld_f16(ch + q4k_d_pos(rr)); }
   __device__ float dmin() const { return ld_f16(ch + q4k_d_pos(rr) + 2); }
   __device__ uint8_t sc(int s) const { return ch[q4k_sc_pos(rr, s)]; }
+  __device__ uint8_t qs(int p) const { return ch[q4k_qs_pos(rr, p)]; }
+};
+struct RawQ5K {
+  const uint8_t* blk;
+  __device__ RawQ5K(const uint8_t* base, int64_t row, int64_t k, int64_t sb) {
+    blk = base + row * (k / 256) * 176 + sb * 176;
+  }
+  __device__ float d() const { return ld_f16(blk); }
+  __device__ float dmin() const { return ld_f16(blk + 2); }
+  __device__ uint8_t sc(int s) const { return blk[4 + s]; }
+  __device__ uint8_t qh(int l) const { return blk[16 + l]; }
+  __device__ uint8_t qs(int p) const { return blk[48 + p]; }
+};
+struct TiledQ5K {
+  const uint8_t* ch;
+  int rr;
+  __device__ TiledQ5K(const uint8_t* base, const TiledGeom& g, int64_t row, int64_t sb) {
+    ch = base + chunk_offset(g, row / kChunkRows, sb);
+    rr = (int)(row % kChunkRows);
+  }
+  __device__ float d() const { return ld_f16(ch + q5k_d_pos(rr)); }
+  __device__ float dmin() const { return ld_f16(ch + q5k_d_pos(rr) + 2); }
+  __device__ uint8_t sc(int s) const { return ch[q5k_sc_pos(rr, s)]; }
+  __device__ uint8_t qh(int l) const { return ch[q5k_qh_pos(rr, l)]; }
   __device__ uint8_t qs(int p) const { return ch[q4k_qs_pos(rr, p)]; }
 };
 struct RawQ6K {
@@ -108,6 +134,25 @@ __device__ __forceinline__ void decode8_q4k(const A& a, int e0, float (&o)[8]) {
 }
 
 template <class A>
+__device__ __forceinline__ void decode8_q5k(const A& a, int e0, float (&o)[8]) {
+  int g4 = e0 >> 6, upper = (e0 & 63) >= 32, j = 2 * g4 + upper;
+  uint8_t scb[12];
+#pragma unroll
+  for (int s = 0; s < 12; ++s) scb[s] = a.sc(s);
+  int sc, m;
+  q4k_scale_min(scb, j, sc, m);
+  float d1 = __fmul_rn(a.d(), (float)sc);
+  float m1 = __fmul_rn(a.dmin(), (float)m);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int l = (e0 + i) & 31;
+    uint8_t byte = a.qs(32 * g4 + l);
+    int q = (upper ? (byte >> 4) : (byte & 15)) | (((a.qh(l) >> j) & 1) << 4);
+    o[i] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+  }
+}
+
+template <class A>
 __device__ __forceinline__ void decode8_q6k(const A& a, int e0, float (&o)[8]) {
   int n = e0 >> 7, r = e0 & 127, i4 = r >> 5, l0 = r & 31;
   int s = 8 * n + 2 * i4 + (l0 >> 4);
@@ -168,6 +213,9 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
   if (QT == kQ4_K) {
     if (TILED) decode8_q4k(TiledQ4K(src, g, row, sb), e0, o);
     else decode8_q4k(RawQ4K(src, row, k, sb), e0, o);
+  } else if (QT == kQ5_K) {
+    if (TILED) decode8_q5k(TiledQ5K(src, g, row, sb), e0, o);
+    else decode8_q5k(RawQ5K(src, row, k, sb), e0, o);
   } else if (QT == kQ6_K) {
     if (TILED) decode8_q6k(TiledQ6K(src, g, row, sb), e0, o);
     else decode8_q6k(RawQ6K(src, row, k, sb, layout), e0, o);
@@ -202,6 +250,16 @@ __global__ void __launch_bounds__(256) repack_kernel(const uint8_t* __restrict__
     ch[dp + 3] = b[3];
     for (int s = 0; s < 12; ++s) ch[q4k_sc_pos(rr, s)] = b[4 + s];
     for (int p = 0; p < 128; ++p) ch[q4k_qs_pos(rr, p)] = b[16 + p];
+  } else if (QT == kQ5_K) {
+    uint8_t* ch = dst + chunk_offset(g, row / kChunkRows, bi);
+    const int dp = q5k_d_pos(rr);
+    ch[dp] = b[0];
+    ch[dp + 1] = b[1];
+    ch[dp + 2] = b[2];
+    ch[dp + 3] = b[3];
+    for (int s = 0; s < 12; ++s) ch[q5k_sc_pos(rr, s)] = b[4 + s];
+    for (int l = 0; l < 32; ++l) ch[q5k_qh_pos(rr, l)] = b[16 + l];
+    for (int p = 0; p < 128; ++p) ch[q4k_qs_pos(rr, p)] = b[48 + p];
   } else if (QT == kQ6_K) {
     uint8_t* ch = dst + chunk_offset(g, row / kChunkRows, bi);
     const Q6Fields f = q6_fields(layout);
@@ -241,6 +299,7 @@ static cudaError_t launch_dequant_t(int qt, int layout, const void* src, OutT* o
     else dequant_kernel<OutT, QT, false><<<grid, 256, 0, st>>>(s, out, n_rows, k, layout);       \
   } while (0)
   if (qt == kQ4_K) DRACO_DQ(kQ4_K);
+  else if (qt == kQ5_K) DRACO_DQ(kQ5_K);
   else if (qt == kQ6_K) DRACO_DQ(kQ6_K);
   else DRACO_DQ(kQ8_0);
 #undef DRACO_DQ
@@ -267,6 +326,7 @@ cudaError_t launch_repack(int qt, int src_layout, const void* src, void* dst, in
   const uint8_t* s = static_cast<const uint8_t*>(src);
   uint8_t* d = static_cast<uint8_t*>(dst);
   if (qt == kQ4_K) repack_kernel<kQ4_K><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
+  else if (qt == kQ5_K) repack_kernel<kQ5_K><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
   else if (qt == kQ6_K) repack_kernel<kQ6_K><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
   else repack_kernel<kQ8_0><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
   return cudaGetLastError();

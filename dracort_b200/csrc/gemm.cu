@@ -244,6 +244,7 @@ __device__ __forceinline__ uint32_t ldg32(const uint8_t* p) {
 // latency hides behind the dequantization of the blocks before):
 //  Q4_K: u0 = qs unit; u1 = scale bytes 0-7 (row g), 8-11 (row g), 0-3 (row g+8);
 //        u2 = scale bytes 4-11 (row g+8), (d, dmin) of row g, of row g+8
+//  Q5_K: as Q4_K, plus u3 = the qh unit (fifth bits, word for word as u0)
 //  Q6_K: u0..u2 = ql/qh units of half q/2; u3 = int8 scales of rows g, g+8, d of both rows
 //  Q8_0: u0, u1 = qs units of blocks 2q, 2q+1; u2.x, u2.y = d of both blocks for rows g, g+8
 struct Packed {
@@ -251,12 +252,14 @@ struct Packed {
 };
 __device__ __forceinline__ void fetch_packed(int qt, const uint8_t* ch, int q, int lane, Packed& pk) {
   const int g = lane >> 2;
-  if (qt == kQ4_K) {
+  if (qt == kQ4_K || qt == kQ5_K) {
+    const int so = qt == kQ5_K ? 2560 : 2048, dof = qt == kQ5_K ? 2752 : 2240;
     pk.u0 = ldg128(ch + 512 * q + 16 * lane);
-    const uint2 a = ldg64(ch + 2048 + 24 * g), b = ldg64(ch + 2056 + 24 * g), c = ldg64(ch + 2064 + 24 * g);
-    const uint2 d = ldg64(ch + 2240 + 8 * g);
+    const uint2 a = ldg64(ch + so + 24 * g), b = ldg64(ch + so + 8 + 24 * g), c = ldg64(ch + so + 16 + 24 * g);
+    const uint2 d = ldg64(ch + dof + 8 * g);
     pk.u1 = make_uint4(a.x, a.y, b.x, b.y);
     pk.u2 = make_uint4(c.x, c.y, d.x, d.y);
+    if (qt == kQ5_K) pk.u3 = ldg128(ch + 2048 + 16 * lane);
   } else if (qt == kQ6_K) {
     const int n = q >> 1, odd = q & 1;
     pk.u0 = ldg128(ch + 512 * (3 * n) + 16 * lane);
@@ -321,6 +324,9 @@ __device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushor
 
 // Q4_K: k-block q = sub-blocks 2q (low nibbles of qs bytes 32q..32q+31) and
 // 2q+1 (high nibbles).  Unit word (hi, h): row g+8hi, qs bytes 16h+4t..+3.
+// Q5_K (K5): each quant also takes its fifth bit from the qh unit's word
+// (hi, h), bit 2q (low nibble) or 2q+1 (high nibble) of each byte.
+template <bool K5>
 __device__ __forceinline__ void deq_q4k(const Packed& pk, int q, int lane, uint8_t* tw) {
   const int g = lane >> 2, t = lane & 3, g0 = g & 1;
   const uint4 U = pk.u0;
@@ -350,10 +356,15 @@ __device__ __forceinline__ void deq_q4k(const Packed& pk, int q, int lane, uint8
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t w = hi ? (h ? U.w : U.z) : (h ? U.y : U.x);
+      const uint32_t hw = hi ? (h ? pk.u3.w : pk.u3.z) : (h ? pk.u3.y : pk.u3.x);
 #pragma unroll
       for (int n0 = 0; n0 < 2; ++n0) {
         const int nib = g0 ^ n0;
-        const uint32_t wq = (w >> (4 * nib)) & 0x0F0F0F0Fu;
+        uint32_t wq = (w >> (4 * nib)) & 0x0F0F0F0Fu;
+        if (K5) {
+          const int b = 2 * q + nib;
+          wq |= (b <= 4 ? (hw << (4 - b)) : (hw >> (b - 4))) & 0x10101010u;
+        }
         st_piece(tw, hi, g, t, 4 * nib + 2 * h + (t >> 1), scale4_fma(wq, bias, n0 ? dsB : dsA, n0 ? dmB : dmA));
       }
     }
@@ -813,7 +824,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       }
       uint8_t* tw = as + (size_t)ra.s * kATile + dw * 2048;
       if (cur.base) {
-        if (cur.qt == kQ4_K) deq_q4k(pk, kb & 3, lane, tw);
+        if (cur.qt == kQ4_K) deq_q4k<false>(pk, kb & 3, lane, tw);
+        else if (cur.qt == kQ5_K) deq_q4k<true>(pk, kb & 3, lane, tw);
         else if (cur.qt == kQ6_K) deq_q6k(pk, kb & 3, lane, tw);
         else deq_q80(pk, lane, tw);
       } else {

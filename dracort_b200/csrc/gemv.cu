@@ -429,14 +429,25 @@ __device__ __forceinline__ void q4k_sm(uint32_t A, uint32_t Bw, uint32_t C, floa
   mm = dmin * u2f(m);
 }
 
-template <int G, int NT>
+// fifth bits of four Q5_K quants: bit `b` of each byte of the qh word h,
+// moved to bit 4 (gguf.py:457-467)
+__device__ __forceinline__ uint32_t q5_bit4(uint32_t h, int b) {
+  return (b <= 4 ? (h << (4 - b)) : (h >> (b - 4))) & 0x10101010u;
+}
+
+// Q4_K and Q5_K (same scales and mins; Q5_K adds a fifth bit per quant from
+// its qh unit, which mirrors the qs unit word for word)
+template <int QT, int G, int NT>
 __device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, const uint8_t* su, int lane,
                                           float (&acc)[NT][2]) {
+  constexpr bool k5 = QT == kQ5_K;
   const int g = lane >> 2, t = lane & 3;
-  const uint8_t* sp0 = ch + 2048 + 24 * g;  // row g: 12 bytes, row g+8: next 12
+  const uint8_t* sp0 = ch + (k5 ? 2560 : 2048) + 24 * g;  // row g: 12 bytes, row g+8: next 12
   const uint32_t A0 = lds32(sp0), B0 = lds32(sp0 + 4), C0 = lds32(sp0 + 8);
   const uint32_t A1 = lds32(sp0 + 12), B1 = lds32(sp0 + 16), C1 = lds32(sp0 + 20);
-  const uint2 dd = lds64(ch + 2240 + 8 * g);
+  const uint2 dd = lds64(ch + (k5 ? 2752 : 2240) + 8 * g);
+  uint4 H = make_uint4(0, 0, 0, 0);
+  if constexpr (k5) H = lds128(ch + 2048 + 16 * lane);
   const float d0 = f16_bits_to_f32(dd.x), m0 = f16_bits_to_f32(dd.x >> 16);
   const float d1 = f16_bits_to_f32(dd.y), m1 = f16_bits_to_f32(dd.y >> 16);
   constexpr int kColBytes = 8 * NT * 32;  // one group's activation entries
@@ -448,17 +459,24 @@ __device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, 
       const uint4 v = lds128(ch + 512 * q + 16 * lane);
       const uint2 bl = lds64(xs + (2 * q) * kColBytes + lane * 8);
       const uint2 bh = lds64(xs + (2 * q + 1) * kColBytes + lane * 8);
-      if ((2 * q) % G == 0)
-        imma_u8_k32_first(fr[(2 * q) / G], v.x & kNib, v.z & kNib, v.y & kNib, v.w & kNib, bl.x, bl.y);
-      else
-        imma_u8_k32(fr[(2 * q) / G], v.x & kNib, v.z & kNib, v.y & kNib, v.w & kNib, bl.x, bl.y);
-      // high nibbles in place: 16 x the quant (exact in the int32 sum)
-      imma_u8_k32(fr[(2 * q + 1) / G], v.x & kNibHi, v.z & kNibHi, v.y & kNibHi, v.w & kNibHi, bh.x, bh.y);
+      uint32_t l0 = v.x & kNib, l1 = v.z & kNib, l2 = v.y & kNib, l3 = v.w & kNib;
+      uint32_t h0, h1, h2, h3;
+      if constexpr (k5) {
+        l0 |= q5_bit4(H.x, 2 * q), l1 |= q5_bit4(H.z, 2 * q), l2 |= q5_bit4(H.y, 2 * q), l3 |= q5_bit4(H.w, 2 * q);
+        h0 = ((v.x >> 4) & kNib) | q5_bit4(H.x, 2 * q + 1), h1 = ((v.z >> 4) & kNib) | q5_bit4(H.z, 2 * q + 1);
+        h2 = ((v.y >> 4) & kNib) | q5_bit4(H.y, 2 * q + 1), h3 = ((v.w >> 4) & kNib) | q5_bit4(H.w, 2 * q + 1);
+      } else {
+        // high nibbles in place: 16 x the quant (exact in the int32 sum)
+        h0 = v.x & kNibHi, h1 = v.z & kNibHi, h2 = v.y & kNibHi, h3 = v.w & kNibHi;
+      }
+      if ((2 * q) % G == 0) imma_u8_k32_first(fr[(2 * q) / G], l0, l1, l2, l3, bl.x, bl.y);
+      else imma_u8_k32(fr[(2 * q) / G], l0, l1, l2, l3, bl.x, bl.y);
+      imma_u8_k32(fr[(2 * q + 1) / G], h0, h1, h2, h3, bh.x, bh.y);
     }
     const int b = t % Bp;
     // this lane's sub-blocks j = f * G + t / Bp all have the same parity: odd
-    // sub-blocks were entered as 16 x the quant, so fold 1/16 into d
-    const float h = ((t / Bp) & 1) ? 0.0625f : 1.f;
+    // Q4_K sub-blocks were entered as 16 x the quant, so fold 1/16 into d
+    const float h = (!k5 && ((t / Bp) & 1)) ? 0.0625f : 1.f;
     const float dq0 = d0 * h, dq1 = d1 * h;
     const float ndq0 = dq0 * -8388608.f, ndq1 = dq1 * -8388608.f;
     const float nm0 = m0 * -8388608.f, nm1 = m1 * -8388608.f;
@@ -498,8 +516,13 @@ __device__ __forceinline__ void chunk_q4k(const uint8_t* ch, const uint8_t* xs, 
       q4k_sm(A0, B0, C0, d0, m0, 2 * q + 1, q >= 2, dsh0, mmh0);
       q4k_sm(A1, B1, C1, d1, m1, 2 * q + 1, q >= 2, dsh1, mmh1);
       const uint4 v = lds128(ch + 512 * q + 16 * lane);
-      const uint32_t l0 = v.x & kNib, l1 = v.z & kNib, l2 = v.y & kNib, l3 = v.w & kNib;
-      const uint32_t h0 = (v.x >> 4) & kNib, h1 = (v.z >> 4) & kNib, h2 = (v.y >> 4) & kNib, h3 = (v.w >> 4) & kNib;
+      uint32_t l0 = v.x & kNib, l1 = v.z & kNib, l2 = v.y & kNib, l3 = v.w & kNib;
+      uint32_t h0 = (v.x >> 4) & kNib, h1 = (v.z >> 4) & kNib, h2 = (v.y >> 4) & kNib, h3 = (v.w >> 4) & kNib;
+      if constexpr (k5) {
+        l0 |= q5_bit4(H.x, 2 * q), l1 |= q5_bit4(H.z, 2 * q), l2 |= q5_bit4(H.y, 2 * q), l3 |= q5_bit4(H.w, 2 * q);
+        h0 |= q5_bit4(H.x, 2 * q + 1), h1 |= q5_bit4(H.z, 2 * q + 1);
+        h2 |= q5_bit4(H.y, 2 * q + 1), h3 |= q5_bit4(H.w, 2 * q + 1);
+      }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const uint2 bl = lds64(xs + (2 * q) * kColBytes + nt * 256 + lane * 8);
@@ -841,7 +864,7 @@ __device__ __forceinline__ bool consume_segment(const GemvParams& P, const uint8
       const uint8_t* ch = stage + rw * cb;
       const uint8_t* xs = stage + P.w_stage;
       const uint8_t* su = xs + P.xs_bytes;
-      if (QT == kQ4_K) chunk_q4k<G, NT>(ch, xs, su, lane, acc);
+      if (QT == kQ4_K || QT == kQ5_K) chunk_q4k<QT, G, NT>(ch, xs, su, lane, acc);
       else if (QT == kQ6_K) chunk_q6k<G, NT>(ch, xs, su, lane, acc);
       else chunk_q80<G, NT>(ch, xs, su, lane, acc);
     }
@@ -1040,6 +1063,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     bool ok;
     if (pr.qt == kQ4_K)
       ok = consume_segment<kQ4_K, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
+                                         pr.cb, lane, abort, acc);
+    else if (pr.qt == kQ5_K)
+      ok = consume_segment<kQ5_K, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
                                          pr.cb, lane, abort, acc);
     else if (pr.qt == kQ6_K)
       ok = consume_segment<kQ6_K, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,

@@ -1,8 +1,8 @@
 """GGUF type ids and block geometry for the quantized-linear hot path.
 
 Values are identical to draco/format/gguf.py: the ggml_type enum
-(gguf.py:56-71) and ``_BLOCK_LAYOUTS`` (gguf.py:75-87), restricted to the three
-block formats this library runs on the GPU.
+(gguf.py:56-71) and ``_BLOCK_LAYOUTS`` (gguf.py:75-87), restricted to the
+block formats this library runs on the GPU (Q8_0, Q4_K, Q5_K, Q6_K).
 """
 
 from __future__ import annotations
@@ -13,6 +13,7 @@ GGML_TYPE_F32 = 0
 GGML_TYPE_F16 = 1
 GGML_TYPE_Q8_0 = 8
 GGML_TYPE_Q4_K = 12
+GGML_TYPE_Q5_K = 13
 GGML_TYPE_Q6_K = 14
 GGML_TYPE_BF16 = 30
 
@@ -20,10 +21,11 @@ GGML_TYPE_BF16 = 30
 BLOCK_LAYOUTS: Dict[int, Tuple[int, int]] = {
     GGML_TYPE_Q8_0: (32, 34),  # d: f16 + qs: int8[32]
     GGML_TYPE_Q4_K: (256, 144),  # d: f16 + dmin: f16 + scales: uint8[12] + qs: uint8[128]
+    GGML_TYPE_Q5_K: (256, 176),  # d: f16 + dmin: f16 + scales: uint8[12] + qh: uint8[32] + qs: uint8[128]
     GGML_TYPE_Q6_K: (256, 210),  # d: f16 + ql: uint8[128] + qh: uint8[64] + scales: int8[16]
 }
 
-TYPE_NAMES = {GGML_TYPE_Q8_0: "Q8_0", GGML_TYPE_Q4_K: "Q4_K", GGML_TYPE_Q6_K: "Q6_K"}
+TYPE_NAMES = {GGML_TYPE_Q8_0: "Q8_0", GGML_TYPE_Q4_K: "Q4_K", GGML_TYPE_Q5_K: "Q5_K", GGML_TYPE_Q6_K: "Q6_K"}
 NAME_TO_TYPE = {v: k for k, v in TYPE_NAMES.items()}
 
 #: Q6_K field order.  "d_first" is the order draco/format/gguf.py:470-474

@@ -1,4 +1,4 @@
-"""Synthetic GGUF encoders (numpy) for Q8_0, Q4_K and Q6_K.
+"""Synthetic GGUF encoders (numpy) for Q8_0, Q4_K, Q5_K and Q6_K.
 
 The reference ships no GGUF K-quant quantizer (draco/format/gguf.py only
 decodes), so these encoders are written from the block formats that
@@ -13,6 +13,8 @@ gguf.py:_dequantize decodes:
   super-block's fp16 d and dmin (d = max scale / 63, dmin = max min / 63), then
   4-bit quants q = rint((w + dmin*m) / (d*sc)).  Packing follows the decode
   in gguf.py:425-456 (6-bit pairs, gguf.py:436-442).
+* Q5_K — the Q4_K fit with 31 levels; the fifth bit of element l of sub-block
+  j goes to bit j of qh[l] (gguf.py:457-467).
 * Q6_K — per 16-element sub-block scale = max|w| / 31, the 16 scales quantized
   to int8 against an fp16 d = max scale / 127, 6-bit quants
   q = rint(w / (d*sc)) + 32 split into low nibbles (ql) and high 2 bits (qh) as
@@ -29,6 +31,7 @@ import numpy as np
 from dracort_b200.format.gguf_types import (
     BLOCK_LAYOUTS,
     GGML_TYPE_Q4_K,
+    GGML_TYPE_Q5_K,
     GGML_TYPE_Q6_K,
     GGML_TYPE_Q8_0,
     Q6K_D_FIRST,
@@ -68,6 +71,54 @@ def _q4k_pack_scales(sc: np.ndarray, m: np.ndarray) -> np.ndarray:
         b[:, j + 4] = (m[:, j] & 63) | ((m[:, j + 4] >> 4) << 6)
         b[:, j + 8] = (sc[:, j + 4] & 15) | ((m[:, j + 4] & 15) << 4)
     return b
+
+
+def _affine_super_blocks(w: np.ndarray, levels: int):
+    """Per 32-element sub-block affine fit q = rint((w + m) / s) in [0, levels],
+    s and m quantised to 6 bits against the super-block's fp16 d / dmin."""
+    a = w.reshape(-1, 8, 32)
+    mn = np.minimum(a.min(axis=2), 0.0)
+    mx = a.max(axis=2)
+    scale = (mx - mn) / np.float32(levels)
+    mins = -mn
+    d = (scale.max(axis=1) / np.float32(63.0)).astype(np.float16).astype(np.float32)
+    dmin = (mins.max(axis=1) / np.float32(63.0)).astype(np.float16).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        sc = np.where(d[:, None] > 0, np.clip(np.rint(scale / d[:, None]), 0, 63), 0).astype(np.int32)
+        m = np.where(dmin[:, None] > 0, np.clip(np.rint(mins / dmin[:, None]), 0, 63), 0).astype(np.int32)
+        eff_s = d[:, None] * sc.astype(np.float32)
+        eff_m = dmin[:, None] * m.astype(np.float32)
+        q = np.where(
+            eff_s[:, :, None] > 0,
+            np.clip(np.rint((a + eff_m[:, :, None]) / eff_s[:, :, None]), 0, levels),
+            0,
+        ).astype(np.uint8)
+    return d, dmin, sc, m, q
+
+
+def encode_q5_k(w: np.ndarray) -> np.ndarray:
+    """[n_rows, k] float -> packed uint8 [n_rows, k/256*176]: the Q4_K fields
+    with 5-bit quants, the fifth bit of element l of sub-block j in bit j of
+    qh[l] (the layout gguf.py:425-468 decodes)."""
+    w = np.asarray(w, dtype=np.float32)
+    n_rows, k = w.shape
+    if k % 256:
+        raise ValueError("Q5_K needs k % 256 == 0")
+    d, dmin, sc, m, q = _affine_super_blocks(w, 31)
+    nb = q.shape[0]
+    out = np.empty((nb, 176), dtype=np.uint8)
+    out[:, 0:2] = _f16_bytes(d)
+    out[:, 2:4] = _f16_bytes(dmin)
+    out[:, 4:16] = _q4k_pack_scales(sc, m)
+    qh = np.zeros((nb, 32), dtype=np.uint8)
+    for j in range(8):
+        qh |= ((q[:, j, :] >> 4) & 1) << j
+    out[:, 16:48] = qh
+    qs = np.empty((nb, 128), dtype=np.uint8)
+    for g in range(4):
+        qs[:, 32 * g : 32 * g + 32] = (q[:, 2 * g, :] & 15) | ((q[:, 2 * g + 1, :] & 15) << 4)
+    out[:, 48:176] = qs
+    return out.reshape(n_rows, (k // 256) * 176)
 
 
 def encode_q4_k(w: np.ndarray) -> np.ndarray:
@@ -169,6 +220,8 @@ def encode(qtype: int, w: np.ndarray, q6k_order: str = Q6K_D_FIRST) -> np.ndarra
         return encode_q8_0(w)
     if qtype == GGML_TYPE_Q4_K:
         return encode_q4_k(w)
+    if qtype == GGML_TYPE_Q5_K:
+        return encode_q5_k(w)
     if qtype == GGML_TYPE_Q6_K:
         return encode_q6_k(w, q6k_order)
     raise ValueError(f"no encoder for ggml type {qtype}; supported: {sorted(BLOCK_LAYOUTS)}")

@@ -27,7 +27,7 @@ import torch.nn.functional as F
 
 from dracort_b200 import gguf_ops as G
 from dracort_b200.exceptions import DracoFormatError
-from dracort_b200.format.gguf_types import GGML_TYPE_Q4_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0
+from dracort_b200.format.gguf_types import GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0
 from dracort_b200.quantization.gguf import GEMV_MAX_ROWS, PREFILL_MIN_ROWS, GGUFLinear, gguf_linear
 
 
@@ -73,7 +73,8 @@ def fused_swiGLU(x: torch.Tensor, gate_proj, up_proj, down_proj) -> torch.Tensor
     return y.reshape(*lead, h).to(x.dtype)
 
 
-_TYPE_OF_NAME = {"gguf_q8_0": GGML_TYPE_Q8_0, "gguf_q4_k": GGML_TYPE_Q4_K, "gguf_q6_k": GGML_TYPE_Q6_K}
+_TYPE_OF_NAME = {"gguf_q8_0": GGML_TYPE_Q8_0, "gguf_q4_k": GGML_TYPE_Q4_K, "gguf_q5_k": GGML_TYPE_Q5_K,
+                 "gguf_q6_k": GGML_TYPE_Q6_K}
 
 
 class GGUFGemmKernel:
@@ -116,13 +117,13 @@ class GGUFGemmKernel:
 
     def _qtype(self, tensor_info) -> int:
         qt = getattr(tensor_info, "ggml_type", None)
-        if qt in (GGML_TYPE_Q8_0, GGML_TYPE_Q4_K, GGML_TYPE_Q6_K):
+        if qt in (GGML_TYPE_Q8_0, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K):
             return int(qt)
         q = getattr(tensor_info, "quantization", None)
         if q in _TYPE_OF_NAME:
             return _TYPE_OF_NAME[q]
         raise DracoFormatError(f"GGUFGemmKernel: tensor type {qt!r} / {q!r} is not a supported GGUF type "
-                               f"(Q8_0, Q4_K, Q6_K)")
+                               f"(Q8_0, Q4_K, Q5_K, Q6_K)")
 
     def _tiled(self, tensor_info, qtype: int, payload_bytes, n_rows: int, k: int) -> torch.Tensor:
         key = (getattr(tensor_info, "name", None), getattr(tensor_info, "offset", None))

@@ -39,6 +39,7 @@ from dracort_b200.exceptions import DracoFormatError, KernelError
 from dracort_b200.format.gguf_types import (
     BLOCK_LAYOUTS,
     GGML_TYPE_Q4_K,
+    GGML_TYPE_Q5_K,
     GGML_TYPE_Q6_K,
     GGML_TYPE_Q8_0,
     Q6K_D_FIRST,
@@ -47,7 +48,7 @@ from dracort_b200.format.gguf_types import (
 )
 from dracort_b200.quantization.base import QuantizationBackend
 
-_BITS = {GGML_TYPE_Q8_0: 8, GGML_TYPE_Q4_K: 4, GGML_TYPE_Q6_K: 6}
+_BITS = {GGML_TYPE_Q8_0: 8, GGML_TYPE_Q4_K: 4, GGML_TYPE_Q5_K: 5, GGML_TYPE_Q6_K: 6}
 
 #: largest activation row count handled by one GEMV launch
 GEMV_MAX_ROWS = N.GEMV_MAX_BATCH
@@ -110,7 +111,7 @@ class GGUFBackend(QuantizationBackend):
 
     def __init__(self, qtype: int, q6k_order: str = Q6K_D_FIRST) -> None:
         if qtype not in _BITS:
-            raise DracoFormatError(f"GGUF type {qtype} has no GPU kernel here (supported: Q8_0, Q4_K, Q6_K)")
+            raise DracoFormatError(f"GGUF type {qtype} has no GPU kernel here (supported: Q8_0, Q4_K, Q5_K, Q6_K)")
         if q6k_order not in (Q6K_D_FIRST, Q6K_D_LAST):
             raise ValueError(f"unknown Q6_K field order {q6k_order!r}")
         self.qtype = qtype

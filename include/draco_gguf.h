@@ -40,6 +40,7 @@ extern "C" {
 /* ggml_type ids, identical to GGML_TYPE_* in draco/format/gguf.py:56-71. */
 #define DRACO_GGML_TYPE_Q8_0 8
 #define DRACO_GGML_TYPE_Q4_K 12
+#define DRACO_GGML_TYPE_Q5_K 13
 #define DRACO_GGML_TYPE_Q6_K 14
 
 /* Byte layouts of a weight buffer.
@@ -81,7 +82,7 @@ const char* draco_version(void);
 const char* draco_last_error_string(void);
 
 /* (block_size, block_bytes) of a qtype: Q8_0 (32, 34), Q4_K (256, 144),
- * Q6_K (256, 210).  Replaces the table lookup _BLOCK_LAYOUTS[qtype]
+ * Q5_K (256, 176), Q6_K (256, 210).  Replaces the table lookup _BLOCK_LAYOUTS[qtype]
  * (gguf.py:75-87).  Returns DRACO_ERR_TYPE for other types.  Host only. */
 int draco_gguf_block_geometry(int qtype, int* block_size, int* block_bytes);
 
@@ -96,7 +97,7 @@ int64_t draco_gguf_tiled_bytes(int qtype, int64_t n_rows, int64_t k);
 
 /* Dequantize a whole weight to fp32, out[n_rows, k] row-major.
  * Bit-exact with draco/format/gguf.py:_dequantize (gguf.py:272-497) for
- * Q8_0 (:300-303), Q4_K (:425-456) and Q6_K (:470-495).
+ * Q8_0 (:300-303), Q4_K and Q5_K (:425-468) and Q6_K (:470-495).
  * `layout` is any DRACO_LAYOUT_*; GGUF layouts need `blocks` 2-byte aligned,
  * TILED needs 16-byte alignment. */
 int draco_gguf_dequant(int qtype, int layout, const void* blocks, float* out,

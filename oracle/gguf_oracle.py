@@ -9,7 +9,7 @@ the path (sadrasa97/DracoRT, paths relative to that project):
 
 * ``f16_from_u8``      — draco/format/gguf.py:256-259 (_f16_from_u8)
 * ``dequantize``       — draco/format/gguf.py:272-497 (_dequantize), branches
-  Q8_0 (:300-303), Q4_K (:425-456, _scale_min :436-442), Q6_K (:470-495),
+  Q8_0 (:300-303), Q4_K and Q5_K (:425-468, _scale_min :436-442), Q6_K (:470-495),
   plus the argument checks of :284-296.  Each element is produced with the
   same fp32 operations in the same order, so results are bit-identical.
 * ``matmul_f32``       — draco/runtime/cpu/kernels/generic.py:32-33
@@ -35,9 +35,11 @@ import numpy as np
 
 GGML_TYPE_Q8_0 = 8
 GGML_TYPE_Q4_K = 12
+GGML_TYPE_Q5_K = 13
 GGML_TYPE_Q6_K = 14
 
-BLOCK_LAYOUTS = {GGML_TYPE_Q8_0: (32, 34), GGML_TYPE_Q4_K: (256, 144), GGML_TYPE_Q6_K: (256, 210)}
+BLOCK_LAYOUTS = {GGML_TYPE_Q8_0: (32, 34), GGML_TYPE_Q4_K: (256, 144), GGML_TYPE_Q5_K: (256, 176),
+                 GGML_TYPE_Q6_K: (256, 210)}
 
 
 class OracleFormatError(ValueError):
@@ -77,11 +79,16 @@ def dequantize(qtype: int, payload, n: int, q6k_order: str = "d_first") -> np.nd
         qs = b[:, 2:34].view(np.int8).astype(np.float32)
         return (qs * d[:, None]).reshape(-1)
 
-    if qtype == GGML_TYPE_Q4_K:
+    if qtype in (GGML_TYPE_Q4_K, GGML_TYPE_Q5_K):
+        # Q5_K (gguf.py:425-468) shares Q4_K's scales; its fifth bits sit in
+        # qh[l] bit j for element l of sub-block j, and numpy forms
+        # d*sc * (q + 16 h) - dmin*m in float64 before the one rounding to
+        # fp32 (same value: the product and the difference are exact there)
         d = f16_from_u8(b[:, 0:2])
         dmin = f16_from_u8(b[:, 2:4])
         sc = b[:, 4:16]
-        qs = b[:, 16:144]
+        qh = b[:, 16:48] if qtype == GGML_TYPE_Q5_K else None
+        qs = b[:, 48:176] if qtype == GGML_TYPE_Q5_K else b[:, 16:144]
 
         def scale_min(j):
             if j < 4:
@@ -98,8 +105,16 @@ def dequantize(qtype: int, payload, n: int, q6k_order: str = "d_first") -> np.nd
             d2 = d * s1.astype(np.float32)
             mm2 = dmin * m1.astype(np.float32)
             q = qs[:, 32 * g : 32 * g + 32]
-            out[:, 64 * g : 64 * g + 32] = d1[:, None] * (q & 0x0F).astype(np.float32) - mm1[:, None]
-            out[:, 64 * g + 32 : 64 * g + 64] = d2[:, None] * (q >> 4).astype(np.float32) - mm2[:, None]
+            if qh is None:
+                out[:, 64 * g : 64 * g + 32] = d1[:, None] * (q & 0x0F).astype(np.float32) - mm1[:, None]
+                out[:, 64 * g + 32 : 64 * g + 64] = d2[:, None] * (q >> 4).astype(np.float32) - mm2[:, None]
+            else:
+                h1 = np.where((qh & np.uint8(1 << (2 * g))) != 0, 16, 0)
+                h2 = np.where((qh & np.uint8(1 << (2 * g + 1))) != 0, 16, 0)
+                v1 = d1[:, None].astype(np.float64) * ((q & 0x0F).astype(np.int64) + h1) - mm1[:, None]
+                v2 = d2[:, None].astype(np.float64) * ((q >> 4).astype(np.int64) + h2) - mm2[:, None]
+                out[:, 64 * g : 64 * g + 32] = v1.astype(np.float32)
+                out[:, 64 * g + 32 : 64 * g + 64] = v2.astype(np.float32)
         return out.reshape(-1)
 
     # Q6_K

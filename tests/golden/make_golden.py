@@ -10,7 +10,7 @@ stubs the top-level packages so that draco/__init__.py, which pulls in torch,
 the server and transformers, is not executed).  Every expected output below is
 produced by reference code:
 
-* ``draco.format.gguf._dequantize`` (gguf.py:272-497) for Q8_0 / Q4_K / Q6_K;
+* ``draco.format.gguf._dequantize`` (gguf.py:272-497) for Q8_0 / Q4_K / Q5_K / Q6_K;
 * ``GenericGemmKernel.matmul_f32`` (runtime/cpu/kernels/generic.py:32-33) for
   the linear-layer goldens;
 * the reference test suite's own helpers (tests/format/test_gguf.py): the Q8_0
@@ -85,8 +85,8 @@ def random_blocks(rng, qtype, nb):
     if qtype == 8:
         b = rng.integers(0, 256, (nb, 34), dtype=np.uint8)
         b[:, 0:2] = finite_f16(rng, nb).view(np.uint8).reshape(nb, 2)
-    elif qtype == 12:
-        b = rng.integers(0, 256, (nb, 144), dtype=np.uint8)
+    elif qtype in (12, 13):
+        b = rng.integers(0, 256, (nb, 144 if qtype == 12 else 176), dtype=np.uint8)
         b[:, 0:2] = finite_f16(rng, nb).view(np.uint8).reshape(nb, 2)
         b[:, 2:4] = finite_f16(rng, nb).view(np.uint8).reshape(nb, 2)
     else:
@@ -146,6 +146,18 @@ def main() -> None:
         x = rng.standard_normal((3, int(k))).astype(np.float32)
         out[f"{name}_lin_x"] = x
         out[f"{name}_lin_y"] = kern.matmul_f32(x, w).astype(np.float32)
+
+    # ---- Q5_K (own stream, so the keys above keep their bytes) ----
+    rng5 = np.random.default_rng(20261202)
+    n_rows, k = 6, 1024
+    blocks = random_blocks(rng5, 13, n_rows * k // 256)
+    out["q5_k_packed"] = blocks.reshape(n_rows, -1)
+    out["q5_k_shape"] = np.array([n_rows, k])
+    w5 = gguf._dequantize(13, blocks.tobytes(), n_rows * k).reshape(n_rows, k)
+    out["q5_k_expected"] = w5.astype(np.float32)
+    x5 = rng5.standard_normal((3, k)).astype(np.float32)
+    out["q5_k_lin_x"] = x5
+    out["q5_k_lin_y"] = kern.matmul_f32(x5, w5).astype(np.float32)
 
     path = HERE / "gguf_golden.npz"
     np.savez_compressed(path, **out)

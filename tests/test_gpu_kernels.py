@@ -20,7 +20,7 @@ from dracort_b200 import gguf_ops as G  # noqa: E402
 from dracort_b200.format import quantize as Q  # noqa: E402
 
 GEMV_TOL = 1e-3
-TYPES = [(8, "q8_0"), (12, "q4_k"), (14, "q6_k")]
+TYPES = [(8, "q8_0"), (12, "q4_k"), (13, "q5_k"), (14, "q6_k")]
 
 
 def dev_bytes(a: np.ndarray) -> "torch.Tensor":
@@ -53,7 +53,7 @@ def test_repack_then_tiled_dequant_is_bit_exact(golden, qtype, name):
     assert bits_equal(got, golden[f"{name}_expected"])
 
 
-@pytest.mark.parametrize("qtype", [8, 12, 14])
+@pytest.mark.parametrize("qtype", [8, 12, 13, 14])
 @pytest.mark.parametrize("shape", [(1, 256), (17, 512), (130, 768), (300, 2304)])
 def test_dequant_random_shapes(qtype, shape):
     n, k = shape
@@ -94,15 +94,15 @@ def _gemv_case(qtype, n, k, batch, seed, bias=False, xscale=1.0):
     return y, ref, O.linear_f64(x, qtype, packed, n, k, bias=b)
 
 
-@pytest.mark.parametrize("qtype", [8, 12, 14])
-@pytest.mark.parametrize("batch", [1, 3, 4, 5, 8, 16, 32])
+@pytest.mark.parametrize("qtype", [8, 12, 13, 14])
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8, 16, 32])
 def test_gemv_small_batches(qtype, batch):
     y, ref, ref64 = _gemv_case(qtype, 272, 1024, batch, seed=batch * 31 + qtype)
     assert O.rel_l2(y, ref) < GEMV_TOL
     assert O.rel_l2(y, ref64) < 3e-4  # int8-digit activations: ~6.5e-5 expected for Gaussian x
 
 
-@pytest.mark.parametrize("qtype", [8, 12, 14])
+@pytest.mark.parametrize("qtype", [8, 12, 13, 14])
 def test_gemv_bias_and_ragged_rows(qtype):
     y, ref, _ = _gemv_case(qtype, 1000, 768, 2, seed=77 + qtype, bias=True)
     assert O.rel_l2(y, ref) < GEMV_TOL
@@ -115,7 +115,8 @@ def test_gemv_activation_range(xscale):
     assert O.rel_l2(y, ref) < GEMV_TOL
 
 
-@pytest.mark.parametrize("qtype,n,k", [(12, 4096, 4096), (12, 4096, 11008), (14, 4096, 11008), (8, 4096, 4096)])
+@pytest.mark.parametrize("qtype,n,k", [(12, 4096, 4096), (12, 4096, 11008), (13, 4096, 11008), (14, 4096, 11008),
+                                        (8, 4096, 4096)])
 def test_gemv_llama_shapes(qtype, n, k):
     # full-size shapes exercise row groups split between CTAs (stream-K fixup)
     y, ref, _ = _gemv_case(qtype, n, k, 1, seed=n + k + qtype)
@@ -125,7 +126,7 @@ def test_gemv_llama_shapes(qtype, n, k):
 def test_gemv_grouped_mixed_types_is_deterministic():
     rng = np.random.default_rng(9)
     specs = [(12, 4096, 4096), (12, 1024, 4096), (14, 1024, 4096), (12, 4096, 4096),
-             (12, 11008, 4096), (12, 11008, 4096), (14, 4096, 11008)]
+             (12, 11008, 4096), (12, 11008, 4096), (14, 4096, 11008), (13, 1024, 4096)]
     batch = 4
     probs, refs = [], []
     for qt, n, k in specs:

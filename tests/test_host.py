@@ -22,7 +22,7 @@ def test_q8_0_encoder_is_byte_identical_to_reference_test_encoder(golden):
     assert np.array_equal(Q.encode_q8_0(golden["q8_0_enc_w"]), golden["q8_0_enc_packed"])
 
 
-@pytest.mark.parametrize("qtype,tol", [(8, 0.01), (12, 0.12), (14, 0.04)])
+@pytest.mark.parametrize("qtype,tol", [(8, 0.01), (12, 0.12), (13, 0.06), (14, 0.04)])
 def test_encoders_round_trip_through_reference_decoder(qtype, tol):
     rng = np.random.default_rng(qtype)
     w = Q.random_weight(rng, 32, 1024)
@@ -73,9 +73,11 @@ def test_size_queries_need_no_gpu():
     # ragged rows pad to 16, Q8_0 rows pad to 256 elements
     assert lib.draco_gguf_tiled_bytes(14, 17, 512) == 32 * 2 * 210
     assert lib.draco_gguf_tiled_bytes(8, 16, 32 * 13) == 16 * 2 * 8 * 34
+    assert lib.draco_gguf_tiled_bytes(13, 4096, 4096) == 4096 * 16 * 176
     bs, bb = ctypes.c_int(), ctypes.c_int()
-    assert lib.draco_gguf_block_geometry(14, ctypes.byref(bs), ctypes.byref(bb)) == 0
-    assert (bs.value, bb.value) == BLOCK_LAYOUTS[14]
+    for qt in (8, 12, 13, 14):
+        assert lib.draco_gguf_block_geometry(qt, ctypes.byref(bs), ctypes.byref(bb)) == 0
+        assert (bs.value, bb.value) == BLOCK_LAYOUTS[qt]
 
 
 def test_argument_errors_map_to_reference_exceptions():
@@ -105,7 +107,7 @@ def test_argument_errors_map_to_reference_exceptions():
 def test_registry_contract():
     from dracort_b200.quantization import QUANT_REGISTRY, QuantizationRegistry, register_into
 
-    assert {"gguf_q8_0", "gguf_q4_k", "gguf_q6_k", "gguf_q6_k_dlast"} <= set(QUANT_REGISTRY.list_methods())
+    assert {"gguf_q8_0", "gguf_q4_k", "gguf_q5_k", "gguf_q6_k", "gguf_q6_k_dlast"} <= set(QUANT_REGISTRY.list_methods())
     assert QUANT_REGISTRY.get("GGUF_Q4_K").name == "gguf_q4_k"
     assert "gguf_q8_0" in QUANT_REGISTRY and len(QUANT_REGISTRY) >= 4
     with pytest.raises(ValueError, match="gguf_q4_k"):  # names what is registered
@@ -129,7 +131,7 @@ def test_registry_contract():
     # re-registering replaces the entry (with a warning), case-insensitively
     first = r.get("gguf_q8_0")
     register_into(r)
-    assert r.get("GGUF_Q8_0") is not first and len(r) == 4
+    assert r.get("GGUF_Q8_0") is not first and len(r) == 5
 
 
 def test_backend_host_logic():

@@ -2,7 +2,7 @@
 
 tests/golden/gguf_golden.npz was produced by the reference itself
 (tests/golden/make_golden.py): draco.format.gguf._dequantize,
-GenericGemmKernel.matmul_f32, the reference tests' _enc_q8_0 and _ref_q4_k,
+GenericGemmKernel.matmul_f32 (Q8_0, Q4_K, Q5_K, Q6_K), the reference tests' _enc_q8_0 and _ref_q4_k,
 and llama.cpp's gguf package for the Q6_K d-last order.
 """
 
@@ -11,7 +11,7 @@ import pytest
 
 from oracle import gguf_oracle as O
 
-TYPES = [(8, "q8_0"), (12, "q4_k"), (14, "q6_k")]
+TYPES = [(8, "q8_0"), (12, "q4_k"), (13, "q5_k"), (14, "q6_k")]
 
 
 def bits_equal(a, b):
