@@ -51,6 +51,8 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv_workspace_bytes",
     "draco_gguf_gemv_grouped",
     "draco_gguf_gemv",
+    "draco_gguf_gemv_grouped_ex",
+    "draco_rmsnorm",
     "draco_gguf_gemv_grouped_noalloc",
     "draco_gguf_gemv_noalloc_status",
     "draco_gguf_gemm",
@@ -87,6 +89,22 @@ class GemvProblem(ctypes.Structure):
         ("ldx", ctypes.c_int64),
         ("ldy", ctypes.c_int64),
     ]
+
+
+class GemvInput(ctypes.Structure):
+    """Mirror of ``draco_gemv_input``."""
+
+    _fields_ = [
+        ("mode", ctypes.c_int),
+        ("eps", ctypes.c_float),
+        ("aux", ctypes.c_void_p),
+        ("ldaux", ctypes.c_int64),
+    ]
+
+
+INPUT_PLAIN = 0
+INPUT_RMSNORM = 1
+INPUT_SWIGLU = 2
 
 
 class GemmProblem(ctypes.Structure):
@@ -166,6 +184,11 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_gemv_workspace_bytes.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int]
         lib.draco_gguf_gemv_grouped.restype = c_int
         lib.draco_gguf_gemv_grouped.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp, ctypes.c_size_t, vp]
+        lib.draco_gguf_gemv_grouped_ex.restype = c_int
+        lib.draco_gguf_gemv_grouped_ex.argtypes = [ctypes.POINTER(GemvProblem), ctypes.POINTER(GemvInput), c_int, c_int,
+                                                   vp, ctypes.c_size_t, vp]
+        lib.draco_rmsnorm.restype = c_int
+        lib.draco_rmsnorm.argtypes = [vp, vp, vp, i64, i64, ctypes.c_float, c_int, vp]
         lib.draco_gguf_gemv_grouped_noalloc.restype = c_int
         lib.draco_gguf_gemv_grouped_noalloc.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp]
         lib.draco_gguf_gemv_noalloc_status.restype = c_int

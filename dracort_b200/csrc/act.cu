@@ -9,11 +9,11 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "common.cuh"
 #include "internal.h"
 
 namespace draco {
 
-__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
 
 __device__ __forceinline__ uint32_t swiglu2(uint32_t g2, uint32_t u2) {
   const float g0 = __uint_as_float(g2 << 16), g1 = __uint_as_float(g2 & 0xFFFF0000u);
@@ -80,6 +80,51 @@ cudaError_t launch_swiglu_bf16_rows(const void* gate, const void* up, void* out,
   swiglu_bf16_rows_kernel<<<grid, threads, 0, st>>>(static_cast<const uint16_t*>(gate),
                                                      static_cast<const uint16_t*>(up), static_cast<uint16_t*>(out),
                                                      cap_rows, width, rows);
+  return cudaGetLastError();
+}
+
+// RMSNorm of rows of k values: out = x * rsqrt(mean(x^2) + eps) * w, fp32
+// arithmetic in the reference's order (draco/kernels/ops.py:29-50); x and out
+// fp32 (dtype 0) or bf16 (dtype 1), w fp32.  One warp per row; the sum of
+// squares in a fixed order.
+template <typename T>
+__device__ __forceinline__ float ld_as_f32(const T* p);
+template <>
+__device__ __forceinline__ float ld_as_f32<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float ld_as_f32<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ void st_from_f32(float* p, float v) { *p = v; }
+__device__ __forceinline__ void st_from_f32(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <typename T>
+__global__ void rmsnorm_kernel(const T* __restrict__ x, const float* __restrict__ w, T* __restrict__ out, int64_t rows,
+                               int64_t k, float eps) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const T* xr = x + row * k;
+  float ss = 0.f;
+  for (int64_t i = lane; i < k; i += 32) {
+    const float v = ld_as_f32(xr + i);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = 1.f / sqrtf(ss / (float)k + eps);
+  T* orow = out + row * k;
+  for (int64_t i = lane; i < k; i += 32) st_from_f32(orow + i, ld_as_f32(xr + i) * inv * w[i]);
+}
+
+cudaError_t launch_rmsnorm(const void* x, const float* w, void* out, int64_t rows, int64_t k, float eps, int bf16,
+                           cudaStream_t st) {
+  const int warps = 8;
+  const dim3 grid((unsigned)((rows + warps - 1) / warps));
+  if (bf16)
+    rmsnorm_kernel<__nv_bfloat16><<<grid, warps * 32, 0, st>>>(static_cast<const __nv_bfloat16*>(x), w,
+                                                                static_cast<__nv_bfloat16*>(out), rows, k, eps);
+  else
+    rmsnorm_kernel<float><<<grid, warps * 32, 0, st>>>(static_cast<const float*>(x), w, static_cast<float*>(out), rows,
+                                                       k, eps);
   return cudaGetLastError();
 }
 

@@ -158,6 +158,28 @@ int draco_gguf_gemv_grouped(const draco_gemv_problem* probs, int n_problems, int
   return ok();
 }
 
+int draco_gguf_gemv_grouped_ex(const draco_gemv_problem* probs, const draco_gemv_input* inputs, int n_problems,
+                               int batch, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_gemv_problems(probs, n_problems, batch);
+  if (rc) return rc;
+  for (int i = 0; inputs && i < n_problems; ++i) {
+    const draco_gemv_input& in = inputs[i];
+    if (in.mode != DRACO_INPUT_PLAIN && in.mode != DRACO_INPUT_RMSNORM && in.mode != DRACO_INPUT_SWIGLU)
+      return fail(DRACO_ERR_ARG, "gemv_ex: problem %d has an unknown input mode %d", i, in.mode);
+    if (in.mode != DRACO_INPUT_PLAIN && !in.aux)
+      return fail(DRACO_ERR_ARG, "gemv_ex: problem %d needs its aux vector", i);
+    if (in.mode == DRACO_INPUT_RMSNORM && !(in.eps >= 0.f))
+      return fail(DRACO_ERR_ARG, "gemv_ex: problem %d has a negative or NaN eps", i);
+    if (in.mode == DRACO_INPUT_SWIGLU && in.ldaux < probs[i].k)
+      return fail(DRACO_ERR_SHAPE, "gemv_ex: problem %d aux row stride too small", i);
+  }
+  char msg[256] = {0};
+  rc = gemv_launch(probs, n_problems, batch, workspace, workspace_bytes, (cudaStream_t)stream, msg, sizeof(msg),
+                   inputs);
+  if (rc) return fail(rc, "%s", msg);
+  return ok();
+}
+
 int draco_gguf_gemv_grouped_noalloc(const draco_gemv_problem* probs, int n_problems, int batch, void* stream) {
   int rc = check_gemv_problems(probs, n_problems, batch);
   if (rc) return rc;
@@ -328,6 +350,17 @@ int draco_swiglu_bf16_rows(const void* gate, const void* up, void* out, int grou
   if (reinterpret_cast<uintptr_t>(rows) & 3) return fail(DRACO_ERR_ALIGN, "swiglu_rows: rows not 4-byte aligned");
   cudaError_t e = draco::launch_swiglu_bf16_rows(gate, up, out, groups, cap_rows, width, rows, (cudaStream_t)stream);
   return e == cudaSuccess ? ok() : cuda_fail(e, "swiglu_rows");
+}
+
+int draco_rmsnorm(const void* x, const float* weight, void* out, int64_t rows, int64_t k, float eps, int dtype,
+                  void* stream) {
+  if (rows < 0 || k < 0) return fail(DRACO_ERR_SHAPE, "rmsnorm: negative shape");
+  if (rows == 0 || k == 0) return ok();
+  if (!x || !weight || !out) return fail(DRACO_ERR_ARG, "rmsnorm: null pointer");
+  if (dtype != DRACO_DTYPE_F32 && dtype != DRACO_DTYPE_BF16) return fail(DRACO_ERR_TYPE, "rmsnorm: dtype %d", dtype);
+  if (!(eps >= 0.f)) return fail(DRACO_ERR_ARG, "rmsnorm: negative or NaN eps");
+  cudaError_t e = draco::launch_rmsnorm(x, weight, out, rows, k, eps, dtype == DRACO_DTYPE_BF16, (cudaStream_t)stream);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "rmsnorm");
 }
 
 int draco_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, void* stream) {

@@ -264,6 +264,9 @@ __device__ __forceinline__ void mma_f16_16816_acc(float (&d)[4], uint32_t a0, ui
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// silu(g) * u in fp32 with CUDA's expf (the SwiGLU product of a gated MLP)
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32_t orv) {
   return (a & mask) | orv;
 }

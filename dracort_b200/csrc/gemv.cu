@@ -97,6 +97,11 @@ struct GemvProbDev {
   int qt, n_rows, k, nb, n_rg, n_tiles, cb;
   int64_t tp_y_off, tp_par_stride;  // tensor-parallel output block in every rank's exchange buffer
   int64_t xcv_off;                   // workspace offset of the pre-converted activation slices
+  int in_mode;                       // DRACO_INPUT_*: transform applied as x is read
+  float eps;                         // RMSNORM epsilon
+  const float* aux;                  // RMSNORM: norm weight [k]; SWIGLU: up [batch, k]
+  int64_t ldaux;
+  int64_t rms_off;                   // RMSNORM: workspace offset of the per-row scales [batch]
 };
 
 struct GemvParams {
@@ -299,6 +304,20 @@ constexpr uint32_t kNibHi = 0xF0F0F0F0u;
 //       (the halves then go to different columns); unused slots hold zeros;
 //   su[m][b] = (S_half0, S_half1, u, S_half0 + S_half1) (all exact).
 // ---------------------------------------------------------------------------
+// 8 consecutive fp32 values at p (16-byte vector loads when aligned); the
+// ones at or past `valid` read as 0
+__device__ __forceinline__ void load8(const float* p, int valid, float (&v)[8]) {
+  if (valid >= 8 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const float4 lo4 = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 hi4 = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = lo4.x, v[1] = lo4.y, v[2] = lo4.z, v[3] = lo4.w;
+    v[4] = hi4.x, v[5] = hi4.y, v[6] = hi4.z, v[7] = hi4.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = i < valid ? __ldg(p + i) : 0.f;
+  }
+}
+
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
 }
@@ -323,15 +342,15 @@ __device__ __forceinline__ void convert_slab(const GemvParams& P, const GemvProb
     for (int q = 0; q < kPre; ++q) {
       const int b = b0 + q;
       if (b >= P.batch) break;
-      const float* xp = pr.x + (int64_t)b * pr.ldx + kk0;
-      if (kk0 + 8 <= pr.k && (reinterpret_cast<uintptr_t>(xp) & 15) == 0) {
-        const float4 lo4 = __ldg(reinterpret_cast<const float4*>(xp));
-        const float4 hi4 = __ldg(reinterpret_cast<const float4*>(xp) + 1);
-        vv[q][0] = lo4.x, vv[q][1] = lo4.y, vv[q][2] = lo4.z, vv[q][3] = lo4.w;
-        vv[q][4] = hi4.x, vv[q][5] = hi4.y, vv[q][6] = hi4.z, vv[q][7] = hi4.w;
-      } else {
+      load8(pr.x + (int64_t)b * pr.ldx + kk0, pr.k - kk0, vv[q]);
+      if (pr.in_mode != DRACO_INPUT_PLAIN) {
+        // the layer boundary, read in place: the RMSNorm weight (the row
+        // scale is applied to the outputs) or the SwiGLU product
+        float a[8];
+        const bool sw = pr.in_mode == DRACO_INPUT_SWIGLU;
+        load8(pr.aux + (sw ? (int64_t)b * pr.ldaux : 0) + kk0, pr.k - kk0, a);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) vv[q][i] = (kk0 + i < pr.k) ? __ldg(xp + i) : 0.f;
+        for (int i = 0; i < 8; ++i) vv[q][i] = sw ? silu_mul(vv[q][i], a[i]) : vv[q][i] * a[i];
       }
     }
 #pragma unroll
@@ -689,6 +708,7 @@ __device__ __forceinline__ void write_rows(const GemvParams& P, const GemvProbDe
       const int64_t row = row0 + 8 * hh;
       if (row < pr.n_rows) {
         float out = v[nt][hh];
+        if (pr.in_mode == DRACO_INPUT_RMSNORM) out *= __ldcg(reinterpret_cast<const float*>(P.ws + pr.rms_off) + b);
         if (pr.bias) out += pr.bias[row];
         if constexpr (!TP) {
           pr.y[(int64_t)b * pr.ldy + row] = out;
@@ -893,7 +913,26 @@ __global__ void __launch_bounds__(kConvertWarpsPerBlock * 32) gemv_convert_kerne
   const int lane = threadIdx.x & 31;
   int u = blockIdx.x * kConvertWarpsPerBlock + (threadIdx.x >> 5), p = 0;
   while (p < P.n_prob && u >= P.prob[p].nb) u -= P.prob[p].nb, ++p;
-  if (p >= P.n_prob) return;
+  if (p >= P.n_prob) {
+    // warps past the conversion units: one RMSNORM (problem, batch row) each,
+    // the row's scale rsqrt(mean(x^2) + eps) (draco/kernels/ops.py:46-48),
+    // summed in a fixed order (deterministic)
+    for (p = 0; p < P.n_prob; ++p) {
+      if (P.prob[p].in_mode != DRACO_INPUT_RMSNORM) continue;
+      if (u < P.batch) break;
+      u -= P.batch;
+    }
+    if (p >= P.n_prob) return;
+    const GemvProbDev& pr = P.prob[p];
+    const float* xr = pr.x + (int64_t)u * pr.ldx;
+    float ss = 0.f;
+    for (int i = lane; i < pr.k; i += 32) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0)
+      reinterpret_cast<float*>(P.ws + pr.rms_off)[u] = 1.f / sqrtf(ss / (float)pr.k + pr.eps);
+    return;
+  }
   const int xb = P.xs_bytes + P.su_bytes;
   uint8_t* dst = P.ws + P.prob[p].xcv_off + (int64_t)u * xb;
   for (int i = lane; i < (xb >> 4); i += 32) reinterpret_cast<uint4*>(dst)[i] = make_uint4(0, 0, 0, 0);
@@ -1132,7 +1171,7 @@ constexpr int kSmemBudget = 216 * 1024;
 // layouts (batch >= 3); the allocation-free entry keeps the in-kernel
 // conversion, whose scratch needs no activation slices.
 static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, HostPlan& hp, char* msg,
-                       size_t ml, bool convert_once = true) {
+                       size_t ml, bool convert_once = true, const draco_gemv_input* inputs = nullptr) {
   GemvParams& P = hp.P;
   memset(&P, 0, sizeof(P));
   P.n_prob = n;
@@ -1161,6 +1200,10 @@ static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_
     d.n_tiles = (int)g.n_tiles;
     d.cb = g.cb;
     d.slab0 = (int)slab0;
+    d.in_mode = inputs ? inputs[p].mode : DRACO_INPUT_PLAIN;
+    d.eps = inputs ? inputs[p].eps : 0.f;
+    d.aux = inputs ? inputs[p].aux : nullptr;
+    d.ldaux = inputs ? inputs[p].ldaux : 0;
     slab0 += g.n_rg * g.nb;
     w_stage = std::max(w_stage, kGroupTiles * g.cb);
   }
@@ -1172,15 +1215,25 @@ static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_
   P.part_off = off;
   off = align256(off + (int64_t)kMaxCta * 2 * kRowWarps * 32 * NT * 2 * 4);
   // dense layouts (batch >= 3): slices of the activations converted once per launch
-#ifndef DRACO_GEMV_PRECVT_MIN_BATCH
-#define DRACO_GEMV_PRECVT_MIN_BATCH 2
-#endif
-  P.precvt = (convert_once && batch >= DRACO_GEMV_PRECVT_MIN_BATCH) ? 1 : 0;
+  // activations converted once per launch by gemv_convert_kernel from batch
+  // 2 on, and at any batch when a problem's input is RMS-normalised (that
+  // kernel also computes the row scales); the workspace always holds the
+  // slices and the scales, so one size serves every input transform
+  bool any_rms = false;
+  for (int p = 0; p < n; ++p) any_rms |= P.prob[p].in_mode == DRACO_INPUT_RMSNORM;
+  if (any_rms && !convert_once) {
+    snprintf(msg, ml, "gemv: RMSNorm inputs need the workspace entry point");
+    return false;
+  }
+  P.precvt = (convert_once && (batch >= 2 || any_rms)) ? 1 : 0;
   for (int p = 0; p < n; ++p) {
     P.prob[p].xcv_off = -1;
-    if (P.precvt) {
+    P.prob[p].rms_off = -1;
+    if (convert_once) {
       P.prob[p].xcv_off = off;
       off = align256(off + (int64_t)P.prob[p].nb * (P.xs_bytes + P.su_bytes));
+      P.prob[p].rms_off = off;
+      off = align256(off + (int64_t)batch * 4);
     }
   }
   P.status_off = kWsStatus;
@@ -1323,10 +1376,11 @@ static int set_tp(HostPlan& hp, const draco_gemv_problem* probs, int n, const dr
 }
 
 static int gemv_launch_impl(const draco_gemv_problem* probs, int n, int batch, const draco_tp_exchange* ex, void* ws,
-                            size_t ws_bytes, cudaStream_t st, char* msg, size_t ml) {
+                            size_t ws_bytes, cudaStream_t st, char* msg, size_t ml,
+                            const draco_gemv_input* inputs = nullptr) {
   HostPlan hp;
   const int n_sm = device_sm_count();
-  if (!build_plan(probs, n, batch, n_sm, hp, msg, ml)) return DRACO_ERR_ARG;
+  if (!build_plan(probs, n, batch, n_sm, hp, msg, ml, true, inputs)) return DRACO_ERR_ARG;
   if (ex) {
     const int rc = set_tp(hp, probs, n, ex, msg, ml);
     if (rc != DRACO_OK) return rc;
@@ -1349,7 +1403,7 @@ static int gemv_launch_impl(const draco_gemv_problem* probs, int n, int batch, c
   hp.P.ws = static_cast<uint8_t*>(ws);
   if (hp.P.precvt) {
     int units = 0;
-    for (int p = 0; p < n; ++p) units += hp.P.prob[p].nb;
+    for (int p = 0; p < n; ++p) units += hp.P.prob[p].nb + (hp.P.prob[p].in_mode == DRACO_INPUT_RMSNORM ? batch : 0);
     const int blocks = (units + kConvertWarpsPerBlock - 1) / kConvertWarpsPerBlock;
     const dim3 grid(blocks), block(kConvertWarpsPerBlock * 32);
     if (hp.P.nt == 1) gemv_convert_kernel<1><<<grid, block, 0, st>>>(hp.P);
@@ -1372,8 +1426,8 @@ static int gemv_launch_impl(const draco_gemv_problem* probs, int n, int batch, c
 }
 
 int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
-                char* msg, size_t ml) {
-  return gemv_launch_impl(probs, n, batch, nullptr, ws, ws_bytes, st, msg, ml);
+                char* msg, size_t ml, const draco_gemv_input* inputs) {
+  return gemv_launch_impl(probs, n, batch, nullptr, ws, ws_bytes, st, msg, ml, inputs);
 }
 
 int gemv_launch_tp(const draco_gemv_problem* probs, int n, int batch, const draco_tp_exchange* ex, void* ws,

@@ -18,7 +18,7 @@ cudaError_t launch_repack(int qt, int src_layout, const void* src, void* dst, in
 // Grouped GEMV: plan + launch.  Returns a DRACO_* status; fills `msg` on error.
 size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch);
 int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
-                char* msg, size_t msg_len);
+                char* msg, size_t msg_len, const draco_gemv_input* inputs = nullptr);
 
 // Tensor-parallel grouped GEMV (outputs to every rank's exchange buffer) and
 // the step's finish on this rank.
@@ -45,6 +45,9 @@ cudaError_t launch_swiglu_bf16(const void* gate, const void* up, void* out, int6
 // Row-counted bf16 form over groups of [cap_rows, width] blocks (rows: device counts).
 cudaError_t launch_swiglu_bf16_rows(const void* gate, const void* up, void* out, int groups, int64_t cap_rows,
                                     int64_t width, const int* rows, cudaStream_t st);
+// RMSNorm of rows x [rows, k] (fp32, or bf16 when bf16 != 0) with fp32 weight w.
+cudaError_t launch_rmsnorm(const void* x, const float* w, void* out, int64_t rows, int64_t k, float eps, int bf16,
+                           cudaStream_t st);
 // out = silu(gate) * up over n fp32 elements (16-byte aligned).
 cudaError_t launch_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, cudaStream_t st);
 

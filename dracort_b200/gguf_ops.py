@@ -131,7 +131,13 @@ def workspace_status(device: Optional[torch.device] = None) -> int:
 
 @dataclass
 class GemvProblem:
-    """One linear layer of a grouped GEMV call (host-side mirror of draco_gemv_problem)."""
+    """One linear layer of a grouped GEMV call (host-side mirror of
+    draco_gemv_problem, with its draco_gemv_input transform).
+
+    norm_weight: x is taken through RMSNorm with this fp32 [k] weight and
+        norm_eps first (the model's norm fused into the read of x);
+    up: x is the gate output and this the up output ([B, k] fp32): the GEMV
+        multiplies silu(x) * up (the SwiGLU product fused into the read)."""
 
     qtype: int
     w_tiled: torch.Tensor
@@ -140,6 +146,9 @@ class GemvProblem:
     n_rows: int
     k: int
     bias: Optional[torch.Tensor] = None
+    norm_weight: Optional[torch.Tensor] = None
+    norm_eps: float = 1e-6
+    up: Optional[torch.Tensor] = None
 
 
 def _to_struct(p: GemvProblem) -> N.GemvProblem:
@@ -169,6 +178,33 @@ def _to_struct(p: GemvProblem) -> N.GemvProblem:
     return s
 
 
+def _input_struct(p: GemvProblem) -> N.GemvInput:
+    s = N.GemvInput()
+    s.mode, s.eps, s.aux, s.ldaux = N.INPUT_PLAIN, 0.0, None, 0
+    if p.norm_weight is not None and p.up is not None:
+        raise ValueError("gemv: a problem takes either an RMSNorm or a SwiGLU input, not both")
+    if p.norm_weight is not None:
+        w = p.norm_weight
+        _require_cuda(w, "norm_weight")
+        if w.dtype != torch.float32 or w.numel() != p.k or not w.is_contiguous():
+            raise ValueError("gemv: norm_weight must be a contiguous float32 [k] tensor")
+        s.mode, s.eps, s.aux = N.INPUT_RMSNORM, float(p.norm_eps), w.data_ptr()
+    elif p.up is not None:
+        u = p.up
+        _require_cuda(u, "up")
+        if u.dtype != torch.float32 or u.shape != p.x.shape or u.stride(1) != 1:
+            raise ValueError("gemv: up must be a float32 tensor shaped like x with unit inner stride")
+        s.mode, s.aux, s.ldaux = N.INPUT_SWIGLU, u.data_ptr(), u.stride(0)
+    return s
+
+
+def _inputs(problems: Sequence[GemvProblem]):
+    """ctypes array of the problems' input transforms, or None when all are plain."""
+    if all(p.norm_weight is None and p.up is None for p in problems):
+        return None
+    return (N.GemvInput * len(problems))(*[_input_struct(p) for p in problems])
+
+
 def gemv_grouped(problems: Sequence[GemvProblem]) -> None:
     """y_i = x_i @ dequant(W_i)^T (+ bias_i) for up to 8 weights in one launch.
 
@@ -188,7 +224,8 @@ def gemv_grouped(problems: Sequence[GemvProblem]) -> None:
     if batch > N.GEMV_MAX_BATCH:
         for b0 in range(0, batch, N.GEMV_MAX_BATCH):
             sub = [GemvProblem(p.qtype, p.w_tiled, p.x[b0:b0 + N.GEMV_MAX_BATCH], p.y[b0:b0 + N.GEMV_MAX_BATCH],
-                               p.n_rows, p.k, p.bias) for p in problems]
+                               p.n_rows, p.k, p.bias, p.norm_weight, p.norm_eps,
+                               None if p.up is None else p.up[b0:b0 + N.GEMV_MAX_BATCH]) for p in problems]
             gemv_grouped(sub)
         return
     lib = N.load()
@@ -198,7 +235,12 @@ def gemv_grouped(problems: Sequence[GemvProblem]) -> None:
         N.check(N.DRACO_ERR_ARG, "gemv workspace query failed")
     dev = problems[0].x.device
     ws = _workspace(dev, int(need))
-    rc = lib.draco_gguf_gemv_grouped(arr, len(problems), batch, ws.data_ptr(), ws.numel(), _stream_ptr(dev))
+    ins = _inputs(problems)
+    if ins is None:
+        rc = lib.draco_gguf_gemv_grouped(arr, len(problems), batch, ws.data_ptr(), ws.numel(), _stream_ptr(dev))
+    else:
+        rc = lib.draco_gguf_gemv_grouped_ex(arr, ins, len(problems), batch, ws.data_ptr(), ws.numel(),
+                                            _stream_ptr(dev))
     N.check(rc, "gemv")
 
 
@@ -220,6 +262,7 @@ class GemvPlan:
             raise ValueError("GemvPlan: all problems need one batch size in 1..32")
         self._lib = N.load()
         self._arr = (N.GemvProblem * len(problems))(*[_to_struct(p) for p in problems])
+        self._ins = _inputs(problems)
         need = self._lib.draco_gguf_gemv_workspace_bytes(self._arr, len(problems), self.batch)
         if need == 0:
             N.check(N.DRACO_ERR_ARG, "gemv workspace query failed")
@@ -228,9 +271,14 @@ class GemvPlan:
         self.bytes_weights = sum(tiled_nbytes(p.qtype, p.n_rows, p.k) for p in problems)
 
     def run(self) -> None:
-        rc = self._lib.draco_gguf_gemv_grouped(self._arr, len(self.problems), self.batch,
-                                               self.workspace.data_ptr(), self.workspace.numel(),
-                                               _stream_ptr(self.device))
+        if self._ins is None:
+            rc = self._lib.draco_gguf_gemv_grouped(self._arr, len(self.problems), self.batch,
+                                                   self.workspace.data_ptr(), self.workspace.numel(),
+                                                   _stream_ptr(self.device))
+        else:
+            rc = self._lib.draco_gguf_gemv_grouped_ex(self._arr, self._ins, len(self.problems), self.batch,
+                                                      self.workspace.data_ptr(), self.workspace.numel(),
+                                                      _stream_ptr(self.device))
         if rc:
             N.check(rc, "gemv")
 
@@ -383,6 +431,24 @@ def swiglu_bf16_rows(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor, ro
     g, c, w = gate.shape
     N.check(N.load().draco_swiglu_bf16_rows(gate.data_ptr(), up.data_ptr(), out.data_ptr(), g, c, w,
                                             rows.data_ptr(), _stream_ptr(gate.device)), "swiglu_rows")
+    return out
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+             out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x * rsqrt(mean(x^2, -1) + eps) * weight on the GPU (draco_rmsnorm): x
+    fp32 or bf16 CUDA, contiguous, last dim k; weight [k] (cast to fp32)."""
+    _require_cuda(x, "x")
+    if x.dtype not in (torch.float32, torch.bfloat16) or not x.is_contiguous():
+        raise ValueError("rms_norm: x must be a contiguous float32 or bfloat16 CUDA tensor")
+    k = x.shape[-1]
+    w = weight.to(device=x.device, dtype=torch.float32).contiguous()
+    if w.numel() != k:
+        raise DracoFormatError(f"rms_norm: weight of {w.numel()} values for rows of {k}")
+    out = out if out is not None else torch.empty_like(x)
+    dt = N.DTYPE_BF16 if x.dtype == torch.bfloat16 else N.DTYPE_F32
+    N.check(N.load().draco_rmsnorm(x.data_ptr(), w.data_ptr(), out.data_ptr(), x.numel() // max(k, 1), k, float(eps),
+                                   dt, _stream_ptr(x.device)), "rms_norm")
     return out
 
 

@@ -68,9 +68,33 @@ def fused_swiGLU(x: torch.Tensor, gate_proj, up_proj, down_proj) -> torch.Tensor
         gu = torch.empty((2, r1 - r0, f), dtype=torch.float32, device=x.device)
         G.gemv_grouped([G.GemvProblem(gate_proj.qtype, gate_proj.tiled, xf[r0:r1], gu[0], f, k),
                         G.GemvProblem(up_proj.qtype, up_proj.tiled, xf[r0:r1], gu[1], f, k)])
-        G.swiglu(gu[0], gu[1], out=gu[0])
-        G.gemv_grouped([G.GemvProblem(down_proj.qtype, down_proj.tiled, gu[0], y[r0:r1], h, f)])
+        # the SwiGLU product is formed as the down GEMV reads its input
+        G.gemv_grouped([G.GemvProblem(down_proj.qtype, down_proj.tiled, gu[0], y[r0:r1], h, f, up=gu[1])])
     return y.reshape(*lead, h).to(x.dtype)
+
+
+def fused_rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """x * rsqrt(mean(x^2, -1) + eps) * weight (draco/kernels/ops.py:29-50) on
+    the GPU for contiguous fp32 / bf16 CUDA tensors; other inputs take the
+    reference's own formula."""
+    if x.is_cuda and x.dtype in (torch.float32, torch.bfloat16) and x.is_contiguous():
+        return G.rms_norm(x, weight, eps)
+    variance = x.pow(2).mean(-1, keepdim=True)
+    return x * torch.rsqrt(variance + eps) * weight
+
+
+def fused_rms_norm_linear(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, projections) -> list:
+    """[proj(fused_rms_norm(x, norm_weight, eps)) for proj in projections] for
+    GGUFLinear projections sharing the normalised input (q/k/v after the
+    input norm, gate/up after the post-attention norm): one grouped GEMV
+    launch that applies the norm as it reads x (decode batches of fp32 rows)."""
+    k = projections[0].in_features
+    x2 = x.reshape(-1, k).float().contiguous()
+    w = norm_weight.to(device=x.device, dtype=torch.float32).contiguous()
+    outs = [torch.empty((x2.shape[0], p.out_features), dtype=torch.float32, device=x.device) for p in projections]
+    G.gemv_grouped([G.GemvProblem(p.qtype, p.tiled, x2, o, p.out_features, k, p.bias, norm_weight=w, norm_eps=eps)
+                    for p, o in zip(projections, outs)])
+    return [o.reshape(*x.shape[:-1], o.shape[-1]) for o in outs]
 
 
 _TYPE_OF_NAME = {"gguf_q8_0": GGML_TYPE_Q8_0, "gguf_q4_k": GGML_TYPE_Q4_K, "gguf_q5_k": GGML_TYPE_Q5_K,

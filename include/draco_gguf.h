@@ -157,6 +157,38 @@ size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* problems, int n
 int draco_gguf_gemv_grouped(const draco_gemv_problem* problems, int n_problems, int batch,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* Input transform of one problem of draco_gguf_gemv_grouped_ex: the layer
+ * boundary fused into the GEMV's activation read.
+ *   PLAIN   : x as it is.
+ *   RMSNORM : x is the hidden state before the model's RMSNorm;
+ *             y = rmsnorm(x) @ dequant(W)^T (+ bias) with
+ *             rmsnorm(x) = x * rsqrt(mean(x^2) + eps) * aux, aux the fp32
+ *             norm weight [k] (draco/kernels/ops.py:29-50, fused_rms_norm,
+ *             ahead of the q/k/v and gate/up projections).  The per-row
+ *             scale is applied to the outputs, the weight to x as it is read.
+ *   SWIGLU  : x is the gate projection's output, aux the up projection's
+ *             ([batch, k], row stride ldaux elements);
+ *             y = (silu(x) * aux) @ dequant(W)^T (+ bias): the SwiGLU
+ *             product ahead of the down projection
+ *             (draco/kernels/ops.py:114-137, fused_swiGLU) read in place. */
+#define DRACO_INPUT_PLAIN 0
+#define DRACO_INPUT_RMSNORM 1
+#define DRACO_INPUT_SWIGLU 2
+typedef struct draco_gemv_input {
+  int mode;
+  float eps;
+  const float* aux;
+  int64_t ldaux;
+} draco_gemv_input;
+
+/* draco_gguf_gemv_grouped with an input transform per problem (`inputs`, a
+ * host array of n_problems entries, or NULL for all PLAIN).  Same workspace
+ * (draco_gguf_gemv_workspace_bytes covers it).  A launch with an RMSNORM
+ * problem computes the row scales and converts the activations in a first
+ * kernel on `stream`, then runs the GEMV. */
+int draco_gguf_gemv_grouped_ex(const draco_gemv_problem* problems, const draco_gemv_input* inputs, int n_problems,
+                               int batch, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Allocation-free form of draco_gguf_gemv_grouped.  No counterpart in the
  * reference: DracoRT's numpy path has no device memory to manage.
  *
@@ -322,6 +354,15 @@ int draco_swiglu_bf16_rows(const void* gate, const void* up, void* out, int grou
  * Replaces the activation step of draco/kernels/ops.py:114-137
  * (fused_swiGLU) between the gate/up and down GEMVs. */
 int draco_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, void* stream);
+
+/* RMSNorm, out = x * rsqrt(mean(x^2) + eps) * weight per row of x [rows, k]
+ * (row-major, contiguous), fp32 arithmetic in the order of
+ * draco/kernels/ops.py:29-50 (fused_rms_norm); x and out DRACO_DTYPE_F32 or
+ * DRACO_DTYPE_BF16 (`dtype`), weight fp32 [k]; out may alias x.  Ahead of a
+ * GEMV the norm can instead be fused into the activation read
+ * (draco_gguf_gemv_grouped_ex, DRACO_INPUT_RMSNORM). */
+int draco_rmsnorm(const void* x, const float* weight, void* out, int64_t rows, int64_t k, float eps, int dtype,
+                  void* stream);
 
 /* Single-weight convenience form of draco_gguf_gemv_grouped. */
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias,
