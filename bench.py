@@ -918,20 +918,31 @@ def run_ours(args):
     sampler.stop()
 
     # -- prefill dequant-GEMM (config 3), the second half of the metric --------
+    # each leg runs inside an NVTX range named after it, so that a profiler
+    # can select one leg's launches (ncu --nvtx --nvtx-include "<leg>/")
+    nvtx = torch.cuda.nvtx
     prefill = None
     if not args.no_prefill:
+        nvtx.range_push("prefill")
         prefill = prefill_leg(args, dev, peaks, rank, world, pg, timed, not args.no_e2e, not args.no_cpu)
+        nvtx.range_pop()
 
     q8 = None
     if not args.no_q8 and world == 1:
+        nvtx.range_push("q8_0")
         q8 = q8_0_leg(args, dev, peaks, timed, not args.no_e2e, rank == 0 and not args.no_cpu)
+        nvtx.range_pop()
 
     moe = None
     if not args.no_moe:
+        nvtx.range_push("moe")
         moe = moe_leg(args, dev, peaks, rank, world, pg, timed)
+        nvtx.range_pop()
     model = None
     if not args.no_model:
+        nvtx.range_push("model")
         model = model_leg(args, dev, peaks, rank, world, pg, timed)
+        nvtx.range_pop()
 
     # -- CPU baseline (rank 0, N=1) --------------------------------------------
     cpu = None
