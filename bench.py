@@ -449,7 +449,9 @@ def prefill_leg(args, dev, peaks, rank, world, pg, timed, want_e2e, want_cpu):
         gemm_ms, _, _ = timed(gemm_only)
         gemm_ms /= K
     achieved = layer.flops_local / (gemm_ms * 1e-3) / 1e12
-    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    # the timed loop is ~0.1 s, at the boost clock (its own clock record
+    # shows it): the burst cuBLAS figure is the denominator
+    peak = peaks["bf16_tflops"]
     out = {
         "metric": "prefill dequant-GEMM TFLOP/s",
         "value": round(value, 2),
@@ -472,10 +474,10 @@ def prefill_leg(args, dev, peaks, rank, world, pg, timed, want_e2e, want_cpu):
             "peak": peak,
             "unit": "TFLOP/s",
             "frac": round(achieved / peak, 4),
-            "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4),
+            "frac_of_sustained": round(achieved / peaks.get("bf16_tflops_sustained", peak), 4),
             "traffic": profiled_traffic("gemm_config3_prefill") if world == 1 else None,
-            "peak_source": f"{peaks['source']} MEASURED_PEAKS.json bf16_tflops_sustained (kernel timed in a "
-                           f"{K}-launch loop under the power cap); frac_of_burst uses bf16_tflops",
+            "peak_source": f"{peaks['source']} MEASURED_PEAKS.json bf16_tflops (burst: a {K}-launch loop of "
+                           f"about 0.1 s runs at the boost clock); frac_of_sustained uses bf16_tflops_sustained",
             "kernel": f"gemm_kernel, one launch per step, {layer.flops_local} algorithmic FLOP per launch per GPU",
         },
         "gpu_launches": layer.launches_per_step * K,
