@@ -145,9 +145,11 @@ class EPMoELayer:
         T = router_logits.shape[0]
         idx, wts = self.router.route(router_logits)
         flat_e = idx.reshape(-1)
-        csum = F.one_hot(flat_e, self.n_exp).to(torch.int32).cumsum(0)
-        pos = csum.gather(1, flat_e[:, None]).squeeze(1) - 1
-        counts = csum[-1].contiguous() if T else torch.zeros(self.n_exp, dtype=torch.int32, device=flat_e.device)
+        # [expert, pair] running counts: a scan along the contiguous dimension
+        # (a scan across rows costs ~150 us on the GPU for 512 x 8 values)
+        csum = F.one_hot(flat_e, self.n_exp).to(torch.int32).t().contiguous().cumsum(1, dtype=torch.int32)
+        pos = csum.gather(0, flat_e[None, :]).squeeze(0) - 1
+        counts = csum[:, -1].contiguous() if T else torch.zeros(self.n_exp, dtype=torch.int32, device=flat_e.device)
         return flat_e * T + pos, wts, counts
 
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
