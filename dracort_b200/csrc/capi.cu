@@ -37,13 +37,13 @@ int device_sm_count() {
   return n;
 }
 
-static bool type_ok(int qt) { return qt == kQ8_0 || qt == kQ4_K || qt == kQ5_K || qt == kQ6_K; }
+static bool type_ok(int qt) { return qt == kQ8_0 || is_q4x(qt) || qt == kQ4_K || qt == kQ5_K || qt == kQ6_K; }
 
 // Shape / type / layout checks shared by the weight entry points.  Mirrors the
 // reference's DracoFormatError cases (gguf.py:284-296).
 static int check_weight(int qt, int layout, const void* p, int64_t n_rows, int64_t k, const char* fn) {
   if (!type_ok(qt))
-    return fail(DRACO_ERR_TYPE, "%s: GGUF quantization type %d is not supported (supported: Q8_0=8, Q4_K=12, Q5_K=13, Q6_K=14)",
+    return fail(DRACO_ERR_TYPE, "%s: GGUF quantization type %d is not supported (supported: Q4_0=2, Q4_1=3, Q5_0=6, Q5_1=7, Q8_0=8, Q4_K=12, Q5_K=13, Q6_K=14)",
                 fn, qt);
   if (layout != DRACO_LAYOUT_GGUF && layout != DRACO_LAYOUT_GGUF_DLAST && layout != DRACO_LAYOUT_TILED)
     return fail(DRACO_ERR_TYPE, "%s: unknown layout %d", fn, layout);

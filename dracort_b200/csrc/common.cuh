@@ -17,13 +17,20 @@ namespace draco {
 // GGUF block geometry (draco/format/gguf.py:75-87)
 // ---------------------------------------------------------------------------
 constexpr int kQ8_0 = DRACO_GGML_TYPE_Q8_0;
+constexpr int kQ4_0 = DRACO_GGML_TYPE_Q4_0;
+constexpr int kQ4_1 = DRACO_GGML_TYPE_Q4_1;
+constexpr int kQ5_0 = DRACO_GGML_TYPE_Q5_0;
+constexpr int kQ5_1 = DRACO_GGML_TYPE_Q5_1;
+// the 32-element types with 4 (+1) bit quants: Q4_0, Q4_1, Q5_0, Q5_1
+__host__ __device__ inline bool is_q4x(int qt) { return qt == kQ4_0 || qt == kQ4_1 || qt == kQ5_0 || qt == kQ5_1; }
 constexpr int kQ4_K = DRACO_GGML_TYPE_Q4_K;
 constexpr int kQ5_K = DRACO_GGML_TYPE_Q5_K;
 constexpr int kQ6_K = DRACO_GGML_TYPE_Q6_K;
 
-__host__ __device__ inline int block_size_of(int qt) { return qt == kQ8_0 ? 32 : 256; }
+__host__ __device__ inline int block_size_of(int qt) { return (qt == kQ8_0 || is_q4x(qt)) ? 32 : 256; }
 __host__ __device__ inline int block_bytes_of(int qt) {
-  return qt == kQ8_0 ? 34 : qt == kQ4_K ? 144 : qt == kQ5_K ? 176 : 210;
+  return qt == kQ8_0 ? 34 : qt == kQ4_K ? 144 : qt == kQ5_K ? 176 : qt == kQ6_K ? 210 :
+         qt == kQ4_0 ? 18 : qt == kQ4_1 ? 20 : qt == kQ5_0 ? 22 : 24;
 }
 
 // Field offsets inside one Q6_K block for the two byte orders.  GGUF (the
@@ -130,6 +137,28 @@ __host__ __device__ inline int q6k_qh_pos(int rr, int p) {
 }
 __host__ __device__ inline int q6k_sc_pos(int rr, int s) { return 3072 + 32 * (rr & 7) + 16 * (rr >> 3) + s; }
 __host__ __device__ inline int q6k_d_pos(int rr) { return 3328 + 4 * (rr & 7) + 2 * (rr >> 3); }
+
+// Q4_0 / Q4_1 / Q5_0 / Q5_1 (8 blocks of 32 per super-block, block b).
+// qs[16] -> [0,2048): the 16-byte unit of lane (g, t) for block pair bp holds
+//   the words (row g, block 2bp), (row g+8, block 2bp), (row g, block 2bp+1),
+//   (row g+8, block 2bp+1), each qs bytes 4t..4t+3 of that block: their low
+//   nibbles are elements 4t..4t+3, their high nibbles 16+4t..16+4t+3;
+// Q5_x: qh (32 bits per block, bit e = element e) -> 512 B at 2048, per
+//   (g, row half, block) one word, read whole by the four lanes of a quad;
+// d (fp16 per block) -> 256 B, m (Q4_1 / Q5_1, fp16 per block) -> 256 B, per
+//   (g, row half, block).
+struct Q4xFields { int qh, d, m; };
+__host__ __device__ inline Q4xFields q4x_fields(int qt) {
+  const bool h = qt == kQ5_0 || qt == kQ5_1;
+  const int d = h ? 2560 : 2048;
+  return {h ? 2048 : -1, d, (qt == kQ4_1 || qt == kQ5_1) ? d + 256 : -1};
+}
+__host__ __device__ inline int q4x_qs_pos(int rr, int b, int p) {
+  const int g = rr & 7, hi = rr >> 3, t = p >> 2, bw = p & 3;
+  return 512 * (b >> 1) + 16 * (4 * g + t) + 4 * (2 * (b & 1) + hi) + bw;
+}
+__host__ __device__ inline int q4x_word_pos(int base, int rr, int b) { return base + 64 * (rr & 7) + 32 * (rr >> 3) + 4 * b; }
+__host__ __device__ inline int q4x_half_pos(int base, int rr, int b) { return base + 32 * (rr & 7) + 16 * (rr >> 3) + 2 * b; }
 
 // Q8_0 (8 blocks per super-block, block b): qs[32] -> [0,4096), d -> [4096,4352).
 __host__ __device__ inline int q80_qs_pos(int rr, int b, int p) {

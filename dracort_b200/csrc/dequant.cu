@@ -1,4 +1,5 @@
-// dequant.cu — GGUF block dequantization (Q8_0, Q4_K, Q5_K, Q6_K) to fp32 / bf16,
+// dequant.cu — GGUF block dequantization (Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K,
+// Q5_K, Q6_K) to fp32 / bf16,
 // and the GGUF -> TILED repack.
 //
 // Parity target: draco/format/gguf.py:_dequantize.  Each output element is
@@ -9,6 +10,9 @@
 //   Q5_K (gguf.py:425-468): the same with q = nibble + 16 * fifth bit (the
 //                           reference forms it in float64: the same value)
 //   Q6_K (gguf.py:470-495): (d*sc) * (q6 - 32)           (d*sc exact, one rounding)
+//   Q4_0 / Q5_0 (gguf.py:310-316, 326-349): (q - 8) * d, (q5 - 16) * d   (exact)
+//   Q4_1 / Q5_1 (gguf.py:318-324, 326-353): q * d + m    (product exact, one
+//                                                         rounding in the add)
 // The multiplies and the subtract are written with explicit _rn intrinsics so
 // that no FMA contraction can change a bit.
 #include "common.cuh"
@@ -111,6 +115,53 @@ struct TiledQ80 {
   __device__ int8_t qs(int b, int p) const { return (int8_t)ch[q80_qs_pos(rr, b, p)]; }
 };
 
+// Q4_0 / Q4_1 / Q5_0 / Q5_1: b is the block index inside the super-block;
+// d, m (Q4_1 / Q5_1), qh (Q5_x, 32 bits, bit e = element e), qs[16].
+struct Q4xRawFields { int m, qh, qs; };
+__host__ __device__ inline Q4xRawFields q4x_raw_fields(int qt) {
+  if (qt == kQ4_0) return {-1, -1, 2};
+  if (qt == kQ4_1) return {2, -1, 4};
+  if (qt == kQ5_0) return {-1, 2, 6};
+  return {2, 4, 8};
+}
+struct RawQ4x {
+  const uint8_t* row_base;
+  int64_t sb;
+  int bb;
+  Q4xRawFields f;
+  __device__ RawQ4x(const uint8_t* base, int64_t row, int64_t k, int64_t sb_, int qt) {
+    bb = block_bytes_of(qt);
+    row_base = base + row * (k / 32) * bb;
+    sb = sb_;
+    f = q4x_raw_fields(qt);
+  }
+  __device__ const uint8_t* blk(int b) const { return row_base + (sb * 8 + b) * bb; }
+  __device__ float d(int b) const { return ld_f16(blk(b)); }
+  __device__ float m(int b) const { return ld_f16(blk(b) + f.m); }
+  __device__ uint32_t qh(int b) const {
+    const uint8_t* h = blk(b) + f.qh;
+    return (uint32_t)h[0] | ((uint32_t)h[1] << 8) | ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+  }
+  __device__ uint8_t qs(int b, int p) const { return blk(b)[f.qs + p]; }
+};
+struct TiledQ4x {
+  const uint8_t* ch;
+  int rr;
+  Q4xFields f;
+  __device__ TiledQ4x(const uint8_t* base, const TiledGeom& g, int64_t row, int64_t sb, int qt) {
+    ch = base + chunk_offset(g, row / kChunkRows, sb);
+    rr = (int)(row % kChunkRows);
+    f = q4x_fields(qt);
+  }
+  __device__ float d(int b) const { return ld_f16(ch + q4x_half_pos(f.d, rr, b)); }
+  __device__ float m(int b) const { return ld_f16(ch + q4x_half_pos(f.m, rr, b)); }
+  __device__ uint32_t qh(int b) const {
+    const uint8_t* h = ch + q4x_word_pos(f.qh, rr, b);
+    return (uint32_t)h[0] | ((uint32_t)h[1] << 8) | ((uint32_t)h[2] << 16) | ((uint32_t)h[3] << 24);
+  }
+  __device__ uint8_t qs(int b, int p) const { return ch[q4x_qs_pos(rr, b, p)]; }
+};
+
 // ---------------------------------------------------------------------------
 // 8 consecutive elements e0..e0+7 (e0 % 8 == 0) of one 256-element super-block
 // ---------------------------------------------------------------------------
@@ -176,6 +227,26 @@ __device__ __forceinline__ void decode8_q80(const A& a, int e0, float (&o)[8]) {
   for (int i = 0; i < 8; ++i) o[i] = __fmul_rn((float)a.qs(b, p0 + i), d);
 }
 
+// element p of a block: low nibble of qs byte p (p < 16) or high nibble of
+// byte p - 16, with bit p of qh as the fifth bit (gguf.py:310-353)
+template <int QT, class A>
+__device__ __forceinline__ void decode8_q4x(const A& a, int e0, float (&o)[8]) {
+  constexpr bool kH = QT == kQ5_0 || QT == kQ5_1, kM = QT == kQ4_1 || QT == kQ5_1;
+  const int b = e0 >> 5, p0 = e0 & 31;
+  const float d = a.d(b);
+  const float m = kM ? a.m(b) : 0.f;
+  const uint32_t h = kH ? a.qh(b) : 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int p = p0 + i;
+    const uint8_t byte = a.qs(b, p & 15);
+    int q = p < 16 ? (byte & 15) : (byte >> 4);
+    if (kH) q |= (int)((h >> p) & 1u) << 4;
+    if (kM) o[i] = __fadd_rn(__fmul_rn((float)q, d), m);
+    else o[i] = __fmul_rn((float)(q - (kH ? 16 : 8)), d);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // dequant kernel: one warp per (row, super-block), lane -> 8 elements
 // ---------------------------------------------------------------------------
@@ -207,7 +278,7 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
   if (warp >= n_rows * nb) return;
   const int64_t row = warp / nb, sb = warp % nb;
   const int e0 = lane * 8;
-  if (sb * 256 + e0 >= k) return;  // Q8_0 tail super-block with fewer than 8 blocks
+  if (sb * 256 + e0 >= k) return;  // tail super-block of a 32-element-block type
   float o[8];
   TiledGeom g = tiled_geom(QT, n_rows, k);
   if (QT == kQ4_K) {
@@ -219,9 +290,12 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict_
   } else if (QT == kQ6_K) {
     if (TILED) decode8_q6k(TiledQ6K(src, g, row, sb), e0, o);
     else decode8_q6k(RawQ6K(src, row, k, sb, layout), e0, o);
-  } else {
+  } else if (QT == kQ8_0) {
     if (TILED) decode8_q80(TiledQ80(src, g, row, sb), e0, o);
     else decode8_q80(RawQ80(src, row, k, sb), e0, o);
+  } else {
+    if (TILED) decode8_q4x<QT>(TiledQ4x(src, g, row, sb, QT), e0, o);
+    else decode8_q4x<QT>(RawQ4x(src, row, k, sb, QT), e0, o);
   }
   store8<OutT>(out + row * k + sb * 256 + e0, o);
 }
@@ -269,7 +343,7 @@ __global__ void __launch_bounds__(256) repack_kernel(const uint8_t* __restrict__
     for (int p = 0; p < 128; ++p) ch[q6k_ql_pos(rr, p)] = b[f.ql + p];
     for (int p = 0; p < 64; ++p) ch[q6k_qh_pos(rr, p)] = b[f.qh + p];
     for (int s = 0; s < 16; ++s) ch[q6k_sc_pos(rr, s)] = b[f.sc + s];
-  } else {
+  } else if (QT == kQ8_0) {
     const int64_t sb = bi / 8;
     const int blk = (int)(bi % 8);
     uint8_t* ch = dst + chunk_offset(g, row / kChunkRows, sb);
@@ -277,6 +351,25 @@ __global__ void __launch_bounds__(256) repack_kernel(const uint8_t* __restrict__
     ch[dp] = b[0];
     ch[dp + 1] = b[1];
     for (int p = 0; p < 32; ++p) ch[q80_qs_pos(rr, blk, p)] = b[2 + p];
+  } else {
+    const int64_t sb = bi / 8;
+    const int blk = (int)(bi % 8);
+    uint8_t* ch = dst + chunk_offset(g, row / kChunkRows, sb);
+    const Q4xFields f = q4x_fields(QT);
+    const Q4xRawFields rf = q4x_raw_fields(QT);
+    const int dp = q4x_half_pos(f.d, rr, blk);
+    ch[dp] = b[0];
+    ch[dp + 1] = b[1];
+    if (f.m >= 0) {
+      const int mp = q4x_half_pos(f.m, rr, blk);
+      ch[mp] = b[rf.m];
+      ch[mp + 1] = b[rf.m + 1];
+    }
+    if (f.qh >= 0) {
+      const int hp = q4x_word_pos(f.qh, rr, blk);
+      for (int i = 0; i < 4; ++i) ch[hp + i] = b[rf.qh + i];
+    }
+    for (int p = 0; p < 16; ++p) ch[q4x_qs_pos(rr, blk, p)] = b[rf.qs + p];
   }
 }
 
@@ -301,6 +394,10 @@ static cudaError_t launch_dequant_t(int qt, int layout, const void* src, OutT* o
   if (qt == kQ4_K) DRACO_DQ(kQ4_K);
   else if (qt == kQ5_K) DRACO_DQ(kQ5_K);
   else if (qt == kQ6_K) DRACO_DQ(kQ6_K);
+  else if (qt == kQ4_0) DRACO_DQ(kQ4_0);
+  else if (qt == kQ4_1) DRACO_DQ(kQ4_1);
+  else if (qt == kQ5_0) DRACO_DQ(kQ5_0);
+  else if (qt == kQ5_1) DRACO_DQ(kQ5_1);
   else DRACO_DQ(kQ8_0);
 #undef DRACO_DQ
   return cudaGetLastError();
@@ -328,6 +425,10 @@ cudaError_t launch_repack(int qt, int src_layout, const void* src, void* dst, in
   if (qt == kQ4_K) repack_kernel<kQ4_K><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
   else if (qt == kQ5_K) repack_kernel<kQ5_K><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
   else if (qt == kQ6_K) repack_kernel<kQ6_K><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
+  else if (qt == kQ4_0) repack_kernel<kQ4_0><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
+  else if (qt == kQ4_1) repack_kernel<kQ4_1><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
+  else if (qt == kQ5_0) repack_kernel<kQ5_0><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
+  else if (qt == kQ5_1) repack_kernel<kQ5_1><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
   else repack_kernel<kQ8_0><<<grid, 256, 0, st>>>(s, d, n_rows, k, src_layout);
   return cudaGetLastError();
 }

@@ -1,6 +1,6 @@
 // gemm.cu — prefill dequant-GEMM  Y[M, N] = X[M, K] (bf16) . dequant(W)[N, K]^T
-// with W in the TILED GGUF layout (Q8_0 / Q4_K / Q6_K), fp32 accumulation in
-// tensor memory, Y in bf16 or fp32.
+// with W in the TILED GGUF layout (Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0 / Q4_K /
+// Q5_K / Q6_K), fp32 accumulation in tensor memory, Y in bf16 or fp32.
 //
 // Replaces the reference's prefill linear: executor._linear
 // (draco/runtime/cpu/executor.py:47-79) -> GenericGemmKernel.matmul_f32
@@ -247,6 +247,9 @@ __device__ __forceinline__ uint32_t ldg32(const uint8_t* p) {
 //  Q5_K: as Q4_K, plus u3 = the qh unit (fifth bits, word for word as u0)
 //  Q6_K: u0..u2 = ql/qh units of half q/2; u3 = int8 scales of rows g, g+8, d of both rows
 //  Q8_0: u0, u1 = qs units of blocks 2q, 2q+1; u2.x, u2.y = d of both blocks for rows g, g+8
+//  Q4_0 / Q4_1 / Q5_0 / Q5_1: u0 = qs unit of block pair q; u2 = d of blocks 2q, 2q+1 for
+//        rows g, g+8, then m (Q4_1 / Q5_1) the same way; u1 = qh words (Q5_x) of
+//        (row g: blocks 2q, 2q+1), (row g+8: blocks 2q, 2q+1)
 struct Packed {
   uint4 u0, u1, u2, u3;
 };
@@ -268,11 +271,24 @@ __device__ __forceinline__ void fetch_packed(int qt, const uint8_t* ch, int q, i
     pk.u3.x = ldg32(ch + 3072 + 32 * g + 8 * n + 4 * odd);
     pk.u3.y = ldg32(ch + 3072 + 32 * g + 16 + 8 * n + 4 * odd);
     pk.u3.z = ldg32(ch + 3328 + 4 * g);
-  } else {
+  } else if (qt == kQ8_0) {
     pk.u0 = ldg128(ch + 512 * (2 * q) + 16 * lane);
     pk.u1 = ldg128(ch + 512 * (2 * q + 1) + 16 * lane);
     pk.u2.x = ldg32(ch + 4096 + 32 * g + 4 * q);
     pk.u2.y = ldg32(ch + 4096 + 32 * g + 16 + 4 * q);
+  } else {
+    const Q4xFields f = q4x_fields(qt);
+    pk.u0 = ldg128(ch + 512 * q + 16 * lane);
+    pk.u2.x = ldg32(ch + f.d + 32 * g + 4 * q);
+    pk.u2.y = ldg32(ch + f.d + 32 * g + 16 + 4 * q);
+    if (f.m >= 0) {
+      pk.u2.z = ldg32(ch + f.m + 32 * g + 4 * q);
+      pk.u2.w = ldg32(ch + f.m + 32 * g + 16 + 4 * q);
+    }
+    if (f.qh >= 0) {
+      const uint2 h0 = ldg64(ch + f.qh + 64 * g + 8 * q), h1 = ldg64(ch + f.qh + 64 * g + 32 + 8 * q);
+      pk.u1 = make_uint4(h0.x, h0.y, h1.x, h1.y);
+    }
   }
 }
 
@@ -425,6 +441,42 @@ __device__ __forceinline__ void deq_q80(const Packed& pk, int lane, uint8_t* tw)
         const int bb = g0 ^ n0;
         st_piece(tw, hi, g, t, 4 * bb + 2 * h + (t >> 1),
                  scale4_mul((bb ? w1 : w0) ^ 0x80808080u, bias8, n0 ? dB : dA));
+      }
+    }
+  }
+}
+
+// Q4_0 / Q4_1 / Q5_0 / Q5_1: k-block q = blocks 2q, 2q+1 (gguf.py:310-353).
+// Unit word 2bb + hi: row g+8hi of block bb, qs bytes 4t..+3, whose low
+// nibbles are elements 4t..+3 and high nibbles 16+4t..+3; the fifth bit of
+// element e is bit e of the block's qh word.
+template <int QT>
+__device__ __forceinline__ void deq_q4x(const Packed& pk, int lane, uint8_t* tw) {
+  constexpr bool kH = QT == kQ5_0 || QT == kQ5_1, kM = QT == kQ4_1 || QT == kQ5_1;
+  const int g = lane >> 2, t = lane & 3, g0 = g & 1;
+  const uint4 U = pk.u0;
+  // q - 8 (Q4_0), q - 16 (Q5_0) or q from the bytes 2^23 + q
+  const uint64_t bias = splat2(QT == kQ4_0 ? -8388616.f : QT == kQ5_0 ? -8388624.f : -8388608.f);
+#pragma unroll
+  for (int hi = 0; hi < 2; ++hi) {
+    const uint32_t dw = hi ? pk.u2.y : pk.u2.x, mw = hi ? pk.u2.w : pk.u2.z;
+    const uint64_t dA = splat2(g0 ? f16hi(dw) : f16lo(dw)), dB = splat2(g0 ? f16lo(dw) : f16hi(dw));
+    uint64_t mA = 0, mB = 0;
+    if (kM) mA = splat2(g0 ? f16hi(mw) : f16lo(mw)), mB = splat2(g0 ? f16lo(mw) : f16hi(mw));
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll
+      for (int n0 = 0; n0 < 2; ++n0) {
+        const int bb = g0 ^ n0;
+        const uint32_t w = bb ? (hi ? U.w : U.z) : (hi ? U.y : U.x);
+        uint32_t wq = (w >> (4 * half)) & 0x0F0F0F0Fu;
+        if (kH) {
+          const uint32_t h = hi ? (bb ? pk.u1.w : pk.u1.z) : (bb ? pk.u1.y : pk.u1.x);
+          wq |= ((h >> (16 * half + 4 * t)) & 15u) * 0x02040810u & 0x10101010u;
+        }
+        const int c = 4 * bb + 2 * half + (t >> 1);
+        if (kM) st_piece(tw, hi, g, t, c, scale4_fma(wq, bias, n0 ? dB : dA, n0 ? mB : mA));
+        else st_piece(tw, hi, g, t, c, scale4_mul(wq, bias, n0 ? dB : dA));
       }
     }
   }
@@ -827,7 +879,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         if (cur.qt == kQ4_K) deq_q4k<false>(pk, kb & 3, lane, tw);
         else if (cur.qt == kQ5_K) deq_q4k<true>(pk, kb & 3, lane, tw);
         else if (cur.qt == kQ6_K) deq_q6k(pk, kb & 3, lane, tw);
-        else deq_q80(pk, lane, tw);
+        else if (cur.qt == kQ8_0) deq_q80(pk, lane, tw);
+        else if (cur.qt == kQ4_0) deq_q4x<kQ4_0>(pk, lane, tw);
+        else if (cur.qt == kQ4_1) deq_q4x<kQ4_1>(pk, lane, tw);
+        else if (cur.qt == kQ5_0) deq_q4x<kQ5_0>(pk, lane, tw);
+        else deq_q4x<kQ5_1>(pk, lane, tw);
       } else {
         zero_rows16(tw, lane);  // row tile past n_rows
       }

@@ -1,5 +1,6 @@
 // gemv.cu — decode GEMV y[B, N] = x[B, K] . dequant(W)^T over TILED GGUF
-// weights (Q8_0 / Q4_K / Q6_K), 1 <= B <= 32, several weights per launch.
+// weights (Q4_0 / Q4_1 / Q5_0 / Q5_1 / Q8_0 / Q4_K / Q5_K / Q6_K), 1 <= B <= 32,
+// several weights per launch.
 //
 // Replaces the reference's decode linear: executor._linear
 // (draco/runtime/cpu/executor.py:47-79) -> GenericGemmKernel.matmul_f32
@@ -51,10 +52,12 @@
 //    before reusing it.
 //  * Warps 0-15 consume: warp w owns row tile (w % 8) of the slabs whose
 //    parity is w / 8.  The quants enter the int8 tensor-core MMA
-//    (m16n8k32, u8 x s8 -> s32) as they are: Q4_K nibbles with one mask,
-//    Q6_K as ql | qh << 4, Q8_0 bytes unchanged; each activation digit is one
-//    MMA column.  Integer accumulation is exact; the sub-block scale and
-//    Q4_K's min / Q6_K's -32 offset are applied in fp32 per sub-block:
+//    (m16n8k32, u8 x s8 -> s32) as they are: Q4_K / Q4_0 / Q4_1 nibbles with
+//    one mask, Q5_x nibbles with their fifth bit or-ed in, Q6_K as
+//    ql | qh << 4, Q8_0 bytes unchanged; each activation digit is one MMA
+//    column.  Integer accumulation is exact; the (sub-)block scale and the
+//    min / offset (Q4_K's and Q5_K's min, Q6_K's -32, Q4_0's -8, Q5_0's -16,
+//    Q4_1's and Q5_1's m) are applied in fp32 per (sub-)block:
 //        y += d_sc * u * (256 * C_hi + C_lo) - d_min_m * S
 //    The activation rounding (one step of u) bounds the result error at
 //    about 5e-5 relative L2 for Gaussian activations.
@@ -687,6 +690,97 @@ __device__ __forceinline__ void chunk_q80(const uint8_t* ch, const uint8_t* xs, 
   }
 }
 
+// fifth bits of four quants at bit 4 of each byte: bit i of the 4-bit x goes
+// to byte i (the four shifted copies of x do not overlap, so no carries)
+__device__ __forceinline__ uint32_t spread4(uint32_t x) { return (x * 0x02040810u) & 0x10101010u; }
+
+// Q4_0 / Q4_1 / Q5_0 / Q5_1 (gguf.py:310-353).  Per block of 32 the quant q
+// (0..15, or 0..31 with the fifth bit) gives w = d * q + c with c = -8 d
+// (Q4_0), -16 d (Q5_0) or m (Q4_1, Q5_1), so a block adds
+//   d * u * (q . X) + c * S
+// to the row: X the activation digits, S = u * sum(X) the group sum.  A lane's
+// word of a block row holds qs bytes 4t..4t+3: the low nibbles are the MMA's
+// k columns 4t..4t+3, the high nibbles its columns 16+4t..16+4t+3.
+template <int QT, int G, int NT>
+__device__ __forceinline__ void chunk_q4x(const uint8_t* ch, const uint8_t* xs, const uint8_t* su, int lane,
+                                          float (&acc)[NT][2]) {
+  constexpr bool kH = QT == kQ5_0 || QT == kQ5_1;  // fifth bit in qh
+  constexpr bool kM = QT == kQ4_1 || QT == kQ5_1;  // fp16 m per block
+  constexpr int kD = kH ? 2560 : 2048, kQh = 2048, kMo = kD + 256;
+  constexpr float kOff = QT == kQ4_0 ? -8.f : -16.f;  // c / d without m
+  const int g = lane >> 2, t = lane & 3;
+  // the 8 fp16 d (and m) of row g, then those of row g + 8
+  const uint4 dv0 = lds128(ch + kD + 32 * g), dv1 = lds128(ch + kD + 32 * g + 16);
+  uint4 mv0 = make_uint4(0, 0, 0, 0), mv1 = mv0;
+  if constexpr (kM) mv0 = lds128(ch + kMo + 32 * g), mv1 = lds128(ch + kMo + 32 * g + 16);
+  auto half_of = [](const uint4& v, int b) {
+    const uint32_t w = b < 2 ? (b == 0 ? v.x : v.x >> 16) : b < 4 ? (b == 2 ? v.y : v.y >> 16)
+                     : b < 6 ? (b == 4 ? v.z : v.z >> 16) : (b == 6 ? v.w : v.w >> 16);
+    return f16_bits_to_f32(w);
+  };
+  // the four A operands of block b (pair word v): rows g / g+8, columns
+  // 4t.. / 16+4t..
+  auto operands = [&](const uint4& v, int b, uint32_t (&a)[4]) {
+    const uint32_t w0 = (b & 1) ? v.z : v.x, w1 = (b & 1) ? v.w : v.y;
+    a[0] = w0 & kNib, a[1] = w1 & kNib, a[2] = (w0 >> 4) & kNib, a[3] = (w1 >> 4) & kNib;
+    if constexpr (kH) {
+      const uint32_t h0 = lds32(ch + kQh + 64 * g + 4 * b), h1 = lds32(ch + kQh + 64 * g + 32 + 4 * b);
+      a[0] |= spread4((h0 >> (4 * t)) & 15u), a[1] |= spread4((h1 >> (4 * t)) & 15u);
+      a[2] |= spread4((h0 >> (16 + 4 * t)) & 15u), a[3] |= spread4((h1 >> (16 + 4 * t)) & 15u);
+    }
+  };
+  constexpr int kColBytes = 8 * NT * 32;
+  if constexpr (G > 1) {
+    constexpr int Bp = 4 / G, NF = 8 / G;
+    int fr[NF][4];
+#pragma unroll
+    for (int pr = 0; pr < 4; ++pr) {
+      const uint4 v = lds128(ch + 512 * pr + 16 * lane);
+#pragma unroll
+      for (int bo = 0; bo < 2; ++bo) {
+        const int bk = 2 * pr + bo;
+        uint32_t a[4];
+        operands(v, bk, a);
+        const uint2 bx = lds64(xs + bk * kColBytes + lane * 8);
+        if (bk % G == 0) imma_u8_k32_first(fr[bk / G], a[0], a[1], a[2], a[3], bx.x, bx.y);
+        else imma_u8_k32(fr[bk / G], a[0], a[1], a[2], a[3], bx.x, bx.y);
+      }
+    }
+    const int b = t % Bp;
+#pragma unroll
+    for (int f = 0; f < NF; ++f) {
+      const int bk = f * G + t / Bp;  // this lane's block in accumulator f
+      const float d0 = half_of(dv0, bk), d1 = half_of(dv1, bk);
+      const float c0 = kM ? half_of(mv0, bk) : kOff * d0, c1 = kM ? half_of(mv1, bk) : kOff * d1;
+      const float4 s = lds128f(su + (bk * 4 + b) * 16);  // (S_half0, S_half1, u, S)
+      acc[0][0] = fmaf(d0 * s.z, digits(fr[f][0], fr[f][1]), fmaf(c0, s.w, acc[0][0]));
+      acc[0][1] = fmaf(d1 * s.z, digits(fr[f][2], fr[f][3]), fmaf(c1, s.w, acc[0][1]));
+    }
+  } else {
+#pragma unroll
+    for (int pr = 0; pr < 4; ++pr) {
+      const uint4 v = lds128(ch + 512 * pr + 16 * lane);
+#pragma unroll
+      for (int bo = 0; bo < 2; ++bo) {
+        const int bk = 2 * pr + bo;
+        uint32_t a[4];
+        operands(v, bk, a);
+        const float d0 = half_of(dv0, bk), d1 = half_of(dv1, bk);
+        const float c0 = kM ? half_of(mv0, bk) : kOff * d0, c1 = kM ? half_of(mv1, bk) : kOff * d1;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint2 bx = lds64(xs + bk * kColBytes + nt * 256 + lane * 8);
+          const float4 s = lds128f(su + (bk * 4 * NT + 4 * nt + t) * 16);
+          int c[4];
+          imma_u8_k32_first(c, a[0], a[1], a[2], a[3], bx.x, bx.y);
+          acc[nt][0] = fmaf(d0 * s.z, digits(c[0], c[1]), fmaf(c0, s.w, acc[nt][0]));
+          acc[nt][1] = fmaf(d1 * s.z, digits(c[2], c[3]), fmaf(c1, s.w, acc[nt][1]));
+        }
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // output of one row group
 // ---------------------------------------------------------------------------
@@ -886,7 +980,8 @@ __device__ __forceinline__ bool consume_segment(const GemvParams& P, const uint8
       const uint8_t* su = xs + P.xs_bytes;
       if (QT == kQ4_K || QT == kQ5_K) chunk_q4k<QT, G, NT>(ch, xs, su, lane, acc);
       else if (QT == kQ6_K) chunk_q6k<G, NT>(ch, xs, su, lane, acc);
-      else chunk_q80<G, NT>(ch, xs, su, lane, acc);
+      else if (QT == kQ8_0) chunk_q80<G, NT>(ch, xs, su, lane, acc);
+      else chunk_q4x<QT, G, NT>(ch, xs, su, lane, acc);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty_bar[st]);
@@ -1109,8 +1204,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     else if (pr.qt == kQ6_K)
       ok = consume_segment<kQ6_K, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
                                          pr.cb, lane, abort, acc);
-    else
+    else if (pr.qt == kQ8_0)
       ok = consume_segment<kQ8_0, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
+                                         pr.cb, lane, abort, acc);
+    else if (pr.qt == kQ4_0)
+      ok = consume_segment<kQ4_0, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
+                                         pr.cb, lane, abort, acc);
+    else if (pr.qt == kQ4_1)
+      ok = consume_segment<kQ4_1, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
+                                         pr.cb, lane, abort, acc);
+    else if (pr.qt == kQ5_0)
+      ok = consume_segment<kQ5_0, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
+                                         pr.cb, lane, abort, acc);
+    else
+      ok = consume_segment<kQ5_1, G, NT>(P, smem, ready_bar + par, empty_bar, i_first, i0 + seg, NS, rw, nrt,
                                          pr.cb, lane, abort, acc);
     if (!ok || !finish_rowgroup<G, NT, TP>(P, cur.p, cur.rg, L++, s_begin, s_end, warp, lane, acc, mb, abort))
       break;

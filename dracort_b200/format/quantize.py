@@ -1,4 +1,5 @@
-"""Synthetic GGUF encoders (numpy) for Q8_0, Q4_K, Q5_K and Q6_K.
+"""Synthetic GGUF encoders (numpy) for Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K,
+Q5_K and Q6_K.
 
 The reference ships no GGUF K-quant quantizer (draco/format/gguf.py only
 decodes), so these encoders are written from the block formats that
@@ -8,6 +9,12 @@ gguf.py:_dequantize decodes:
   reference's own test encoder uses (tests/format/test_gguf.py:145-155): per
   32-element block, d = max|w| / 127 stored as fp16, q = clip(rint(w / d),
   -127, 127).
+* Q4_0 / Q5_0 — per 32-element block d = max|w| / 8 (/ 16), q = rint(w / d)
+  + 8 (+ 16) clipped to 4 (5) bits; Q4_1 / Q5_1 — per block the affine fit
+  m = min w, d = (max - min) / 15 (/ 31), q = rint((w - m) / d).  Element e
+  goes to the low nibble of qs byte e (e < 16) or the high nibble of byte
+  e - 16, its fifth bit to bit e of the little-endian qh word
+  (gguf.py:310-353).
 * Q4_K — per 32-element sub-block an affine fit (scale = (max - min) / 15,
   min clipped at 0), the 8 scales and mins quantized to 6 bits against the
   super-block's fp16 d and dmin (d = max scale / 63, dmin = max min / 63), then
@@ -30,7 +37,11 @@ import numpy as np
 
 from dracort_b200.format.gguf_types import (
     BLOCK_LAYOUTS,
+    GGML_TYPE_Q4_0,
+    GGML_TYPE_Q4_1,
     GGML_TYPE_Q4_K,
+    GGML_TYPE_Q5_0,
+    GGML_TYPE_Q5_1,
     GGML_TYPE_Q5_K,
     GGML_TYPE_Q6_K,
     GGML_TYPE_Q8_0,
@@ -59,6 +70,45 @@ def encode_q8_0(w: np.ndarray) -> np.ndarray:
     out[:, 0:2] = _f16_bytes(d)
     out[:, 2:34] = qs.view(np.uint8)
     return out.reshape(n_rows, (k // 32) * 34)
+
+
+def encode_q4_legacy(qtype: int, w: np.ndarray) -> np.ndarray:
+    """[n_rows, k] float -> packed uint8 [n_rows, k/32*bb] for Q4_0, Q4_1,
+    Q5_0 or Q5_1 (fields d, m, qh, qs as gguf.py:310-353 decodes them)."""
+    affine = qtype in (GGML_TYPE_Q4_1, GGML_TYPE_Q5_1)
+    bits = 5 if qtype in (GGML_TYPE_Q5_0, GGML_TYPE_Q5_1) else 4
+    if qtype not in (GGML_TYPE_Q4_0, GGML_TYPE_Q4_1, GGML_TYPE_Q5_0, GGML_TYPE_Q5_1):
+        raise ValueError(f"ggml type {qtype} is not a 32-element 4/5-bit type")
+    w = np.asarray(w, dtype=np.float32)
+    n_rows, k = w.shape
+    if k % 32:
+        raise ValueError("32-element block types need k % 32 == 0")
+    a = w.reshape(-1, 32)
+    nb = a.shape[0]
+    top = (1 << bits) - 1
+    with np.errstate(divide="ignore", invalid="ignore"):
+        if affine:
+            m = a.min(axis=1).astype(np.float16).astype(np.float32)
+            d = ((a.max(axis=1) - m) / np.float32(top)).astype(np.float16).astype(np.float32)
+            q = np.where(d[:, None] > 0, np.rint((a - m[:, None]) / d[:, None]), 0)
+        else:
+            half = 1 << (bits - 1)
+            d = (np.abs(a).max(axis=1) / np.float32(half)).astype(np.float16).astype(np.float32)
+            q = np.where(d[:, None] > 0, np.rint(a / d[:, None]), 0) + half
+    q = np.clip(q, 0, top).astype(np.uint8)
+    bb = BLOCK_LAYOUTS[qtype][1]
+    out = np.empty((nb, bb), dtype=np.uint8)
+    out[:, 0:2] = _f16_bytes(d)
+    pos = 2
+    if affine:
+        out[:, 2:4] = _f16_bytes(m)
+        pos = 4
+    if bits == 5:
+        qh = (((q >> 4) & 1).astype(np.uint32) << np.arange(32, dtype=np.uint32)).sum(axis=1, dtype=np.uint32)
+        out[:, pos:pos + 4] = qh.astype("<u4").view(np.uint8).reshape(nb, 4)
+        pos += 4
+    out[:, pos:pos + 16] = (q[:, :16] & 15) | ((q[:, 16:] & 15) << 4)
+    return out.reshape(n_rows, (k // 32) * bb)
 
 
 def _q4k_pack_scales(sc: np.ndarray, m: np.ndarray) -> np.ndarray:
@@ -218,6 +268,8 @@ def encode(qtype: int, w: np.ndarray, q6k_order: str = Q6K_D_FIRST) -> np.ndarra
     """Encode a float [n_rows, k] matrix into packed GGUF blocks of `qtype`."""
     if qtype == GGML_TYPE_Q8_0:
         return encode_q8_0(w)
+    if qtype in (GGML_TYPE_Q4_0, GGML_TYPE_Q4_1, GGML_TYPE_Q5_0, GGML_TYPE_Q5_1):
+        return encode_q4_legacy(qtype, w)
     if qtype == GGML_TYPE_Q4_K:
         return encode_q4_k(w)
     if qtype == GGML_TYPE_Q5_K:

@@ -195,7 +195,8 @@ def load_gguf(source: Union[str, GGUFFile], device: Union[str, torch.device] = "
               chunk_bytes: int = 64 << 20) -> Dict[str, Union[DeviceWeight, torch.Tensor]]:
     """Load tensors of a GGUF file onto one GPU.
 
-    names  : tensors to load (default: all); quantized ones (Q8_0, Q4_K, Q5_K, Q6_K)
+    names  : tensors to load (default: all); quantized ones (Q4_0, Q4_1, Q5_0, Q5_1,
+             Q8_0, Q4_K, Q5_K, Q6_K)
              become DeviceWeight (TILED layout), dense ones (F32/F16/BF16)
              torch tensors of their own dtype (skipped when dense=False).
     shards : per-name Shard for tensor-parallel ranks (others load whole).

@@ -27,7 +27,7 @@ import torch.nn.functional as F
 
 from dracort_b200 import gguf_ops as G
 from dracort_b200.exceptions import DracoFormatError
-from dracort_b200.format.gguf_types import GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0
+from dracort_b200.format.gguf_types import GGML_TYPE_Q6_K, SUPPORTED_TYPES_TEXT, TYPE_NAMES
 from dracort_b200.quantization.gguf import GEMV_MAX_ROWS, PREFILL_MIN_ROWS, GGUFLinear, gguf_linear
 
 
@@ -97,8 +97,7 @@ def fused_rms_norm_linear(x: torch.Tensor, norm_weight: torch.Tensor, eps: float
     return [o.reshape(*x.shape[:-1], o.shape[-1]) for o in outs]
 
 
-_TYPE_OF_NAME = {"gguf_q8_0": GGML_TYPE_Q8_0, "gguf_q4_k": GGML_TYPE_Q4_K, "gguf_q5_k": GGML_TYPE_Q5_K,
-                 "gguf_q6_k": GGML_TYPE_Q6_K}
+_TYPE_OF_NAME = {"gguf_" + n.lower(): t for t, n in TYPE_NAMES.items()}
 
 
 class GGUFGemmKernel:
@@ -106,7 +105,7 @@ class GGUFGemmKernel:
 
     ``matmul(activation, tensor_info, payload_bytes)`` takes a tensor
     description with ``ggml_type`` (a ``GgufTensorInfo``, gguf.py:505-520) or a
-    ``quantization`` name ``gguf_q8_0`` / ``gguf_q4_k`` / ``gguf_q6_k``, and
+    ``quantization`` name ``gguf_<type>`` (``gguf_q4_0`` ... ``gguf_q6_k``), and
     ``shape == (n_rows, k)``; the payload is the tensor's packed GGUF bytes
     (Q6_K in the reference's byte order unless ``q6k_order="d_last"``).  The
     regrouped weight is cached per (name, offset), up to ``cache_bytes`` of
@@ -141,13 +140,13 @@ class GGUFGemmKernel:
 
     def _qtype(self, tensor_info) -> int:
         qt = getattr(tensor_info, "ggml_type", None)
-        if qt in (GGML_TYPE_Q8_0, GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K):
+        if qt in TYPE_NAMES:
             return int(qt)
         q = getattr(tensor_info, "quantization", None)
         if q in _TYPE_OF_NAME:
             return _TYPE_OF_NAME[q]
         raise DracoFormatError(f"GGUFGemmKernel: tensor type {qt!r} / {q!r} is not a supported GGUF type "
-                               f"(Q8_0, Q4_K, Q5_K, Q6_K)")
+                               f"({SUPPORTED_TYPES_TEXT})")
 
     def _tiled(self, tensor_info, qtype: int, payload_bytes, n_rows: int, k: int) -> torch.Tensor:
         key = (getattr(tensor_info, "name", None), getattr(tensor_info, "offset", None))

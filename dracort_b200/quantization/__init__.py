@@ -7,7 +7,7 @@ backends into any registry with a ``register(name, backend)`` method — the
 reference's own ``draco.quantization.QUANT_REGISTRY`` included.
 """
 
-from dracort_b200.format.gguf_types import GGML_TYPE_Q4_K, GGML_TYPE_Q5_K, GGML_TYPE_Q6_K, GGML_TYPE_Q8_0, Q6K_D_LAST
+from dracort_b200.format.gguf_types import GGML_TYPE_Q6_K, Q6K_D_LAST, TYPE_NAMES
 from dracort_b200.quantization.base import QuantizationBackend
 from dracort_b200.quantization.gguf import GGUFBackend, GGUFLinear, gguf_linear
 from dracort_b200.quantization.registry import QUANT_REGISTRY, QuantizationRegistry
@@ -15,8 +15,7 @@ from dracort_b200.quantization.registry import QUANT_REGISTRY, QuantizationRegis
 
 def gguf_backends():
     """Fresh instances of every GGUF backend, keyed by registry name."""
-    bes = [GGUFBackend(GGML_TYPE_Q8_0), GGUFBackend(GGML_TYPE_Q4_K), GGUFBackend(GGML_TYPE_Q5_K), GGUFBackend(GGML_TYPE_Q6_K),
-           GGUFBackend(GGML_TYPE_Q6_K, q6k_order=Q6K_D_LAST)]
+    bes = [GGUFBackend(qt) for qt in TYPE_NAMES] + [GGUFBackend(GGML_TYPE_Q6_K, q6k_order=Q6K_D_LAST)]
     return {b.name: b for b in bes}
 
 

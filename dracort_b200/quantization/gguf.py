@@ -1,14 +1,14 @@
 """GGUF quantization backend and drop-in linear module (CUDA, sm_100a).
 
 ``GGUFBackend`` implements the QuantizationBackend contract
-(draco/quantization/base.py:17-133) for the GGUF block formats Q8_0, Q4_K and
-Q6_K, with the payload layout the reference decodes (draco/format/gguf.py:
+(draco/quantization/base.py:17-133) for the GGUF block formats Q4_0, Q4_1,
+Q5_0, Q5_1, Q8_0, Q4_K, Q5_K and Q6_K, with the payload layout the reference decodes (draco/format/gguf.py:
 _BLOCK_LAYOUTS :75-87, _dequantize :272-497):
 
 * ``weights`` is the packed uint8 payload of a GGUF tensor, shaped
   [n_rows, k / block_size * block_bytes]; ``scales``/``zeros`` are not used
   (GGUF interleaves them inside each block) and must be None;
-* ``group_size`` is the block size (32 for Q8_0, 256 for the K-quants).
+* ``group_size`` is the block size (32 for Q4_0 ... Q8_0, 256 for the K-quants).
 
 ``dequantize`` returns the fp32 weight bit-identical to gguf._dequantize.
 ``quantized_linear`` runs the fused dequant kernels: the weight is regrouped
@@ -38,17 +38,23 @@ from dracort_b200 import gguf_ops as G
 from dracort_b200.exceptions import DracoFormatError, KernelError
 from dracort_b200.format.gguf_types import (
     BLOCK_LAYOUTS,
+    GGML_TYPE_Q4_0,
+    GGML_TYPE_Q4_1,
     GGML_TYPE_Q4_K,
+    GGML_TYPE_Q5_0,
+    GGML_TYPE_Q5_1,
     GGML_TYPE_Q5_K,
     GGML_TYPE_Q6_K,
     GGML_TYPE_Q8_0,
     Q6K_D_FIRST,
     Q6K_D_LAST,
+    SUPPORTED_TYPES_TEXT,
     TYPE_NAMES,
 )
 from dracort_b200.quantization.base import QuantizationBackend
 
-_BITS = {GGML_TYPE_Q8_0: 8, GGML_TYPE_Q4_K: 4, GGML_TYPE_Q5_K: 5, GGML_TYPE_Q6_K: 6}
+_BITS = {GGML_TYPE_Q4_0: 4, GGML_TYPE_Q4_1: 4, GGML_TYPE_Q5_0: 5, GGML_TYPE_Q5_1: 5, GGML_TYPE_Q8_0: 8,
+         GGML_TYPE_Q4_K: 4, GGML_TYPE_Q5_K: 5, GGML_TYPE_Q6_K: 6}
 
 #: largest activation row count handled by one GEMV launch
 GEMV_MAX_ROWS = N.GEMV_MAX_BATCH
@@ -111,7 +117,7 @@ class GGUFBackend(QuantizationBackend):
 
     def __init__(self, qtype: int, q6k_order: str = Q6K_D_FIRST) -> None:
         if qtype not in _BITS:
-            raise DracoFormatError(f"GGUF type {qtype} has no GPU kernel here (supported: Q8_0, Q4_K, Q5_K, Q6_K)")
+            raise DracoFormatError(f"GGUF type {qtype} has no GPU kernel here (supported: {SUPPORTED_TYPES_TEXT})")
         if q6k_order not in (Q6K_D_FIRST, Q6K_D_LAST):
             raise ValueError(f"unknown Q6_K field order {q6k_order!r}")
         self.qtype = qtype

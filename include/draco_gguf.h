@@ -38,6 +38,10 @@ extern "C" {
 #endif
 
 /* ggml_type ids, identical to GGML_TYPE_* in draco/format/gguf.py:56-71. */
+#define DRACO_GGML_TYPE_Q4_0 2
+#define DRACO_GGML_TYPE_Q4_1 3
+#define DRACO_GGML_TYPE_Q5_0 6
+#define DRACO_GGML_TYPE_Q5_1 7
 #define DRACO_GGML_TYPE_Q8_0 8
 #define DRACO_GGML_TYPE_Q4_K 12
 #define DRACO_GGML_TYPE_Q5_K 13
@@ -81,7 +85,8 @@ const char* draco_version(void);
 /* Message of the last failing call on this host thread ("" if none). */
 const char* draco_last_error_string(void);
 
-/* (block_size, block_bytes) of a qtype: Q8_0 (32, 34), Q4_K (256, 144),
+/* (block_size, block_bytes) of a qtype: Q4_0 (32, 18), Q4_1 (32, 20),
+ * Q5_0 (32, 22), Q5_1 (32, 24), Q8_0 (32, 34), Q4_K (256, 144),
  * Q5_K (256, 176), Q6_K (256, 210).  Replaces the table lookup _BLOCK_LAYOUTS[qtype]
  * (gguf.py:75-87).  Returns DRACO_ERR_TYPE for other types.  Host only. */
 int draco_gguf_block_geometry(int qtype, int* block_size, int* block_bytes);
@@ -97,7 +102,8 @@ int64_t draco_gguf_tiled_bytes(int qtype, int64_t n_rows, int64_t k);
 
 /* Dequantize a whole weight to fp32, out[n_rows, k] row-major.
  * Bit-exact with draco/format/gguf.py:_dequantize (gguf.py:272-497) for
- * Q8_0 (:300-303), Q4_K and Q5_K (:425-468) and Q6_K (:470-495).
+ * Q8_0 (:300-303), Q4_0 / Q4_1 (:310-324), Q5_0 / Q5_1 (:326-353), Q4_K and
+ * Q5_K (:425-468) and Q6_K (:470-495).
  * `layout` is any DRACO_LAYOUT_*; GGUF layouts need `blocks` 2-byte aligned,
  * TILED needs 16-byte alignment. */
 int draco_gguf_dequant(int qtype, int layout, const void* blocks, float* out,

@@ -9,7 +9,8 @@ the path (sadrasa97/DracoRT, paths relative to that project):
 
 * ``f16_from_u8``      — draco/format/gguf.py:256-259 (_f16_from_u8)
 * ``dequantize``       — draco/format/gguf.py:272-497 (_dequantize), branches
-  Q8_0 (:300-303), Q4_K and Q5_K (:425-468, _scale_min :436-442), Q6_K (:470-495),
+  Q8_0 (:300-303), Q4_0 / Q4_1 (:310-324), Q5_0 / Q5_1 (:326-353), Q4_K and
+  Q5_K (:425-468, _scale_min :436-442), Q6_K (:470-495),
   plus the argument checks of :284-296.  Each element is produced with the
   same fp32 operations in the same order, so results are bit-identical.
 * ``matmul_f32``       — draco/runtime/cpu/kernels/generic.py:32-33
@@ -33,13 +34,21 @@ from __future__ import annotations
 
 import numpy as np
 
+GGML_TYPE_Q4_0 = 2
+GGML_TYPE_Q4_1 = 3
+GGML_TYPE_Q5_0 = 6
+GGML_TYPE_Q5_1 = 7
 GGML_TYPE_Q8_0 = 8
 GGML_TYPE_Q4_K = 12
 GGML_TYPE_Q5_K = 13
 GGML_TYPE_Q6_K = 14
 
-BLOCK_LAYOUTS = {GGML_TYPE_Q8_0: (32, 34), GGML_TYPE_Q4_K: (256, 144), GGML_TYPE_Q5_K: (256, 176),
-                 GGML_TYPE_Q6_K: (256, 210)}
+BLOCK_LAYOUTS = {GGML_TYPE_Q4_0: (32, 18), GGML_TYPE_Q4_1: (32, 20), GGML_TYPE_Q5_0: (32, 22),
+                 GGML_TYPE_Q5_1: (32, 24), GGML_TYPE_Q8_0: (32, 34), GGML_TYPE_Q4_K: (256, 144),
+                 GGML_TYPE_Q5_K: (256, 176), GGML_TYPE_Q6_K: (256, 210)}
+# 32-element types with 4-bit quants: (has m, has qh) per type
+_LEGACY = {GGML_TYPE_Q4_0: (False, False), GGML_TYPE_Q4_1: (True, False), GGML_TYPE_Q5_0: (False, True),
+           GGML_TYPE_Q5_1: (True, True)}
 
 
 class OracleFormatError(ValueError):
@@ -78,6 +87,24 @@ def dequantize(qtype: int, payload, n: int, q6k_order: str = "d_first") -> np.nd
         d = f16_from_u8(b[:, 0:2])
         qs = b[:, 2:34].view(np.int8).astype(np.float32)
         return (qs * d[:, None]).reshape(-1)
+    if qtype in _LEGACY:
+        # gguf.py:310-353.  Fields in order: d, m (Q4_1 / Q5_1), qh (Q5_x, a
+        # little-endian uint32 whose bit e is the fifth bit of element e),
+        # qs[16]: element e < 16 is the low nibble of byte e, element e >= 16
+        # the high nibble of byte e - 16.
+        has_m, has_h = _LEGACY[qtype]
+        d = f16_from_u8(b[:, 0:2])
+        pos = 2
+        if has_m:
+            m = f16_from_u8(b[:, 2:4])
+            pos = 4
+        q = np.concatenate([b[:, pos + 4 * has_h:] & 15, b[:, pos + 4 * has_h:] >> 4], axis=1).astype(np.int32)
+        if has_h:
+            qh = np.ascontiguousarray(b[:, pos:pos + 4]).view("<u4")[:, 0]
+            q |= ((qh[:, None] >> np.arange(32, dtype=np.uint32)) & 1).astype(np.int32) << 4
+        if has_m:  # q * d + m: the product is exact, one rounding in the add
+            return (q.astype(np.float32) * d[:, None] + m[:, None]).reshape(-1)
+        return ((q - (16 if has_h else 8)).astype(np.float32) * d[:, None]).reshape(-1)
 
     if qtype in (GGML_TYPE_Q4_K, GGML_TYPE_Q5_K):
         # Q5_K (gguf.py:425-468) shares Q4_K's scales; its fifth bits sit in

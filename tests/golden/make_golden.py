@@ -10,7 +10,8 @@ stubs the top-level packages so that draco/__init__.py, which pulls in torch,
 the server and transformers, is not executed).  Every expected output below is
 produced by reference code:
 
-* ``draco.format.gguf._dequantize`` (gguf.py:272-497) for Q8_0 / Q4_K / Q5_K / Q6_K;
+* ``draco.format.gguf._dequantize`` (gguf.py:272-497) for Q8_0 / Q4_K / Q5_K /
+  Q6_K and Q4_0 / Q4_1 / Q5_0 / Q5_1;
 * ``GenericGemmKernel.matmul_f32`` (runtime/cpu/kernels/generic.py:32-33) for
   the linear-layer goldens;
 * the reference test suite's own helpers (tests/format/test_gguf.py): the Q8_0
@@ -89,6 +90,11 @@ def random_blocks(rng, qtype, nb):
         b = rng.integers(0, 256, (nb, 144 if qtype == 12 else 176), dtype=np.uint8)
         b[:, 0:2] = finite_f16(rng, nb).view(np.uint8).reshape(nb, 2)
         b[:, 2:4] = finite_f16(rng, nb).view(np.uint8).reshape(nb, 2)
+    elif qtype in (2, 3, 6, 7):
+        b = rng.integers(0, 256, (nb, {2: 18, 3: 20, 6: 22, 7: 24}[qtype]), dtype=np.uint8)
+        b[:, 0:2] = finite_f16(rng, nb).view(np.uint8).reshape(nb, 2)
+        if qtype in (3, 7):  # m
+            b[:, 2:4] = finite_f16(rng, nb).view(np.uint8).reshape(nb, 2)
     else:
         b = rng.integers(0, 256, (nb, 210), dtype=np.uint8)
         b[:, 0:2] = finite_f16(rng, nb).view(np.uint8).reshape(nb, 2)
@@ -158,6 +164,30 @@ def main() -> None:
     x5 = rng5.standard_normal((3, k)).astype(np.float32)
     out["q5_k_lin_x"] = x5
     out["q5_k_lin_y"] = kern.matmul_f32(x5, w5).astype(np.float32)
+
+    # ---- Q4_0 / Q4_1 / Q5_0 / Q5_1 (own stream; k = 320 leaves a ragged
+    # tail super-block of two 32-element blocks) ----
+    rngl = np.random.default_rng(20261203)
+    for qtype, name in [(2, "q4_0"), (3, "q4_1"), (6, "q5_0"), (7, "q5_1")]:
+        n_rows, k = 6, 320
+        blocks = random_blocks(rngl, qtype, n_rows * k // 32)
+        wl = gguf._dequantize(qtype, blocks.tobytes(), n_rows * k).reshape(n_rows, k)
+        out[f"{name}_packed"] = blocks.reshape(n_rows, -1)
+        out[f"{name}_shape"] = np.array([n_rows, k])
+        out[f"{name}_expected"] = wl.astype(np.float32)
+        xl = rngl.standard_normal((3, k)).astype(np.float32)
+        out[f"{name}_lin_x"] = xl
+        out[f"{name}_lin_y"] = kern.matmul_f32(xl, wl).astype(np.float32)
+        try:  # second opinion: llama.cpp's own decoder
+            import gguf as gguf_pkg
+            from gguf import GGMLQuantizationType
+
+            pkg = gguf_pkg.quants.dequantize(blocks.reshape(n_rows, -1), GGMLQuantizationType(qtype))
+            same = np.array_equal(np.asarray(pkg, np.float32).reshape(n_rows, k).view(np.uint32),
+                                  wl.astype(np.float32).view(np.uint32))
+            print(f"{name}: reference decode {'==' if same else '!='} gguf package decode")
+        except Exception as e:  # pragma: no cover
+            print("gguf package unavailable:", e)
 
     path = HERE / "gguf_golden.npz"
     np.savez_compressed(path, **out)

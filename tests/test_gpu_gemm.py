@@ -22,6 +22,7 @@ from dracort_b200 import gguf_ops as G  # noqa: E402
 from dracort_b200.format import quantize as Q  # noqa: E402
 
 PREFILL_TOL = 5e-3
+ALL = [2, 3, 6, 7, 8, 12, 13, 14]
 
 
 def _case(qtype, m, n, k, seed, ydtype=torch.float32):
@@ -47,13 +48,13 @@ def _check(qtype, packed, xb, tiled, y, n, k, tight=2e-5):
         assert O.rel_l2(got, exact) < tight
 
 
-@pytest.mark.parametrize("qtype", [12, 13, 14, 8])
+@pytest.mark.parametrize("qtype", ALL)
 def test_gemm_one_tile(qtype):
     m, n, k = 256, 128, 256
     _check(qtype, *_case(qtype, m, n, k, seed=qtype), n, k)
 
 
-@pytest.mark.parametrize("qtype", [12, 13, 14, 8])
+@pytest.mark.parametrize("qtype", ALL)
 @pytest.mark.parametrize("m,n,k", [(300, 200, 512), (1, 16, 256), (777, 384, 1024)])
 def test_gemm_ragged(qtype, m, n, k):
     _check(qtype, *_case(qtype, m, n, k, seed=m + n + qtype), n, k)
@@ -67,7 +68,8 @@ def test_gemm_bf16_output():
 
 def test_gemm_grouped_mixed_types():
     rng = np.random.default_rng(8)
-    specs = [(12, 1024, 2048), (14, 512, 2048), (12, 256, 4096), (13, 384, 2048)]
+    specs = [(12, 1024, 2048), (14, 512, 2048), (12, 256, 4096), (13, 384, 2048), (2, 256, 1024), (3, 128, 2048),
+             (6, 384, 512), (7, 256, 1024), (8, 128, 768)]
     m = 600
     probs, refs = [], []
     for qt, n, k in specs:
@@ -85,7 +87,8 @@ def test_gemm_grouped_mixed_types():
         assert O.rel_l2(p.y.cpu().numpy(), r) < PREFILL_TOL
 
 
-@pytest.mark.parametrize("qtype,n,k", [(12, 11008, 4096), (13, 11008, 4096), (14, 4096, 11008)])
+@pytest.mark.parametrize("qtype,n,k", [(12, 11008, 4096), (13, 11008, 4096), (14, 4096, 11008), (2, 11008, 4096),
+                                        (7, 4096, 11008)])
 def test_gemm_prefill_config_shapes(qtype, n, k):
     # config 3: M = 2048 tokens; gate/up N=11008 K=4096, down N=4096 K=11008
     m = 2048

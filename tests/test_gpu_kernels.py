@@ -20,7 +20,9 @@ from dracort_b200 import gguf_ops as G  # noqa: E402
 from dracort_b200.format import quantize as Q  # noqa: E402
 
 GEMV_TOL = 1e-3
-TYPES = [(8, "q8_0"), (12, "q4_k"), (13, "q5_k"), (14, "q6_k")]
+TYPES = [(2, "q4_0"), (3, "q4_1"), (6, "q5_0"), (7, "q5_1"), (8, "q8_0"), (12, "q4_k"), (13, "q5_k"), (14, "q6_k")]
+ALL = [t for t, _ in TYPES]
+SMALL_BLOCK = [2, 3, 6, 7, 8]  # 32-element blocks: k need not be a multiple of 256
 
 
 def dev_bytes(a: np.ndarray) -> "torch.Tensor":
@@ -53,7 +55,7 @@ def test_repack_then_tiled_dequant_is_bit_exact(golden, qtype, name):
     assert bits_equal(got, golden[f"{name}_expected"])
 
 
-@pytest.mark.parametrize("qtype", [8, 12, 13, 14])
+@pytest.mark.parametrize("qtype", ALL)
 @pytest.mark.parametrize("shape", [(1, 256), (17, 512), (130, 768), (300, 2304)])
 def test_dequant_random_shapes(qtype, shape):
     n, k = shape
@@ -69,15 +71,17 @@ def test_dequant_random_shapes(qtype, shape):
     assert np.array_equal(bf, torch.from_numpy(exp).bfloat16().float().numpy())
 
 
-def test_q8_0_row_length_not_multiple_of_256():
+@pytest.mark.parametrize("qtype", SMALL_BLOCK)
+@pytest.mark.parametrize("batch", [1, 3])
+def test_row_length_not_multiple_of_256(qtype, batch):
     n, k = 40, 32 * 13
-    rng = np.random.default_rng(5)
-    packed = Q.encode_q8_0(Q.random_weight(rng, n, k))
-    exp = O.dequantize_matrix(8, packed, n, k)
-    t = G.repack(8, dev_bytes(packed), n, k)
-    assert bits_equal(G.dequantize(8, t, n, k, layout="tiled").cpu().numpy(), exp)
-    x = rng.standard_normal((3, k)).astype(np.float32)
-    y = G.gemv(8, t, torch.from_numpy(x).cuda(), n, k).cpu().numpy()
+    rng = np.random.default_rng(5 + qtype)
+    packed = Q.encode(qtype, Q.random_weight(rng, n, k))
+    exp = O.dequantize_matrix(qtype, packed, n, k)
+    t = G.repack(qtype, dev_bytes(packed), n, k)
+    assert bits_equal(G.dequantize(qtype, t, n, k, layout="tiled").cpu().numpy(), exp)
+    x = rng.standard_normal((batch, k)).astype(np.float32)
+    y = G.gemv(qtype, t, torch.from_numpy(x).cuda(), n, k).cpu().numpy()
     assert O.rel_l2(y, O.matmul_f32(x, exp)) < GEMV_TOL
 
 
@@ -94,7 +98,7 @@ def _gemv_case(qtype, n, k, batch, seed, bias=False, xscale=1.0):
     return y, ref, O.linear_f64(x, qtype, packed, n, k, bias=b)
 
 
-@pytest.mark.parametrize("qtype", [8, 12, 13, 14])
+@pytest.mark.parametrize("qtype", ALL)
 @pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 8, 16, 32])
 def test_gemv_small_batches(qtype, batch):
     y, ref, ref64 = _gemv_case(qtype, 272, 1024, batch, seed=batch * 31 + qtype)
@@ -102,7 +106,7 @@ def test_gemv_small_batches(qtype, batch):
     assert O.rel_l2(y, ref64) < 3e-4  # int8-digit activations: ~6.5e-5 expected for Gaussian x
 
 
-@pytest.mark.parametrize("qtype", [8, 12, 13, 14])
+@pytest.mark.parametrize("qtype", ALL)
 def test_gemv_bias_and_ragged_rows(qtype):
     y, ref, _ = _gemv_case(qtype, 1000, 768, 2, seed=77 + qtype, bias=True)
     assert O.rel_l2(y, ref) < GEMV_TOL
@@ -116,7 +120,8 @@ def test_gemv_activation_range(xscale):
 
 
 @pytest.mark.parametrize("qtype,n,k", [(12, 4096, 4096), (12, 4096, 11008), (13, 4096, 11008), (14, 4096, 11008),
-                                        (8, 4096, 4096)])
+                                        (8, 4096, 4096), (2, 4096, 4096), (3, 11008, 4096), (6, 4096, 11008),
+                                        (7, 4096, 4096)])
 def test_gemv_llama_shapes(qtype, n, k):
     # full-size shapes exercise row groups split between CTAs (stream-K fixup)
     y, ref, _ = _gemv_case(qtype, n, k, 1, seed=n + k + qtype)
@@ -126,7 +131,8 @@ def test_gemv_llama_shapes(qtype, n, k):
 def test_gemv_grouped_mixed_types_is_deterministic():
     rng = np.random.default_rng(9)
     specs = [(12, 4096, 4096), (12, 1024, 4096), (14, 1024, 4096), (12, 4096, 4096),
-             (12, 11008, 4096), (12, 11008, 4096), (14, 4096, 11008), (13, 1024, 4096)]
+             (12, 11008, 4096), (12, 11008, 4096), (14, 4096, 11008), (13, 1024, 4096),
+             (2, 1024, 4096), (3, 512, 2048), (6, 768, 4096), (7, 1024, 1024), (8, 256, 4096)]
     batch = 4
     probs, refs = [], []
     for qt, n, k in specs:

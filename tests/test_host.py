@@ -22,7 +22,8 @@ def test_q8_0_encoder_is_byte_identical_to_reference_test_encoder(golden):
     assert np.array_equal(Q.encode_q8_0(golden["q8_0_enc_w"]), golden["q8_0_enc_packed"])
 
 
-@pytest.mark.parametrize("qtype,tol", [(8, 0.01), (12, 0.12), (13, 0.06), (14, 0.04)])
+@pytest.mark.parametrize("qtype,tol", [(2, 0.12), (3, 0.1), (6, 0.06), (7, 0.05), (8, 0.01), (12, 0.12), (13, 0.06),
+                                      (14, 0.04)])
 def test_encoders_round_trip_through_reference_decoder(qtype, tol):
     rng = np.random.default_rng(qtype)
     w = Q.random_weight(rng, 32, 1024)
@@ -74,8 +75,13 @@ def test_size_queries_need_no_gpu():
     assert lib.draco_gguf_tiled_bytes(14, 17, 512) == 32 * 2 * 210
     assert lib.draco_gguf_tiled_bytes(8, 16, 32 * 13) == 16 * 2 * 8 * 34
     assert lib.draco_gguf_tiled_bytes(13, 4096, 4096) == 4096 * 16 * 176
+    # the 32-element types pad rows to 16 and k to 256 like Q8_0
+    assert lib.draco_gguf_tiled_bytes(2, 17, 32 * 13) == 32 * 2 * 8 * 18
+    assert lib.draco_gguf_tiled_bytes(7, 4096, 4096) == 4096 * 16 * 8 * 24
+    assert lib.draco_gguf_packed_bytes(3, 10, 96) == 10 * 3 * 20
+    assert lib.draco_gguf_packed_bytes(6, 10, 100) == -1
     bs, bb = ctypes.c_int(), ctypes.c_int()
-    for qt in (8, 12, 13, 14):
+    for qt in (2, 3, 6, 7, 8, 12, 13, 14):
         assert lib.draco_gguf_block_geometry(qt, ctypes.byref(bs), ctypes.byref(bb)) == 0
         assert (bs.value, bb.value) == BLOCK_LAYOUTS[qt]
 
@@ -107,7 +113,8 @@ def test_argument_errors_map_to_reference_exceptions():
 def test_registry_contract():
     from dracort_b200.quantization import QUANT_REGISTRY, QuantizationRegistry, register_into
 
-    assert {"gguf_q8_0", "gguf_q4_k", "gguf_q5_k", "gguf_q6_k", "gguf_q6_k_dlast"} <= set(QUANT_REGISTRY.list_methods())
+    assert {"gguf_q4_0", "gguf_q4_1", "gguf_q5_0", "gguf_q5_1", "gguf_q8_0", "gguf_q4_k", "gguf_q5_k", "gguf_q6_k",
+            "gguf_q6_k_dlast"} <= set(QUANT_REGISTRY.list_methods())
     assert QUANT_REGISTRY.get("GGUF_Q4_K").name == "gguf_q4_k"
     assert "gguf_q8_0" in QUANT_REGISTRY and len(QUANT_REGISTRY) >= 4
     with pytest.raises(ValueError, match="gguf_q4_k"):  # names what is registered
@@ -131,7 +138,7 @@ def test_registry_contract():
     # re-registering replaces the entry (with a warning), case-insensitively
     first = r.get("gguf_q8_0")
     register_into(r)
-    assert r.get("GGUF_Q8_0") is not first and len(r) == 5
+    assert r.get("GGUF_Q8_0") is not first and len(r) == 9
 
 
 def test_backend_host_logic():
@@ -145,7 +152,8 @@ def test_backend_host_logic():
     with pytest.raises(DracoFormatError):
         infer_k(12, 100)
     with pytest.raises(DracoFormatError):
-        GGUFBackend(2)
+        GGUFBackend(10)  # Q2_K: decoded by the reference, no GPU kernel here
+    assert GGUFBackend(2).supported_bits == [4] and GGUFBackend(7).name == "gguf_q5_1"
     assert not be.supports_gpu_kernel(torch.device("cpu"))
     with pytest.raises(ValueError, match="CUDA"):
         be.dequantize(torch.zeros((4, 144), dtype=torch.uint8))  # no CPU path

@@ -2,8 +2,10 @@
 
 tests/golden/gguf_golden.npz was produced by the reference itself
 (tests/golden/make_golden.py): draco.format.gguf._dequantize,
-GenericGemmKernel.matmul_f32 (Q8_0, Q4_K, Q5_K, Q6_K), the reference tests' _enc_q8_0 and _ref_q4_k,
-and llama.cpp's gguf package for the Q6_K d-last order.
+GenericGemmKernel.matmul_f32 (Q4_0, Q4_1, Q5_0, Q5_1, Q8_0, Q4_K, Q5_K, Q6_K),
+the reference tests' _enc_q8_0 and _ref_q4_k, and llama.cpp's gguf package for
+the Q6_K d-last order (the same script checks that package's decode of the
+Q4_0 / Q4_1 / Q5_0 / Q5_1 goldens against the reference's).
 """
 
 import numpy as np
@@ -11,7 +13,7 @@ import pytest
 
 from oracle import gguf_oracle as O
 
-TYPES = [(8, "q8_0"), (12, "q4_k"), (13, "q5_k"), (14, "q6_k")]
+TYPES = [(2, "q4_0"), (3, "q4_1"), (6, "q5_0"), (7, "q5_1"), (8, "q8_0"), (12, "q4_k"), (13, "q5_k"), (14, "q6_k")]
 
 
 def bits_equal(a, b):
@@ -49,6 +51,15 @@ def test_oracle_rejects_what_the_reference_rejects():
         O.dequantize(16, b"\x00" * 100, 32)  # unsupported type (gguf.py:284-289)
     with pytest.raises(O.OracleFormatError):
         O.dequantize(12, b"\x00" * 144, 100)  # n not a multiple of the block (gguf.py:291-296)
+
+
+def test_planted_fifth_bit_mistake_is_caught(golden):
+    """Reading the Q5_0 fifth bits in big-endian order must fail the golden check."""
+    n, k = (int(v) for v in golden["q5_0_shape"])
+    b = golden["q5_0_packed"].reshape(-1, 22).copy()
+    b[:, 2:6] = b[:, 2:6][:, ::-1]
+    got = O.dequantize_matrix(6, b, n, k)
+    assert not bits_equal(got, golden["q5_0_expected"])
 
 
 def test_planted_mistake_is_caught(golden):
