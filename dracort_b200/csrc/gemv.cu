@@ -76,58 +76,18 @@
 #include <cstring>
 
 #include "common.cuh"
+#include "gemv_plan.h"
 #include "internal.h"
 
 namespace draco {
 
-constexpr int kMaxCta = 192;
 constexpr int kMaxStages = 8;
-constexpr int kRowWarps = 8;                   // one per row tile of a slab
 constexpr int kConsumerWarps = 2 * kRowWarps;  // even / odd slabs
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kConvWarps = 3;
 constexpr int kThreads = (kConsumerWarps + 1 + kConvWarps) * 32;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far beyond any legitimate wait
 constexpr int kMaxMboxSlots = 4;
 
-struct GemvProbDev {
-  const uint8_t* w;
-  const float* x;
-  float* y;
-  const float* bias;
-  int64_t ldx, ldy;
-  int slab0;  // global index of the problem's first slab
-  int qt, n_rows, k, nb, n_rg, n_tiles, cb;
-  int64_t tp_y_off, tp_par_stride;  // tensor-parallel output block in every rank's exchange buffer
-  int64_t xcv_off;                   // workspace offset of the pre-converted activation slices
-  int in_mode;                       // DRACO_INPUT_*: transform applied as x is read
-  float eps;                         // RMSNORM epsilon
-  const float* aux;                  // RMSNORM: norm weight [k]; SWIGLU: up [batch, k]
-  int64_t ldaux;
-  int64_t rms_off;                   // RMSNORM: workspace offset of the per-row scales [batch]
-};
-
-struct GemvParams {
-  GemvProbDev prob[DRACO_GEMV_MAX_PROBLEMS];
-  uint8_t* ws;
-  int64_t status_off, cnt_off, part_off;
-  int total_slabs;
-  int n_prob, batch, nt, n_cta;
-  int w_stage, xs_bytes, su_bytes, stage_bytes, n_stages;
-  int mbox_slots, mbox_off;  // row-group mailbox after the stages in dynamic shared memory
-  int precvt;                // activations converted by gemv_convert_kernel before the launch
-  int tp_world, tp_rank;     // tensor-parallel exchange (tp_world 0: plain outputs)
-  uint8_t* tp_buf[DRACO_TP_MAX_WORLD];
-  int64_t tp_flags_off, tp_counter_off;
-  int cta_start[kMaxCta + 1];
-};
-
-// workspace layout (bytes)
-constexpr int64_t kWsStatus = 0;
-constexpr int64_t kWsGridDone = 128;  // CTAs finished (tensor-parallel form)
-constexpr int64_t kWsCounters = 256;
-constexpr int64_t kWsCountersBytes = (int64_t)kMaxCta * 2 * kRowWarps * 4;  // per (CTA, end, row tile)
-static inline int64_t align256(int64_t v) { return (v + 255) & ~(int64_t)255; }
 
 // ---------------------------------------------------------------------------
 // small device helpers
@@ -160,14 +120,6 @@ __device__ __forceinline__ void mma_acc(float (&d)[4], uint32_t a0, uint32_t a1,
   mma_f16_16816_acc(d, a0, a1, a2, a3, b0, b1);
 }
 
-__device__ __forceinline__ int rg_tile_count(const GemvProbDev& pr, int rg) {
-  const int r = pr.n_tiles - rg * kGroupTiles;
-  return r < kGroupTiles ? r : kGroupTiles;
-}
-
-__device__ __forceinline__ void record_error(const GemvParams& P, int code) {
-  atomicCAS(reinterpret_cast<int*>(P.ws + P.status_off), 0, code);
-}
 
 // Wait for the barrier phase with the given parity.  Returns false when the CTA
 // has aborted, or when the wait ran out (then this thread records the timeout
@@ -212,28 +164,6 @@ __device__ __forceinline__ bool wait_generation(const GemvParams& P, const int* 
   return true;
 }
 
-// Slab cursor: (problem, row group, super-block) of a global slab index,
-// advanced incrementally.
-struct SlabCursor {
-  int p, rg, j;
-  __device__ void seek(const GemvParams& P, int s) {
-    p = 0;
-    for (int q = 1; q < P.n_prob; ++q)
-      if (s >= P.prob[q].slab0) p = q;
-    const int local = s - P.prob[p].slab0;
-    rg = local / P.prob[p].nb;
-    j = local - rg * P.prob[p].nb;
-  }
-  __device__ void next(const GemvParams& P) {
-    if (++j == P.prob[p].nb) {
-      j = 0;
-      if (++rg == P.prob[p].n_rg) {
-        rg = 0;
-        ++p;
-      }
-    }
-  }
-};
 
 // ---------------------------------------------------------------------------
 // int8 tensor-core MMA (legacy warp-level path, exact int32 accumulation)
@@ -307,19 +237,6 @@ constexpr uint32_t kNibHi = 0xF0F0F0F0u;
 //       (the halves then go to different columns); unused slots hold zeros;
 //   su[m][b] = (S_half0, S_half1, u, S_half0 + S_half1) (all exact).
 // ---------------------------------------------------------------------------
-// 8 consecutive fp32 values at p (16-byte vector loads when aligned); the
-// ones at or past `valid` read as 0
-__device__ __forceinline__ void load8(const float* p, int valid, float (&v)[8]) {
-  if (valid >= 8 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
-    const float4 lo4 = __ldg(reinterpret_cast<const float4*>(p));
-    const float4 hi4 = __ldg(reinterpret_cast<const float4*>(p) + 1);
-    v[0] = lo4.x, v[1] = lo4.y, v[2] = lo4.z, v[3] = lo4.w;
-    v[4] = hi4.x, v[5] = hi4.y, v[6] = hi4.z, v[7] = hi4.w;
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = i < valid ? __ldg(p + i) : 0.f;
-  }
-}
 
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -1262,11 +1179,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 // ---------------------------------------------------------------------------
 // host side: plan + launch
 // ---------------------------------------------------------------------------
-struct HostPlan {
-  GemvParams P;
-  size_t ws_needed;
-  size_t smem_bytes;
-};
 
 static int nt_of_batch(int batch) { return batch <= 4 ? 1 : batch <= 8 ? 2 : batch <= 16 ? 4 : 8; }
 
@@ -1277,8 +1189,8 @@ constexpr int kSmemBudget = 216 * 1024;
 // convert_once: convert the activations once per launch in the dense
 // layouts (batch >= 3); the allocation-free entry keeps the in-kernel
 // conversion, whose scratch needs no activation slices.
-static bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, HostPlan& hp, char* msg,
-                       size_t ml, bool convert_once = true, const draco_gemv_input* inputs = nullptr) {
+bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, HostPlan& hp, char* msg, size_t ml,
+                bool convert_once, const draco_gemv_input* inputs) {
   GemvParams& P = hp.P;
   memset(&P, 0, sizeof(P));
   P.n_prob = n;
@@ -1404,7 +1316,8 @@ size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch) {
   HostPlan local;
   char msg[128];
   if (!build_plan(probs, n, batch, kMaxCta, local, msg, sizeof(msg))) return 0;
-  return local.ws_needed;
+  // one size serves both kernels (the tensor-memory one may take the launch)
+  return std::max(local.ws_needed, gemv_tc_workspace_bytes(probs, n, batch, nullptr));
 }
 
 template <int G, int NT, bool TP>
@@ -1507,6 +1420,8 @@ static int gemv_launch_impl(const draco_gemv_problem* probs, int n, int batch, c
     snprintf(msg, ml, "gemv: workspace must be 256-byte aligned");
     return DRACO_ERR_ALIGN;
   }
+  // batches of 17 and more over K-quants: the tensor-memory kernel
+  if (!ex && gemv_tc_eligible(probs, n, batch)) return gemv_tc_launch(hp, inputs, ws, ws_bytes, st, msg, ml);
   hp.P.ws = static_cast<uint8_t*>(ws);
   if (hp.P.precvt) {
     int units = 0;

@@ -103,7 +103,10 @@ def _gemv_case(qtype, n, k, batch, seed, bias=False, xscale=1.0):
 def test_gemv_small_batches(qtype, batch):
     y, ref, ref64 = _gemv_case(qtype, 272, 1024, batch, seed=batch * 31 + qtype)
     assert O.rel_l2(y, ref) < GEMV_TOL
-    assert O.rel_l2(y, ref64) < 3e-4  # int8-digit activations: ~6.5e-5 expected for Gaussian x
+    # int8-digit activations (warp-MMA kernel): ~6.5e-5 for Gaussian x; fp16
+    # activations (tensor-memory kernel, K-quants from batch 17): ~2e-4
+    tc = batch >= 17 and qtype in (12, 13, 14)
+    assert O.rel_l2(y, ref64) < (6e-4 if tc else 3e-4)
 
 
 @pytest.mark.parametrize("qtype", ALL)
