@@ -316,6 +316,58 @@ def cpu_moe_leg(expert, hidden, ffn, tokens_per_expert, n_experts, seed):
             "threads": torch.get_num_threads()}
 
 
+def pipelined_e2e(dev, x_dev, y_dev, make_run, n_copies, timed, K, warmup):
+    """End-to-end steps through the public API with host buffers, the way a
+    serving loop overlaps them: two device input/output buffer pairs, step i's
+    inputs uploaded from pinned memory on one copy stream while step i-1
+    computes, its outputs downloaded on another.  Every step still moves its
+    own inputs in and its outputs out inside the timed region (the first
+    upload starts after the timing event, the timing ends after the last
+    download).  make_run(x, y) -> [callable per weight copy] launching one
+    step's GEMV on the current stream with inputs x and outputs y.
+    Returns (ms over K steps, h2d bytes per step, d2h bytes per step)."""
+    import torch
+
+    xs = [x_dev, torch.empty_like(x_dev)]
+    ys = [y_dev, torch.empty_like(y_dev)]
+    runs = [make_run(xs[j], ys[j]) for j in range(2)]
+    g = torch.Generator().manual_seed(977)
+    xh = [torch.randn(x_dev.shape, generator=g).pin_memory() for _ in range(2)]
+    yh = [torch.empty(y_dev.shape).pin_memory() for _ in range(2)]
+    comp = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_up = [torch.cuda.Event() for _ in range(2)]
+    ev_comp = [torch.cuda.Event() for _ in range(2)]
+    ev_down = [torch.cuda.Event() for _ in range(2)]
+
+    def steps(n):
+        start = torch.cuda.Event()
+        start.record(comp)
+        up.wait_event(start)
+        down.wait_event(start)
+        for i in range(n):
+            j = i & 1
+            up.wait_event(ev_comp[j])  # step i-2's GEMV has read buffer j
+            with torch.cuda.stream(up):
+                xs[j].copy_(xh[j], non_blocking=True)
+                ev_up[j].record(up)
+            comp.wait_event(ev_up[j])
+            comp.wait_event(ev_down[j])  # step i-2's outputs have left buffer j
+            runs[j][i % n_copies]()
+            ev_comp[j].record(comp)
+            down.wait_event(ev_comp[j])
+            with torch.cuda.stream(down):
+                yh[j].copy_(ys[j], non_blocking=True)
+                ev_down[j].record(down)
+        comp.wait_event(ev_down[0])
+        comp.wait_event(ev_down[1])
+
+    steps(max(3, warmup))
+    torch.cuda.synchronize()
+    ms, _, _ = timed(lambda: steps(K))
+    return ms, xh[0].numel() * 4, yh[0].numel() * 4
+
+
 def q8_0_leg(args, dev, peaks, timed, want_e2e, want_cpu):
     """Config 1: the Q8_0 GEMV, W 4096x4096 (fp16 d = max|w|/127, int8 rint(w/d)
     per 32-element block, as the reference test encoder), x fp32 [1, 4096],
@@ -373,26 +425,20 @@ def q8_0_leg(args, dev, peaks, timed, want_e2e, want_cpu):
                      "traffic": profiled_traffic("gemv_q8_0_config1"),
                      "peak_source": f"{peaks['source']} MEASURED_PEAKS.json hbm_gbs",
                      "kernel": f"gemv_kernel, one launch per step; algorithmic bytes {alg} per step"},
-        "gpu_launches": K,
+        "gpu_launches": plans[0].launches * K,
         "clocks": clocks,
     }
     if want_e2e:
-        xh = torch.randn((1, s.k), generator=g).pin_memory()
-        yh = torch.empty((1, s.n_rows)).pin_memory()
+        def make_run(xd, yd):
+            pls = plans if xd is x else [G.GemvPlan([G.GemvProblem(s.qtype, c, xd, yd, s.n_rows, s.k)]) for c in copies]
+            return [pl.run for pl in pls]
 
-        def e2e_steps(n):
-            for i in range(n):
-                x.copy_(xh, non_blocking=True)
-                plans[i % n_copies].run()
-                yh.copy_(y, non_blocking=True)
-
-        e2e_steps(max(3, args.warmup))
-        torch.cuda.synchronize()
-        ms_e, _, _ = timed(lambda: e2e_steps(K))
+        ms_e, h2d, d2h = pipelined_e2e(dev, x, y, make_run, n_copies, timed, K, args.warmup)
         out["e2e"] = {"value": round(alg / (ms_e / K * 1e-3) / 1e9, 3), "unit": "GB/s",
-                      "h2d_bytes_per_step": xh.numel() * 4, "d2h_bytes_per_step": yh.numel() * 4,
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                       "ms_per_step": round(ms_e / K, 6),
-                      "path": "pinned host x -> cuda -> GemvPlan.run (C ABI) -> pinned host y, eager"}
+                      "path": "pinned host x -> H2D copy stream -> GemvPlan.run (C ABI) -> D2H copy stream -> "
+                              "pinned host y; two buffer pairs, step i's copies overlap its neighbours' GEMVs"}
     if want_cpu:
         per, t_dq = cpu_layer_steps(specs, [packed], 1, args.seed, 3, 200)
         cpu_gbs = alg * len(per) / sum(per) / 1e9
@@ -535,7 +581,9 @@ def model_leg(args, dev, peaks, rank, world, pg, timed):
                       "weights": "per layer q,k,o,gate,up Q4_K; v,down Q6_K (Llama-7B shapes)",
                       "parallelism": f"tp{world}" + (" (in-kernel NVLink exchange + finish kernel per layer)"
                                                      if world > 1 else ""),
-                      "step": "the 7 projections of every layer (one grouped GEMV launch per layer)"},
+                      "step": "the 7 projections of every layer (one grouped GEMV call per layer: the GEMV "
+                              "kernel, after an activation conversion kernel from batch 2, and a partial-sum "
+                              "kernel on the tensor-memory path)"},
            "batches": {}}
     for batch in (1, 32):
         if world == 1:
@@ -549,7 +597,7 @@ def model_leg(args, dev, peaks, rank, world, pg, timed):
             def step():
                 for pl in plans:
                     pl.run()
-            launches = n_layers
+            launches = sum(pl.launches for pl in plans)
             graph = torch.cuda.CUDAGraph()
             for _ in range(3):
                 step()
@@ -768,7 +816,7 @@ def run_ours(args):
         plans = [G.GemvPlan([G.GemvProblem(s.qtype, c[i], xs[i], ys[i], s.n_rows, s.k)
                              for i, s in enumerate(specs_full)]) for c in copies]
         local_bytes = set_bytes
-        gpu_launches_per_step = 1  # the grouped GEMV (activation conversion runs inside it)
+        gpu_launches_per_step = plans[0].launches  # the grouped GEMV (batch 1: one kernel)
 
         def step_fn(i):
             plans[i % n_copies].run()
@@ -873,24 +921,25 @@ def run_ours(args):
     # -- end to end through the public API, host buffers -----------------------
     e2e = None
     if not args.no_e2e and world == 1:
-        xh = torch.randn(xbuf.shape).pin_memory()
-        yh = torch.empty(ybuf.shape).pin_memory()
-        h2d, d2h = xh.numel() * 4, yh.numel() * 4
+        def make_run(xd, yd):
+            if xd is xbuf:
+                return [pl.run for pl in plans]
+            xv, yv, ox, oy = [], [], 0, 0
+            for s in specs_full:
+                xv.append(xd[ox:ox + batch * s.k].view(batch, s.k))
+                yv.append(yd[oy:oy + batch * s.n_rows].view(batch, s.n_rows))
+                ox += batch * s.k
+                oy += batch * s.n_rows
+            return [G.GemvPlan([G.GemvProblem(s.qtype, c[i], xv[i], yv[i], s.n_rows, s.k)
+                                for i, s in enumerate(specs_full)]).run for c in copies]
 
-        def e2e_steps(n):
-            for i in range(n):
-                xbuf.copy_(xh, non_blocking=True)
-                plans[i % n_copies].run()
-                yh.copy_(ybuf, non_blocking=True)
-
-        e2e_steps(max(3, args.warmup))
-        torch.cuda.synchronize()
-        ms_e2e, _, _ = timed(lambda: e2e_steps(K))
+        ms_e2e, h2d, d2h = pipelined_e2e(dev, xbuf, ybuf, make_run, n_copies, timed, K, args.warmup)
         e2e = {"value": round(alg / (ms_e2e / K * 1e-3) / 1e9, 3), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "ms_per_step": round(ms_e2e / K, 5),
-               "path": "pinned host x (one buffer, one copy) -> cuda -> GemvPlan.run (C ABI) -> pinned host y "
-                       "(one buffer, one copy), eager"}
+               "path": "pinned host x (one buffer) -> H2D copy stream -> GemvPlan.run (C ABI) -> D2H copy "
+                       "stream -> pinned host y (one buffer); two buffer pairs, step i's copies overlap its "
+                       "neighbours' GEMVs"}
     elif world > 1 and not args.no_e2e and layer is not None:
         e2e = layer.e2e(K, timed)
         e2e.update({"value": round(alg / (e2e["ms_per_step"] * 1e-3) / 1e9, 3), "unit": "GB/s",

@@ -49,6 +49,7 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_dequant_bf16",
     "draco_gguf_repack",
     "draco_gguf_gemv_workspace_bytes",
+    "draco_gguf_gemv_launch_count",
     "draco_gguf_gemv_grouped",
     "draco_gguf_gemv",
     "draco_gguf_gemv_grouped_ex",
@@ -182,6 +183,8 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_repack.argtypes = [c_int, c_int, vp, vp, i64, i64, vp]
         lib.draco_gguf_gemv_workspace_bytes.restype = ctypes.c_size_t
         lib.draco_gguf_gemv_workspace_bytes.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int]
+        lib.draco_gguf_gemv_launch_count.restype = c_int
+        lib.draco_gguf_gemv_launch_count.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int]
         lib.draco_gguf_gemv_grouped.restype = c_int
         lib.draco_gguf_gemv_grouped.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int, vp, ctypes.c_size_t, vp]
         lib.draco_gguf_gemv_grouped_ex.restype = c_int

@@ -148,6 +148,11 @@ size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* probs, int n_pr
   return gemv_workspace_bytes(probs, n_problems, batch);
 }
 
+int draco_gguf_gemv_launch_count(const draco_gemv_problem* probs, int n_problems, int batch) {
+  if (check_gemv_problems(probs, n_problems, batch, false)) return -1;
+  return gemv_launch_count(probs, n_problems, batch);
+}
+
 int draco_gguf_gemv_grouped(const draco_gemv_problem* probs, int n_problems, int batch, void* workspace,
                             size_t workspace_bytes, void* stream) {
   int rc = check_gemv_problems(probs, n_problems, batch);

@@ -1320,6 +1320,15 @@ size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch) {
   return std::max(local.ws_needed, gemv_tc_workspace_bytes(probs, n, batch, nullptr));
 }
 
+int gemv_launch_count(const draco_gemv_problem* probs, int n, int batch) {
+  HostPlan hp;
+  char msg[128];
+  if (!build_plan(probs, n, batch, device_sm_count(), hp, msg, sizeof(msg))) return -1;
+  if (hp.P.total_slabs == 0) return 0;
+  if (gemv_tc_eligible(probs, n, batch)) return gemv_tc_split_count(hp) > 0 ? 3 : 2;
+  return hp.P.precvt ? 2 : 1;
+}
+
 template <int G, int NT, bool TP>
 static cudaError_t launch_gemv(const HostPlan& hp, cudaStream_t st) {
   static int attr_set[64] = {0};

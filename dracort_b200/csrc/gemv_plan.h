@@ -116,6 +116,8 @@ bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, Hos
 bool gemv_tc_eligible(const draco_gemv_problem* probs, int n, int batch);
 // Workspace bytes it needs (0 when not eligible).
 size_t gemv_tc_workspace_bytes(const draco_gemv_problem* probs, int n, int batch, const draco_gemv_input* inputs);
+// Row groups of the plan split between CTAs (each costs the fixup kernel a CTA).
+int gemv_tc_split_count(const HostPlan& hp);
 // Convert the activations and launch it over the plan's slab ranges; ws has
 // gemv_tc_workspace_bytes bytes, zero at rest.
 int gemv_tc_launch(const HostPlan& hp, const draco_gemv_input* inputs, void* ws, size_t ws_bytes, cudaStream_t st,

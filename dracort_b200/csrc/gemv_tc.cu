@@ -942,6 +942,31 @@ static cudaError_t tc_launch(const TcParams& P, size_t smem, int conv_units, cud
   return cudaLaunchKernelEx(&fcfg, gemv_tc_fixup<NP>, P);
 }
 
+// Row groups whose slabs span more than one CTA's range, into P.split.
+static bool tc_splits(const GemvParams& G, TcParams& P) {
+  auto cta_of = [&](int s) {
+    int c = 0;
+    while (c + 1 < G.n_cta && G.cta_start[c + 1] <= s) ++c;
+    return c;
+  };
+  P.n_split = 0;
+  for (int p = 0; p < G.n_prob; ++p) {
+    const GemvProbDev& d = G.prob[p];
+    for (int rg = 0; rg < d.n_rg; ++rg) {
+      const int a = d.slab0 + rg * d.nb, c0 = cta_of(a), c1 = cta_of(a + d.nb - 1);
+      if (c0 == c1) continue;
+      if (P.n_split == kMaxCta) return false;
+      P.split[P.n_split++] = {p, rg, c0, c1};
+    }
+  }
+  return true;
+}
+
+int gemv_tc_split_count(const HostPlan& hp) {
+  TcParams P;  // only n_split is read
+  return tc_splits(hp.P, P) ? P.n_split : kMaxCta;
+}
+
 int gemv_tc_launch(const HostPlan& hp, const draco_gemv_input* inputs, void* ws, size_t ws_bytes, cudaStream_t st,
                    char* msg, size_t ml) {
   (void)inputs;  // the plan carries the input transforms
@@ -996,24 +1021,9 @@ int gemv_tc_launch(const HostPlan& hp, const draco_gemv_input* inputs, void* ws,
     conv_units += s.nb * L.np + (s.in_mode == DRACO_INPUT_RMSNORM ? G.batch : 0);
   }
   for (int c = 0; c <= G.n_cta; ++c) P.cta_start[c] = G.cta_start[c];
-  // row groups whose slabs span more than one CTA's range
-  auto cta_of = [&](int s) {
-    int c = 0;
-    while (c + 1 < G.n_cta && G.cta_start[c + 1] <= s) ++c;
-    return c;
-  };
-  P.n_split = 0;
-  for (int p = 0; p < G.n_prob; ++p) {
-    const GemvProbDev& d = G.prob[p];
-    for (int rg = 0; rg < d.n_rg; ++rg) {
-      const int a = d.slab0 + rg * d.nb, c0 = cta_of(a), c1 = cta_of(a + d.nb - 1);
-      if (c0 == c1) continue;
-      if (P.n_split == kMaxCta) {
-        snprintf(msg, ml, "gemv: more than %d split row groups", kMaxCta);
-        return DRACO_ERR_ARG;
-      }
-      P.split[P.n_split++] = {p, rg, c0, c1};
-    }
+  if (!tc_splits(G, P)) {
+    snprintf(msg, ml, "gemv: more than %d split row groups", kMaxCta);
+    return DRACO_ERR_ARG;
   }
   P.raw_bytes = (int)align1024(G.w_stage);
   P.stage_bytes = P.raw_bytes + P.bt_bytes;

@@ -17,6 +17,7 @@ cudaError_t launch_repack(int qt, int src_layout, const void* src, void* dst, in
 
 // Grouped GEMV: plan + launch.  Returns a DRACO_* status; fills `msg` on error.
 size_t gemv_workspace_bytes(const draco_gemv_problem* probs, int n, int batch);
+int gemv_launch_count(const draco_gemv_problem* probs, int n, int batch);
 int gemv_launch(const draco_gemv_problem* probs, int n, int batch, void* ws, size_t ws_bytes, cudaStream_t st,
                 char* msg, size_t msg_len, const draco_gemv_input* inputs = nullptr);
 

@@ -269,6 +269,9 @@ class GemvPlan:
         self.device = problems[0].x.device
         self.workspace = torch.zeros(int(need), dtype=torch.uint8, device=self.device)
         self.bytes_weights = sum(tiled_nbytes(p.qtype, p.n_rows, p.k) for p in problems)
+        with torch.cuda.device(self.device):
+            #: kernel launches one run() makes (activation conversion, GEMV, split-row-group sums)
+            self.launches = int(self._lib.draco_gguf_gemv_launch_count(self._arr, len(problems), self.batch))
 
     def run(self) -> None:
         if self._ins is None:

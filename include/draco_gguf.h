@@ -152,10 +152,20 @@ typedef struct draco_gemv_problem {
 size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* problems, int n_problems,
                                        int batch);
 
+/* Number of kernel launches one draco_gguf_gemv_grouped call over these
+ * problems makes on the current device: 1 (batch 1, the GEMV alone), 2 (an
+ * activation conversion kernel first), or 3 (batches 17-32 of K-quants on
+ * the tensor-memory kernel, plus a kernel adding the partial sums of row
+ * groups split between CTAs).  -1 on invalid arguments.  Host only. */
+int draco_gguf_gemv_launch_count(const draco_gemv_problem* problems, int n_problems, int batch);
+
 /* Decode GEMV over 1..DRACO_GEMV_MAX_PROBLEMS weights in one persistent
  * launch (the 7 projections of a decoder layer fit in one call).
- * 1 <= batch <= DRACO_GEMV_MAX_BATCH.  fp32 in, fp32 out.  The quants and the
- * activations meet in int8 tensor-core MMAs with exact integer accumulation;
+ * 1 <= batch <= DRACO_GEMV_MAX_BATCH.  fp32 in, fp32 out.  Batches of 17-32
+ * over K-quants (Q4_K / Q5_K / Q6_K) run on the tensor-memory kernel (fp16
+ * operands scaled per super-block, ~2e-4 relative L2); otherwise the quants
+ * and the activations meet in int8 tensor-core MMAs with exact integer
+ * accumulation;
  * each 32-element group of activations is represented to one step of a
  * power-of-two scale u (max|x| / u in [2^13, 2^14)), which keeps results
  * within ~1e-4 relative L2 of the fp32 oracle (~6.5e-5 for Gaussian inputs).

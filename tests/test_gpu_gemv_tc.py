@@ -165,3 +165,24 @@ def test_tc_and_warp_mma_kernels_agree_with_the_oracle():
     for y in outs:
         assert O.rel_l2(y, ref) < GEMV_TOL
     assert not np.array_equal(outs[0], outs[1])  # two different kernels ran
+
+
+def test_launch_count_query():
+    """draco_gguf_gemv_launch_count matches the kernels each path launches."""
+    rng = np.random.default_rng(2)
+
+    def plan(specs, batch):
+        probs = []
+        for qt, n, k in specs:
+            t = G.repack(qt, dev_bytes(Q.encode(qt, Q.random_weight(rng, n, k))), n, k)
+            probs.append(G.GemvProblem(qt, t, torch.randn((batch, k), device="cuda"),
+                                       torch.empty((batch, n), device="cuda"), n, k))
+        return G.GemvPlan(probs)
+
+    assert plan([(12, 512, 1024)], 1).launches == 1          # warp-MMA kernel alone
+    assert plan([(12, 512, 1024)], 4).launches == 2          # + activation conversion
+    assert plan([(12, 512, 1024), (8, 256, 1024)], 32).launches == 2  # Q8_0 keeps the warp-MMA kernel
+    big = plan([(12, 4096, 4096), (14, 4096, 11008)], 32)   # row groups split between CTAs
+    assert big.launches == 3
+    big.run()
+    assert big.status() == 0
