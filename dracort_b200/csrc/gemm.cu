@@ -253,6 +253,11 @@ __device__ __forceinline__ uint32_t ldg32(const uint8_t* p) {
 struct Packed {
   uint4 u0, u1, u2, u3;
 };
+// kLegacy: the launch holds a Q4_0 / Q4_1 / Q5_0 / Q5_1 weight.  The kernel is
+// compiled once with and once without that code, so the K-quant and Q8_0
+// launches run a dequant loop free of it (with it inlined the config-3
+// prefill lost ~2.5 % through instruction-cache pressure).
+template <bool kLegacy>
 __device__ __forceinline__ void fetch_packed(int qt, const uint8_t* ch, int q, int lane, Packed& pk) {
   const int g = lane >> 2;
   if (qt == kQ4_K || qt == kQ5_K) {
@@ -271,12 +276,12 @@ __device__ __forceinline__ void fetch_packed(int qt, const uint8_t* ch, int q, i
     pk.u3.x = ldg32(ch + 3072 + 32 * g + 8 * n + 4 * odd);
     pk.u3.y = ldg32(ch + 3072 + 32 * g + 16 + 8 * n + 4 * odd);
     pk.u3.z = ldg32(ch + 3328 + 4 * g);
-  } else if (qt == kQ8_0) {
+  } else if (!kLegacy || qt == kQ8_0) {
     pk.u0 = ldg128(ch + 512 * (2 * q) + 16 * lane);
     pk.u1 = ldg128(ch + 512 * (2 * q + 1) + 16 * lane);
     pk.u2.x = ldg32(ch + 4096 + 32 * g + 4 * q);
     pk.u2.y = ldg32(ch + 4096 + 32 * g + 16 + 4 * q);
-  } else {
+  } else if constexpr (kLegacy) {
     const Q4xFields f = q4x_fields(qt);
     pk.u0 = ldg128(ch + 512 * q + 16 * lane);
     pk.u2.x = ldg32(ch + f.d + 32 * g + 4 * q);
@@ -449,20 +454,21 @@ __device__ __forceinline__ void deq_q80(const Packed& pk, int lane, uint8_t* tw)
 // Q4_0 / Q4_1 / Q5_0 / Q5_1: k-block q = blocks 2q, 2q+1 (gguf.py:310-353).
 // Unit word 2bb + hi: row g+8hi of block bb, qs bytes 4t..+3, whose low
 // nibbles are elements 4t..+3 and high nibbles 16+4t..+3; the fifth bit of
-// element e is bit e of the block's qh word.
-template <int QT>
-__device__ __forceinline__ void deq_q4x(const Packed& pk, int lane, uint8_t* tw) {
-  constexpr bool kH = QT == kQ5_0 || QT == kQ5_1, kM = QT == kQ4_1 || QT == kQ5_1;
+// element e is bit e of the block's qh word.  One copy for the four types
+// (the type is a run-time value): four inlined instantiations in the dequant
+// loop cost the K-quants ~4 % through instruction-cache pressure; launches
+// without these types use the kernel instantiation without this code.
+__device__ __forceinline__ void deq_q4x(const Packed& pk, int lane, uint8_t* tw, int qt) {
+  const bool has_h = qt == kQ5_0 || qt == kQ5_1, has_m = qt == kQ4_1 || qt == kQ5_1;
   const int g = lane >> 2, t = lane & 3, g0 = g & 1;
   const uint4 U = pk.u0;
   // q - 8 (Q4_0), q - 16 (Q5_0) or q from the bytes 2^23 + q
-  const uint64_t bias = splat2(QT == kQ4_0 ? -8388616.f : QT == kQ5_0 ? -8388624.f : -8388608.f);
+  const uint64_t bias = splat2(qt == kQ4_0 ? -8388616.f : qt == kQ5_0 ? -8388624.f : -8388608.f);
 #pragma unroll
   for (int hi = 0; hi < 2; ++hi) {
-    const uint32_t dw = hi ? pk.u2.y : pk.u2.x, mw = hi ? pk.u2.w : pk.u2.z;
+    const uint32_t dw = hi ? pk.u2.y : pk.u2.x, mw = has_m ? (hi ? pk.u2.w : pk.u2.z) : 0u;
     const uint64_t dA = splat2(g0 ? f16hi(dw) : f16lo(dw)), dB = splat2(g0 ? f16lo(dw) : f16hi(dw));
-    uint64_t mA = 0, mB = 0;
-    if (kM) mA = splat2(g0 ? f16hi(mw) : f16lo(mw)), mB = splat2(g0 ? f16lo(mw) : f16hi(mw));
+    const uint64_t mA = splat2(g0 ? f16hi(mw) : f16lo(mw)), mB = splat2(g0 ? f16lo(mw) : f16hi(mw));
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
 #pragma unroll
@@ -470,13 +476,12 @@ __device__ __forceinline__ void deq_q4x(const Packed& pk, int lane, uint8_t* tw)
         const int bb = g0 ^ n0;
         const uint32_t w = bb ? (hi ? U.w : U.z) : (hi ? U.y : U.x);
         uint32_t wq = (w >> (4 * half)) & 0x0F0F0F0Fu;
-        if (kH) {
+        if (has_h) {
           const uint32_t h = hi ? (bb ? pk.u1.w : pk.u1.z) : (bb ? pk.u1.y : pk.u1.x);
           wq |= ((h >> (16 * half + 4 * t)) & 15u) * 0x02040810u & 0x10101010u;
         }
-        const int c = 4 * bb + 2 * half + (t >> 1);
-        if (kM) st_piece(tw, hi, g, t, c, scale4_fma(wq, bias, n0 ? dB : dA, n0 ? mB : mA));
-        else st_piece(tw, hi, g, t, c, scale4_mul(wq, bias, n0 ? dB : dA));
+        // q * d + m (m = 0 for Q4_0 / Q5_0, whose offset is in the bias)
+        st_piece(tw, hi, g, t, 4 * bb + 2 * half + (t >> 1), scale4_fma(wq, bias, n0 ? dB : dA, n0 ? mB : mA));
       }
     }
   }
@@ -621,8 +626,9 @@ struct DeqTile {
     sb_stride = (int64_t)nch * pr.cb;
     return true;
   }
+  template <bool kLegacy>
   __device__ __forceinline__ void fetch(int kb, int lane, Packed& pk) const {
-    if (base) fetch_packed(qt, base + (kb >> 2) * sb_stride, kb & 3, lane, pk);
+    if (base) fetch_packed<kLegacy>(qt, base + (kb >> 2) * sb_stride, kb & 3, lane, pk);
   }
   // next k-block of this CTA's sequence (crossing into its next pair tile)
   __device__ __forceinline__ bool advance(const GemmParams& P, int& kb, int pair, int npairs, int rank, int dw) {
@@ -632,6 +638,7 @@ struct DeqTile {
   }
 };
 
+template <bool kLegacy>
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_constant__ GemmParams P) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -859,14 +866,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     c1 = c0;
     bool h1 = h0 && c1.advance(P, kb1, pair, npairs, (int)rank, dw);
     Packed p0, p1;
-    if (h0) c0.fetch(kb0, lane, p0);
-    if (h1) c1.fetch(kb1, lane, p1);
+    if (h0) c0.template fetch<kLegacy>(kb0, lane, p0);
+    if (h1) c1.template fetch<kLegacy>(kb1, lane, p1);
     while (h0) {
       DeqTile c2 = c1;
       int kb2 = kb1;
       const bool h2 = h1 && c2.advance(P, kb2, pair, npairs, (int)rank, dw);
       Packed p2;
-      if (h2) c2.fetch(kb2, lane, p2);
+      if (h2) c2.template fetch<kLegacy>(kb2, lane, p2);
       const DeqTile& cur = c0;
       const int kb = kb0;
       const Packed& pk = p0;
@@ -879,11 +886,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
         if (cur.qt == kQ4_K) deq_q4k<false>(pk, kb & 3, lane, tw);
         else if (cur.qt == kQ5_K) deq_q4k<true>(pk, kb & 3, lane, tw);
         else if (cur.qt == kQ6_K) deq_q6k(pk, kb & 3, lane, tw);
-        else if (cur.qt == kQ8_0) deq_q80(pk, lane, tw);
-        else if (cur.qt == kQ4_0) deq_q4x<kQ4_0>(pk, lane, tw);
-        else if (cur.qt == kQ4_1) deq_q4x<kQ4_1>(pk, lane, tw);
-        else if (cur.qt == kQ5_0) deq_q4x<kQ5_0>(pk, lane, tw);
-        else deq_q4x<kQ5_1>(pk, lane, tw);
+        else if (!kLegacy || cur.qt == kQ8_0) deq_q80(pk, lane, tw);
+        else deq_q4x(pk, lane, tw, cur.qt);
       } else {
         zero_rows16(tw, lane);  // row tile past n_rows
       }
@@ -936,12 +940,13 @@ static int gemm_max_pairs(int* dyn_smem, char* msg, size_t ml) {
   int optin = 0;
   cudaFuncAttributes fa;
   if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-      cudaFuncGetAttributes(&fa, gemm_kernel) != cudaSuccess) {
+      cudaFuncGetAttributes(&fa, gemm_kernel<true>) != cudaSuccess) {
     snprintf(msg, ml, "gemm: cannot query shared-memory limits");
     return -1;
   }
   const int dyn = optin - (int)fa.sharedSizeBytes;
-  cudaError_t e = cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+  cudaError_t e = cudaFuncSetAttribute(gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
   if (e != cudaSuccess) {
     snprintf(msg, ml, "gemm: cudaFuncSetAttribute(%d bytes) failed: %s", dyn, cudaGetErrorString(e));
     return -1;
@@ -958,7 +963,7 @@ static int gemm_max_pairs(int* dyn_smem, char* msg, size_t ml) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel, &cfg);
+  e = cudaOccupancyMaxActiveClusters(&n, gemm_kernel<true>, &cfg);
   if (e != cudaSuccess || n < 1) {
     snprintf(msg, ml, "gemm: no CTA pair fits on this device (%s)", cudaGetErrorString(e));
     return -1;
@@ -1148,7 +1153,9 @@ int gemm_launch(const draco_gemm_problem* probs, int n, const int* rows, int* st
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_kernel, P);
+  bool legacy = false;
+  for (int i = 0; i < P.n_prob; ++i) legacy |= is_q4x(P.prob[i].qt);
+  cudaError_t e = legacy ? cudaLaunchKernelEx(&cfg, gemm_kernel<true>, P) : cudaLaunchKernelEx(&cfg, gemm_kernel<false>, P);
   if (e != cudaSuccess) {
     snprintf(msg, ml, "gemm: launch failed: %s", cudaGetErrorString(e));
     return DRACO_ERR_CUDA;
