@@ -50,6 +50,8 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_repack",
     "draco_gguf_gemv_workspace_bytes",
     "draco_gguf_gemv_launch_count",
+    "draco_rope_kv_append",
+    "draco_attention_cached",
     "draco_gguf_gemv_grouped",
     "draco_gguf_gemv",
     "draco_gguf_gemv_grouped_ex",
@@ -183,6 +185,10 @@ def load() -> ctypes.CDLL:
         lib.draco_gguf_repack.argtypes = [c_int, c_int, vp, vp, i64, i64, vp]
         lib.draco_gguf_gemv_workspace_bytes.restype = ctypes.c_size_t
         lib.draco_gguf_gemv_workspace_bytes.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int]
+        lib.draco_rope_kv_append.restype = c_int
+        lib.draco_rope_kv_append.argtypes = [vp] * 9 + [c_int] * 6 + [vp]
+        lib.draco_attention_cached.restype = c_int
+        lib.draco_attention_cached.argtypes = [vp] * 5 + [c_int, vp] + [c_int] * 6 + [vp]
         lib.draco_gguf_gemv_launch_count.restype = c_int
         lib.draco_gguf_gemv_launch_count.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int]
         lib.draco_gguf_gemv_grouped.restype = c_int

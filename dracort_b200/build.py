@@ -28,7 +28,7 @@ LIB_PATH = LIB_DIR / "libdraco_gguf.so"
 STAMP_PATH = LIB_DIR / "build.stamp"
 INCLUDE = REPO_DIR / "include"
 
-SOURCES = ["capi.cu", "dequant.cu", "gemv.cu", "gemv_tc.cu", "gemm.cu", "act.cu", "tp.cu"]
+SOURCES = ["capi.cu", "dequant.cu", "gemv.cu", "gemv_tc.cu", "gemm.cu", "act.cu", "tp.cu", "attn.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr"]
 

@@ -148,6 +148,43 @@ size_t draco_gguf_gemv_workspace_bytes(const draco_gemv_problem* probs, int n_pr
   return gemv_workspace_bytes(probs, n_problems, batch);
 }
 
+static int check_attention(int n, int heads, int kv_heads, int head_dim, int capacity, int n_slots, const char* fn) {
+  if (n < 0 || heads < 1 || kv_heads < 1 || heads % kv_heads || head_dim < 2 || (head_dim & 1) || capacity < 1 ||
+      n_slots < 1)
+    return fail(DRACO_ERR_SHAPE, "%s: invalid shape (n %d, heads %d, kv_heads %d, head_dim %d, capacity %d, slots %d)",
+                fn, n, heads, kv_heads, head_dim, capacity, n_slots);
+  return DRACO_OK;
+}
+
+int draco_rope_kv_append(float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                         const float* cos_table, const float* sin_table, const int* seq, const int* pos, int n,
+                         int heads, int kv_heads, int head_dim, int capacity, int n_slots, void* stream) {
+  int rc = check_attention(n, heads, kv_heads, head_dim, capacity, n_slots, "rope_kv_append");
+  if (rc) return rc;
+  if (n > 0 && (!q || !k || !v || !k_cache || !v_cache || !cos_table || !sin_table || !seq || !pos))
+    return fail(DRACO_ERR_ARG, "rope_kv_append: null pointer");
+  char msg[160] = {0};
+  rc = attention_launch(0, q, k, v, k_cache, v_cache, cos_table, sin_table, seq, pos, nullptr, n, heads, kv_heads,
+                        head_dim, capacity, n_slots, capacity - 1, (cudaStream_t)stream, msg, sizeof(msg));
+  return rc ? fail(rc, "%s", msg) : DRACO_OK;
+}
+
+int draco_attention_cached(const float* q, const float* k_cache, const float* v_cache, const int* seq,
+                           const int* pos, int max_pos, float* out, int n, int heads, int kv_heads, int head_dim,
+                           int capacity, int n_slots, void* stream) {
+  int rc = check_attention(n, heads, kv_heads, head_dim, capacity, n_slots, "attention_cached");
+  if (rc) return rc;
+  if (max_pos < 0 || max_pos >= capacity)
+    return fail(DRACO_ERR_SHAPE, "attention_cached: max_pos %d outside the cache capacity %d", max_pos, capacity);
+  if (n > 0 && (!q || !k_cache || !v_cache || !seq || !pos || !out))
+    return fail(DRACO_ERR_ARG, "attention_cached: null pointer");
+  char msg[160] = {0};
+  rc = attention_launch(1, const_cast<float*>(q), nullptr, nullptr, const_cast<float*>(k_cache),
+                        const_cast<float*>(v_cache), nullptr, nullptr, seq, pos, out, n, heads, kv_heads, head_dim,
+                        capacity, n_slots, max_pos, (cudaStream_t)stream, msg, sizeof(msg));
+  return rc ? fail(rc, "%s", msg) : DRACO_OK;
+}
+
 int draco_gguf_gemv_launch_count(const draco_gemv_problem* probs, int n_problems, int batch) {
   if (check_gemv_problems(probs, n_problems, batch, false)) return -1;
   return gemv_launch_count(probs, n_problems, batch);

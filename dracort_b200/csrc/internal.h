@@ -52,6 +52,12 @@ cudaError_t launch_rmsnorm(const void* x, const float* w, void* out, int64_t row
 // out = silu(gate) * up over n fp32 elements (16-byte aligned).
 cudaError_t launch_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, cudaStream_t st);
 
+// RoPE + key/value-cache append (op 0) or cached attention (op 1) for the GPU
+// decode step; see draco_rope_kv_append / draco_attention_cached.
+int attention_launch(int op, float* q, const float* k, const float* v, float* kc, float* vc, const float* cos_t,
+                     const float* sin_t, const int* seq, const int* pos, float* out, int n, int heads, int kv_heads,
+                     int hd, int capacity, int n_slots, int max_pos, cudaStream_t st, char* msg, size_t ml);
+
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 

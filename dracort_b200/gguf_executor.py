@@ -1,0 +1,329 @@
+"""GPU decode step for llama-family GGUF models: a drop-in for the reference's
+``CPUExecutionBackend`` (draco/runtime/cpu/executor.py:132-396) on the GGUF
+path, where ``LLM._generate_single_gguf`` (draco/engine/llm.py:1158-1199)
+drives it through ``new_sequence`` / ``forward_step`` / ``end_sequence``.
+
+The reference dequantizes every weight to an fp32 cache on the host and runs
+numpy.  Here the whole step runs on one GPU:
+
+* weights stay packed (the TILED layout of ``gguf_loader.load_gguf``); each
+  layer takes three grouped GEMV calls — q/k/v with the attention RMSNorm
+  fused into the activation read, gate/up with the MLP RMSNorm fused, down
+  with the SwiGLU product fused — plus o_proj and the output head; dense
+  (F16 / F32) projections of a file go through an fp32 matmul instead;
+* RoPE (rotate-half, draco/runtime/cpu/ops.py:77-95) and the key/value-cache
+  append run in ``draco_rope_kv_append``, the causal attention over the
+  cache (draco/runtime/cpu/attention.py) in ``draco_attention_cached``
+  (fp32, grouped-query heads);
+* the key/value cache is a per-layer fp32 tensor [slot, kv_heads, capacity,
+  head_dim]: a sequence owns one slot from ``new_sequence`` to
+  ``end_sequence``.
+
+Rows go through the GEMV 32 at a time, so prompts are processed in chunks
+of 32 tokens (each chunk attends to everything cached before it).  Results
+follow the decode GEMV's accuracy (about 1e-4 relative L2 per projection
+against the fp32 reference); ``forward_step`` / ``forward_batch_decode``
+return numpy fp32 logits like the reference.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Union
+
+import numpy as np
+import torch
+
+from dracort_b200 import _native as N
+from dracort_b200 import gguf_ops as G
+from dracort_b200.exceptions import DracoFormatError
+from dracort_b200.format.gguf_file import GGUFFile
+from dracort_b200.format.gguf_types import Q6K_D_LAST
+from dracort_b200.gguf_loader import DeviceWeight, load_gguf
+
+_ROWS = N.GEMV_MAX_BATCH  # activation rows per GEMV call
+
+
+@dataclass
+class LlamaConfig:
+    """The llama-family configuration the reference derives from GGUF metadata
+    (draco/format/gguf.py:680-770)."""
+
+    hidden_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    vocab_size: int
+    max_position_embeddings: int
+    rope_theta: float
+    rms_norm_eps: float
+    tie_word_embeddings: bool
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_attention_heads
+
+    @classmethod
+    def from_gguf(cls, gf: GGUFFile) -> "LlamaConfig":
+        meta = gf.metadata
+        arch = str(meta.get("general.architecture", "llama"))
+        if arch == "gpt2":
+            raise DracoFormatError("the GPU decode step runs llama-family GGUF models (gpt2 is not supported)")
+        p = arch + "."
+
+        def get(key, default=None):
+            v = meta.get(p + key)
+            return default if v is None else v
+
+        hidden, layers, heads = get("embedding_length"), get("block_count"), get("attention.head_count")
+        vocab = get("vocab_size")
+        if vocab is None and "token_embd.weight" in gf.tensors:
+            vocab = gf.tensor("token_embd.weight").shape[0]
+        if None in (hidden, layers, heads, vocab):
+            raise DracoFormatError(f"GGUF '{gf.path}' is missing required architecture metadata "
+                                   f"(embedding_length / block_count / attention.head_count / vocab_size).")
+        key_len = get("attention.key_length")
+        if key_len is not None and int(key_len) != int(hidden) // int(heads):
+            raise DracoFormatError(f"GGUF '{gf.path}' uses a non-standard key_length {key_len}")
+        eps = get("attention.layer_norm_rms_epsilon") or get("attention.layer_norm_epsilon") or 1e-5
+        return cls(hidden_size=int(hidden), num_hidden_layers=int(layers), num_attention_heads=int(heads),
+                   num_key_value_heads=int(get("attention.head_count_kv") or heads), vocab_size=int(vocab),
+                   max_position_embeddings=int(get("context_length") or 4096),
+                   rope_theta=float(get("rope.freq_base", 10000.0)), rms_norm_eps=float(eps),
+                   tie_word_embeddings=bool(get("tie_embeddings", "output.weight" not in gf.tensors)))
+
+
+def rope_tables(head_dim: int, max_positions: int, theta: float):
+    """cos / sin [max_positions, head_dim / 2] fp32, computed on the host in the
+    reference's order (build_rope_cache, draco/runtime/cpu/ops.py:77-83)."""
+    inv_freq = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))
+    freqs = np.outer(np.arange(max_positions, dtype=np.float32), inv_freq)
+    return np.cos(freqs).astype(np.float32), np.sin(freqs).astype(np.float32)
+
+
+_LAYER_KEYS = {"attn_norm": "attn_norm.weight", "q": "attn_q.weight", "k": "attn_k.weight", "v": "attn_v.weight",
+               "o": "attn_output.weight", "ffn_norm": "ffn_norm.weight", "gate": "ffn_gate.weight",
+               "up": "ffn_up.weight", "down": "ffn_down.weight"}
+
+
+class GPUExecutionBackend:
+    """``CPUExecutionBackend`` for llama-family GGUF files, on one GPU.
+
+    source      : path of a .gguf file or an open GGUFFile;
+    max_num_seqs: sequences that may hold a key/value cache at once;
+    max_seq_len : cache rows per sequence (default: the model's context length);
+    q6k_order   : byte order of the file's Q6_K blocks ("d_last" for llama.cpp
+                  files, "d_first" for the order the reference decodes).
+    """
+
+    def __init__(self, source: Union[str, GGUFFile], device: Union[str, torch.device] = "cuda",
+                 max_num_seqs: int = 4, max_seq_len: Optional[int] = None, q6k_order: str = Q6K_D_LAST) -> None:
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("GPUExecutionBackend runs on a CUDA device (this library has no CPU path)")
+        own = not isinstance(source, GGUFFile)
+        gf = GGUFFile(str(source)) if own else source
+        try:
+            self.config = cfg = LlamaConfig.from_gguf(gf)
+            with torch.cuda.device(self.device):
+                loaded = load_gguf(gf, self.device, q6k_order=q6k_order)
+        finally:
+            if own:
+                gf.close()
+        if cfg.num_attention_heads % cfg.num_key_value_heads or cfg.head_dim % 2:
+            raise DracoFormatError("heads must be a multiple of key/value heads and head_dim even")
+
+        def dense_f32(t):
+            return t.to(torch.float32).contiguous()
+
+        def entry(name):
+            if name not in loaded:
+                raise DracoFormatError(f"GGUF model has no tensor '{name}'")
+            w = loaded[name]
+            return w if isinstance(w, DeviceWeight) else dense_f32(w)
+
+        emb = entry("token_embd.weight")
+        if isinstance(emb, DeviceWeight):
+            emb = G.dequantize(emb.qtype, emb.tiled, emb.n_rows, emb.k, layout="tiled")
+        self.embed = emb  # [vocab, hidden] fp32
+        self.layers: List[Dict[str, object]] = []
+        for i in range(cfg.num_hidden_layers):
+            self.layers.append({key: entry(f"blk.{i}.{suffix}") for key, suffix in _LAYER_KEYS.items()})
+        self.final_norm = entry("output_norm.weight")
+        self.lm_head = None if cfg.tie_word_embeddings else entry("output.weight")
+        cap = min(int(max_seq_len or cfg.max_position_embeddings), cfg.max_position_embeddings)
+        self.capacity = cap
+        cos, sin = rope_tables(cfg.head_dim, cap, cfg.rope_theta)
+        self.cos = torch.from_numpy(cos).to(self.device)
+        self.sin = torch.from_numpy(sin).to(self.device)
+        self.max_num_seqs = int(max_num_seqs)
+        shape = (self.max_num_seqs, cfg.num_key_value_heads, cap, cfg.head_dim)
+        self.k_cache = [torch.zeros(shape, dtype=torch.float32, device=self.device) for _ in self.layers]
+        self.v_cache = [torch.zeros(shape, dtype=torch.float32, device=self.device) for _ in self.layers]
+        self._free = list(range(self.max_num_seqs))
+        self._slot: Dict[int, int] = {}
+        self._len: Dict[int, int] = {}
+        self._next_seq_id = 0
+        self._lib = N.load()
+
+    # -- sequences (executor.py:172-183) --------------------------------------
+    def new_sequence(self) -> int:
+        if not self._free:
+            raise RuntimeError(f"all {self.max_num_seqs} key/value cache slots are in use")
+        seq_id = self._next_seq_id
+        self._next_seq_id += 1
+        self._slot[seq_id] = self._free.pop(0)
+        self._len[seq_id] = 0
+        return seq_id
+
+    def end_sequence(self, seq_id: int) -> None:
+        slot = self._slot.pop(seq_id, None)
+        self._len.pop(seq_id, None)
+        if slot is not None:
+            self._free.append(slot)
+
+    def truncate_sequence(self, seq_id: int, new_length: int) -> None:
+        """Forget cached positions from new_length on (the rows are rewritten
+        by the next steps)."""
+        if seq_id not in self._slot or not 0 <= new_length <= self._len[seq_id]:
+            raise ValueError(f"cannot truncate sequence {seq_id} to {new_length}")
+        self._len[seq_id] = new_length
+
+    # -- compute --------------------------------------------------------------
+    def _linear(self, weights: Sequence[object], x: torch.Tensor, norm: Optional[torch.Tensor] = None,
+                up: Optional[torch.Tensor] = None) -> List[torch.Tensor]:
+        """x [n <= 32, k] fp32 -> one [n, rows] fp32 output per weight: packed
+        weights in one grouped GEMV (RMSNorm of x by `norm`, or silu(x) * up,
+        fused into the read), dense ones as an fp32 matmul of the transformed x."""
+        n = x.shape[0]
+        outs: List[Optional[torch.Tensor]] = [None] * len(weights)
+        probs, slots = [], []
+        dense_x = None
+        for i, w in enumerate(weights):
+            if isinstance(w, DeviceWeight):
+                y = torch.empty((n, w.n_rows), dtype=torch.float32, device=self.device)
+                probs.append(G.GemvProblem(w.qtype, w.tiled, x, y, w.n_rows, w.k, norm_weight=norm,
+                                           norm_eps=self.config.rms_norm_eps, up=up))
+                slots.append((i, y))
+            else:
+                if dense_x is None:
+                    if norm is not None:
+                        dense_x = G.rms_norm(x, norm, self.config.rms_norm_eps)
+                    elif up is not None:
+                        dense_x = x * torch.sigmoid(x) * up
+                    else:
+                        dense_x = x
+                outs[i] = dense_x @ w.t()
+        if probs:
+            G.gemv_grouped(probs)
+            for i, y in slots:
+                outs[i] = y
+        return outs
+
+    def _forward(self, slots: Sequence[int], tokens: Sequence[int], positions: Sequence[int]) -> torch.Tensor:
+        """One pass of n <= 32 tokens (token i of cache slot slots[i] at
+        positions[i]) through every layer; returns logits [n, vocab] fp32."""
+        cfg = self.config
+        n = len(tokens)
+        dev = self.device
+        tok = torch.tensor(list(tokens), dtype=torch.int64, device=dev)
+        seq_t = torch.tensor(list(slots), dtype=torch.int32, device=dev)
+        pos_t = torch.tensor(list(positions), dtype=torch.int32, device=dev)
+        max_pos = int(max(positions))
+        hd, heads, kvh = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        hidden = self.embed.index_select(0, tok)
+        stream = G._stream_ptr(dev)
+        for li, L in enumerate(self.layers):
+            q, k, v = self._linear([L["q"], L["k"], L["v"]], hidden, norm=L["attn_norm"])
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            N.check(self._lib.draco_rope_kv_append(q.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(),
+                                                   vc.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(),
+                                                   seq_t.data_ptr(), pos_t.data_ptr(), n, heads, kvh, hd,
+                                                   self.capacity, self.max_num_seqs, stream), "rope_kv_append")
+            attn = torch.empty((n, heads * hd), dtype=torch.float32, device=dev)
+            N.check(self._lib.draco_attention_cached(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), seq_t.data_ptr(),
+                                                     pos_t.data_ptr(), max_pos, attn.data_ptr(), n, heads, kvh, hd,
+                                                     self.capacity, self.max_num_seqs, stream), "attention_cached")
+            (o,) = self._linear([L["o"]], attn)
+            hidden = hidden + o
+            gate, upv = self._linear([L["gate"], L["up"]], hidden, norm=L["ffn_norm"])
+            (down,) = self._linear([L["down"]], gate, up=upv)
+            hidden = hidden + down
+        if self.lm_head is not None:
+            (logits,) = self._linear([self.lm_head], hidden, norm=self.final_norm)
+        else:
+            logits = G.rms_norm(hidden, self.final_norm, cfg.rms_norm_eps) @ self.embed.t()
+        return logits
+
+    def _check_tokens(self, tokens: Sequence[int]) -> None:
+        for t in tokens:
+            if not 0 <= int(t) < self.config.vocab_size:
+                raise ValueError(f"token id {t} outside the vocabulary of {self.config.vocab_size}")
+
+    def forward_step(self, seq_id: int, token_ids, start_position: int,
+                     return_all_positions: bool = False) -> np.ndarray:
+        """token_ids (seq_len,) of sequence seq_id from start_position (the
+        number of positions it has cached) -> logits of the last position
+        (vocab,), or of every position (seq_len, vocab) (executor.py:282-341)."""
+        if seq_id not in self._slot:
+            raise ValueError(f"unknown sequence {seq_id}")
+        ids = [int(t) for t in np.asarray(token_ids).reshape(-1)]
+        self._check_tokens(ids)
+        if start_position != self._len[seq_id]:
+            raise ValueError(f"sequence {seq_id} holds {self._len[seq_id]} positions; start_position "
+                             f"{start_position} must continue it (truncate_sequence rewinds)")
+        if start_position + len(ids) > self.capacity:
+            raise ValueError(f"sequence {seq_id} would exceed the cache capacity of {self.capacity} positions")
+        slot = self._slot[seq_id]
+        chunks = []
+        with torch.cuda.device(self.device):
+            for c0 in range(0, len(ids), _ROWS):
+                part = ids[c0:c0 + _ROWS]
+                pos = [start_position + c0 + j for j in range(len(part))]
+                logits = self._forward([slot] * len(part), part, pos)
+                chunks.append(logits if return_all_positions else logits[-1:])
+            out = torch.cat(chunks).cpu().numpy()
+        self._len[seq_id] = start_position + len(ids)
+        return out if return_all_positions else out[-1]
+
+    def forward_batch_decode(self, seq_ids: Sequence[int], token_ids: Sequence[int],
+                             positions: Sequence[int]) -> np.ndarray:
+        """One decode token for each of N sequences at once -> logits (N, vocab)
+        (executor.py:343-396)."""
+        n = len(seq_ids)
+        if not (len(token_ids) == len(positions) == n):
+            raise ValueError("seq_ids, token_ids, and positions must be the same length.")
+        if len(set(seq_ids)) != n:
+            raise ValueError("forward_batch_decode takes each sequence once")
+        for s, p in zip(seq_ids, positions):
+            if s not in self._slot:
+                raise ValueError(f"unknown sequence {s}")
+            if int(p) != self._len[s] or int(p) >= self.capacity:
+                raise ValueError(f"sequence {s}: position {p} must continue its {self._len[s]} cached positions "
+                                 f"within the capacity of {self.capacity}")
+        ids = [int(t) for t in token_ids]
+        self._check_tokens(ids)
+        outs = []
+        with torch.cuda.device(self.device):
+            for c0 in range(0, n, _ROWS):
+                sl = slice(c0, c0 + _ROWS)
+                outs.append(self._forward([self._slot[s] for s in seq_ids[sl]], ids[sl],
+                                          [int(p) for p in positions[sl]]))
+            out = torch.cat(outs).cpu().numpy()
+        for s in seq_ids:
+            self._len[s] += 1
+        return out
+
+    def generate_greedy(self, prompt_ids: Sequence[int], max_new_tokens: int) -> List[int]:
+        """Greedy generation (executor.py:398-413)."""
+        seq_id = self.new_sequence()
+        try:
+            ids = list(prompt_ids)
+            logits = self.forward_step(seq_id, np.array(ids), 0)
+            for _ in range(max_new_tokens):
+                nxt = int(np.argmax(logits))
+                ids.append(nxt)
+                logits = self.forward_step(seq_id, np.array([nxt]), len(ids) - 1)
+            return ids
+        finally:
+            self.end_sequence(seq_id)

@@ -380,6 +380,32 @@ int draco_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, 
 int draco_rmsnorm(const void* x, const float* weight, void* out, int64_t rows, int64_t k, float eps, int dtype,
                   void* stream);
 
+/* ---- attention of the GPU decode step (llama family) -------------------
+ * Key/value cache per layer: fp32 [n_slots][kv_heads][capacity][head_dim];
+ * token i of a call belongs to cache slot seq[i] at absolute position pos[i]
+ * (device int32 arrays).  Tokens whose slot or position falls outside the
+ * cache are skipped (no memory access; their attention output is zero).
+ *
+ * Rotary position embedding, rotate-half form (draco/runtime/cpu/ops.py:
+ * 86-95: x1' = x1 c - x2 s, x2' = x2 c + x1 s, no fused multiply-add), with
+ * cos / sin tables [max_positions, head_dim / 2] fp32 built as
+ * build_rope_cache (ops.py:77-83) builds them: q [n, heads, head_dim] is
+ * rotated in place; k [n, kv_heads, head_dim] is rotated into the cache row
+ * pos[i] of slot seq[i] and v copied beside it (attention.py: the cache
+ * append of prefill / decode).  head_dim even, heads a multiple of kv_heads. */
+int draco_rope_kv_append(float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                         const float* cos_table, const float* sin_table, const int* seq, const int* pos, int n,
+                         int heads, int kv_heads, int head_dim, int capacity, int n_slots, void* stream);
+
+/* Causal attention of n query tokens over their slots' cached keys 0..pos[i]
+ * (CPUAttentionBackend.prefill / decode, draco/runtime/cpu/attention.py):
+ * softmax(q K^T / sqrt(head_dim)) V in fp32, query head h reading key/value
+ * head h / (heads / kv_heads); out [n, heads, head_dim].  max_pos bounds
+ * every pos[i] (max_pos < capacity; positions above it count as outside). */
+int draco_attention_cached(const float* q, const float* k_cache, const float* v_cache, const int* seq,
+                           const int* pos, int max_pos, float* out, int n, int heads, int kv_heads, int head_dim,
+                           int capacity, int n_slots, void* stream);
+
 /* Single-weight convenience form of draco_gguf_gemv_grouped. */
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias,
                     int batch, int64_t n_rows, int64_t k, void* workspace,

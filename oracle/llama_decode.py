@@ -1,0 +1,224 @@
+"""CPU oracle for the GGUF decode step — TEST INFRASTRUCTURE ONLY.
+
+Only tests/ may import this module; the product never calls it.
+
+It restates, in numpy, the reference's CPU executor for llama-family GGUF
+models (sadrasa97/DracoRT, paths relative to that project), operation by
+operation in the same fp32 / float64 order:
+
+* ``config_from_metadata`` — the llama branch of GGUFReader's metadata
+  mapping, draco/format/gguf.py:680-770 (hidden size, layers, heads, key/value
+  heads, vocab, rope_theta, rms epsilon, tied embeddings);
+* ``rms_norm``, ``swiglu``, ``build_rope_cache``, ``apply_rope``, ``softmax`` —
+  draco/runtime/cpu/ops.py:15-27, 68-95;
+* ``OracleLlama.forward_step`` — CPUExecutionBackend.forward_step,
+  draco/runtime/cpu/executor.py:282-341 (embedding gather, per layer
+  RMSNorm -> q/k/v -> RoPE -> cached causal attention -> o_proj -> residual,
+  RMSNorm -> gate/up -> SwiGLU -> down -> residual, final norm, lm_head or
+  tied embedding);
+* ``OracleLlama.forward_batch_decode`` — executor.py:343-396;
+* the attention — CPUAttentionBackend.prefill / decode,
+  draco/runtime/cpu/attention.py (append k / v, then
+  softmax(q K^T * (1 / sqrt(d))) V, causal mask for prefill; the scale is a
+  numpy float64 scalar, so the scores and the softmax are float64 there);
+* every linear layer — executor._linear (executor.py:47-79) on weights
+  dequantized by gguf_oracle.dequantize, i.e. matmul_f32 (x @ W.T in fp32).
+
+The GGUF container is parsed with dracort_b200.format.gguf_file (checked on
+its own against the reference reader's index); only the arithmetic is
+restated here.  Pinning: tests/golden/tiny_llama_decode_ref.npz holds the
+reference executor's logits for tests/golden/tiny_llama_decode.gguf
+(tests/golden/make_decode_golden.py), and test_decode_oracle.py checks this
+module against them.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List
+
+import numpy as np
+
+from oracle import gguf_oracle as O
+
+_BLOCK_NAMES = {
+    "attn_norm.weight": "input_layernorm.weight",
+    "attn_q.weight": "q_proj",
+    "attn_k.weight": "k_proj",
+    "attn_v.weight": "v_proj",
+    "attn_output.weight": "o_proj",
+    "ffn_norm.weight": "post_attention_layernorm.weight",
+    "ffn_gate.weight": "gate_proj",
+    "ffn_up.weight": "up_proj",
+    "ffn_down.weight": "down_proj",
+}
+
+
+def config_from_metadata(meta: Dict, tensor_names) -> Dict:
+    """gguf.py:680-770, llama branch."""
+    arch = meta.get("general.architecture", "llama")
+    p = arch + "."
+    hidden = int(meta[p + "embedding_length"])
+    heads = int(meta[p + "attention.head_count"])
+    kv_heads = int(meta.get(p + "attention.head_count_kv") or heads)
+    vocab = meta.get(p + "vocab_size")
+    if vocab is None:
+        vocab = None  # taken from the embedding shape by the caller
+    rms = meta.get(p + "attention.layer_norm_rms_epsilon") or meta.get(p + "attention.layer_norm_epsilon") or 1e-5
+    has_output = "output.weight" in tensor_names
+    return {
+        "hidden_size": hidden,
+        "num_hidden_layers": int(meta[p + "block_count"]),
+        "num_attention_heads": heads,
+        "num_key_value_heads": kv_heads,
+        "vocab_size": vocab,
+        "max_position_embeddings": int(meta.get(p + "context_length") or 4096),
+        "rope_theta": float(meta.get(p + "rope.freq_base", 10000.0)),
+        "rms_norm_eps": float(rms),
+        "tie_word_embeddings": bool(meta.get(p + "tie_embeddings", not has_output)),
+    }
+
+
+def rms_norm(x, weight, eps):
+    x32 = x.astype(np.float32)
+    variance = np.mean(x32 * x32, axis=-1, keepdims=True)
+    normed = x32 / np.sqrt(variance + eps)
+    return (normed * weight).astype(x.dtype)
+
+
+def swiglu(gate, up):
+    return gate * (1.0 / (1.0 + np.exp(-gate))) * up
+
+
+def softmax(x, axis=-1):
+    x = x - np.max(x, axis=axis, keepdims=True)
+    e = np.exp(x)
+    return e / np.sum(e, axis=axis, keepdims=True)
+
+
+def build_rope_cache(head_dim, max_positions, theta):
+    inv_freq = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))
+    positions = np.arange(max_positions, dtype=np.float32)
+    freqs = np.outer(positions, inv_freq)
+    return np.cos(freqs), np.sin(freqs)
+
+
+def apply_rope(x, cos, sin, positions):
+    half = x.shape[-1] // 2
+    x1, x2 = x[..., :half], x[..., half:]
+    c = cos[positions][:, None, :]
+    s = sin[positions][:, None, :]
+    return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1).astype(x.dtype)
+
+
+class OracleLlama:
+    """CPUExecutionBackend restated for one GGUF file (q6k_order: byte order of
+    the file's Q6_K blocks, "d_first" as the reference decodes them)."""
+
+    def __init__(self, gguf_file, q6k_order: str = "d_first") -> None:
+        gf = gguf_file
+        self.cfg = cfg = config_from_metadata(gf.metadata, gf.tensors)
+        self.w: Dict[str, np.ndarray] = {}
+        for name, t in gf.tensors.items():
+            payload = np.asarray(gf.payload(name)).reshape(-1)
+            if t.is_quantized:
+                arr = O.dequantize(t.ggml_type, payload, int(np.prod(t.shape)), q6k_order=q6k_order)
+            elif t.ggml_type == 1:
+                arr = payload.view(np.float16).astype(np.float32)
+            else:
+                arr = payload.view(np.float32).astype(np.float32)
+            self.w[name] = arr.reshape(t.shape)
+        if cfg["vocab_size"] is None:
+            cfg["vocab_size"] = self.w["token_embd.weight"].shape[0]
+        self.head_dim = cfg["hidden_size"] // cfg["num_attention_heads"]
+        self.cos, self.sin = build_rope_cache(self.head_dim, cfg["max_position_embeddings"], cfg["rope_theta"])
+        self.group = cfg["num_attention_heads"] // cfg["num_key_value_heads"]
+        self.kv: Dict[int, List[List[np.ndarray]]] = {}  # seq -> layer -> [k list, v list]
+        self._next = 0
+
+    # -- sequences (executor.py:172-183) --------------------------------------
+    def new_sequence(self) -> int:
+        s = self._next
+        self._next += 1
+        self.kv[s] = [[[], []] for _ in range(self.cfg["num_hidden_layers"])]
+        return s
+
+    def end_sequence(self, s: int) -> None:
+        self.kv.pop(s, None)
+
+    def _linear(self, name, x):
+        return x.astype(np.float32) @ self.w[name].astype(np.float32).T
+
+    def _attention(self, s, layer, q, k, v, causal):
+        """attention.py prefill: append, then attend over the whole cache."""
+        ks, vs = self.kv[s][layer]
+        for t in range(q.shape[0]):
+            ks.append(k[t])
+            vs.append(v[t])
+        ck = np.repeat(np.stack(ks).astype(np.float32), self.group, axis=1)
+        cv = np.repeat(np.stack(vs).astype(np.float32), self.group, axis=1)
+        scale = 1.0 / np.sqrt(q.shape[-1])
+        q_t = np.transpose(q.astype(np.float32), (1, 0, 2))
+        k_t = np.transpose(ck, (1, 0, 2))
+        v_t = np.transpose(cv, (1, 0, 2))
+        scores = np.einsum("hqd,hkd->hqk", q_t, k_t) * scale
+        if causal:
+            total = k_t.shape[1]
+            qpos = np.arange(total - q.shape[0], total)
+            mask = np.arange(total)[None, :] > qpos[:, None]
+            scores = np.where(mask[None, :, :], -np.inf, scores)
+        out = np.einsum("hqk,hkd->hqd", softmax(scores, axis=-1), v_t)
+        return np.transpose(out, (1, 0, 2)).astype(q.dtype)
+
+    def _layer_qkv(self, layer, hidden, n):
+        cfg, p = self.cfg, f"blk.{layer}."
+        normed = rms_norm(hidden, self.w[p + "attn_norm.weight"], cfg["rms_norm_eps"])
+        q = self._linear(p + "attn_q.weight", normed).reshape(n, cfg["num_attention_heads"], self.head_dim)
+        k = self._linear(p + "attn_k.weight", normed).reshape(n, cfg["num_key_value_heads"], self.head_dim)
+        v = self._linear(p + "attn_v.weight", normed).reshape(n, cfg["num_key_value_heads"], self.head_dim)
+        return q, k, v
+
+    def _layer_rest(self, layer, hidden, attn_out):
+        cfg, p = self.cfg, f"blk.{layer}."
+        hidden = hidden + self._linear(p + "attn_output.weight", attn_out)
+        normed = rms_norm(hidden, self.w[p + "ffn_norm.weight"], cfg["rms_norm_eps"])
+        gate = self._linear(p + "ffn_gate.weight", normed)
+        up = self._linear(p + "ffn_up.weight", normed)
+        return hidden + self._linear(p + "ffn_down.weight", swiglu(gate, up))
+
+    def _head(self, hidden):
+        cfg = self.cfg
+        hidden = rms_norm(hidden, self.w["output_norm.weight"], cfg["rms_norm_eps"])
+        if cfg["tie_word_embeddings"]:
+            return hidden @ self.w["token_embd.weight"].T
+        return self._linear("output.weight", hidden)
+
+    def forward_step(self, s, token_ids, start_position, return_all_positions=False):
+        """executor.py:282-341."""
+        cfg = self.cfg
+        n = len(token_ids)
+        positions = np.arange(start_position, start_position + n)
+        hidden = self.w["token_embd.weight"][np.asarray(token_ids)].astype(np.float32)
+        for layer in range(cfg["num_hidden_layers"]):
+            q, k, v = self._layer_qkv(layer, hidden, n)
+            q = apply_rope(q, self.cos, self.sin, positions)
+            k = apply_rope(k, self.cos, self.sin, positions)
+            attn = self._attention(s, layer, q, k, v, causal=True).reshape(n, -1)
+            hidden = self._layer_rest(layer, hidden, attn)
+        logits = self._head(hidden)
+        return logits if return_all_positions else logits[-1]
+
+    def forward_batch_decode(self, seq_ids, token_ids, positions):
+        """executor.py:343-396 (one token per sequence)."""
+        cfg = self.cfg
+        n = len(seq_ids)
+        pos = np.array(positions)
+        hidden = self.w["token_embd.weight"][np.array(token_ids)].astype(np.float32)
+        for layer in range(cfg["num_hidden_layers"]):
+            q, k, v = self._layer_qkv(layer, hidden, n)
+            attn = np.empty((n, cfg["num_attention_heads"], self.head_dim), dtype=np.float32)
+            for i in range(n):
+                qi = apply_rope(q[i:i + 1], self.cos, self.sin, pos[i:i + 1])
+                ki = apply_rope(k[i:i + 1], self.cos, self.sin, pos[i:i + 1])
+                attn[i] = self._attention(seq_ids[i], layer, qi, ki, v[i:i + 1], causal=False)[0]
+            hidden = self._layer_rest(layer, hidden, attn.reshape(n, -1))
+        return self._head(hidden)

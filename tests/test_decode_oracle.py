@@ -1,0 +1,77 @@
+"""The decode-step oracle (oracle/llama_decode.py) is pinned to the reference
+executor's own logits on tests/golden/tiny_llama_decode.gguf
+(tests/golden/make_decode_golden.py ran draco.runtime.cpu.executor on it)."""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from dracort_b200.format.gguf_file import GGUFFile
+from oracle.llama_decode import OracleLlama
+
+HERE = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module")
+def ref():
+    return np.load(HERE / "tiny_llama_decode_ref.npz")
+
+
+@pytest.fixture()
+def model():
+    gf = GGUFFile(str(HERE / "tiny_llama_decode.gguf"))
+    try:
+        yield OracleLlama(gf, q6k_order="d_first")
+    finally:
+        gf.close()
+
+
+def rel(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+def test_oracle_prefill_matches_reference_executor(model, ref):
+    s = model.new_sequence()
+    got = model.forward_step(s, ref["prompt"], 0, return_all_positions=True)
+    assert got.shape == ref["prefill_logits"].shape
+    assert rel(got, ref["prefill_logits"]) < 1e-6
+
+
+def test_oracle_greedy_decode_matches_reference_executor(model, ref):
+    s = model.new_sequence()
+    ids = list(ref["prompt"])
+    logits = model.forward_step(s, np.array(ids), 0)
+    for t_ref, l_ref in zip(ref["decode_tokens"], ref["decode_logits"]):
+        t = int(np.argmax(logits))
+        assert t == int(t_ref)
+        ids.append(t)
+        logits = model.forward_step(s, np.array([t]), len(ids) - 1)
+        assert rel(logits, l_ref) < 1e-6
+
+
+def test_oracle_batch_decode_matches_reference_executor(model, ref):
+    sa, sb = model.new_sequence(), model.new_sequence()
+    la = model.forward_step(sa, ref["prompt"], 0)
+    lb = model.forward_step(sb, ref["prompt_b"], 0)
+    toks = [int(np.argmax(la)), int(np.argmax(lb))]
+    assert toks == [int(t) for t in ref["batch_tokens"]]
+    got = model.forward_batch_decode([sa, sb], toks, [len(ref["prompt"]), len(ref["prompt_b"])])
+    assert rel(got, ref["batch_logits"]) < 1e-6
+
+
+def test_product_rope_tables_equal_the_reference_construction():
+    from dracort_b200.gguf_executor import LlamaConfig, rope_tables
+    from oracle.llama_decode import build_rope_cache
+
+    gf = GGUFFile(str(HERE / "tiny_llama_decode.gguf"))
+    try:
+        cfg = LlamaConfig.from_gguf(gf)
+    finally:
+        gf.close()
+    assert (cfg.hidden_size, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.vocab_size) == (256, 8, 4, 96)
+    assert not cfg.tie_word_embeddings and cfg.head_dim == 32
+    c, s = rope_tables(cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta)
+    rc, rs = build_rope_cache(cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta)
+    assert np.array_equal(c.view(np.uint32), rc.astype(np.float32).view(np.uint32))
+    assert np.array_equal(s.view(np.uint32), rs.astype(np.float32).view(np.uint32))
