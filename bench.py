@@ -75,6 +75,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-moe", action="store_true", help="skip the MoE expert-parallel leg")
     ap.add_argument("--model-steps", type=int, default=20, help="timed steps of the 32-layer decode leg")
     ap.add_argument("--no-model", action="store_true", help="skip the 32-layer decode (config 4) leg")
+    ap.add_argument("--decode-steps", type=int, default=20, help="timed steps of the GGUF decode-step leg")
+    ap.add_argument("--decode-layers", type=int, default=32, help=argparse.SUPPRESS)
+    ap.add_argument("--no-decode", action="store_true", help="skip the 32-layer GGUF decode-step (f4) leg")
     ap.add_argument("--q8-steps", type=int, default=2000, help="timed steps of the Q8_0 (config 1) leg")
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0 GEMV (config 1) leg")
     return ap.parse_args(argv)
@@ -663,6 +666,123 @@ def model_leg(args, dev, peaks, rank, world, pg, timed):
     return out
 
 
+def decode_leg(args, dev, peaks, timed):
+    """The f4 row: one full decode step of a 32-layer Llama-7B Q4_K_M GGUF model
+    through GPUExecutionBackend (the drop-in for the reference's
+    CPUExecutionBackend): embedding, per layer RMSNorm-fused q/k/v GEMV, RoPE +
+    key/value append, cached attention over 1025 positions, o_proj with the
+    residual add, RMSNorm-fused gate/up, SwiGLU-fused down with the residual
+    add, then the final norm and a Q6_K output head over 32000 tokens.
+    Batch 1 (forward_step) and batch 32 (forward_batch_decode), device-timed
+    (logits left on the device) and end to end (host token ids in, host
+    logits out, through the public methods)."""
+    import shutil
+    import tempfile
+
+    import torch
+
+    from dracort_b200 import gguf_ops as G
+    from dracort_b200.format.gguf_file import write_gguf
+    from dracort_b200.gguf_executor import GPUExecutionBackend
+    from dracort_b200.telemetry import ClockSampler
+    from dracort_b200.workloads import model_layers
+
+    n_layers = getattr(args, "decode_layers", 32)
+    pos0, vocab, hidden, ffn, heads = 1024, 32000, 4096, 11008, 32
+    specs, layers = model_layers(args.seed + 700, n_layers=n_layers)
+    rng = np.random.default_rng(args.seed + 701)
+
+    def raw(a):
+        return np.ascontiguousarray(a).reshape(-1).view(np.uint8)
+
+    names = ["attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"]
+    tensors = [("token_embd.weight", 1, (vocab, hidden),
+                raw((rng.standard_normal((vocab, hidden)) * 0.5).astype(np.float16)))]
+    for li, lay in enumerate(layers):
+        norm = raw((1 + 0.1 * rng.standard_normal(hidden)).astype(np.float32))
+        tensors.append((f"blk.{li}.attn_norm.weight", 0, (hidden,), norm))
+        tensors.append((f"blk.{li}.ffn_norm.weight", 0, (hidden,), norm))
+        for nm, sp, pk in zip(names, specs, lay):
+            tensors.append((f"blk.{li}.{nm}.weight", sp.qtype, (sp.n_rows, sp.k), raw(pk)))
+    v_spec, v_rows = specs[2], layers[0][2]  # Q6_K rows of width 4096
+    head_rows = v_rows[rng.integers(0, v_spec.n_rows, vocab)]
+    tensors += [("output_norm.weight", 0, (hidden,), raw((1 + 0.1 * rng.standard_normal(hidden)).astype(np.float32))),
+                ("output.weight", v_spec.qtype, (vocab, hidden), raw(head_rows))]
+    meta = {"general.architecture": "llama", "general.name": "bench-llama7b-q4_k_m",
+            "llama.embedding_length": hidden, "llama.block_count": n_layers, "llama.feed_forward_length": ffn,
+            "llama.attention.head_count": heads, "llama.attention.head_count_kv": heads,
+            "llama.context_length": 4096, "llama.rope.freq_base": 10000.0,
+            "llama.attention.layer_norm_rms_epsilon": 1e-5, "llama.vocab_size": vocab}
+    tmp = tempfile.mkdtemp(prefix="draco_decode_")
+    try:
+        path = os.path.join(tmp, "llama7b_q4_k_m.gguf")
+        write_gguf(path, tensors, meta)
+        del tensors, layers
+        be = GPUExecutionBackend(path, device=dev, max_num_seqs=32, max_seq_len=pos0 + 64, q6k_order="d_first")
+    finally:
+        shutil.rmtree(tmp, ignore_errors=True)
+    for t in be.k_cache + be.v_cache:  # 1024 cached positions of every sequence
+        t.normal_()
+    seqs = [be.new_sequence() for _ in range(32)]
+    for s in seqs:
+        be._len[s] = pos0
+    hd = be.config.head_dim
+    w_bytes = sum(G.tiled_nbytes(w.qtype, w.n_rows, w.k) for L in be.layers for key, w in L.items()
+                  if hasattr(w, "qtype")) + G.tiled_nbytes(be.lm_head.qtype, be.lm_head.n_rows, be.lm_head.k)
+    kv_bytes = 2 * n_layers * be.config.num_key_value_heads * (pos0 + 1) * hd * 4  # per sequence, read
+    K = max(1, args.decode_steps)
+    out = {"metric": "32-layer Q4_K_M decode step through GPUExecutionBackend: tokens/s",
+           "unit": "tokens/s", "dtype": "f32",
+           "config": {"workload": "llama7b_q4_k_m_gguf_decode", "layers": n_layers, "vocab": vocab,
+                      "cached_positions": pos0, "kv_cache": "fp32 [slot, kv_heads, capacity, head_dim]",
+                      "weights": "per layer q,k,o,gate,up Q4_K; v,down Q6_K; output Q6_K; embedding F16",
+                      "graph": bool(be.use_graphs)},
+           "launches_per_layer": be.launches_per_layer, "batches": {}}
+    for batch in (1, 32):
+        ss = seqs[:batch]
+        toks = [int(t) for t in rng.integers(0, vocab, batch)]
+        bufs = be._buffers(batch)
+        per_layer = sum(g.launches for g in bufs["layers"][0]) + 3  # GEMV steps + RoPE, attention, combine
+        head_launches = bufs["head"].launches
+        slots = [be._slot[s] for s in ss]
+
+        def device_steps(k=K):
+            for _ in range(k):
+                be._forward(slots, toks, [pos0] * batch)
+
+        def e2e_steps(k=K):
+            for _ in range(k):
+                for s in ss:
+                    be.truncate_sequence(s, pos0)
+                if batch == 1:
+                    be.forward_step(ss[0], np.array(toks), pos0)
+                else:
+                    be.forward_batch_decode(ss, toks, [pos0] * batch)
+
+        device_steps(max(3, args.warmup))
+        e2e_steps(3)
+        torch.cuda.synchronize()
+        sampler = ClockSampler(dev.index or 0).start()
+        ms, tw0, tw1 = timed(device_steps)
+        clocks = sampler.summary(tw0, tw1)
+        sampler.stop()
+        ms_e2e, _, _ = timed(e2e_steps)
+        step = ms / K
+        alg = w_bytes + batch * kv_bytes
+        gbs = alg / (step * 1e-3) / 1e9
+        out["batches"][str(batch)] = {
+            "ms_per_step": round(step, 4), "tokens_per_s": round(batch / (step * 1e-3), 1),
+            "e2e": {"value": round(batch / (ms_e2e / K * 1e-3), 1), "unit": "tokens/s",
+                    "ms_per_step": round(ms_e2e / K, 4), "h2d_bytes_per_step": 3 * 8 * batch,
+                    "d2h_bytes_per_step": batch * vocab * 4},
+            "algorithmic_bytes": alg, "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peaks["hbm_gbs"], 4),
+            "gpu_launches": (per_layer * n_layers + head_launches) * K, "clocks": clocks}
+    out["value"] = out["batches"]["1"]["tokens_per_s"]
+    del be
+    torch.cuda.empty_cache()
+    return out
+
+
 def moe_leg(args, dev, peaks, rank, world, pg, timed):
     """Config 5: Mixtral-shaped MoE FFN, expert-parallel over the ranks."""
     import torch
@@ -995,6 +1115,12 @@ def run_ours(args):
         model = model_leg(args, dev, peaks, rank, world, pg, timed)
         nvtx.range_pop()
 
+    decode = None
+    if not args.no_decode and world == 1:
+        nvtx.range_push("decode")
+        decode = decode_leg(args, dev, peaks, timed)
+        nvtx.range_pop()
+
     # -- CPU baseline (rank 0, N=1) --------------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1068,6 +1194,8 @@ def run_ours(args):
             line["moe"] = moe
         if model is not None:
             line["model"] = model
+        if decode is not None:
+            line["decode"] = decode
         print(json.dumps(line), flush=True)
 
     if layer is not None:

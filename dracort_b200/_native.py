@@ -35,6 +35,7 @@ LAYOUT_TILED = 2
 
 GEMV_MAX_PROBLEMS = 8
 GEMV_MAX_BATCH = 32
+GEMV_ACCUMULATE = 1  # draco_gemv_problem.flags: y += result
 TP_MAX_WORLD = 8
 IPC_HANDLE_BYTES = 64
 
@@ -52,6 +53,7 @@ EXPORTED_SYMBOLS = (
     "draco_gguf_gemv_launch_count",
     "draco_rope_kv_append",
     "draco_attention_cached",
+    "draco_attention_workspace_bytes",
     "draco_gguf_gemv_grouped",
     "draco_gguf_gemv",
     "draco_gguf_gemv_grouped_ex",
@@ -82,7 +84,7 @@ class GemvProblem(ctypes.Structure):
 
     _fields_ = [
         ("qtype", ctypes.c_int),
-        ("reserved", ctypes.c_int),
+        ("flags", ctypes.c_int),
         ("w", ctypes.c_void_p),
         ("x", ctypes.c_void_p),
         ("y", ctypes.c_void_p),
@@ -188,7 +190,9 @@ def load() -> ctypes.CDLL:
         lib.draco_rope_kv_append.restype = c_int
         lib.draco_rope_kv_append.argtypes = [vp] * 9 + [c_int] * 6 + [vp]
         lib.draco_attention_cached.restype = c_int
-        lib.draco_attention_cached.argtypes = [vp] * 5 + [c_int, vp] + [c_int] * 6 + [vp]
+        lib.draco_attention_cached.argtypes = [vp] * 5 + [c_int, vp] + [c_int] * 6 + [vp, ctypes.c_size_t, vp]
+        lib.draco_attention_workspace_bytes.restype = ctypes.c_size_t
+        lib.draco_attention_workspace_bytes.argtypes = [c_int] * 4
         lib.draco_gguf_gemv_launch_count.restype = c_int
         lib.draco_gguf_gemv_launch_count.argtypes = [ctypes.POINTER(GemvProblem), c_int, c_int]
         lib.draco_gguf_gemv_grouped.restype = c_int

@@ -138,6 +138,8 @@ static int check_gemv_problems(const draco_gemv_problem* probs, int n, int batch
       return fail(DRACO_ERR_ARG, "gemv: problem %d has a null x or y", i);
     if (q.ldx < q.k || q.ldy < q.n_rows)
       return fail(DRACO_ERR_SHAPE, "gemv: problem %d leading dimensions too small", i);
+    if (q.flags & ~DRACO_GEMV_ACCUMULATE)
+      return fail(DRACO_ERR_ARG, "gemv: problem %d has unknown flags 0x%x", i, q.flags);
   }
   return DRACO_OK;
 }
@@ -165,13 +167,13 @@ int draco_rope_kv_append(float* q, const float* k, const float* v, float* k_cach
     return fail(DRACO_ERR_ARG, "rope_kv_append: null pointer");
   char msg[160] = {0};
   rc = attention_launch(0, q, k, v, k_cache, v_cache, cos_table, sin_table, seq, pos, nullptr, n, heads, kv_heads,
-                        head_dim, capacity, n_slots, capacity - 1, (cudaStream_t)stream, msg, sizeof(msg));
+                        head_dim, capacity, n_slots, capacity - 1, nullptr, 0, (cudaStream_t)stream, msg, sizeof(msg));
   return rc ? fail(rc, "%s", msg) : DRACO_OK;
 }
 
 int draco_attention_cached(const float* q, const float* k_cache, const float* v_cache, const int* seq,
                            const int* pos, int max_pos, float* out, int n, int heads, int kv_heads, int head_dim,
-                           int capacity, int n_slots, void* stream) {
+                           int capacity, int n_slots, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_attention(n, heads, kv_heads, head_dim, capacity, n_slots, "attention_cached");
   if (rc) return rc;
   if (max_pos < 0 || max_pos >= capacity)
@@ -181,8 +183,14 @@ int draco_attention_cached(const float* q, const float* k_cache, const float* v_
   char msg[160] = {0};
   rc = attention_launch(1, const_cast<float*>(q), nullptr, nullptr, const_cast<float*>(k_cache),
                         const_cast<float*>(v_cache), nullptr, nullptr, seq, pos, out, n, heads, kv_heads, head_dim,
-                        capacity, n_slots, max_pos, (cudaStream_t)stream, msg, sizeof(msg));
+                        capacity, n_slots, max_pos, static_cast<float*>(workspace), workspace_bytes,
+                        (cudaStream_t)stream, msg, sizeof(msg));
   return rc ? fail(rc, "%s", msg) : DRACO_OK;
+}
+
+size_t draco_attention_workspace_bytes(int n, int heads, int head_dim, int max_pos) {
+  if (n < 0 || heads < 1 || head_dim < 1 || max_pos < 0) return 0;
+  return attention_workspace_bytes(n, heads, head_dim, max_pos);
 }
 
 int draco_gguf_gemv_launch_count(const draco_gemv_problem* probs, int n_problems, int batch) {
@@ -349,6 +357,10 @@ int draco_gguf_gemv_grouped_tp(const draco_gemv_problem* probs, int n_problems, 
                                const draco_tp_exchange* ex, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_gemv_problems(probs, n_problems, batch, false);
   if (rc) return rc;
+  for (int i = 0; i < n_problems; ++i)
+    if (probs[i].flags)
+      return fail(DRACO_ERR_ARG, "gemv_tp: problem %d has flags 0x%x (the tensor-parallel outputs take none)", i,
+                  probs[i].flags);
   if (!ex) return fail(DRACO_ERR_ARG, "gemv_tp: null exchange description");
   char msg[256] = {0};
   rc = gemv_launch_tp(probs, n_problems, batch, ex, workspace, workspace_bytes, (cudaStream_t)stream, msg,

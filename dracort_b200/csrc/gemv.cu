@@ -722,6 +722,7 @@ __device__ __forceinline__ void write_rows(const GemvParams& P, const GemvProbDe
         if (pr.in_mode == DRACO_INPUT_RMSNORM) out *= __ldcg(reinterpret_cast<const float*>(P.ws + pr.rms_off) + b);
         if (pr.bias) out += pr.bias[row];
         if constexpr (!TP) {
+          if (pr.accumulate) out += pr.y[(int64_t)b * pr.ldy + row];
           pr.y[(int64_t)b * pr.ldy + row] = out;
         } else {
           const int64_t off = pr.tp_y_off + (int64_t)tp_par * pr.tp_par_stride + ((int64_t)b * pr.ldy + row) * 4;
@@ -1209,6 +1210,7 @@ bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, Hos
     d.x = q.x;
     d.y = q.y;
     d.bias = q.bias;
+    d.accumulate = (q.flags & DRACO_GEMV_ACCUMULATE) != 0;
     d.ldx = q.ldx;
     d.ldy = q.ldy;
     d.qt = q.qtype;

@@ -26,6 +26,7 @@ struct GemvProbDev {
   const float* aux;                  // RMSNORM: norm weight [k]; SWIGLU: up [batch, k]
   int64_t ldaux;
   int64_t rms_off;                   // RMSNORM: workspace offset of the per-row scales [batch]
+  int accumulate;                    // y += result (DRACO_GEMV_ACCUMULATE)
 };
 
 struct GemvParams {

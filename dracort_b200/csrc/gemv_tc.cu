@@ -93,6 +93,7 @@ struct TcProb {
   int64_t bt_off;   // workspace offset of the converted activation tiles, one per super-block
   int64_t rms_off;  // RMSNORM: workspace offset of the per-row scales [batch]
   int qt, n_rows, k, nb, n_rg, n_tiles, cb, slab0, in_mode;
+  int accumulate;  // y += result
   float eps;
 };
 
@@ -450,7 +451,9 @@ __device__ __forceinline__ void tc_write_row(const TcParams& P, const TcProb& pr
     if (b < P.batch) {
       float out = y[b];
       if (pr.in_mode == DRACO_INPUT_RMSNORM) out *= __ldcg(rms + b);
-      pr.y[(int64_t)b * pr.ldy + row] = out + bias;
+      out += bias;
+      if (pr.accumulate) out += pr.y[(int64_t)b * pr.ldy + row];
+      pr.y[(int64_t)b * pr.ldy + row] = out;
     }
   }
 }
@@ -1017,6 +1020,7 @@ int gemv_tc_launch(const HostPlan& hp, const draco_gemv_input* inputs, void* ws,
     d.cb = s.cb;
     d.slab0 = s.slab0;
     d.in_mode = s.in_mode;
+    d.accumulate = s.accumulate;
     d.eps = s.eps;
     conv_units += s.nb * L.np + (s.in_mode == DRACO_INPUT_RMSNORM ? G.batch : 0);
   }

@@ -56,7 +56,11 @@ cudaError_t launch_swiglu_f32(const float* gate, const float* up, float* out, in
 // decode step; see draco_rope_kv_append / draco_attention_cached.
 int attention_launch(int op, float* q, const float* k, const float* v, float* kc, float* vc, const float* cos_t,
                      const float* sin_t, const int* seq, const int* pos, float* out, int n, int heads, int kv_heads,
-                     int hd, int capacity, int n_slots, int max_pos, cudaStream_t st, char* msg, size_t ml);
+                     int hd, int capacity, int n_slots, int max_pos, float* part, size_t part_bytes, cudaStream_t st,
+                     char* msg, size_t ml);
+// Bytes of the per-(token, head, 32-key chunk) partials draco_attention_cached
+// needs for n tokens over positions 0..max_pos.
+size_t attention_workspace_bytes(int n, int heads, int hd, int max_pos);
 
 // Number of SMs of the current device (cached per device).
 int device_sm_count();

@@ -29,7 +29,7 @@ return numpy fp32 logits like the reference.
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Dict, List, Optional, Sequence, Union
+from typing import Callable, Dict, List, Optional, Sequence, Tuple, Union
 
 import numpy as np
 import torch
@@ -165,6 +165,11 @@ class GPUExecutionBackend:
         self._len: Dict[int, int] = {}
         self._next_seq_id = 0
         self._lib = N.load()
+        self._bufs: Dict[int, Dict[str, object]] = {}
+        self._graphs: Dict[Tuple[int, int], torch.cuda.CUDAGraph] = {}
+        self._eager_seen: set = set()
+        #: replay a captured CUDA graph per (rows, attention bound) after its first eager pass
+        self.use_graphs = True
 
     # -- sequences (executor.py:172-183) --------------------------------------
     def new_sequence(self) -> int:
@@ -190,70 +195,151 @@ class GPUExecutionBackend:
         self._len[seq_id] = new_length
 
     # -- compute --------------------------------------------------------------
-    def _linear(self, weights: Sequence[object], x: torch.Tensor, norm: Optional[torch.Tensor] = None,
-                up: Optional[torch.Tensor] = None) -> List[torch.Tensor]:
-        """x [n <= 32, k] fp32 -> one [n, rows] fp32 output per weight: packed
-        weights in one grouped GEMV (RMSNorm of x by `norm`, or silu(x) * up,
-        fused into the read), dense ones as an fp32 matmul of the transformed x."""
-        n = x.shape[0]
-        outs: List[Optional[torch.Tensor]] = [None] * len(weights)
-        probs, slots = [], []
-        dense_x = None
-        for i, w in enumerate(weights):
+    def _group(self, weights: Sequence[object], x: torch.Tensor, ys: Sequence[torch.Tensor],
+               norm: Optional[torch.Tensor] = None, up: Optional[torch.Tensor] = None,
+               accumulate: bool = False) -> Callable[[], None]:
+        """One projection step over fixed buffers: ys[i] (+)= f(x) @ W_i^T with
+        f the RMSNorm by `norm`, silu(x) * up, or nothing.  Packed weights go
+        in one GemvPlan (the transform fused into the activation read, the
+        add into the output write); dense ones through an fp32 matmul of the
+        transformed x.  Returns a callable enqueuing the step on the current
+        stream; its ``launches`` counts the library kernels it starts."""
+        eps = self.config.rms_norm_eps
+        probs, dense = [], []
+        for w, y in zip(weights, ys):
             if isinstance(w, DeviceWeight):
-                y = torch.empty((n, w.n_rows), dtype=torch.float32, device=self.device)
-                probs.append(G.GemvProblem(w.qtype, w.tiled, x, y, w.n_rows, w.k, norm_weight=norm,
-                                           norm_eps=self.config.rms_norm_eps, up=up))
-                slots.append((i, y))
+                probs.append(G.GemvProblem(w.qtype, w.tiled, x, y, w.n_rows, w.k, norm_weight=norm, norm_eps=eps,
+                                           up=up, accumulate=accumulate))
             else:
-                if dense_x is None:
-                    if norm is not None:
-                        dense_x = G.rms_norm(x, norm, self.config.rms_norm_eps)
-                    elif up is not None:
-                        dense_x = x * torch.sigmoid(x) * up
+                dense.append((w, y))
+        plans = [G.GemvPlan(probs[i:i + N.GEMV_MAX_PROBLEMS]) for i in range(0, len(probs), N.GEMV_MAX_PROBLEMS)]
+
+        def run() -> None:
+            for pl in plans:
+                pl.run()
+            if dense:
+                if norm is not None:
+                    xd = G.rms_norm(x, norm, eps)
+                elif up is not None:
+                    xd = x * torch.sigmoid(x) * up
+                else:
+                    xd = x
+                for w, y in dense:
+                    if accumulate:
+                        y.addmm_(xd, w.t())
                     else:
-                        dense_x = x
-                outs[i] = dense_x @ w.t()
-        if probs:
-            G.gemv_grouped(probs)
-            for i, y in slots:
-                outs[i] = y
-        return outs
+                        torch.matmul(xd, w.t(), out=y)
+
+        run.launches = sum(pl.launches for pl in plans)  # type: ignore[attr-defined]
+        return run
+
+    def _buffers(self, n: int) -> Dict[str, object]:
+        """Fixed device buffers and GEMV plans of a pass over n rows (built on
+        first use, kept for the backend's lifetime)."""
+        b = self._bufs.get(n)
+        if b is not None:
+            return b
+        cfg, dev = self.config, self.device
+        hd, heads, kvh = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+
+        def f32(*shape):
+            return torch.zeros(shape, dtype=torch.float32, device=dev)
+
+        g0 = self.layers[0]["gate"]
+        ffn = g0.n_rows if isinstance(g0, DeviceWeight) else g0.shape[0]
+
+        b = {"ids": torch.zeros((3, n), dtype=torch.int64, device=dev),  # token, slot, position
+             "stage": torch.zeros((3, n), dtype=torch.int64).pin_memory(),
+             "seq": torch.zeros(n, dtype=torch.int32, device=dev),
+             "pos": torch.zeros(n, dtype=torch.int32, device=dev),
+             "hidden": f32(n, cfg.hidden_size), "q": f32(n, heads * hd), "k": f32(n, kvh * hd),
+             "v": f32(n, kvh * hd), "attn": f32(n, heads * hd), "gate": f32(n, ffn),
+             "up": f32(n, ffn), "logits": f32(n, cfg.vocab_size),
+             "copied": torch.cuda.Event()}
+        ws_bytes = self._lib.draco_attention_workspace_bytes(n, heads, hd, self.capacity - 1)
+        b["attn_ws"] = torch.zeros(int(ws_bytes), dtype=torch.uint8, device=dev)
+        h = b["hidden"]
+        b["layers"] = [
+            (self._group([L["q"], L["k"], L["v"]], h, [b["q"], b["k"], b["v"]], norm=L["attn_norm"]),
+             self._group([L["o"]], b["attn"], [h], accumulate=True),
+             self._group([L["gate"], L["up"]], h, [b["gate"], b["up"]], norm=L["ffn_norm"]),
+             self._group([L["down"]], b["gate"], [h], up=b["up"], accumulate=True))
+            for L in self.layers]
+        b["head"] = (self._group([self.lm_head], h, [b["logits"]], norm=self.final_norm)
+                     if self.lm_head is not None else None)
+        self._bufs[n] = b
+        return b
+
+    @property
+    def launches_per_layer(self) -> int:
+        """Library kernels one decode token (a pass of one row) starts per
+        layer: the four GEMV steps plus RoPE, attention chunks and combine."""
+        return sum(g.launches for g in self._buffers(1)["layers"][0]) + 3
+
+    def _run(self, n: int, b: Dict[str, object], max_pos: int) -> None:
+        """Enqueue one pass of the n staged rows on the current stream."""
+        cfg = self.config
+        hd, heads, kvh = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+        ids = b["ids"]
+        b["seq"].copy_(ids[1])
+        b["pos"].copy_(ids[2])
+        torch.index_select(self.embed, 0, ids[0], out=b["hidden"])
+        stream = G._stream_ptr(self.device)
+        q, k, v, attn, ws = b["q"], b["k"], b["v"], b["attn"], b["attn_ws"]
+        seq, pos = b["seq"].data_ptr(), b["pos"].data_ptr()
+        for li, (qkv, o_proj, gate_up, down) in enumerate(b["layers"]):
+            qkv()
+            kc, vc = self.k_cache[li], self.v_cache[li]
+            N.check(self._lib.draco_rope_kv_append(q.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(),
+                                                   vc.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(), seq, pos,
+                                                   n, heads, kvh, hd, self.capacity, self.max_num_seqs, stream),
+                    "rope_kv_append")
+            N.check(self._lib.draco_attention_cached(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), seq, pos, max_pos,
+                                                     attn.data_ptr(), n, heads, kvh, hd, self.capacity,
+                                                     self.max_num_seqs, ws.data_ptr(), ws.numel(), stream),
+                    "attention_cached")
+            o_proj()   # hidden += attn @ Wo^T
+            gate_up()
+            down()     # hidden += (silu(gate) * up) @ Wdown^T
+        if b["head"] is not None:
+            b["head"]()
+        else:
+            torch.matmul(G.rms_norm(b["hidden"], self.final_norm, cfg.rms_norm_eps), self.embed.t(), out=b["logits"])
 
     def _forward(self, slots: Sequence[int], tokens: Sequence[int], positions: Sequence[int]) -> torch.Tensor:
         """One pass of n <= 32 tokens (token i of cache slot slots[i] at
-        positions[i]) through every layer; returns logits [n, vocab] fp32."""
-        cfg = self.config
+        positions[i]) through every layer; returns logits [n, vocab] fp32 in a
+        buffer that the next pass over n rows overwrites.
+
+        The attention covers positions up to a power-of-two bound of the
+        largest one (at least 64, at most the capacity), so that one CUDA
+        graph per (n, bound) replays every step: the first pass of a key runs
+        eagerly, the second captures the graph, later ones replay it."""
         n = len(tokens)
-        dev = self.device
-        tok = torch.tensor(list(tokens), dtype=torch.int64, device=dev)
-        seq_t = torch.tensor(list(slots), dtype=torch.int32, device=dev)
-        pos_t = torch.tensor(list(positions), dtype=torch.int32, device=dev)
-        max_pos = int(max(positions))
-        hd, heads, kvh = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
-        hidden = self.embed.index_select(0, tok)
-        stream = G._stream_ptr(dev)
-        for li, L in enumerate(self.layers):
-            q, k, v = self._linear([L["q"], L["k"], L["v"]], hidden, norm=L["attn_norm"])
-            kc, vc = self.k_cache[li], self.v_cache[li]
-            N.check(self._lib.draco_rope_kv_append(q.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(),
-                                                   vc.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(),
-                                                   seq_t.data_ptr(), pos_t.data_ptr(), n, heads, kvh, hd,
-                                                   self.capacity, self.max_num_seqs, stream), "rope_kv_append")
-            attn = torch.empty((n, heads * hd), dtype=torch.float32, device=dev)
-            N.check(self._lib.draco_attention_cached(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), seq_t.data_ptr(),
-                                                     pos_t.data_ptr(), max_pos, attn.data_ptr(), n, heads, kvh, hd,
-                                                     self.capacity, self.max_num_seqs, stream), "attention_cached")
-            (o,) = self._linear([L["o"]], attn)
-            hidden = hidden + o
-            gate, upv = self._linear([L["gate"], L["up"]], hidden, norm=L["ffn_norm"])
-            (down,) = self._linear([L["down"]], gate, up=upv)
-            hidden = hidden + down
-        if self.lm_head is not None:
-            (logits,) = self._linear([self.lm_head], hidden, norm=self.final_norm)
+        b = self._buffers(n)
+        b["copied"].synchronize()  # the previous upload from the staging buffer has finished
+        st = b["stage"]
+        st[0, :] = torch.as_tensor(list(tokens), dtype=torch.int64)
+        st[1, :] = torch.as_tensor(list(slots), dtype=torch.int64)
+        st[2, :] = torch.as_tensor(list(positions), dtype=torch.int64)
+        b["ids"].copy_(st, non_blocking=True)
+        b["copied"].record()
+        need = int(max(positions)) + 1
+        bound = min(self.capacity, max(64, 1 << (need - 1).bit_length()))
+        key = (n, bound)
+        g = self._graphs.get(key)
+        if g is not None:
+            g.replay()
+        elif not self.use_graphs or key not in self._eager_seen:
+            self._eager_seen.add(key)
+            self._run(n, b, bound - 1)
         else:
-            logits = G.rms_norm(hidden, self.final_norm, cfg.rms_norm_eps) @ self.embed.t()
-        return logits
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._run(n, b, bound - 1)
+            self._graphs[key] = g
+            g.replay()
+        return b["logits"]
 
     def _check_tokens(self, tokens: Sequence[int]) -> None:
         for t in tokens:
@@ -281,7 +367,7 @@ class GPUExecutionBackend:
                 part = ids[c0:c0 + _ROWS]
                 pos = [start_position + c0 + j for j in range(len(part))]
                 logits = self._forward([slot] * len(part), part, pos)
-                chunks.append(logits if return_all_positions else logits[-1:])
+                chunks.append(logits.clone() if return_all_positions else logits[-1:].clone())
             out = torch.cat(chunks).cpu().numpy()
         self._len[seq_id] = start_position + len(ids)
         return out if return_all_positions else out[-1]
@@ -308,7 +394,7 @@ class GPUExecutionBackend:
             for c0 in range(0, n, _ROWS):
                 sl = slice(c0, c0 + _ROWS)
                 outs.append(self._forward([self._slot[s] for s in seq_ids[sl]], ids[sl],
-                                          [int(p) for p in positions[sl]]))
+                                          [int(p) for p in positions[sl]]).clone())
             out = torch.cat(outs).cpu().numpy()
         for s in seq_ids:
             self._len[s] += 1

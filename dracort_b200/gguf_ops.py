@@ -149,6 +149,7 @@ class GemvProblem:
     norm_weight: Optional[torch.Tensor] = None
     norm_eps: float = 1e-6
     up: Optional[torch.Tensor] = None
+    accumulate: bool = False  # y += result (a residual add folded into the GEMV)
 
 
 def _to_struct(p: GemvProblem) -> N.GemvProblem:
@@ -175,6 +176,7 @@ def _to_struct(p: GemvProblem) -> N.GemvProblem:
     s.k = p.k
     s.ldx = p.x.stride(0)
     s.ldy = p.y.stride(0)
+    s.flags = N.GEMV_ACCUMULATE if p.accumulate else 0
     return s
 
 
@@ -225,7 +227,8 @@ def gemv_grouped(problems: Sequence[GemvProblem]) -> None:
         for b0 in range(0, batch, N.GEMV_MAX_BATCH):
             sub = [GemvProblem(p.qtype, p.w_tiled, p.x[b0:b0 + N.GEMV_MAX_BATCH], p.y[b0:b0 + N.GEMV_MAX_BATCH],
                                p.n_rows, p.k, p.bias, p.norm_weight, p.norm_eps,
-                               None if p.up is None else p.up[b0:b0 + N.GEMV_MAX_BATCH]) for p in problems]
+                               None if p.up is None else p.up[b0:b0 + N.GEMV_MAX_BATCH], p.accumulate)
+                   for p in problems]
             gemv_grouped(sub)
         return
     lib = N.load()

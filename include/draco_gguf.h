@@ -125,13 +125,19 @@ int draco_gguf_repack(int qtype, int src_layout, const void* src, void* dst,
 /* One linear layer of a grouped GEMV launch: y = x @ dequant(W)^T (+ bias).
  *   w     : TILED weight [n_rows, k] of type qtype
  *   x     : fp32 [batch, k], row stride ldx elements
- *   y     : fp32 [batch, n_rows], row stride ldy elements (written, not added)
+ *   y     : fp32 [batch, n_rows], row stride ldy elements (written, or added
+ *           to with DRACO_GEMV_ACCUMULATE: y += x @ dequant(W)^T + bias, the
+ *           residual add of a layer folded into its projection)
  *   bias  : fp32 [n_rows] or NULL
+ *   flags : 0 or DRACO_GEMV_ACCUMULATE (other bits are rejected; the
+ *           tensor-parallel entry takes no flags)
  * Replaces one executor._linear call (executor.py:47-79) whose matmul is
  * GenericGemmKernel.matmul_f32 (generic.py:32-33). */
+#define DRACO_GEMV_ACCUMULATE 1
+
 typedef struct draco_gemv_problem {
   int qtype;
-  int reserved;
+  int flags;
   const void* w;
   const float* x;
   float* y;
@@ -401,10 +407,18 @@ int draco_rope_kv_append(float* q, const float* k, const float* v, float* k_cach
  * (CPUAttentionBackend.prefill / decode, draco/runtime/cpu/attention.py):
  * softmax(q K^T / sqrt(head_dim)) V in fp32, query head h reading key/value
  * head h / (heads / kv_heads); out [n, heads, head_dim].  max_pos bounds
- * every pos[i] (max_pos < capacity; positions above it count as outside). */
+ * every pos[i] (max_pos < capacity; positions above it count as outside).
+ * The keys are taken in chunks of 32 (one CTA per token, head and chunk),
+ * merged by a second kernel through the caller's device workspace of at
+ * least draco_attention_workspace_bytes(n, heads, head_dim, max_pos) bytes,
+ * 16-byte aligned (DRACO_ERR_WORKSPACE otherwise).  head_dim a multiple of 4
+ * up to 256. */
 int draco_attention_cached(const float* q, const float* k_cache, const float* v_cache, const int* seq,
                            const int* pos, int max_pos, float* out, int n, int heads, int kv_heads, int head_dim,
-                           int capacity, int n_slots, void* stream);
+                           int capacity, int n_slots, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes draco_attention_cached needs (0 for invalid arguments). */
+size_t draco_attention_workspace_bytes(int n, int heads, int head_dim, int max_pos);
 
 /* Single-weight convenience form of draco_gguf_gemv_grouped. */
 int draco_gguf_gemv(int qtype, const void* w_tiled, const float* x, float* y, const float* bias,

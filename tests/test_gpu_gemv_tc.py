@@ -186,3 +186,36 @@ def test_launch_count_query():
     assert big.launches == 3
     big.run()
     assert big.status() == 0
+
+
+@pytest.mark.parametrize("batch", [1, 4, 32])
+def test_accumulate_flag_adds_into_y(batch):
+    """DRACO_GEMV_ACCUMULATE: y += x @ W^T + bias (the residual add of a layer),
+    on the warp-MMA kernel (batch 1, 4) and the tensor-memory one (batch 32),
+    including row groups split between CTAs."""
+    from dracort_b200 import _native as N
+
+    rng = np.random.default_rng(40 + batch)
+    probs, refs = [], []
+    for qt, n, k in [(12, 4096, 4096), (14, 1000, 768), (2, 512, 1024)]:
+        packed = Q.encode(qt, Q.random_weight(rng, n, k))
+        x = rng.standard_normal((batch, k)).astype(np.float32)
+        y0 = rng.standard_normal((batch, n)).astype(np.float32)
+        b = rng.standard_normal(n).astype(np.float32)
+        t = G.repack(qt, dev_bytes(packed), n, k)
+        probs.append(G.GemvProblem(qt, t, torch.from_numpy(x).cuda(), torch.from_numpy(y0).cuda(), n, k,
+                                   bias=torch.from_numpy(b).cuda(), accumulate=True))
+        refs.append((y0, O.linear(x, qt, packed, n, k, bias=b)))
+    G.gemv_grouped(probs)
+    for p, (y0, lin) in zip(probs, refs):
+        assert O.rel_l2(p.y.cpu().numpy() - y0, lin) < GEMV_TOL
+    # unknown flag bits and flags on the tensor-parallel entry are rejected
+    s = G._to_struct(probs[0])
+    s.flags = 2
+    arr = (N.GemvProblem * 1)(s)
+    assert N.load().draco_gguf_gemv_workspace_bytes(arr, 1, batch) == 0
+    assert "flags" in N.last_error()
+    s.flags = N.GEMV_ACCUMULATE
+    arr = (N.GemvProblem * 1)(s)
+    assert N.load().draco_gguf_gemv_grouped_tp(arr, 1, batch, None, None, 0, None) == N.DRACO_ERR_ARG
+    assert "flags" in N.last_error()
