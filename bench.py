@@ -666,31 +666,22 @@ def model_leg(args, dev, peaks, rank, world, pg, timed):
     return out
 
 
-def decode_leg(args, dev, peaks, timed):
-    """The f4 row: one full decode step of a 32-layer Llama-7B Q4_K_M GGUF model
-    through GPUExecutionBackend (the drop-in for the reference's
-    CPUExecutionBackend): embedding, per layer RMSNorm-fused q/k/v GEMV, RoPE +
-    key/value append, cached attention over 1025 positions, o_proj with the
-    residual add, RMSNorm-fused gate/up, SwiGLU-fused down with the residual
-    add, then the final norm and a Q6_K output head over 32000 tokens.
-    Batch 1 (forward_step) and batch 32 (forward_batch_decode), device-timed
-    (logits left on the device) and end to end (host token ids in, host
-    logits out, through the public methods)."""
+def decode_backend(seed, dev, n_layers=32, pos0=1024, max_num_seqs=32):
+    """A GPUExecutionBackend over a synthetic Llama-7B Q4_K_M GGUF file of
+    n_layers layers (q,k,o,gate,up Q4_K; v,down Q6_K; Q6_K output head over
+    32000 tokens; F16 embedding), with room for pos0 + 64 positions per
+    sequence.  The file is written to a temporary directory and removed once
+    loaded."""
     import shutil
     import tempfile
 
-    import torch
-
-    from dracort_b200 import gguf_ops as G
     from dracort_b200.format.gguf_file import write_gguf
     from dracort_b200.gguf_executor import GPUExecutionBackend
-    from dracort_b200.telemetry import ClockSampler
     from dracort_b200.workloads import model_layers
 
-    n_layers = getattr(args, "decode_layers", 32)
-    pos0, vocab, hidden, ffn, heads = 1024, 32000, 4096, 11008, 32
-    specs, layers = model_layers(args.seed + 700, n_layers=n_layers)
-    rng = np.random.default_rng(args.seed + 701)
+    vocab, hidden, ffn, heads = 32000, 4096, 11008, 32
+    specs, layers = model_layers(seed + 700, n_layers=n_layers)
+    rng = np.random.default_rng(seed + 701)
 
     def raw(a):
         return np.ascontiguousarray(a).reshape(-1).view(np.uint8)
@@ -718,9 +709,31 @@ def decode_leg(args, dev, peaks, timed):
         path = os.path.join(tmp, "llama7b_q4_k_m.gguf")
         write_gguf(path, tensors, meta)
         del tensors, layers
-        be = GPUExecutionBackend(path, device=dev, max_num_seqs=32, max_seq_len=pos0 + 64, q6k_order="d_first")
+        return GPUExecutionBackend(path, device=dev, max_num_seqs=max_num_seqs, max_seq_len=pos0 + 64,
+                                   q6k_order="d_first")
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
+
+
+def decode_leg(args, dev, peaks, timed):
+    """The f4 row: one full decode step of a 32-layer Llama-7B Q4_K_M GGUF model
+    through GPUExecutionBackend (the drop-in for the reference's
+    CPUExecutionBackend): embedding, per layer RMSNorm-fused q/k/v GEMV, RoPE +
+    key/value append, cached attention over 1025 positions, o_proj with the
+    residual add, RMSNorm-fused gate/up, SwiGLU-fused down with the residual
+    add, then the final norm and a Q6_K output head over 32000 tokens.
+    Batch 1 (forward_step) and batch 32 (forward_batch_decode), device-timed
+    (logits left on the device) and end to end (host token ids in, host
+    logits out, through the public methods)."""
+    import torch
+
+    from dracort_b200 import gguf_ops as G
+    from dracort_b200.telemetry import ClockSampler
+
+    n_layers = getattr(args, "decode_layers", 32)
+    pos0, vocab = 1024, 32000
+    rng = np.random.default_rng(args.seed + 702)
+    be = decode_backend(args.seed, dev, n_layers, pos0)
     for t in be.k_cache + be.v_cache:  # 1024 cached positions of every sequence
         t.normal_()
     seqs = [be.new_sequence() for _ in range(32)]
@@ -742,7 +755,7 @@ def decode_leg(args, dev, peaks, timed):
         ss = seqs[:batch]
         toks = [int(t) for t in rng.integers(0, vocab, batch)]
         bufs = be._buffers(batch)
-        per_layer = sum(g.launches for g in bufs["layers"][0]) + 3  # GEMV steps + RoPE, attention, combine
+        per_layer = sum(g.launches for g in bufs["layers"][0]) + 1  # GEMV steps + the decode attention
         head_launches = bufs["head"].launches
         slots = [be._slot[s] for s in ss]
 

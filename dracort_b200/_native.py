@@ -54,6 +54,7 @@ EXPORTED_SYMBOLS = (
     "draco_rope_kv_append",
     "draco_attention_cached",
     "draco_attention_workspace_bytes",
+    "draco_attention_decode",
     "draco_gguf_gemv_grouped",
     "draco_gguf_gemv",
     "draco_gguf_gemv_grouped_ex",
@@ -191,6 +192,8 @@ def load() -> ctypes.CDLL:
         lib.draco_rope_kv_append.argtypes = [vp] * 9 + [c_int] * 6 + [vp]
         lib.draco_attention_cached.restype = c_int
         lib.draco_attention_cached.argtypes = [vp] * 5 + [c_int, vp] + [c_int] * 6 + [vp, ctypes.c_size_t, vp]
+        lib.draco_attention_decode.restype = c_int
+        lib.draco_attention_decode.argtypes = [vp] * 9 + [c_int, vp] + [c_int] * 6 + [vp, ctypes.c_size_t, vp]
         lib.draco_attention_workspace_bytes.restype = ctypes.c_size_t
         lib.draco_attention_workspace_bytes.argtypes = [c_int] * 4
         lib.draco_gguf_gemv_launch_count.restype = c_int

@@ -188,6 +188,23 @@ int draco_attention_cached(const float* q, const float* k_cache, const float* v_
   return rc ? fail(rc, "%s", msg) : DRACO_OK;
 }
 
+int draco_attention_decode(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                           const float* cos_table, const float* sin_table, const int* seq, const int* pos,
+                           int max_pos, float* out, int n, int heads, int kv_heads, int head_dim, int capacity,
+                           int n_slots, void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_attention(n, heads, kv_heads, head_dim, capacity, n_slots, "attention_decode");
+  if (rc) return rc;
+  if (max_pos < 0 || max_pos >= capacity)
+    return fail(DRACO_ERR_SHAPE, "attention_decode: max_pos %d outside the cache capacity %d", max_pos, capacity);
+  if (n > 0 && (!q || !k || !v || !k_cache || !v_cache || !cos_table || !sin_table || !seq || !pos || !out))
+    return fail(DRACO_ERR_ARG, "attention_decode: null pointer");
+  char msg[160] = {0};
+  rc = attention_launch(2, const_cast<float*>(q), k, v, k_cache, v_cache, cos_table, sin_table, seq, pos, out, n,
+                        heads, kv_heads, head_dim, capacity, n_slots, max_pos, static_cast<float*>(workspace),
+                        workspace_bytes, (cudaStream_t)stream, msg, sizeof(msg));
+  return rc ? fail(rc, "%s", msg) : DRACO_OK;
+}
+
 size_t draco_attention_workspace_bytes(int n, int heads, int head_dim, int max_pos) {
   if (n < 0 || heads < 1 || head_dim < 1 || max_pos < 0) return 0;
   return attention_workspace_bytes(n, heads, head_dim, max_pos);

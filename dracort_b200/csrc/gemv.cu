@@ -698,6 +698,24 @@ __device__ __forceinline__ void chunk_q4x(const uint8_t* ch, const uint8_t* xs, 
   }
 }
 
+// RMSNorm row scales of a batch-1 launch, computed by the converter warps of
+// every CTA (one warp per problem, the conversion kernel's summation order)
+__shared__ float g_rms_scale[DRACO_GEMV_MAX_PROBLEMS];
+constexpr int kRmsBarrier = 2;  // named barrier: converters publish g_rms_scale, consumers wait
+
+// rsqrt(mean(x^2) + eps) of one row (draco/kernels/ops.py:46-48), summed in a
+// fixed order by one warp: lane l takes elements l, l + 32, ..., then a
+// butterfly; gemv_convert_kernel and the batch-1 converters share it, so
+// every CTA and both paths get the same bits
+__device__ __forceinline__ float rms_row_scale(const float* xr, int k, float eps, int lane) {
+  float ss = 0.f;
+#pragma unroll 8
+  for (int i = lane; i < k; i += 32) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  return 1.f / sqrtf(ss / (float)k + eps);
+}
+
 // ---------------------------------------------------------------------------
 // output of one row group
 // ---------------------------------------------------------------------------
@@ -719,7 +737,8 @@ __device__ __forceinline__ void write_rows(const GemvParams& P, const GemvProbDe
       const int64_t row = row0 + 8 * hh;
       if (row < pr.n_rows) {
         float out = v[nt][hh];
-        if (pr.in_mode == DRACO_INPUT_RMSNORM) out *= __ldcg(reinterpret_cast<const float*>(P.ws + pr.rms_off) + b);
+        if (pr.in_mode == DRACO_INPUT_RMSNORM)
+          out *= P.rms_inkernel ? g_rms_scale[pr.pidx] : __ldcg(reinterpret_cast<const float*>(P.ws + pr.rms_off) + b);
         if (pr.bias) out += pr.bias[row];
         if constexpr (!TP) {
           if (pr.accumulate) out += pr.y[(int64_t)b * pr.ldy + row];
@@ -937,13 +956,8 @@ __global__ void __launch_bounds__(kConvertWarpsPerBlock * 32) gemv_convert_kerne
     }
     if (p >= P.n_prob) return;
     const GemvProbDev& pr = P.prob[p];
-    const float* xr = pr.x + (int64_t)u * pr.ldx;
-    float ss = 0.f;
-    for (int i = lane; i < pr.k; i += 32) ss = fmaf(xr[i], xr[i], ss);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0)
-      reinterpret_cast<float*>(P.ws + pr.rms_off)[u] = 1.f / sqrtf(ss / (float)pr.k + pr.eps);
+    const float r = rms_row_scale(pr.x + (int64_t)u * pr.ldx, pr.k, pr.eps, lane);
+    if (lane == 0) reinterpret_cast<float*>(P.ws + pr.rms_off)[u] = r;
     return;
   }
   const int xb = P.xs_bytes + P.su_bytes;
@@ -1057,6 +1071,18 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     // ---------------- converters: activations ----------------
     const int c = warp - kProducerWarp - 1;
     grid_dependency_wait();  // x is written by the preceding kernel
+    if (P.rms_inkernel) {
+      // batch 1: the RMSNorm row scales first (problem p by converter p % 3),
+      // published to the consumers through a named barrier
+      for (int p = c; p < P.n_prob; p += kConvWarps) {
+        const GemvProbDev& pr = P.prob[p];
+        if (pr.in_mode != DRACO_INPUT_RMSNORM) continue;
+        const float r = rms_row_scale(pr.x, pr.k, pr.eps, lane);
+        if (lane == 0) g_rms_scale[p] = r;
+      }
+      __syncwarp();
+      asm volatile("bar.arrive %0, %1;" ::"n"(kRmsBarrier), "n"((kConvWarps + kConsumerWarps) * 32) : "memory");
+    }
     SlabCursor cur;
     cur.seek(P, s_begin);
     for (int q = 0; q < c && q < n; ++q) cur.next(P);
@@ -1096,6 +1122,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
 
   // ---------------- consumers ----------------
   grid_dependency_wait();  // y may still be read by the preceding kernel
+  if (P.rms_inkernel)  // the converters' RMSNorm row scales (before any slab is ready)
+    asm volatile("bar.sync %0, %1;" ::"n"(kRmsBarrier), "n"((kConvWarps + kConsumerWarps) * 32) : "memory");
   const int par = warp / kRowWarps, rw = warp % kRowWarps;
 
   float acc[NT][2];
@@ -1222,6 +1250,7 @@ bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, Hos
     d.cb = g.cb;
     d.slab0 = (int)slab0;
     d.in_mode = inputs ? inputs[p].mode : DRACO_INPUT_PLAIN;
+    d.pidx = p;
     d.eps = inputs ? inputs[p].eps : 0.f;
     d.aux = inputs ? inputs[p].aux : nullptr;
     d.ldaux = inputs ? inputs[p].ldaux : 0;
@@ -1235,18 +1264,19 @@ bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, Hos
   int64_t off = align256(kWsCounters + kWsCountersBytes);
   P.part_off = off;
   off = align256(off + (int64_t)kMaxCta * 2 * kRowWarps * 32 * NT * 2 * 4);
-  // dense layouts (batch >= 3): slices of the activations converted once per launch
   // activations converted once per launch by gemv_convert_kernel from batch
-  // 2 on, and at any batch when a problem's input is RMS-normalised (that
-  // kernel also computes the row scales); the workspace always holds the
-  // slices and the scales, so one size serves every input transform
+  // 2 on (that kernel also computes the RMSNorm row scales); at batch 1 the
+  // converter warps convert in the kernel and compute the row scales there
+  // too; the workspace always holds the slices and the scales, so one size
+  // serves every input transform
   bool any_rms = false;
   for (int p = 0; p < n; ++p) any_rms |= P.prob[p].in_mode == DRACO_INPUT_RMSNORM;
-  if (any_rms && !convert_once) {
-    snprintf(msg, ml, "gemv: RMSNorm inputs need the workspace entry point");
+  if (any_rms && !convert_once && batch >= 2) {
+    snprintf(msg, ml, "gemv: RMSNorm inputs at batch 2 and above need the workspace entry point");
     return false;
   }
-  P.precvt = (convert_once && (batch >= 2 || any_rms)) ? 1 : 0;
+  P.precvt = (convert_once && batch >= 2) ? 1 : 0;
+  P.rms_inkernel = (batch == 1 && any_rms) ? 1 : 0;
   for (int p = 0; p < n; ++p) {
     P.prob[p].xcv_off = -1;
     P.prob[p].rms_off = -1;
@@ -1311,6 +1341,16 @@ bool build_plan(const draco_gemv_problem* probs, int n, int batch, int n_sm, Hos
     P.cta_start[c++] = (int)s;
   }
   P.cta_start[n_cta] = (int)total;
+  // A CTA needs no more stages than it has slabs.  The smaller footprint lets
+  // the next kernel's CTAs (programmatic launch) share the SM and stream
+  // their weights while this one drains.
+  int max_run = 0;
+  for (int c2 = 0; c2 < n_cta; ++c2) max_run = std::max(max_run, P.cta_start[c2 + 1] - P.cta_start[c2]);
+  if (max_run < P.n_stages) {
+    P.n_stages = std::max(2, max_run);
+    P.mbox_off = P.n_stages * P.stage_bytes;
+    hp.smem_bytes = (size_t)P.mbox_off + mbox_bytes;
+  }
   return true;
 }
 

@@ -27,6 +27,7 @@ struct GemvProbDev {
   int64_t ldaux;
   int64_t rms_off;                   // RMSNORM: workspace offset of the per-row scales [batch]
   int accumulate;                    // y += result (DRACO_GEMV_ACCUMULATE)
+  int pidx;                          // index of the problem in the launch
 };
 
 struct GemvParams {
@@ -38,6 +39,7 @@ struct GemvParams {
   int w_stage, xs_bytes, su_bytes, stage_bytes, n_stages;
   int mbox_slots, mbox_off;  // row-group mailbox after the stages in dynamic shared memory
   int precvt;                // activations converted by gemv_convert_kernel before the launch
+  int rms_inkernel;          // batch 1: RMSNorm row scales computed by the converter warps
   int tp_world, tp_rank;     // tensor-parallel exchange (tp_world 0: plain outputs)
   uint8_t* tp_buf[DRACO_TP_MAX_WORLD];
   int64_t tp_flags_off, tp_counter_off;

@@ -52,14 +52,16 @@ cudaError_t launch_rmsnorm(const void* x, const float* w, void* out, int64_t row
 // out = silu(gate) * up over n fp32 elements (16-byte aligned).
 cudaError_t launch_swiglu_f32(const float* gate, const float* up, float* out, int64_t n, cudaStream_t st);
 
-// RoPE + key/value-cache append (op 0) or cached attention (op 1) for the GPU
-// decode step; see draco_rope_kv_append / draco_attention_cached.
+// RoPE + key/value-cache append (op 0), cached attention (op 1) or the decode
+// form with rotation and append inside (op 2) for the GPU decode step; see
+// draco_rope_kv_append / draco_attention_cached / draco_attention_decode.
 int attention_launch(int op, float* q, const float* k, const float* v, float* kc, float* vc, const float* cos_t,
                      const float* sin_t, const int* seq, const int* pos, float* out, int n, int heads, int kv_heads,
                      int hd, int capacity, int n_slots, int max_pos, float* part, size_t part_bytes, cudaStream_t st,
                      char* msg, size_t ml);
-// Bytes of the per-(token, head, 32-key chunk) partials draco_attention_cached
-// needs for n tokens over positions 0..max_pos.
+// Workspace bytes of the attention (status word, per-(token, head) counters,
+// per-(token, head, 32-key chunk) partials) for n tokens over positions
+// 0..max_pos.
 size_t attention_workspace_bytes(int n, int heads, int hd, int max_pos);
 
 // Number of SMs of the current device (cached per device).

@@ -11,10 +11,15 @@ numpy.  Here the whole step runs on one GPU:
   fused into the activation read, gate/up with the MLP RMSNorm fused, down
   with the SwiGLU product fused — plus o_proj and the output head; dense
   (F16 / F32) projections of a file go through an fp32 matmul instead;
-* RoPE (rotate-half, draco/runtime/cpu/ops.py:77-95) and the key/value-cache
-  append run in ``draco_rope_kv_append``, the causal attention over the
-  cache (draco/runtime/cpu/attention.py) in ``draco_attention_cached``
-  (fp32, grouped-query heads);
+* RoPE (rotate-half, draco/runtime/cpu/ops.py:77-95), the key/value-cache
+  append and the causal attention over the cache
+  (draco/runtime/cpu/attention.py; fp32, grouped-query heads) run as one
+  kernel, ``draco_attention_decode``, when a pass's tokens hold distinct
+  slots (decode steps), and as ``draco_rope_kv_append`` +
+  ``draco_attention_cached`` for a prompt;
+* each pass is recorded once as a CUDA graph per (rows, attention bound,
+  form) and replayed, over fixed buffers, with the residual adds folded into
+  the o_proj / down GEMVs (DRACO_GEMV_ACCUMULATE);
 * the key/value cache is a per-layer fp32 tensor [slot, kv_heads, capacity,
   head_dim]: a sequence owns one slot from ``new_sequence`` to
   ``end_sequence``.
@@ -166,7 +171,7 @@ class GPUExecutionBackend:
         self._next_seq_id = 0
         self._lib = N.load()
         self._bufs: Dict[int, Dict[str, object]] = {}
-        self._graphs: Dict[Tuple[int, int], torch.cuda.CUDAGraph] = {}
+        self._graphs: Dict[Tuple[int, int, bool], torch.cuda.CUDAGraph] = {}
         self._eager_seen: set = set()
         #: replay a captured CUDA graph per (rows, attention bound) after its first eager pass
         self.use_graphs = True
@@ -273,11 +278,13 @@ class GPUExecutionBackend:
     @property
     def launches_per_layer(self) -> int:
         """Library kernels one decode token (a pass of one row) starts per
-        layer: the four GEMV steps plus RoPE, attention chunks and combine."""
-        return sum(g.launches for g in self._buffers(1)["layers"][0]) + 3
+        layer: the four GEMV steps plus the attention."""
+        return sum(g.launches for g in self._buffers(1)["layers"][0]) + 1
 
-    def _run(self, n: int, b: Dict[str, object], max_pos: int) -> None:
-        """Enqueue one pass of the n staged rows on the current stream."""
+    def _run(self, n: int, b: Dict[str, object], max_pos: int, decode: bool) -> None:
+        """Enqueue one pass of the n staged rows on the current stream (decode:
+        the rows hold distinct cache slots, so that RoPE, the cache append and
+        the attention run as one kernel per layer)."""
         cfg = self.config
         hd, heads, kvh = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
         ids = b["ids"]
@@ -290,6 +297,15 @@ class GPUExecutionBackend:
         for li, (qkv, o_proj, gate_up, down) in enumerate(b["layers"]):
             qkv()
             kc, vc = self.k_cache[li], self.v_cache[li]
+            if decode:
+                N.check(self._lib.draco_attention_decode(
+                    q.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(), vc.data_ptr(), self.cos.data_ptr(),
+                    self.sin.data_ptr(), seq, pos, max_pos, attn.data_ptr(), n, heads, kvh, hd, self.capacity,
+                    self.max_num_seqs, ws.data_ptr(), ws.numel(), stream), "attention_decode")
+                o_proj()
+                gate_up()
+                down()
+                continue
             N.check(self._lib.draco_rope_kv_append(q.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(),
                                                    vc.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(), seq, pos,
                                                    n, heads, kvh, hd, self.capacity, self.max_num_seqs, stream),
@@ -326,17 +342,18 @@ class GPUExecutionBackend:
         b["copied"].record()
         need = int(max(positions)) + 1
         bound = min(self.capacity, max(64, 1 << (need - 1).bit_length()))
-        key = (n, bound)
+        decode = len(set(slots)) == n
+        key = (n, bound, decode)
         g = self._graphs.get(key)
         if g is not None:
             g.replay()
         elif not self.use_graphs or key not in self._eager_seen:
             self._eager_seen.add(key)
-            self._run(n, b, bound - 1)
+            self._run(n, b, bound - 1, decode)
         else:
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                self._run(n, b, bound - 1)
+                self._run(n, b, bound - 1, decode)
             self._graphs[key] = g
             g.replay()
         return b["logits"]

@@ -409,15 +409,35 @@ int draco_rope_kv_append(float* q, const float* k, const float* v, float* k_cach
  * head h / (heads / kv_heads); out [n, heads, head_dim].  max_pos bounds
  * every pos[i] (max_pos < capacity; positions above it count as outside).
  * The keys are taken in chunks of 32 (one CTA per token, head and chunk),
- * merged by a second kernel through the caller's device workspace of at
- * least draco_attention_workspace_bytes(n, heads, head_dim, max_pos) bytes,
- * 16-byte aligned (DRACO_ERR_WORKSPACE otherwise).  head_dim a multiple of 4
- * up to 256. */
+ * merged by the last chunk to finish through the caller's device workspace
+ * of at least draco_attention_workspace_bytes(n, heads, head_dim, max_pos)
+ * bytes, 16-byte aligned (DRACO_ERR_WORKSPACE otherwise), zeroed before its
+ * first use (the kernels leave its counters at zero).  Its first int32 is a
+ * status word: nonzero (DRACO_ERR_TIMEOUT) after a bounded wait for a copy
+ * ran out, the outputs of that launch then being invalid; zero the
+ * workspace again before reusing it.  head_dim a multiple of 4 up to 256;
+ * caches 16-byte aligned. */
 int draco_attention_cached(const float* q, const float* k_cache, const float* v_cache, const int* seq,
                            const int* pos, int max_pos, float* out, int n, int heads, int kv_heads, int head_dim,
                            int capacity, int n_slots, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Workspace bytes draco_attention_cached needs (0 for invalid arguments). */
+/* The decode form of a step's attention in one launch: draco_rope_kv_append
+ * followed by draco_attention_cached, for tokens that hold DISTINCT slots
+ * (one new token per sequence, as in CPUExecutionBackend.forward_batch_decode,
+ * draco/runtime/cpu/executor.py:343-396, and a one-token forward_step).  q
+ * and k arrive unrotated and q is left so; each token's new key (rotated)
+ * and value go to cache row pos[i] of slot seq[i], and the attention reads
+ * rows 0..pos[i] - 1 from the cache.  Results equal the two-call form's:
+ * the same rotation arithmetic and the same chunked attention.  Tokens of
+ * one launch sharing a slot give undefined outputs (use the two-call form
+ * for a prompt).  Workspace as for draco_attention_cached. */
+int draco_attention_decode(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                           const float* cos_table, const float* sin_table, const int* seq, const int* pos,
+                           int max_pos, float* out, int n, int heads, int kv_heads, int head_dim, int capacity,
+                           int n_slots, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes draco_attention_cached / draco_attention_decode need (0
+ * for invalid arguments). */
 size_t draco_attention_workspace_bytes(int n, int heads, int head_dim, int max_pos);
 
 /* Single-weight convenience form of draco_gguf_gemv_grouped. */

@@ -6,7 +6,10 @@
 * cached attention: within 1e-5 relative L2 of a float64 softmax(q K^T /
   sqrt(d)) V (the reference computes the scores in float64,
   draco/runtime/cpu/attention.py), per token, across 32-key chunk edges,
-  with grouped-query heads and tokens outside the cache (zero output).
+  with grouped-query heads and tokens outside the cache (zero output);
+* the one-launch decode form (draco_attention_decode): bit-identical outputs
+  and caches to RoPE + append followed by the cached attention, q untouched,
+  the workspace's status word and counters left at zero.
 """
 
 import numpy as np
@@ -137,7 +140,8 @@ def test_attention_argument_errors():
     pos = np.array([3, 4], dtype=np.int32)
     lib = N.load()
     need = lib.draco_attention_workspace_bytes(2, 4, 64, 95)
-    assert need == 2 * 4 * 3 * (64 + 4) * 4  # 96 positions = three 32-key chunks of hd + 4 floats
+    # status word, 8 counters, 96 positions = three 32-key chunk records of hd + 4 floats
+    assert need == 16 + 32 + 2 * 4 * 3 * (64 + 4) * 4
     rc, _ = _run_attention(q, kc, kc, seq, pos, 95, ws_bytes=need - 4)
     assert rc == N.DRACO_ERR_WORKSPACE and "workspace" in N.last_error()
     rc, _ = _run_attention(q, kc, kc, seq, pos, 96)  # max_pos beyond the capacity
@@ -147,3 +151,84 @@ def test_attention_argument_errors():
     kc6 = np.zeros((1, 2, 96, 6), dtype=np.float32)
     rc, _ = _run_attention(q6, kc6, kc6, seq, pos, 95)  # head_dim not a multiple of 4
     assert rc == N.DRACO_ERR_SHAPE and "head_dim" in N.last_error()
+
+
+def _workspace(n, heads, hd, max_pos):
+    need = N.load().draco_attention_workspace_bytes(n, heads, hd, max_pos)
+    return torch.zeros(int(need), dtype=torch.uint8, device="cuda")
+
+
+@pytest.mark.parametrize("heads,kv_heads,hd", [(8, 4, 32), (32, 32, 128), (4, 1, 64), (2, 2, 256)])
+def test_decode_form_equals_rope_then_cached_attention(heads, kv_heads, hd):
+    rng = np.random.default_rng(11 * hd + heads)
+    slots, cap = 9, 1100
+    # one token per slot, positions on both sides of the chunk edges (0 = an empty history)
+    pos = np.array([0, 5, 31, 32, 33, 64, 1023, 1024, 1099], dtype=np.int32)
+    seq = np.array([3, 0, 8, 1, 7, 2, 6, 4, 5], dtype=np.int32)
+    n = len(pos)
+    kc0 = torch.from_numpy(rng.standard_normal((slots, kv_heads, cap, hd)).astype(np.float32)).cuda()
+    vc0 = torch.from_numpy(rng.standard_normal((slots, kv_heads, cap, hd)).astype(np.float32)).cuda()
+    q = torch.from_numpy(rng.standard_normal((n, heads, hd)).astype(np.float32)).cuda()
+    k = torch.from_numpy(rng.standard_normal((n, kv_heads, hd)).astype(np.float32)).cuda()
+    v = torch.from_numpy(rng.standard_normal((n, kv_heads, hd)).astype(np.float32)).cuda()
+    cos, sin = (_cuda(t) for t in rope_tables(hd, cap, 10000.0))
+    seqd, posd = _cuda(seq), _cuda(pos)
+    lib = N.load()
+    out = []
+    caches = []
+    for form in ("two_call", "decode"):
+        kc, vc, qq = kc0.clone(), vc0.clone(), q.clone()
+        ws = _workspace(n, heads, hd, cap - 1)
+        o = torch.full((n, heads, hd), float("nan"), device="cuda")
+        if form == "decode":
+            rc = lib.draco_attention_decode(qq.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                            cos.data_ptr(), sin.data_ptr(), seqd.data_ptr(), posd.data_ptr(), cap - 1,
+                                            o.data_ptr(), n, heads, kv_heads, hd, cap, slots, ws.data_ptr(),
+                                            ws.numel(), None)
+            assert rc == 0, N.last_error()
+            assert torch.equal(qq, q)  # q is rotated in shared memory only
+        else:
+            rc = lib.draco_rope_kv_append(qq.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                          cos.data_ptr(), sin.data_ptr(), seqd.data_ptr(), posd.data_ptr(), n, heads,
+                                          kv_heads, hd, cap, slots, None)
+            assert rc == 0, N.last_error()
+            rc = lib.draco_attention_cached(qq.data_ptr(), kc.data_ptr(), vc.data_ptr(), seqd.data_ptr(),
+                                            posd.data_ptr(), cap - 1, o.data_ptr(), n, heads, kv_heads, hd, cap,
+                                            slots, ws.data_ptr(), ws.numel(), None)
+            assert rc == 0, N.last_error()
+        torch.cuda.synchronize()
+        assert int(ws[:16 + 4 * n * heads].count_nonzero()) == 0  # status and counters back at zero
+        out.append(o)
+        caches.append((kc, vc))
+    assert torch.equal(out[0], out[1])
+    assert torch.equal(caches[0][0], caches[1][0]) and torch.equal(caches[0][1], caches[1][1])
+    ref = _attention_ref(D.apply_rope(q.cpu().numpy(), *D.build_rope_cache(hd, cap, 10000.0), pos),
+                         caches[1][0].cpu().numpy(), caches[1][1].cpu().numpy(), seq, pos)
+    got = out[1].cpu().numpy()
+    for i in range(n):
+        assert O_rel(got[i], ref[i]) < ATTN_TOL, i
+
+
+def test_decode_form_is_repeatable_on_one_workspace():
+    """The merge counters reset themselves: ten launches on one workspace give
+    the same bits."""
+    rng = np.random.default_rng(5)
+    slots, kvh, heads, hd, cap = 4, 4, 8, 128, 300
+    kc = torch.from_numpy(rng.standard_normal((slots, kvh, cap, hd)).astype(np.float32)).cuda()
+    vc = torch.from_numpy(rng.standard_normal((slots, kvh, cap, hd)).astype(np.float32)).cuda()
+    q, k, v = (torch.from_numpy(rng.standard_normal((4, h, hd)).astype(np.float32)).cuda() for h in (heads, kvh, kvh))
+    cos, sin = (_cuda(t) for t in rope_tables(hd, cap, 10000.0))
+    seqd, posd = _cuda(np.arange(4, dtype=np.int32)), _cuda(np.array([299, 100, 40, 7], dtype=np.int32))
+    ws = _workspace(4, heads, hd, cap - 1)
+    lib = N.load()
+    outs = []
+    for _ in range(10):
+        o = torch.empty((4, heads, hd), device="cuda")
+        rc = lib.draco_attention_decode(q.data_ptr(), k.data_ptr(), v.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                        cos.data_ptr(), sin.data_ptr(), seqd.data_ptr(), posd.data_ptr(), cap - 1,
+                                        o.data_ptr(), 4, heads, kvh, hd, cap, slots, ws.data_ptr(), ws.numel(), None)
+        assert rc == 0, N.last_error()
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert all(torch.equal(o, outs[0]) for o in outs)
+    assert int(ws[:16 + 4 * 4 * heads].count_nonzero()) == 0

@@ -180,6 +180,14 @@ def test_launch_count_query():
         return G.GemvPlan(probs)
 
     assert plan([(12, 512, 1024)], 1).launches == 1          # warp-MMA kernel alone
+    # batch 1 with an RMSNorm input: the converter warps compute the row scale, no extra kernel
+    t = G.repack(12, dev_bytes(Q.encode(12, Q.random_weight(rng, 512, 1024))), 512, 1024)
+    normed = G.GemvPlan([G.GemvProblem(12, t, torch.randn((1, 1024), device="cuda"),
+                                       torch.empty((1, 512), device="cuda"), 512, 1024,
+                                       norm_weight=torch.ones(1024, device="cuda"))])
+    assert normed.launches == 1
+    normed.run()
+    assert normed.status() == 0
     assert plan([(12, 512, 1024)], 4).launches == 2          # + activation conversion
     assert plan([(12, 512, 1024), (8, 256, 1024)], 32).launches == 2  # Q8_0 keeps the warp-MMA kernel
     big = plan([(12, 4096, 4096), (14, 4096, 11008)], 32)   # row groups split between CTAs

@@ -70,6 +70,13 @@ def test_generate_greedy(backend, ref):
     assert out == list(ref["prompt"]) + [int(t) for t in ref["decode_tokens"]]
 
 
+def test_one_token_pass_launches(backend):
+    """A one-token pass starts five library kernels per layer: the q/k/v,
+    o_proj, gate/up and down GEMVs (RMSNorm scales computed inside at batch
+    1) and the attention with RoPE and the cache append inside."""
+    assert backend.launches_per_layer == 5
+
+
 def test_batch_decode_of_two_sequences(backend, ref):
     sa, sb = backend.new_sequence(), backend.new_sequence()
     try:
