@@ -33,6 +33,7 @@ return numpy fp32 logits like the reference.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Callable, Dict, List, Optional, Sequence, Tuple, Union
 
@@ -111,23 +112,61 @@ _LAYER_KEYS = {"attn_norm": "attn_norm.weight", "q": "attn_q.weight", "k": "attn
                "up": "ffn_up.weight", "down": "ffn_down.weight"}
 
 
+def cache_capacity(cfg: LlamaConfig, max_num_seqs: int, max_seq_len: Optional[int] = None,
+                   kv_budget_bytes: Optional[int] = None) -> int:
+    """Cache rows per sequence: max_seq_len, else as many as kv_budget_bytes
+    holds for max_num_seqs sequences (fp32 keys and values of every layer,
+    the budget CPUExecutionBackend takes, executor.py:145-159), else the
+    model's context length; never above the context length."""
+    cap = int(cfg.max_position_embeddings)
+    if max_seq_len is not None:
+        cap = min(int(max_seq_len), cap)
+    elif kv_budget_bytes is not None:
+        per_pos = int(max_num_seqs) * cfg.num_hidden_layers * 2 * cfg.num_key_value_heads * cfg.head_dim * 4
+        cap = min(int(kv_budget_bytes) // per_pos, cap)
+    if cap < 1:
+        raise ValueError(f"the key/value cache holds no position for {max_num_seqs} sequences "
+                         f"(max_seq_len {max_seq_len}, kv_budget_bytes {kv_budget_bytes})")
+    return cap
+
+
 class GPUExecutionBackend:
     """``CPUExecutionBackend`` for llama-family GGUF files, on one GPU.
 
-    source      : path of a .gguf file or an open GGUFFile;
-    max_num_seqs: sequences that may hold a key/value cache at once;
-    max_seq_len : cache rows per sequence (default: the model's context length);
+    Positional arguments as the reference's constructor (executor.py:133-140):
+
+    source          : path of a .gguf file, an open GGUFFile, or any reader with
+                      a ``path`` attribute (the reference's GGUFReader);
+    max_num_seqs    : sequences that may hold a key/value cache at once;
+    kv_cache_dtype  : "f32" (the cache is fp32, as the reference's default);
+    kv_budget_bytes : sizes the cache when max_seq_len is not given;
+    memory_utilization: accepted for the reference's signature; the cache is
+                      sized by max_seq_len, kv_budget_bytes or the context.
+
+    Keyword-only:
+
+    device      : the CUDA device;
+    max_seq_len : cache rows per sequence (default: from kv_budget_bytes, else
+                  the model's context length);
     q6k_order   : byte order of the file's Q6_K blocks ("d_last" for llama.cpp
                   files, "d_first" for the order the reference decodes).
     """
 
-    def __init__(self, source: Union[str, GGUFFile], device: Union[str, torch.device] = "cuda",
-                 max_num_seqs: int = 4, max_seq_len: Optional[int] = None, q6k_order: str = Q6K_D_LAST) -> None:
+    def __init__(self, source, max_num_seqs: int = 1, kv_cache_dtype: str = "f32",
+                 kv_budget_bytes: Optional[int] = None, memory_utilization: Optional[float] = None, *,
+                 device: Union[str, torch.device] = "cuda", max_seq_len: Optional[int] = None,
+                 q6k_order: str = Q6K_D_LAST) -> None:
+        if kv_cache_dtype not in ("f32", "fp32", "float32"):
+            raise ValueError(f"kv_cache_dtype {kv_cache_dtype!r}: the GPU decode step keeps an fp32 cache")
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("GPUExecutionBackend runs on a CUDA device (this library has no CPU path)")
         own = not isinstance(source, GGUFFile)
-        gf = GGUFFile(str(source)) if own else source
+        if own and not isinstance(source, (str, os.PathLike)):
+            if not hasattr(source, "path"):
+                raise TypeError("source must be a path, a GGUFFile or a reader with a 'path' attribute")
+            source = source.path
+        gf = GGUFFile(os.fspath(source)) if own else source
         try:
             self.config = cfg = LlamaConfig.from_gguf(gf)
             with torch.cuda.device(self.device):
@@ -156,7 +195,7 @@ class GPUExecutionBackend:
             self.layers.append({key: entry(f"blk.{i}.{suffix}") for key, suffix in _LAYER_KEYS.items()})
         self.final_norm = entry("output_norm.weight")
         self.lm_head = None if cfg.tie_word_embeddings else entry("output.weight")
-        cap = min(int(max_seq_len or cfg.max_position_embeddings), cfg.max_position_embeddings)
+        cap = cache_capacity(cfg, max_num_seqs, max_seq_len, kv_budget_bytes)
         self.capacity = cap
         cos, sin = rope_tables(cfg.head_dim, cap, cfg.rope_theta)
         self.cos = torch.from_numpy(cos).to(self.device)
