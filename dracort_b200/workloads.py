@@ -18,6 +18,7 @@ N(0, 1).  Algorithmic bytes count the packed weights plus fp32 x and y once.
 
 from __future__ import annotations
 
+import functools
 from dataclasses import dataclass
 from typing import List, Sequence, Tuple
 
@@ -93,7 +94,14 @@ def model_layers(seed: int, n_layers: int = MODEL_LAYERS, mix: str = "q4_k_m"):
     """Config 4: packed projections of an n-layer Llama-7B-shaped model.  One
     layer is encoded from seeded N(0, 0.02) weights; every other layer's
     projections are seeded row permutations of its packed rows (each row a
-    valid quantized N(0, 0.02) row).  Returns (specs, [layer][projection] packed)."""
+    valid quantized N(0, 0.02) row).  Returns (specs, [layer][projection] packed).
+    The last result is kept (the 32-layer step and the decode-step benchmark
+    use the same model); callers must not modify the arrays."""
+    return _model_layers(int(seed), int(n_layers), str(mix))
+
+
+@functools.lru_cache(maxsize=1)
+def _model_layers(seed: int, n_layers: int, mix: str):
     specs = layer_specs(mix)
     base = encode_specs(specs, seed)
     rng = np.random.default_rng(seed + 1)
