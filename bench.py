@@ -265,6 +265,24 @@ def cpu_prefill_leg(specs, packed, seed, tokens=64):
             "step_s": sum(best)}
 
 
+_DEQ_LAYER = {}
+
+
+def dequant_layer(specs, layer_packed):
+    """The reference's first-access transform of one layer's projections (the
+    fp32 cache, oracle port of gguf._dequantize) and its time in seconds; the
+    last layer is kept, so the config-4 and decode-step CPU legs share it."""
+    from oracle import gguf_oracle as O
+
+    key = id(layer_packed)
+    if key not in _DEQ_LAYER:
+        t0 = time.perf_counter()
+        weights = [O.dequantize_matrix(s.qtype, p, s.n_rows, s.k) for s, p in zip(specs, layer_packed)]
+        _DEQ_LAYER.clear()
+        _DEQ_LAYER[key] = (layer_packed, weights, time.perf_counter() - t0)
+    return _DEQ_LAYER[key][1], _DEQ_LAYER[key][2]
+
+
 def cpu_model_leg(specs, layer_packed, seed, n_layers, batches=(1, 32)):
     """Config 4 on the host (the reference's path): one layer's seven projections
     dequantized to the fp32 cache, then x @ W.T per projection (median of 3),
@@ -272,9 +290,7 @@ def cpu_model_leg(specs, layer_packed, seed, n_layers, batches=(1, 32)):
     from oracle import gguf_oracle as O
 
     rng = np.random.default_rng(seed + 13)
-    t0 = time.perf_counter()
-    weights = [O.dequantize_matrix(s.qtype, p, s.n_rows, s.k) for s, p in zip(specs, layer_packed)]
-    t_dequant = time.perf_counter() - t0
+    weights, t_dequant = dequant_layer(specs, layer_packed)
     out = {"dequant_layer_s": round(t_dequant, 3)}
     for b in batches:
         xs = [rng.standard_normal((b, s.k)).astype(np.float32) for s in specs]
@@ -289,6 +305,61 @@ def cpu_model_leg(specs, layer_packed, seed, n_layers, batches=(1, 32)):
             layer_s += float(np.median(ts))
         out[str(b)] = {"ms_per_step": round(layer_s * n_layers * 1e3, 3),
                        "tokens_per_s": round(b / (layer_s * n_layers), 2)}
+    return out
+
+
+def cpu_decode_leg(specs, layer_packed, seed, n_layers, pos0, vocab=32000, batches=(1, 32)):
+    """The decode step on the host, the reference's path: CPUExecutionBackend's
+    per-layer body over the fp32 weight cache and an fp32 key/value cache
+    (the oracle's restatement, layer_decode_step / layer_decode_batch, pinned
+    to OracleLlama), one layer of the model over pos0 cached positions per
+    sequence (median of 3) times n_layers, plus the final norm and a Q6_K
+    output head of `vocab` rows sampled from the layer's v rows."""
+    from oracle import llama_decode as D
+
+    rng = np.random.default_rng(seed + 17)
+    names = ["q", "k", "v", "o", "gate", "up", "down"]
+    weights, t_dequant = dequant_layer(specs, layer_packed)
+    w = dict(zip(names, weights))
+    # the head's rows are v rows (as in the GPU leg's model): its fp32 cache is
+    # the dequantized v rows gathered
+    w_out = w["v"][rng.integers(0, specs[2].n_rows, vocab)]
+    hidden_size = specs[0].k
+    heads = kvh = 32
+    hd = hidden_size // heads
+    w["attn_norm"] = (1 + 0.1 * rng.standard_normal(hidden_size)).astype(np.float32)
+    w["ffn_norm"] = (1 + 0.1 * rng.standard_normal(hidden_size)).astype(np.float32)
+    norm_out = (1 + 0.1 * rng.standard_normal(hidden_size)).astype(np.float32)
+    cos, sin = D.build_rope_cache(hd, pos0 + 1, 10000.0)
+    out = {"dequant_s": round(t_dequant, 3)}
+    for b in batches:
+        # one sequence's rows drawn, every sequence its own copy (distinct memory)
+        k0 = rng.standard_normal((pos0 + 1, kvh, hd)).astype(np.float32)
+        v0 = rng.standard_normal((pos0 + 1, kvh, hd)).astype(np.float32)
+        caches = [(k0.copy(), v0.copy()) for _ in range(b)]
+        x = rng.standard_normal((b, hidden_size)).astype(np.float32)
+
+        def layer():
+            if b == 1:
+                return D.layer_decode_step(x, w, caches[0][0], caches[0][1], pos0, cos, sin, 1e-5, heads, kvh)
+            return D.layer_decode_batch(x, w, caches, [pos0] * b, cos, sin, 1e-5, heads, kvh)
+
+        def head():
+            return D.head_step(x, norm_out, w_out, 1e-5)
+
+        times = {}
+        for nm, fn in (("layer", layer), ("head", head)):
+            fn()
+            ts = []
+            for _ in range(3):
+                t = time.perf_counter()
+                fn()
+                ts.append(time.perf_counter() - t)
+            times[nm] = float(np.median(ts))
+        step_s = times["layer"] * n_layers + times["head"]
+        out[str(b)] = {"ms_per_step": round(step_s * 1e3, 2), "tokens_per_s": round(b / step_s, 2),
+                       "layer_ms": round(times["layer"] * 1e3, 3), "head_ms": round(times["head"] * 1e3, 3)}
+        del caches
     return out
 
 
@@ -793,6 +864,20 @@ def decode_leg(args, dev, peaks, timed):
     out["value"] = out["batches"]["1"]["tokens_per_s"]
     del be
     torch.cuda.empty_cache()
+    if not args.no_cpu:
+        from dracort_b200.workloads import model_layers
+
+        specs, layers = model_layers(args.seed + 700, n_layers=n_layers)  # the GPU leg's model (cached)
+        res = cpu_decode_leg(specs, layers[0], args.seed, n_layers, pos0, vocab=vocab)
+        out["cpu_baseline"] = {
+            "value": res["1"]["tokens_per_s"], "unit": "tokens/s (batch 1)", "cores": os.cpu_count(),
+            "kind": "port", "batches": {b: res[b] for b in ("1", "32")},
+            "sample": (f"reference path (oracle port of CPUExecutionBackend's layer body: RMSNorm, matmul_f32 on "
+                       f"the fp32 weight cache, RoPE, float64-score attention over {pos0} cached fp32 positions, "
+                       f"SwiGLU, residuals; pinned to OracleLlama): one layer timed (median of 3) x {n_layers} "
+                       f"layers + the final norm and head; batch 32 as forward_batch_decode (attention per "
+                       f"sequence); first-touch dequant of one layer {res['dequant_s']:.1f} s; numpy/OpenBLAS "
+                       f"default threads")}
     return out
 
 

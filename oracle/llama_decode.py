@@ -22,7 +22,12 @@ operation in the same fp32 / float64 order:
   softmax(q K^T * (1 / sqrt(d))) V, causal mask for prefill; the scale is a
   numpy float64 scalar, so the scores and the softmax are float64 there);
 * every linear layer — executor._linear (executor.py:47-79) on weights
-  dequantized by gguf_oracle.dequantize, i.e. matmul_f32 (x @ W.T in fp32).
+  dequantized by gguf_oracle.dequantize, i.e. matmul_f32 (x @ W.T in fp32);
+* ``layer_decode_step`` / ``layer_decode_batch`` / ``head_step`` — the same
+  per-layer body (one new token; or one token for each of n sequences, as
+  forward_batch_decode) and head over contiguous cache arrays (the reference's
+  CPUKVCache.get returns the rows contiguous; attention.py:36-74), the form
+  the CPU baseline of the decode-step benchmark times.
 
 The GGUF container is parsed with dracort_b200.format.gguf_file (checked on
 its own against the reference reader's index); only the arithmetic is
@@ -146,7 +151,7 @@ class OracleLlama:
         self.kv.pop(s, None)
 
     def _linear(self, name, x):
-        return x.astype(np.float32) @ self.w[name].astype(np.float32).T
+        return x.astype(np.float32, copy=False) @ self.w[name].astype(np.float32, copy=False).T
 
     def _attention(self, s, layer, q, k, v, causal):
         """attention.py prefill: append, then attend over the whole cache."""
@@ -222,3 +227,78 @@ class OracleLlama:
                 attn[i] = self._attention(seq_ids[i], layer, qi, ki, v[i:i + 1], causal=False)[0]
             hidden = self._layer_rest(layer, hidden, attn.reshape(n, -1))
         return self._head(hidden)
+
+
+def _mm(x, w):
+    """executor._linear's matmul_f32: x @ W.T in fp32."""
+    return x.astype(np.float32, copy=False) @ w.astype(np.float32, copy=False).T
+
+
+def layer_decode_step(hidden, w, k_cache, v_cache, length, cos, sin, eps, heads, kv_heads):
+    """One decoder layer of forward_step for one new token (executor.py:282-341,
+    the loop body), attention as CPUAttentionBackend.prefill / decode computes
+    it (attention.py:36-74: append, gather rows 0..length, fp32 cast, GQA
+    repeat, float64 scores through the float64 scale, softmax, weighted sum).
+
+    hidden [1, H] fp32; w: fp32 arrays "attn_norm", "q", "k", "v", "o",
+    "ffn_norm", "gate", "up", "down" (projections [out, in]); k_cache /
+    v_cache [capacity, kv_heads, head_dim] holding `length` rows, the token's
+    key and value written to row `length`.  Returns the layer's output."""
+    hd = hidden.shape[-1] // heads
+    normed = rms_norm(hidden, w["attn_norm"], eps)
+    q = _mm(normed, w["q"]).reshape(1, heads, hd)
+    k = _mm(normed, w["k"]).reshape(1, kv_heads, hd)
+    v = _mm(normed, w["v"]).reshape(1, kv_heads, hd)
+    pos = np.array([length])
+    q = apply_rope(q, cos, sin, pos)
+    k = apply_rope(k, cos, sin, pos)
+    k_cache[length] = k[0]
+    v_cache[length] = v[0]
+    group = heads // kv_heads
+    ck = np.repeat(k_cache[:length + 1].astype(np.float32), group, axis=1)
+    cv = np.repeat(v_cache[:length + 1].astype(np.float32), group, axis=1)
+    scale = 1.0 / np.sqrt(hd)
+    q_t = np.transpose(q.astype(np.float32), (1, 0, 2))
+    scores = np.einsum("hqd,hkd->hqk", q_t, np.transpose(ck, (1, 0, 2))) * scale
+    out = np.einsum("hqk,hkd->hqd", softmax(scores, axis=-1), np.transpose(cv, (1, 0, 2)))
+    attn = np.transpose(out, (1, 0, 2)).astype(np.float32).reshape(1, -1)
+    hidden = hidden + _mm(attn, w["o"])
+    normed = rms_norm(hidden, w["ffn_norm"], eps)
+    return hidden + _mm(swiglu(_mm(normed, w["gate"]), _mm(normed, w["up"])), w["down"])
+
+
+def layer_decode_batch(hidden, w, caches, lengths, cos, sin, eps, heads, kv_heads):
+    """One decoder layer of forward_batch_decode (executor.py:343-396): the
+    projections over all n rows at once, RoPE and the attention per sequence
+    (row i over caches[i] = (k_cache, v_cache) holding lengths[i] rows, its
+    key and value written to row lengths[i]), then o_proj and the MLP over
+    all rows.  hidden [n, H] fp32."""
+    n = hidden.shape[0]
+    hd = hidden.shape[-1] // heads
+    normed = rms_norm(hidden, w["attn_norm"], eps)
+    q = _mm(normed, w["q"]).reshape(n, heads, hd)
+    k = _mm(normed, w["k"]).reshape(n, kv_heads, hd)
+    v = _mm(normed, w["v"]).reshape(n, kv_heads, hd)
+    group = heads // kv_heads
+    scale = 1.0 / np.sqrt(hd)
+    attn = np.empty((n, heads, hd), dtype=np.float32)
+    for i in range(n):
+        length = int(lengths[i])
+        kc, vc = caches[i]
+        qi = apply_rope(q[i:i + 1], cos, sin, np.array([length]))
+        ki = apply_rope(k[i:i + 1], cos, sin, np.array([length]))
+        kc[length] = ki[0]
+        vc[length] = v[i]
+        ck = np.repeat(kc[:length + 1].astype(np.float32), group, axis=1)
+        cv = np.repeat(vc[:length + 1].astype(np.float32), group, axis=1)
+        scores = np.einsum("hqd,hkd->hqk", np.transpose(qi, (1, 0, 2)), np.transpose(ck, (1, 0, 2))) * scale
+        o = np.einsum("hqk,hkd->hqd", softmax(scores, axis=-1), np.transpose(cv, (1, 0, 2)))
+        attn[i] = np.transpose(o, (1, 0, 2))[0]
+    hidden = hidden + _mm(attn.reshape(n, -1), w["o"])
+    normed = rms_norm(hidden, w["ffn_norm"], eps)
+    return hidden + _mm(swiglu(_mm(normed, w["gate"]), _mm(normed, w["up"])), w["down"])
+
+
+def head_step(hidden, norm_w, w_out, eps):
+    """The final RMSNorm and the output projection (executor.py:330-341)."""
+    return _mm(rms_norm(hidden, norm_w, eps), w_out)

@@ -8,6 +8,7 @@ import numpy as np
 import pytest
 
 from dracort_b200.format.gguf_file import GGUFFile
+from oracle import llama_decode as D
 from oracle.llama_decode import OracleLlama
 
 HERE = Path(__file__).resolve().parent / "golden"
@@ -75,3 +76,76 @@ def test_product_rope_tables_equal_the_reference_construction():
     rc, rs = build_rope_cache(cfg.head_dim, cfg.max_position_embeddings, cfg.rope_theta)
     assert np.array_equal(c.view(np.uint32), rc.astype(np.float32).view(np.uint32))
     assert np.array_equal(s.view(np.uint32), rs.astype(np.float32).view(np.uint32))
+
+
+def test_layer_decode_step_equals_the_oracle_model():
+    """layer_decode_step + head_step over array caches reproduce
+    OracleLlama.forward_step for a decode token (the form the decode-step
+    benchmark's CPU baseline times)."""
+    gf = GGUFFile(str(HERE / "tiny_llama_decode.gguf"))
+    try:
+        m = D.OracleLlama(gf, "d_first")
+    finally:
+        gf.close()
+    cfg = m.cfg
+    heads, kvh, hd = cfg["num_attention_heads"], cfg["num_key_value_heads"], m.head_dim
+    s = m.new_sequence()
+    prompt = [1, 5, 17, 42, 7, 63]
+    m.forward_step(s, prompt, 0)
+    pos, tok = len(prompt), 9
+    caches = []
+    for layer in range(cfg["num_hidden_layers"]):
+        kc = np.zeros((16, kvh, hd), dtype=np.float32)
+        vc = np.zeros_like(kc)
+        kc[:pos] = np.stack(m.kv[s][layer][0])
+        vc[:pos] = np.stack(m.kv[s][layer][1])
+        caches.append((kc, vc))
+    want = m.forward_step(s, [tok], pos)
+    hidden = m.w["token_embd.weight"][[tok]].astype(np.float32)
+    for layer, (kc, vc) in enumerate(caches):
+        p = f"blk.{layer}."
+        w = {"attn_norm": m.w[p + "attn_norm.weight"], "q": m.w[p + "attn_q.weight"], "k": m.w[p + "attn_k.weight"],
+             "v": m.w[p + "attn_v.weight"], "o": m.w[p + "attn_output.weight"],
+             "ffn_norm": m.w[p + "ffn_norm.weight"], "gate": m.w[p + "ffn_gate.weight"],
+             "up": m.w[p + "ffn_up.weight"], "down": m.w[p + "ffn_down.weight"]}
+        hidden = D.layer_decode_step(hidden, w, kc, vc, pos, m.cos, m.sin, cfg["rms_norm_eps"], heads, kvh)
+    got = D.head_step(hidden, m.w["output_norm.weight"], m.w["output.weight"], cfg["rms_norm_eps"])[0]
+    assert np.allclose(got, want, rtol=1e-6, atol=1e-6)
+
+
+def test_layer_decode_batch_equals_the_oracle_model():
+    """layer_decode_batch + head_step reproduce OracleLlama.forward_batch_decode
+    for two sequences at different lengths."""
+    gf = GGUFFile(str(HERE / "tiny_llama_decode.gguf"))
+    try:
+        m = D.OracleLlama(gf, "d_first")
+    finally:
+        gf.close()
+    cfg = m.cfg
+    heads, kvh, hd = cfg["num_attention_heads"], cfg["num_key_value_heads"], m.head_dim
+    prompts = [[1, 5, 17, 42, 7, 63], [3, 88, 12]]
+    seqs = [m.new_sequence() for _ in prompts]
+    for sq, pr in zip(seqs, prompts):
+        m.forward_step(sq, pr, 0)
+    toks, lengths = [11, 30], [len(p) for p in prompts]
+    caches = []
+    for layer in range(cfg["num_hidden_layers"]):
+        per = []
+        for sq, n0 in zip(seqs, lengths):
+            kc = np.zeros((16, kvh, hd), dtype=np.float32)
+            vc = np.zeros_like(kc)
+            kc[:n0] = np.stack(m.kv[sq][layer][0])
+            vc[:n0] = np.stack(m.kv[sq][layer][1])
+            per.append((kc, vc))
+        caches.append(per)
+    want = m.forward_batch_decode(seqs, toks, lengths)
+    hidden = m.w["token_embd.weight"][toks].astype(np.float32)
+    for layer in range(cfg["num_hidden_layers"]):
+        p = f"blk.{layer}."
+        w = {"attn_norm": m.w[p + "attn_norm.weight"], "q": m.w[p + "attn_q.weight"], "k": m.w[p + "attn_k.weight"],
+             "v": m.w[p + "attn_v.weight"], "o": m.w[p + "attn_output.weight"],
+             "ffn_norm": m.w[p + "ffn_norm.weight"], "gate": m.w[p + "ffn_gate.weight"],
+             "up": m.w[p + "ffn_up.weight"], "down": m.w[p + "ffn_down.weight"]}
+        hidden = D.layer_decode_batch(hidden, w, caches[layer], lengths, m.cos, m.sin, cfg["rms_norm_eps"], heads, kvh)
+    got = D.head_step(hidden, m.w["output_norm.weight"], m.w["output.weight"], cfg["rms_norm_eps"])
+    assert np.allclose(got, want, rtol=1e-6, atol=1e-6)
