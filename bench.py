@@ -1190,34 +1190,49 @@ def run_ours(args):
     # each leg runs inside an NVTX range named after it, so that a profiler
     # can select one leg's launches (ncu --nvtx --nvtx-include "<leg>/")
     nvtx = torch.cuda.nvtx
+
+    def leg(name, fn):
+        """One leg inside an NVTX range.  At one rank a leg that fails reports
+        its error in the line instead of ending the run (the headline value is
+        already measured); with several ranks an error propagates, so that no
+        rank skips collectives the others enter."""
+        nvtx.range_push(name)
+        try:
+            if world > 1:
+                return fn()
+            try:
+                return fn()
+            except Exception as e:  # noqa: BLE001 - reported in the JSON line
+                import traceback
+
+                traceback.print_exc()
+                err = {"error": f"{type(e).__name__}: {e}"[:500]}
+                del e
+                try:
+                    torch.cuda.synchronize()
+                    torch.cuda.empty_cache()
+                except Exception:  # noqa: BLE001 - a sticky device error: later legs report theirs
+                    pass
+                return err
+        finally:
+            nvtx.range_pop()
+
     prefill = None
     if not args.no_prefill:
-        nvtx.range_push("prefill")
-        prefill = prefill_leg(args, dev, peaks, rank, world, pg, timed, not args.no_e2e, not args.no_cpu)
-        nvtx.range_pop()
-
+        prefill = leg("prefill", lambda: prefill_leg(args, dev, peaks, rank, world, pg, timed, not args.no_e2e,
+                                                     not args.no_cpu))
     q8 = None
     if not args.no_q8 and world == 1:
-        nvtx.range_push("q8_0")
-        q8 = q8_0_leg(args, dev, peaks, timed, not args.no_e2e, rank == 0 and not args.no_cpu)
-        nvtx.range_pop()
-
+        q8 = leg("q8_0", lambda: q8_0_leg(args, dev, peaks, timed, not args.no_e2e, rank == 0 and not args.no_cpu))
     moe = None
     if not args.no_moe:
-        nvtx.range_push("moe")
-        moe = moe_leg(args, dev, peaks, rank, world, pg, timed)
-        nvtx.range_pop()
+        moe = leg("moe", lambda: moe_leg(args, dev, peaks, rank, world, pg, timed))
     model = None
     if not args.no_model:
-        nvtx.range_push("model")
-        model = model_leg(args, dev, peaks, rank, world, pg, timed)
-        nvtx.range_pop()
-
+        model = leg("model", lambda: model_leg(args, dev, peaks, rank, world, pg, timed))
     decode = None
     if not args.no_decode and world == 1:
-        nvtx.range_push("decode")
-        decode = decode_leg(args, dev, peaks, timed)
-        nvtx.range_pop()
+        decode = leg("decode", lambda: decode_leg(args, dev, peaks, timed))
 
     # -- CPU baseline (rank 0, N=1) --------------------------------------------
     cpu = None

@@ -1,5 +1,5 @@
 """GPU decode step for llama-family GGUF models: a drop-in for the reference's
-``CPUExecutionBackend`` (draco/runtime/cpu/executor.py:132-396) on the GGUF
+``CPUExecutionBackend`` (draco/runtime/cpu/executor.py:132-413) on the GGUF
 path, where ``LLM._generate_single_gguf`` (draco/engine/llm.py:1158-1199)
 drives it through ``new_sequence`` / ``forward_step`` / ``end_sequence``.
 
@@ -7,10 +7,11 @@ The reference dequantizes every weight to an fp32 cache on the host and runs
 numpy.  Here the whole step runs on one GPU:
 
 * weights stay packed (the TILED layout of ``gguf_loader.load_gguf``); each
-  layer takes three grouped GEMV calls — q/k/v with the attention RMSNorm
-  fused into the activation read, gate/up with the MLP RMSNorm fused, down
-  with the SwiGLU product fused — plus o_proj and the output head; dense
-  (F16 / F32) projections of a file go through an fp32 matmul instead;
+  layer takes four GEMV steps — q/k/v with the attention RMSNorm fused into
+  the activation read, o_proj adding into the hidden state, gate/up with the
+  MLP RMSNorm fused, down reading the SwiGLU product and adding into the
+  hidden state — and the output head reads the final RMSNorm the same way;
+  dense (F16 / F32) projections of a file go through an fp32 matmul instead;
 * RoPE (rotate-half, draco/runtime/cpu/ops.py:77-95), the key/value-cache
   append and the causal attention over the cache
   (draco/runtime/cpu/attention.py; fp32, grouped-query heads) run as one
