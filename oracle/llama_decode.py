@@ -59,7 +59,8 @@ _BLOCK_NAMES = {
 
 
 def config_from_metadata(meta: Dict, tensor_names) -> Dict:
-    """gguf.py:680-770, llama branch."""
+    """gguf.py:680-770, llama branch (the flags of gguf.py:765-768 tested on
+    layer 0's tensors under their GGUF names)."""
     arch = meta.get("general.architecture", "llama")
     p = arch + "."
     hidden = int(meta[p + "embedding_length"])
@@ -78,6 +79,9 @@ def config_from_metadata(meta: Dict, tensor_names) -> Dict:
         "vocab_size": vocab,
         "max_position_embeddings": int(meta.get(p + "context_length") or 4096),
         "rope_theta": float(meta.get(p + "rope.freq_base", 10000.0)),
+        "qkv_fused": "blk.0.attn_qkv.weight" in tensor_names,
+        "attention_bias": "blk.0.attn_q.bias" in tensor_names,
+        "mlp_bias": "blk.0.ffn_gate.bias" in tensor_names,
         "rms_norm_eps": float(rms),
         "tie_word_embeddings": bool(meta.get(p + "tie_embeddings", not has_output)),
     }
@@ -150,8 +154,13 @@ class OracleLlama:
     def end_sequence(self, s: int) -> None:
         self.kv.pop(s, None)
 
-    def _linear(self, name, x):
-        return x.astype(np.float32, copy=False) @ self.w[name].astype(np.float32, copy=False).T
+    def _linear(self, name, x, bias=None):
+        """executor._linear (executor.py:47-79): matmul_f32, then `+ bias` when
+        the bias tensor exists."""
+        out = x.astype(np.float32, copy=False) @ self.w[name].astype(np.float32, copy=False).T
+        if bias is not None and bias in self.w:
+            out = out + self.w[bias]
+        return out
 
     def _attention(self, s, layer, q, k, v, causal):
         """attention.py prefill: append, then attend over the whole cache."""
@@ -175,20 +184,32 @@ class OracleLlama:
         return np.transpose(out, (1, 0, 2)).astype(q.dtype)
 
     def _layer_qkv(self, layer, hidden, n):
+        """executor.py:243-271.  A fused q/k/v weight is split by columns of its
+        output; its bias is looked up under the GPT-2 name there, which a
+        llama-family file never has, so none is added."""
         cfg, p = self.cfg, f"blk.{layer}."
+        heads, kvh, hd = cfg["num_attention_heads"], cfg["num_key_value_heads"], self.head_dim
         normed = rms_norm(hidden, self.w[p + "attn_norm.weight"], cfg["rms_norm_eps"])
-        q = self._linear(p + "attn_q.weight", normed).reshape(n, cfg["num_attention_heads"], self.head_dim)
-        k = self._linear(p + "attn_k.weight", normed).reshape(n, cfg["num_key_value_heads"], self.head_dim)
-        v = self._linear(p + "attn_v.weight", normed).reshape(n, cfg["num_key_value_heads"], self.head_dim)
-        return q, k, v
+        if cfg["qkv_fused"]:
+            qkv = self._linear(p + "attn_qkv.weight", normed)
+            q, k, v = qkv[:, :heads * hd], qkv[:, heads * hd:(heads + kvh) * hd], qkv[:, (heads + kvh) * hd:]
+        else:
+            b = cfg["attention_bias"]
+            q = self._linear(p + "attn_q.weight", normed, p + "attn_q.bias" if b else None)
+            k = self._linear(p + "attn_k.weight", normed, p + "attn_k.bias" if b else None)
+            v = self._linear(p + "attn_v.weight", normed, p + "attn_v.bias" if b else None)
+        return q.reshape(n, heads, hd), k.reshape(n, kvh, hd), v.reshape(n, kvh, hd)
 
     def _layer_rest(self, layer, hidden, attn_out):
+        """o_proj (executor.py:273-277, its bias under attention_bias) and the
+        gated MLP (executor.py:208-224, biases under mlp_bias)."""
         cfg, p = self.cfg, f"blk.{layer}."
-        hidden = hidden + self._linear(p + "attn_output.weight", attn_out)
+        ab, mb = cfg["attention_bias"], cfg["mlp_bias"]
+        hidden = hidden + self._linear(p + "attn_output.weight", attn_out, p + "attn_output.bias" if ab else None)
         normed = rms_norm(hidden, self.w[p + "ffn_norm.weight"], cfg["rms_norm_eps"])
-        gate = self._linear(p + "ffn_gate.weight", normed)
-        up = self._linear(p + "ffn_up.weight", normed)
-        return hidden + self._linear(p + "ffn_down.weight", swiglu(gate, up))
+        gate = self._linear(p + "ffn_gate.weight", normed, p + "ffn_gate.bias" if mb else None)
+        up = self._linear(p + "ffn_up.weight", normed, p + "ffn_up.bias" if mb else None)
+        return hidden + self._linear(p + "ffn_down.weight", swiglu(gate, up), p + "ffn_down.bias" if mb else None)
 
     def _head(self, hidden):
         cfg = self.cfg

@@ -1,6 +1,9 @@
 """The decode-step oracle (oracle/llama_decode.py) is pinned to the reference
-executor's own logits on tests/golden/tiny_llama_decode.gguf
-(tests/golden/make_decode_golden.py ran draco.runtime.cpu.executor on it)."""
+executor's own logits on three fixtures (tests/golden/make_decode_golden.py
+ran draco.runtime.cpu.executor on each): tiny_llama_decode.gguf (every GPU
+block type), tiny_qwen2_decode.gguf (q/k/v and o_proj biases, tied
+embeddings, rope base 1e6) and tiny_fused_decode.gguf (a fused q/k/v weight
+with grouped-query rows, gate/up/down biases)."""
 
 from pathlib import Path
 
@@ -14,14 +17,22 @@ from oracle.llama_decode import OracleLlama
 HERE = Path(__file__).resolve().parent / "golden"
 
 
+FIXTURES = ["tiny_llama_decode", "tiny_qwen2_decode", "tiny_fused_decode"]
+
+
+@pytest.fixture(scope="module", params=FIXTURES)
+def name(request):
+    return request.param
+
+
 @pytest.fixture(scope="module")
-def ref():
-    return np.load(HERE / "tiny_llama_decode_ref.npz")
+def ref(name):
+    return np.load(HERE / f"{name}_ref.npz")
 
 
 @pytest.fixture()
-def model():
-    gf = GGUFFile(str(HERE / "tiny_llama_decode.gguf"))
+def model(name):
+    gf = GGUFFile(str(HERE / f"{name}.gguf"))
     try:
         yield OracleLlama(gf, q6k_order="d_first")
     finally:
@@ -149,3 +160,17 @@ def test_layer_decode_batch_equals_the_oracle_model():
         hidden = D.layer_decode_batch(hidden, w, caches[layer], lengths, m.cos, m.sin, cfg["rms_norm_eps"], heads, kvh)
     got = D.head_step(hidden, m.w["output_norm.weight"], m.w["output.weight"], cfg["rms_norm_eps"])
     assert np.allclose(got, want, rtol=1e-6, atol=1e-6)
+
+
+def test_fixture_flags_follow_the_reference_mapping():
+    """gguf.py:765-768: the flags come from layer 0's tensors."""
+    want = {"tiny_llama_decode": (False, False, False, False),
+            "tiny_qwen2_decode": (False, True, False, True),
+            "tiny_fused_decode": (True, False, True, False)}
+    for nm, flags in want.items():
+        gf = GGUFFile(str(HERE / f"{nm}.gguf"))
+        try:
+            cfg = D.config_from_metadata(gf.metadata, gf.tensors)
+        finally:
+            gf.close()
+        assert (cfg["qkv_fused"], cfg["attention_bias"], cfg["mlp_bias"], cfg["tie_word_embeddings"]) == flags, nm
