@@ -45,7 +45,7 @@ from dracort_b200 import _native as N
 from dracort_b200 import gguf_ops as G
 from dracort_b200.exceptions import DracoFormatError
 from dracort_b200.format.gguf_file import GGUFFile
-from dracort_b200.format.gguf_types import Q6K_D_LAST
+from dracort_b200.format.gguf_types import BLOCK_LAYOUTS, GGML_TYPE_Q6_K, Q6K_D_LAST
 from dracort_b200.gguf_loader import DeviceWeight, load_gguf
 
 _ROWS = N.GEMV_MAX_BATCH  # activation rows per GEMV call
@@ -65,6 +65,9 @@ class LlamaConfig:
     rope_theta: float
     rms_norm_eps: float
     tie_word_embeddings: bool
+    qkv_fused: bool = False       # one attn_qkv weight per layer (q rows, then k, then v)
+    attention_bias: bool = False  # q/k/v (unfused) and o_proj biases where the file has them
+    mlp_bias: bool = False        # gate/up/down biases where the file has them
 
     @property
     def head_dim(self) -> int:
@@ -97,7 +100,11 @@ class LlamaConfig:
                    num_key_value_heads=int(get("attention.head_count_kv") or heads), vocab_size=int(vocab),
                    max_position_embeddings=int(get("context_length") or 4096),
                    rope_theta=float(get("rope.freq_base", 10000.0)), rms_norm_eps=float(eps),
-                   tie_word_embeddings=bool(get("tie_embeddings", "output.weight" not in gf.tensors)))
+                   tie_word_embeddings=bool(get("tie_embeddings", "output.weight" not in gf.tensors)),
+                   # the flags of gguf.py:765-768, from layer 0's tensors
+                   qkv_fused="blk.0.attn_qkv.weight" in gf.tensors,
+                   attention_bias="blk.0.attn_q.bias" in gf.tensors,
+                   mlp_bias="blk.0.ffn_gate.bias" in gf.tensors)
 
 
 def rope_tables(head_dim: int, max_positions: int, theta: float):
@@ -108,9 +115,50 @@ def rope_tables(head_dim: int, max_positions: int, theta: float):
     return np.cos(freqs).astype(np.float32), np.sin(freqs).astype(np.float32)
 
 
-_LAYER_KEYS = {"attn_norm": "attn_norm.weight", "q": "attn_q.weight", "k": "attn_k.weight", "v": "attn_v.weight",
-               "o": "attn_output.weight", "ffn_norm": "ffn_norm.weight", "gate": "ffn_gate.weight",
-               "up": "ffn_up.weight", "down": "ffn_down.weight"}
+_PROJ = {"q": "attn_q", "k": "attn_k", "v": "attn_v", "o": "attn_output", "gate": "ffn_gate", "up": "ffn_up",
+         "down": "ffn_down"}
+
+
+def layer_tensors(cfg: LlamaConfig, tensor_names, layer: int) -> Dict[str, object]:
+    """The tensors behind layer `layer`, as the reference's executor picks them
+    (executor.py:208-277 with the flags of gguf.py:765-768):
+
+    "attn_norm", "ffn_norm": norm weight names;
+    "proj": {q, k, v, o, gate, up, down: (tensor name, (row0, row1) or None)}
+        — a fused attn_qkv weight gives q, k and v as row ranges of it;
+    "bias": {projection: bias tensor name or None} — q/k/v and o_proj under
+        attention_bias (none for a fused weight: the reference looks its bias
+        up under the GPT-2 name, which a llama-family file never has),
+        gate/up/down under mlp_bias; only biases the file has."""
+    p = f"blk.{layer}."
+    names = set(tensor_names)
+    proj = {key: (p + stem + ".weight", None) for key, stem in _PROJ.items()}
+    if cfg.qkv_fused:
+        hd = cfg.head_dim
+        qr, kr = cfg.num_attention_heads * hd, cfg.num_key_value_heads * hd
+        fused = p + "attn_qkv.weight"
+        proj["q"], proj["k"], proj["v"] = (fused, (0, qr)), (fused, (qr, qr + kr)), (fused, (qr + kr, qr + 2 * kr))
+    bias = {}
+    for key, stem in _PROJ.items():
+        on = cfg.mlp_bias if key in ("gate", "up", "down") else cfg.attention_bias
+        if key in ("q", "k", "v") and cfg.qkv_fused:
+            on = False
+        name = p + stem + ".bias"
+        bias[key] = name if on and name in names else None
+    return {"attn_norm": p + "attn_norm.weight", "ffn_norm": p + "ffn_norm.weight", "proj": proj, "bias": bias}
+
+
+def _row_range_weight(gf: GGUFFile, name: str, r0: int, r1: int, device: torch.device,
+                      q6k_order: str) -> DeviceWeight:
+    """Rows [r0, r1) of a quantized GGUF weight, regrouped on the device (the
+    rows of a GGUF weight are independent runs of blocks)."""
+    t = gf.tensor(name)
+    bs, bb = BLOCK_LAYOUTS[t.ggml_type]
+    rows = np.ascontiguousarray(np.asarray(gf.payload(name)).reshape(t.n_rows, t.k // bs * bb)[r0:r1])
+    raw = torch.from_numpy(rows.reshape(-1)).to(device)
+    layout = "gguf_dlast" if (t.ggml_type == GGML_TYPE_Q6_K and q6k_order == Q6K_D_LAST) else "gguf"
+    tiled = G.repack(t.ggml_type, raw, r1 - r0, t.k, layout=layout)
+    return DeviceWeight(name, t.ggml_type, tiled, r1 - r0, t.k, r0, r1, 0, t.k)
 
 
 def cache_capacity(cfg: LlamaConfig, max_num_seqs: int, max_seq_len: Optional[int] = None,
@@ -170,8 +218,16 @@ class GPUExecutionBackend:
         gf = GGUFFile(os.fspath(source)) if own else source
         try:
             self.config = cfg = LlamaConfig.from_gguf(gf)
+            plans = [layer_tensors(cfg, gf.tensors, i) for i in range(cfg.num_hidden_layers)]
+            # quantized fused q/k/v weights load as three row ranges; everything else whole
+            ranged = {(nm, rr) for pl in plans for nm, rr in pl["proj"].values() if rr is not None}
+            by_rows = {nm for nm, _ in ranged if gf.tensor(nm).is_quantized}
             with torch.cuda.device(self.device):
-                loaded = load_gguf(gf, self.device, q6k_order=q6k_order)
+                loaded = load_gguf(gf, self.device, q6k_order=q6k_order,
+                                   names=[n for n in gf.tensors if n not in by_rows])
+                for nm, (r0, r1) in ranged:
+                    if nm in by_rows:
+                        loaded[(nm, (r0, r1))] = _row_range_weight(gf, nm, r0, r1, self.device, q6k_order)
         finally:
             if own:
                 gf.close()
@@ -191,9 +247,22 @@ class GPUExecutionBackend:
         if isinstance(emb, DeviceWeight):
             emb = G.dequantize(emb.qtype, emb.tiled, emb.n_rows, emb.k, layout="tiled")
         self.embed = emb  # [vocab, hidden] fp32
+
+        def proj(name, rows):
+            if rows is None:
+                return entry(name)
+            if (name, rows) in loaded:  # a quantized fused weight, loaded by rows
+                return loaded[(name, rows)]
+            return entry(name)[rows[0]:rows[1]].contiguous()  # a dense fused weight
+
         self.layers: List[Dict[str, object]] = []
-        for i in range(cfg.num_hidden_layers):
-            self.layers.append({key: entry(f"blk.{i}.{suffix}") for key, suffix in _LAYER_KEYS.items()})
+        for pl in plans:
+            L = {"attn_norm": entry(pl["attn_norm"]), "ffn_norm": entry(pl["ffn_norm"])}
+            for key, (name, rows) in pl["proj"].items():
+                L[key] = proj(name, rows)
+                b = pl["bias"][key]
+                L[key + "_bias"] = None if b is None else entry(b).reshape(-1)
+            self.layers.append(L)
         self.final_norm = entry("output_norm.weight")
         self.lm_head = None if cfg.tie_word_embeddings else entry("output.weight")
         cap = cache_capacity(cfg, max_num_seqs, max_seq_len, kv_budget_bytes)
@@ -242,21 +311,24 @@ class GPUExecutionBackend:
     # -- compute --------------------------------------------------------------
     def _group(self, weights: Sequence[object], x: torch.Tensor, ys: Sequence[torch.Tensor],
                norm: Optional[torch.Tensor] = None, up: Optional[torch.Tensor] = None,
-               accumulate: bool = False) -> Callable[[], None]:
-        """One projection step over fixed buffers: ys[i] (+)= f(x) @ W_i^T with
-        f the RMSNorm by `norm`, silu(x) * up, or nothing.  Packed weights go
-        in one GemvPlan (the transform fused into the activation read, the
-        add into the output write); dense ones through an fp32 matmul of the
-        transformed x.  Returns a callable enqueuing the step on the current
-        stream; its ``launches`` counts the library kernels it starts."""
+               accumulate: bool = False, biases: Optional[Sequence[Optional[torch.Tensor]]] = None
+               ) -> Callable[[], None]:
+        """One projection step over fixed buffers: ys[i] (+)= f(x) @ W_i^T
+        (+ biases[i]) with f the RMSNorm by `norm`, silu(x) * up, or nothing.
+        Packed weights go in one GemvPlan (the transform fused into the
+        activation read, the bias and the add into the output write); dense
+        ones through an fp32 matmul of the transformed x.  Returns a callable
+        enqueuing the step on the current stream; its ``launches`` counts the
+        library kernels it starts."""
         eps = self.config.rms_norm_eps
+        biases = list(biases) if biases is not None else [None] * len(weights)
         probs, dense = [], []
-        for w, y in zip(weights, ys):
+        for w, y, bias in zip(weights, ys, biases):
             if isinstance(w, DeviceWeight):
-                probs.append(G.GemvProblem(w.qtype, w.tiled, x, y, w.n_rows, w.k, norm_weight=norm, norm_eps=eps,
-                                           up=up, accumulate=accumulate))
+                probs.append(G.GemvProblem(w.qtype, w.tiled, x, y, w.n_rows, w.k, bias=bias, norm_weight=norm,
+                                           norm_eps=eps, up=up, accumulate=accumulate))
             else:
-                dense.append((w, y))
+                dense.append((w, y, bias))
         plans = [G.GemvPlan(probs[i:i + N.GEMV_MAX_PROBLEMS]) for i in range(0, len(probs), N.GEMV_MAX_PROBLEMS)]
 
         def run() -> None:
@@ -269,11 +341,13 @@ class GPUExecutionBackend:
                     xd = x * torch.sigmoid(x) * up
                 else:
                     xd = x
-                for w, y in dense:
+                for w, y, bias in dense:
                     if accumulate:
                         y.addmm_(xd, w.t())
                     else:
                         torch.matmul(xd, w.t(), out=y)
+                    if bias is not None:
+                        y.add_(bias)
 
         run.launches = sum(pl.launches for pl in plans)  # type: ignore[attr-defined]
         return run
@@ -299,16 +373,18 @@ class GPUExecutionBackend:
              "pos": torch.zeros(n, dtype=torch.int32, device=dev),
              "hidden": f32(n, cfg.hidden_size), "q": f32(n, heads * hd), "k": f32(n, kvh * hd),
              "v": f32(n, kvh * hd), "attn": f32(n, heads * hd), "gate": f32(n, ffn),
-             "up": f32(n, ffn), "logits": f32(n, cfg.vocab_size),
+             "up": f32(n, ffn), "logits": f32(n, cfg.vocab_size), "normed": f32(n, cfg.hidden_size),
              "copied": torch.cuda.Event()}
         ws_bytes = self._lib.draco_attention_workspace_bytes(n, heads, hd, self.capacity - 1)
         b["attn_ws"] = torch.zeros(int(ws_bytes), dtype=torch.uint8, device=dev)
         h = b["hidden"]
         b["layers"] = [
-            (self._group([L["q"], L["k"], L["v"]], h, [b["q"], b["k"], b["v"]], norm=L["attn_norm"]),
-             self._group([L["o"]], b["attn"], [h], accumulate=True),
-             self._group([L["gate"], L["up"]], h, [b["gate"], b["up"]], norm=L["ffn_norm"]),
-             self._group([L["down"]], b["gate"], [h], up=b["up"], accumulate=True))
+            (self._group([L["q"], L["k"], L["v"]], h, [b["q"], b["k"], b["v"]], norm=L["attn_norm"],
+                         biases=[L["q_bias"], L["k_bias"], L["v_bias"]]),
+             self._group([L["o"]], b["attn"], [h], accumulate=True, biases=[L["o_bias"]]),
+             self._group([L["gate"], L["up"]], h, [b["gate"], b["up"]], norm=L["ffn_norm"],
+                         biases=[L["gate_bias"], L["up_bias"]]),
+             self._group([L["down"]], b["gate"], [h], up=b["up"], accumulate=True, biases=[L["down_bias"]]))
             for L in self.layers]
         b["head"] = (self._group([self.lm_head], h, [b["logits"]], norm=self.final_norm)
                      if self.lm_head is not None else None)
@@ -360,7 +436,9 @@ class GPUExecutionBackend:
         if b["head"] is not None:
             b["head"]()
         else:
-            torch.matmul(G.rms_norm(b["hidden"], self.final_norm, cfg.rms_norm_eps), self.embed.t(), out=b["logits"])
+            # tied embeddings (executor.py:333-334): the final norm, then x @ embed^T
+            G.rms_norm(b["hidden"], self.final_norm, cfg.rms_norm_eps, out=b["normed"])
+            torch.matmul(b["normed"], self.embed.t(), out=b["logits"])
 
     def _forward(self, slots: Sequence[int], tokens: Sequence[int], positions: Sequence[int]) -> torch.Tensor:
         """One pass of n <= 32 tokens (token i of cache slot slots[i] at

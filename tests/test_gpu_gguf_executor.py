@@ -1,6 +1,9 @@
-"""GPU decode step for GGUF llama models (dracort_b200.gguf_executor) against
-the reference executor's logits on tests/golden/tiny_llama_decode.gguf
-(tests/golden/make_decode_golden.py) and against the pinned decode oracle.
+"""GPU decode step for GGUF llama-family models (dracort_b200.gguf_executor)
+against the reference executor's logits on three fixtures
+(tests/golden/make_decode_golden.py): tiny_llama_decode.gguf (every GPU block
+type), tiny_qwen2_decode.gguf (q/k/v and o_proj biases, tied embeddings,
+rope base 1e6) and tiny_fused_decode.gguf (a fused q/k/v weight, gate/up/down
+biases), and against the pinned decode oracle.
 
 Bar: the decode GEMV's 1e-3 relative L2 per projection, carried through two
 layers and the output head: logits within 2e-3 relative L2, and the greedy
@@ -22,18 +25,23 @@ from dracort_b200.gguf_executor import GPUExecutionBackend  # noqa: E402
 from oracle.llama_decode import OracleLlama  # noqa: E402
 
 HERE = Path(__file__).resolve().parent / "golden"
-PATH = HERE / "tiny_llama_decode.gguf"
+FIXTURES = ["tiny_llama_decode", "tiny_qwen2_decode", "tiny_fused_decode"]
 TOL = 2e-3
 
 
-@pytest.fixture(scope="module")
-def ref():
-    return np.load(HERE / "tiny_llama_decode_ref.npz")
+@pytest.fixture(scope="module", params=FIXTURES)
+def name(request):
+    return request.param
 
 
 @pytest.fixture(scope="module")
-def backend():
-    return GPUExecutionBackend(str(PATH), max_num_seqs=4, q6k_order="d_first")
+def ref(name):
+    return np.load(HERE / f"{name}_ref.npz")
+
+
+@pytest.fixture(scope="module")
+def backend(name):
+    return GPUExecutionBackend(str(HERE / f"{name}.gguf"), max_num_seqs=4, q6k_order="d_first")
 
 
 def rel(a, b):
@@ -91,12 +99,12 @@ def test_batch_decode_of_two_sequences(backend, ref):
         backend.end_sequence(sb)
 
 
-def test_long_prompt_in_chunks_matches_oracle(backend):
+def test_long_prompt_in_chunks_matches_oracle(backend, name):
     """60 tokens (the fixture's context is 64): chunks of rows through the
     GEMV, each attending to the cache the earlier chunks wrote."""
     rng = np.random.default_rng(5)
     prompt = rng.integers(0, backend.config.vocab_size, 40)
-    gf = GGUFFile(str(PATH))
+    gf = GGUFFile(str(HERE / f"{name}.gguf"))
     try:
         orc = OracleLlama(gf, q6k_order="d_first")
     finally:
