@@ -90,11 +90,13 @@ class LlamaConfig:
         if vocab is None and "token_embd.weight" in gf.tensors:
             vocab = gf.tensor("token_embd.weight").shape[0]
         if None in (hidden, layers, heads, vocab):
-            raise DracoFormatError(f"GGUF '{gf.path}' is missing required architecture metadata "
-                                   f"(embedding_length / block_count / attention.head_count / vocab_size).")
+            missing = [k for k, v in (("embedding_length", hidden), ("block_count", layers),
+                                      ("attention.head_count", heads), ("vocab_size", vocab)) if v is None]
+            raise DracoFormatError(f"{gf.path}: no {', '.join(p + k for k in missing)} in the GGUF metadata")
         key_len = get("attention.key_length")
         if key_len is not None and int(key_len) != int(hidden) // int(heads):
-            raise DracoFormatError(f"GGUF '{gf.path}' uses a non-standard key_length {key_len}")
+            raise DracoFormatError(f"{gf.path}: attention key length {key_len} differs from "
+                                   f"embedding_length / head_count = {int(hidden) // int(heads)}")
         eps = get("attention.layer_norm_rms_epsilon") or get("attention.layer_norm_epsilon") or 1e-5
         return cls(hidden_size=int(hidden), num_hidden_layers=int(layers), num_attention_heads=int(heads),
                    num_key_value_heads=int(get("attention.head_count_kv") or heads), vocab_size=int(vocab),
