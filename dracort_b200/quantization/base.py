@@ -26,22 +26,22 @@ import torch.nn as nn
 
 
 class QuantizationBackend(abc.ABC):
-    """Abstract base class for quantization backends."""
+    """The contract a quantization method implements to plug into the registry."""
 
     @property
     @abc.abstractmethod
     def name(self) -> str:
-        """Human-readable name for this quantization method."""
+        """The method's registry name (lower case)."""
 
     @property
     @abc.abstractmethod
     def supported_bits(self) -> List[int]:
-        """Bit widths supported by this backend."""
+        """Weight bit widths the method stores."""
 
     @property
     @abc.abstractmethod
     def supported_schemes(self) -> List[str]:
-        """Quantization schemes (e.g. 'weight_only', 'w8a8')."""
+        """Which tensors are quantized: e.g. 'weight_only' or 'w8a8'."""
 
     @abc.abstractmethod
     def load_quantized_weights(
@@ -76,7 +76,7 @@ class QuantizationBackend(abc.ABC):
         return torch.nn.functional.linear(input, dequant_weight, bias)
 
     def supports_gpu_kernel(self, device: torch.device) -> bool:
-        """Whether this backend has GPU-optimized kernels available."""
+        """True when `device` runs this method with its own kernels rather than a dequantize-then-matmul fallback."""
         return device.type == "cuda"
 
     def get_kernel_info(self) -> Dict[str, Any]:
