@@ -22,16 +22,23 @@ GGML_TYPE_Q5_K = 13
 GGML_TYPE_Q6_K = 14
 GGML_TYPE_BF16 = 30
 
-#: (block_size, block_bytes) per supported quantized type (gguf.py:75-87)
+#: (block_size, block_bytes) per supported quantized type (gguf.py:75-87).
+#: Byte budget of one block, in field order: Q4_0 scale 2 + 16 nibble bytes;
+#: Q4_1 scale 2 + min 2 + 16; Q5_0 scale 2 + 4 fifth-bit bytes + 16; Q5_1
+#: scale 2 + min 2 + 4 + 16; Q8_0 scale 2 + 32 signed bytes; Q4_K super-scale
+#: 2 + super-min 2 + 12 packed 6-bit sub-scales/mins + 128 nibble bytes; Q5_K
+#: the same with 32 fifth-bit bytes before the nibbles; Q6_K (the order the
+#: reference decodes) scale 2 + 128 low-nibble bytes + 64 high-pair bytes + 16
+#: signed sub-scales.
 BLOCK_LAYOUTS: Dict[int, Tuple[int, int]] = {
-    GGML_TYPE_Q4_0: (32, 18),  # d: f16 + qs: uint8[16]
-    GGML_TYPE_Q4_1: (32, 20),  # d: f16 + m: f16 + qs: uint8[16]
-    GGML_TYPE_Q5_0: (32, 22),  # d: f16 + qh: uint8[4] + qs: uint8[16]
-    GGML_TYPE_Q5_1: (32, 24),  # d: f16 + m: f16 + qh: uint8[4] + qs: uint8[16]
-    GGML_TYPE_Q8_0: (32, 34),  # d: f16 + qs: int8[32]
-    GGML_TYPE_Q4_K: (256, 144),  # d: f16 + dmin: f16 + scales: uint8[12] + qs: uint8[128]
-    GGML_TYPE_Q5_K: (256, 176),  # d: f16 + dmin: f16 + scales: uint8[12] + qh: uint8[32] + qs: uint8[128]
-    GGML_TYPE_Q6_K: (256, 210),  # d: f16 + ql: uint8[128] + qh: uint8[64] + scales: int8[16]
+    GGML_TYPE_Q4_0: (32, 2 + 16),
+    GGML_TYPE_Q4_1: (32, 2 + 2 + 16),
+    GGML_TYPE_Q5_0: (32, 2 + 4 + 16),
+    GGML_TYPE_Q5_1: (32, 2 + 2 + 4 + 16),
+    GGML_TYPE_Q8_0: (32, 2 + 32),
+    GGML_TYPE_Q4_K: (256, 2 + 2 + 12 + 128),
+    GGML_TYPE_Q5_K: (256, 2 + 2 + 12 + 32 + 128),
+    GGML_TYPE_Q6_K: (256, 2 + 128 + 64 + 16),
 }
 
 TYPE_NAMES = {GGML_TYPE_Q4_0: "Q4_0", GGML_TYPE_Q4_1: "Q4_1", GGML_TYPE_Q5_0: "Q5_0", GGML_TYPE_Q5_1: "Q5_1",
